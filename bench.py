@@ -1,0 +1,320 @@
+"""Benchmark of the cwen B200 verify-decode engine (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload gemv]
+
+Workload `gemv`: the B=8 Q4_0 verify GEMV, W 17408x5120,
+X fp32 8x5120 ~N(0,1), scales |N(0,0.01)|, nibbles uniform.  A step is one
+call over a weight copy from a ring of 8 distinct copies (400 MB > 126 MB L2),
+so every step streams W from HBM.  value = algorithmic bytes / device time.
+
+Multi-GPU: one process per GPU (torchrun); the GEMV has no exchange, each
+rank runs the same per-GPU work ("scaling": "weak"), the barrier-bracketed
+device time is max-reduced over ranks.
+
+The CPU baseline (rank 0, N=1) and `--impl reference` run the reference's own
+C code (maci0/cwen run.c compiled into oracle/_ref) on the same bytes.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import json
+import os
+import platform
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+sys.path.insert(0, str(ROOT / "tests"))
+
+GEMV_K, GEMV_M, GEMV_B = 5120, 17408, 8
+GEMV_BYTES = (GEMV_K // 32) * 18 * GEMV_M + GEMV_B * GEMV_K * 4 + GEMV_B * GEMV_M * 4  # 50,855,936
+RING = 8
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle sampling during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.rows = []
+        self._stop = threading.Event()
+        self._t = None
+
+    def start(self):
+        def run():
+            while not self._stop.is_set():
+                try:
+                    out = subprocess.run(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits"], capture_output=True, text=True,
+                                         timeout=5).stdout.strip()
+                    if out:
+                        self.rows.append([s.strip() for s in out.split(",")])
+                except Exception:
+                    pass
+                self._stop.wait(0.2)
+        self._t = threading.Thread(target=run, daemon=True)
+        self._t.start()
+
+    def stop(self):
+        self._stop.set()
+        if self._t:
+            self._t.join(timeout=10)
+        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in self.rows:
+            for n, v in zip(names, r[5:9]):
+                if v.strip().lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(self.rows)}
+
+
+def dist_init(args):
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if ws > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+    return ws, rank, local
+
+
+def barrier_max(ws, value: float) -> float:
+    if ws == 1:
+        return value
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(ws):
+    if ws > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+# ---------------- reference (CPU) ----------------
+def ref_lib_path():
+    flags = ""
+    try:
+        flags = Path("/proc/cpuinfo").read_text()
+    except Exception:
+        pass
+    need = ["avx512f", "avx512bw", "avx512vl", "avx512dq", "avx512_vnni"]
+    v = "avx512" if all(f in flags for f in need) else "avx2"
+    return ROOT / "oracle" / "_ref" / f"libcwref_{v}.so", v
+
+
+def host_cores():
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def cpu_gemv_baseline(W, X, budget_s: float = 12.0):
+    """Reference gemvb (run.c:1577) on the GGUF Q4_0 layout and on its split
+    T_Q4_0RS layout (dot_q4_bcol, run.c:1544), best of the two; bounded by
+    a time budget.  Returns (GB/s of the config-0 algorithmic bytes, info)."""
+    path, variant = ref_lib_path()
+    if not path.exists():
+        return None
+    os.environ.setdefault("OMP_NUM_THREADS", str(host_cores()))
+    os.environ.setdefault("OMP_PROC_BIND", "close")
+    os.environ.setdefault("OMP_PLACES", "cores")
+    ref = C.CDLL(str(path))
+    ref.cwref_threads.restype = C.c_int
+    vp = lambda a: a.ctypes.data_as(C.c_void_p)
+    K, M, B = GEMV_K, GEMV_M, GEMV_B
+    Y = np.zeros((B, M), np.float32)
+    nb = K // 32
+    qs = np.zeros(nb * M * 16 + 64, np.uint8)
+    off = (-qs.ctypes.data) % 64
+    qs = qs[off:off + nb * M * 16]
+    sc = np.zeros(nb * M, np.uint16)
+    ref.cwref_split_q4_0(vp(W), K, M, vp(qs), vp(sc))
+    best = None
+    for name, fn in (("gguf_q4_0", lambda: ref.cwref_gemvb(2, vp(W), K, M, vp(X), K, vp(Y), M, B)),
+                     ("split_q4_0rs", lambda: ref.cwref_gemvb_split(vp(qs), vp(sc), K, M, vp(X), K, vp(Y), M, B))):
+        fn()
+        n, t0 = 0, time.perf_counter()
+        while True:
+            fn()
+            n += 1
+            el = time.perf_counter() - t0
+            if el > budget_s / 2 or n >= 200:
+                break
+        gbs = GEMV_BYTES * n / el / 1e9
+        if best is None or gbs > best[0]:
+            best = (gbs, name, n, el)
+    gbs, name, n, el = best
+    return gbs, {"kind": "reference", "cores": int(ref.cwref_threads()), "variant": f"{variant}/{name}",
+                 "sample": f"{n} B=8 gemvb calls on W 17408x5120 Q4_0 ({el:.1f} s)"}
+
+
+# ---------------- our engine ----------------
+def make_gemv_inputs(seed=1):
+    from oracle_lib import gen_normal, gen_q, load_oracle
+    orc = load_oracle()
+    W = gen_q(orc, seed, "bench.gemv.w", 2, GEMV_K, GEMV_M)
+    X = gen_normal(orc, seed + 1, "bench.gemv.x", GEMV_B * GEMV_K).reshape(GEMV_B, GEMV_K)
+    return W, X
+
+
+def run_gemv_ours(args, ws, rank, local):
+    import torch
+
+    import cwen_b200
+    from cwen_b200 import build
+    build.build()
+    L = cwen_b200.lib()
+    cwen_b200.check(L.cwen_cuda_init(local, 64, 16), "init")
+    W, X = make_gemv_inputs()
+    wids = []
+    for _ in range(RING):
+        wid = C.c_int(-1)
+        cwen_b200.check(L.cwen_cuda_weight_upload(2, W.ctypes.data_as(C.c_void_p), GEMV_K, GEMV_M, C.byref(wid)))
+        wids.append(wid.value)
+    dev = torch.device("cuda", local)
+    dX = torch.from_numpy(X).to(dev)
+    dY = torch.zeros((GEMV_B, GEMV_M), dtype=torch.float32, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+    sp = C.c_void_p(stream.cuda_stream)
+
+    def step(i):
+        cwen_b200.check(L.cwen_cuda_gemvb(wids[i % RING], C.c_void_p(dX.data_ptr()), GEMV_K,
+                                          C.c_void_p(dY.data_ptr()), GEMV_M, GEMV_B, sp))
+
+    with torch.cuda.stream(stream):
+        for i in range(args.warmup):
+            step(i)
+    torch.cuda.synchronize()
+    barrier(ws)
+    clocks = ClockSampler(local)
+    clocks.start()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    cwen_b200.check(L.cwen_cuda_profile(1), "profile")
+    torch.cuda.synchronize()
+    ev0.record(stream)
+    for i in range(args.steps):
+        step(i)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1) / args.steps
+    clk = clocks.stop()
+    gm, gb, gc, nl = C.c_double(), C.c_double(), C.c_longlong(), C.c_longlong()
+    cwen_b200.check(L.cwen_cuda_profile_read(C.byref(gm), C.byref(gb), C.byref(gc), C.byref(nl)), "profile_read")
+    cwen_b200.check(L.cwen_cuda_profile(0), "profile")
+    kern = {"ms": gm.value / max(gc.value, 1), "bytes": gb.value / max(gc.value, 1), "launches": nl.value}
+    ms = barrier_max(ws, ms)
+
+    # end to end through the host-buffer entry point (copies in the timed region)
+    hX = np.ascontiguousarray(X)
+    hY = np.zeros((GEMV_B, GEMV_M), np.float32)
+    for i in range(3):
+        cwen_b200.check(L.cwen_cuda_gemvb_host(wids[i % RING], hX.ctypes.data_as(C.c_void_p), GEMV_K,
+                                               hY.ctypes.data_as(C.c_void_p), GEMV_M, GEMV_B))
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        cwen_b200.check(L.cwen_cuda_gemvb_host(wids[i % RING], hX.ctypes.data_as(C.c_void_p), GEMV_K,
+                                               hY.ctypes.data_as(C.c_void_p), GEMV_M, GEMV_B))
+    e2e_s = (time.perf_counter() - t0) / args.steps
+    e2e_s = barrier_max(ws, e2e_s)
+    L.cwen_cuda_shutdown()
+    return ms, kern, e2e_s, clk, W, X
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="gemv", choices=["gemv"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    ws, rank, local = dist_init(args)
+    hbm, bf16, peak_kind = peaks()
+    config = {"workload": "config0: Q4_0 verify GEMV W[17408x5120], X fp32[8x5120], Y[8x17408]",
+              "B": GEMV_B, "K": GEMV_K, "M": GEMV_M,
+              "l2": "weight ring of 8 copies (400 MB > 126 MB L2), new copy every step",
+              "parallelism": f"replicas{ws}" if ws > 1 else "single"}
+    if args.impl == "reference":
+        if rank != 0:
+            return 0
+        W, X = make_gemv_inputs()
+        res = cpu_gemv_baseline(W, X, budget_s=max(4.0, min(60.0, 2.0 * args.steps)))
+        if res is None:
+            print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref reference build missing"}))
+            return 0
+        gbs, info = res
+        line = {"impl": "reference", "metric": "verify-GEMV GB/s (B=8 Q4_0, config 0)", "value": round(gbs, 2),
+                "unit": "GB/s", "n_gpus": 0, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": round(GEMV_BYTES / gbs / 1e6, 4), "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "q4_0 x fp32 -> fp32", "data": "synthetic (seeded)",
+                "config": config, "cpu_baseline": {**info, "value": round(gbs, 2), "unit": "GB/s"},
+                "e2e": {"value": round(gbs, 2), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line))
+        return 0
+
+    ms, kern, e2e_s, clk, W, X = run_gemv_ours(args, ws, rank, local)
+    gbs = GEMV_BYTES / (ms * 1e-3) / 1e9
+    total = gbs * ws
+    line = {"metric": "verify-GEMV GB/s (B=8 Q4_0, config 0)", "value": round(total, 2), "unit": "GB/s",
+            "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "q4_0 x fp32 -> fp32",
+            "data": "synthetic (seeded)", "config": config, "gpu_launches": kern["launches"], "clocks": clk}
+    kern_ms = kern["ms"]
+    ach = kern["bytes"] / (kern_ms * 1e-3) / 1e9
+    line["roofline"] = {"bound": "hbm", "achieved": round(ach, 1), "peak": hbm, "unit": "GB/s",
+                        "frac": round(ach / hbm, 4), "peak_kind": peak_kind, "traffic": None,
+                        "kernel": "qgemv_kernel<Q4_0,NT=1>", "kernel_ms": round(kern_ms, 5)}
+    e2e_gbs = GEMV_BYTES / e2e_s / 1e9
+    line["e2e"] = {"value": round(e2e_gbs * ws, 2), "unit": "GB/s", "h2d_bytes_per_step": GEMV_B * GEMV_K * 4,
+                   "d2h_bytes_per_step": GEMV_B * GEMV_M * 4,
+                   "note": "cwen_cuda_gemvb_host: pinned-free host X in, host Y out, synchronous"}
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+        res = cpu_gemv_baseline(W, X)
+        if res:
+            line["cpu_baseline"] = {**res[1], "value": round(res[0], 2), "unit": "GB/s"}
+    if rank == 0:
+        print(json.dumps(line))
+    if ws > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,256 @@
+// C ABI entry points (include/cwen_cuda.h): engine lifetime and the
+// stand-alone verify GEMV.
+#include <string.h>
+
+#include "engine.cuh"
+
+namespace cw {
+
+static Engine g_engine;
+static char g_err[512] = "no error";
+
+Engine &engine() { return g_engine; }
+
+void set_error(const char *fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof g_err, fmt, ap);
+  va_end(ap);
+}
+
+int cuda_fail(cudaError_t e, const char *what) {
+  set_error("%s: %s", what, cudaGetErrorString(e));
+  return e == cudaErrorMemoryAllocation ? CWEN_ENOMEM : CWEN_ECUDA;
+}
+
+int ensure_staging(size_t bytes) {
+  Engine &E = engine();
+  if (E.staging_bytes >= bytes) return CWEN_OK;
+  if (E.staging) cudaFree(E.staging);
+  E.staging = nullptr;
+  E.staging_bytes = 0;
+  CW_CHECK(cudaMalloc(&E.staging, bytes));
+  E.staging_bytes = bytes;
+  return CWEN_OK;
+}
+
+int ensure_io(size_t floats) {
+  Engine &E = engine();
+  if (E.io_floats >= floats) return CWEN_OK;
+  if (E.io) cudaFree(E.io);
+  E.io = nullptr;
+  E.io_floats = 0;
+  CW_CHECK(cudaMalloc(&E.io, floats * sizeof(float)));
+  E.io_floats = floats;
+  return CWEN_OK;
+}
+
+static int upload_qmat(int type, const void *host, int ne0, int ne1, QMat &m, int mt_off, int mt_stride) {
+  Engine &E = engine();
+  const size_t rb = (size_t)(ne0 / 32) * (type == CWEN_T_Q8_0 ? 34 : 18);
+  const size_t bytes = rb * (size_t)ne1;
+  // Chunk by whole 16-row groups so each repack sees complete m-tiles.
+  const size_t max_chunk = (size_t)256 << 20;
+  size_t rows_per = (max_chunk / rb) / 16 * 16;
+  if (rows_per < 16) rows_per = 16;
+  int rc = ensure_staging(rows_per * rb < bytes ? rows_per * rb : bytes);
+  if (rc) return rc;
+  for (size_t r0 = 0; r0 < (size_t)ne1; r0 += rows_per) {
+    const size_t nr = (size_t)ne1 - r0 < rows_per ? (size_t)ne1 - r0 : rows_per;
+    CW_CHECK(cudaMemcpyAsync(E.staging, (const uint8_t *)host + r0 * rb, nr * rb, cudaMemcpyHostToDevice, E.stream));
+    CW_CHECK(qmat_repack(m, E.staging, (int)nr, mt_off + (int)(r0 / 16) * mt_stride, mt_stride, E.stream));
+    CW_CHECK(cudaStreamSynchronize(E.stream));
+  }
+  return CWEN_OK;
+}
+
+cudaError_t timed_gemv(const QMat &m, int B, float *Y, int ys, int epi, cudaStream_t st) {
+  Engine &E = engine();
+  Prof &P = E.prof;
+  E.prof.launches += 1;
+  if (!P.on) return gemv_run(m, B, Y, ys, epi, E.gs, st);
+  if (P.used + 2 > P.ev.size()) {
+    for (int i = 0; i < 256; i++) {
+      cudaEvent_t e;
+      cudaError_t r = cudaEventCreate(&e);
+      if (r != cudaSuccess) return r;
+      P.ev.push_back(e);
+    }
+  }
+  cudaEvent_t a = P.ev[P.used], b = P.ev[P.used + 1];
+  cudaEventRecord(a, st);
+  cudaError_t r = gemv_run(m, B, Y, ys, epi, E.gs, st);
+  cudaEventRecord(b, st);
+  P.used += 2;
+  const double wbytes = (double)(m.K / 32) * (m.type == 8 ? 34 : 18) * (double)m.M;
+  P.bytes.push_back(wbytes + 4.0 * B * m.K + 4.0 * B * m.M);
+  return r;
+}
+
+int alloc_qmat(QMat &m, int type, int K, int n_mt, int M) {
+  m.type = type;
+  m.K = K;
+  m.n_mt = n_mt;
+  m.M = M;
+  m.bytes = qmat_bytes(type, K, n_mt);
+  CW_CHECK(cudaMalloc(&m.w, m.bytes));
+  CW_CHECK(cudaMemsetAsync(m.w, 0, m.bytes, engine().stream));
+  return CWEN_OK;
+}
+
+}  // namespace cw
+
+using namespace cw;
+
+extern "C" {
+
+const char *cwen_cuda_last_error(void) { return g_err; }
+
+int cwen_cuda_init(int device, int ctx, int bmax) {
+  Engine &E = engine();
+  if (E.live) {
+    set_error("cwen_cuda_init: already initialised");
+    return CWEN_ESTATE;
+  }
+  if (bmax < 1 || bmax > QG_MAXB || ctx < 1) {
+    set_error("cwen_cuda_init: bmax must be in [1,%d] and ctx >= 1", QG_MAXB);
+    return CWEN_EINVAL;
+  }
+  CW_CHECK(cudaSetDevice(device));
+  E.device = device;
+  E.ctx = ctx;
+  E.bmax = bmax;
+  CW_CHECK(cudaDeviceGetAttribute(&E.n_sm, cudaDevAttrMultiProcessorCount, device));
+  CW_CHECK(cudaStreamCreateWithFlags(&E.stream, cudaStreamNonBlocking));
+  GemvScratch &s = E.gs;
+  s.kmax = 32768;
+  s.G = 2 * E.n_sm;
+  s.max_tiles = 1 << 16;
+  CW_CHECK(cudaMalloc(&s.xf, (size_t)(s.kmax / 32) * 2 * 2 * 32 * sizeof(uint4)));
+  CW_CHECK(cudaMalloc(&s.xexp, QG_MAXB * sizeof(int)));
+  CW_CHECK(cudaMalloc(&s.ws, gemv_scratch_ws_floats(s.G) * sizeof(float)));
+  CW_CHECK(cudaMalloc(&s.cnt, (size_t)s.max_tiles * sizeof(int)));
+  CW_CHECK(cudaMemset(s.cnt, 0, (size_t)s.max_tiles * sizeof(int)));
+  E.live = true;
+  return CWEN_OK;
+}
+
+void cwen_cuda_shutdown(void) {
+  Engine &E = engine();
+  if (!E.live) return;
+  cudaStreamSynchronize(E.stream);
+  for (auto &m : E.mats) cudaFree(m.w);
+  E.mats.clear();
+  for (auto e : E.prof.ev) cudaEventDestroy(e);
+  cudaFree(E.gs.xf);
+  cudaFree(E.gs.xexp);
+  cudaFree(E.gs.ws);
+  cudaFree(E.gs.cnt);
+  if (E.staging) cudaFree(E.staging);
+  if (E.io) cudaFree(E.io);
+  cudaStreamDestroy(E.stream);
+  E = Engine();
+}
+
+int cwen_cuda_weight_upload(int type, const void *host, int ne0, int ne1, int *wid) {
+  Engine &E = engine();
+  if (!E.live) {
+    set_error("cwen_cuda_weight_upload: engine not initialised");
+    return CWEN_ESTATE;
+  }
+  if ((type != CWEN_T_Q4_0 && type != CWEN_T_Q8_0) || !host || !wid || ne0 <= 0 || ne1 <= 0 || ne0 % 64 ||
+      ne0 > E.gs.kmax) {
+    set_error("cwen_cuda_weight_upload: need Q4_0/Q8_0, ne0 a positive multiple of 64 <= %d, ne1 > 0", E.gs.kmax);
+    return CWEN_EINVAL;
+  }
+  QMat m;
+  int rc = alloc_qmat(m, type, ne0, (ne1 + 15) / 16, ne1);
+  if (rc) return rc;
+  rc = upload_qmat(type, host, ne0, ne1, m, 0, 1);
+  if (rc) {
+    cudaFree(m.w);
+    return rc;
+  }
+  E.mats.push_back(m);
+  *wid = (int)E.mats.size() - 1;
+  return CWEN_OK;
+}
+
+int cwen_cuda_gemvb(int wid, const float *dX, int xs, float *dY, int ys, int B, void *stream) {
+  Engine &E = engine();
+  if (!E.live || wid < 0 || wid >= (int)E.mats.size()) {
+    set_error("cwen_cuda_gemvb: bad weight handle %d", wid);
+    return E.live ? CWEN_EINVAL : CWEN_ESTATE;
+  }
+  const QMat &m = E.mats[wid];
+  if (B < 1 || B > E.bmax || !dX || !dY || xs < m.K || ys < m.M) {
+    set_error("cwen_cuda_gemvb: need 1 <= B <= %d, xs >= K, ys >= M", E.bmax);
+    return CWEN_EINVAL;
+  }
+  cudaStream_t st = stream ? (cudaStream_t)stream : E.stream;
+  CW_CHECK(gemv_prep_x(dX, xs, B, m.K, E.gs, st));
+  E.prof.launches += 1;
+  CW_CHECK(timed_gemv(m, B, dY, ys, EPI_STORE, st));
+  return CWEN_OK;
+}
+
+int cwen_cuda_profile(int on) {
+  Engine &E = engine();
+  if (!E.live) {
+    set_error("cwen_cuda_profile: engine not initialised");
+    return CWEN_ESTATE;
+  }
+  CW_CHECK(cudaStreamSynchronize(E.stream));
+  E.prof.on = on != 0;
+  E.prof.used = 0;
+  E.prof.bytes.clear();
+  E.prof.launches = 0;
+  return CWEN_OK;
+}
+
+int cwen_cuda_profile_read(double *gemv_ms, double *gemv_bytes, long long *gemv_calls, long long *launches) {
+  Engine &E = engine();
+  if (!E.live) {
+    set_error("cwen_cuda_profile_read: engine not initialised");
+    return CWEN_ESTATE;
+  }
+  Prof &P = E.prof;
+  double ms = 0, by = 0;
+  for (size_t i = 0; i + 1 < P.used; i += 2) {
+    CW_CHECK(cudaEventSynchronize(P.ev[i + 1]));
+    float t = 0;
+    CW_CHECK(cudaEventElapsedTime(&t, P.ev[i], P.ev[i + 1]));
+    ms += t;
+    by += P.bytes[i / 2];
+  }
+  if (gemv_ms) *gemv_ms = ms;
+  if (gemv_bytes) *gemv_bytes = by;
+  if (gemv_calls) *gemv_calls = (long long)(P.used / 2);
+  if (launches) *launches = P.launches;
+  return CWEN_OK;
+}
+
+int cwen_cuda_gemvb_host(int wid, const float *hX, int xs, float *hY, int ys, int B) {
+  Engine &E = engine();
+  if (!E.live || wid < 0 || wid >= (int)E.mats.size()) {
+    set_error("cwen_cuda_gemvb_host: bad weight handle %d", wid);
+    return E.live ? CWEN_EINVAL : CWEN_ESTATE;
+  }
+  const QMat &m = E.mats[wid];
+  if (B < 1 || B > E.bmax || !hX || !hY || xs < m.K || ys < m.M) {
+    set_error("cwen_cuda_gemvb_host: need 1 <= B <= %d, xs >= K, ys >= M", E.bmax);
+    return CWEN_EINVAL;
+  }
+  const size_t nx = (size_t)B * xs, ny = (size_t)B * ys;
+  int rc = ensure_io(nx + ny);
+  if (rc) return rc;
+  float *dX = E.io, *dY = E.io + nx;
+  CW_CHECK(cudaMemcpyAsync(dX, hX, nx * sizeof(float), cudaMemcpyHostToDevice, E.stream));
+  rc = cwen_cuda_gemvb(wid, dX, xs, dY, ys, B, E.stream);
+  if (rc) return rc;
+  CW_CHECK(cudaMemcpyAsync(hY, dY, ny * sizeof(float), cudaMemcpyDeviceToHost, E.stream));
+  CW_CHECK(cudaStreamSynchronize(E.stream));
+  return CWEN_OK;
+}
+
+}  // extern "C"

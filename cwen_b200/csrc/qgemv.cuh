@@ -1,0 +1,61 @@
+// Batched quantized GEMV (verify GEMV) -- host-side interface.
+//
+// Y[b*ys + i] = sum_k W[i,k] * X[b*xs + k] for b < B <= 16, W in GGUF Q4_0 or
+// Q8_0 (f16 scale per 32 weights).  Replaces gemvb()/gemv() of the reference
+// (run.c:1577, run.c:1419).
+#pragma once
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace cw {
+
+// Device layout of one (possibly fused) weight matrix: rows grouped in
+// 16-row m-tiles; per (m-tile, pair of 32-blocks) one 576-byte chunk
+// [512 B nibbles in mma A-fragment order | 64 B f16 scales].
+// Q8_0 uses 1088-byte chunks [1024 B int8 | 64 B scales].
+struct QMat {
+  uint8_t *w = nullptr;  // device
+  int type = 0;          // 2 = Q4_0, 8 = Q8_0
+  int K = 0;             // row length
+  int n_mt = 0;          // m-tiles (16 rows)
+  int M = 0;             // valid rows (n_mt*16 >= M)
+  size_t bytes = 0;
+};
+
+enum { EPI_STORE = 0, EPI_ADD = 1, EPI_SWIGLU = 2 };
+
+constexpr int QG_MAXB = 16;
+constexpr int QG_WARPS = 8;
+constexpr int QG_TILE_MT = 2 * QG_WARPS;  // m-tiles per CTA tile
+constexpr int QG_STAGES = 6;
+
+inline size_t qmat_chunk_bytes(int type) { return type == 8 ? 1088 : 576; }
+inline size_t qmat_bytes(int type, int K, int n_mt) { return qmat_chunk_bytes(type) * (size_t)(K / 64) * (size_t)n_mt; }
+
+// Scratch the GEMV needs (owned by the caller, reused across calls on one stream).
+struct GemvScratch {
+  uint4 *xf = nullptr;   // X fragments, >= (Kmax/32) * 2 ntiles * 2 * 32 uint4
+  int *xexp = nullptr;   // [16] per-column exponents
+  float *ws = nullptr;   // split-K partials [G][2][16*16*16]
+  int *cnt = nullptr;    // per CTA-tile arrival counters (zeroed once)
+  int G = 0;             // persistent grid size (CTAs)
+  int kmax = 0;
+  int max_tiles = 0;
+};
+size_t gemv_scratch_ws_floats(int G);
+
+// Repack `M` GGUF rows (Q4_0 18 B/block or Q8_0 34 B/block) already on the
+// device at `src` into `dst`: source row r lands in m-tile
+// mt_off + (r/16)*mt_stride, row r%16 of that tile.
+cudaError_t qmat_repack(const QMat &dst, const uint8_t *src, int M, int mt_off, int mt_stride, cudaStream_t st);
+
+// X fp32 [B][xs] -> fragments + exponents (scratch).
+cudaError_t gemv_prep_x(const float *X, int xs, int B, int K, GemvScratch &s, cudaStream_t st);
+// GEMV over prepared X.  epi selects the output: store, add into Y
+// (residual), or SiLU(gate)*up of an interleaved gate/up matrix.
+cudaError_t gemv_run(const QMat &m, int B, float *Y, int ys, int epi, GemvScratch &s, cudaStream_t st);
+// Kernel-count helper for bench bookkeeping.
+inline int gemv_launches() { return 2; }
+
+}  // namespace cw

@@ -1,0 +1,82 @@
+/* cwen_cuda.h -- C ABI of the B200 speculative block-verify decode engine.
+ *
+ * The reference (maci0/cwen, single file run.c) has no FFI: its hot path is a
+ * set of static C functions over process globals.  Each entry point below
+ * replaces one of them for a C host that keeps the reference's loaders,
+ * knobs and drafters; the reference function it stands in for is cited.
+ *
+ * Conventions (differences from the reference are deliberate):
+ *  - every function returns 0 or a negative CWEN_E* code and never exits the
+ *    process (the reference calls exit(1) on bad input);
+ *    cwen_cuda_last_error() describes the most recent failure;
+ *  - the library owns all device memory; one engine per process, driven
+ *    from one host thread (the reference is likewise single-threaded and
+ *    not re-entrant), bound to one GPU;
+ *  - weights arrive in GGUF layout (Q4_0 / Q8_0 / F32) from host memory and
+ *    are repacked on the device.
+ */
+#ifndef CWEN_CUDA_H
+#define CWEN_CUDA_H
+#include <stddef.h>
+#include <stdint.h>
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  CWEN_OK = 0,
+  CWEN_EINVAL = -1,   /* bad argument (the reference: exit(1)/assert) */
+  CWEN_ECUDA = -2,    /* CUDA runtime error */
+  CWEN_ENOMEM = -3,   /* device allocation failed */
+  CWEN_ESTATE = -4,   /* call out of order (no init / model incomplete) */
+  CWEN_ERANGE = -5,   /* token id or position out of range */
+  CWEN_ETIMEOUT = -6  /* a bounded device wait gave up */
+};
+
+/* ggml tensor types accepted by the upload calls (GGUF numbering). */
+enum { CWEN_T_F32 = 0, CWEN_T_Q4_0 = 2, CWEN_T_Q8_0 = 8 };
+
+/* Model geometry; the reference fixes it at compile time (run.c:83-91). */
+typedef struct {
+  int n_embd, n_ff, n_vocab, n_layer;
+  int n_head, n_head_kv, head_dim, n_rot;
+  int ssm_n_kh, ssm_n_vh, ssm_d, conv_k;
+  int full_interval;
+  int has_mtp;
+} cwen_dims;
+
+/* Description of the last failure (static storage, never NULL). */
+const char *cwen_cuda_last_error(void);
+
+/* Select `device`, create the engine's stream and GEMV scratch.  `ctx` is the
+ * context window (CWEN_CTX, run.c:4098-4104) and `bmax` the largest verify
+ * block (SPEC_BMAX = 16, run.c:192).  Replaces alloc_state (run.c:3928) for
+ * the kernel-level scratch. */
+int cwen_cuda_init(int device, int ctx, int bmax);
+/* Free everything (process exit in the reference). */
+void cwen_cuda_shutdown(void);
+
+/* ---- stand-alone verify GEMV (gemvb, run.c:1577) ---- */
+/* Upload one GGUF Q4_0/Q8_0 matrix (ne0 = K row length, ne1 = M rows) from
+ * host memory; returns a handle in *wid. */
+int cwen_cuda_weight_upload(int type, const void *host, int ne0, int ne1, int *wid);
+/* Y[b*ys + i] = row i of W . X[b*xs ...], b < B <= 16, device pointers,
+ * ordered on `stream` (NULL: the engine's stream).  Batch-invariant: column b
+ * is bit-identical for every B.  Replaces gemvb (run.c:1577). */
+int cwen_cuda_gemvb(int wid, const float *dX, int xs, float *dY, int ys, int B, void *stream);
+/* The same with host buffers: copies X in, runs, copies Y out, synchronizes. */
+int cwen_cuda_gemvb_host(int wid, const float *hX, int xs, float *hY, int ys, int B);
+
+/* ---- instrumentation (the reference's CWEN_SPEC_DEBUG timers, run.c:3133) ---- */
+/* Reset counters and turn per-launch CUDA-event timing of the verify-GEMV
+ * kernel on or off (timing adds two event records per GEMV launch). */
+int cwen_cuda_profile(int on);
+/* Sum of GEMV kernel durations (ms) and of their algorithmic bytes, number of
+ * timed GEMV launches, and the number of kernels the engine launched since
+ * cwen_cuda_profile(); synchronizes on the recorded events. */
+int cwen_cuda_profile_read(double *gemv_ms, double *gemv_bytes, long long *gemv_calls, long long *launches);
+
+#ifdef __cplusplus
+}
+#endif
+#endif
