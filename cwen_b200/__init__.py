@@ -22,6 +22,14 @@ class Dims(C.Structure):
         "ssm_n_kh", "ssm_n_vh", "ssm_d", "conv_k", "full_interval", "has_mtp")]
 
 
+class SpecCfg(C.Structure):
+    _fields_ = [(n, C.c_int) for n in ("spec", "use_mtp", "max_draft", "min_draft", "n_key", "cooldown", "debug")]
+
+
+class SpecStats(C.Structure):
+    _fields_ = [(n, C.c_longlong) for n in ("cycles", "drafted", "full", "shortw", "kept", "plain_steps")]
+
+
 class CwenError(RuntimeError):
     pass
 
@@ -36,6 +44,30 @@ _SIGS = {
     "cwen_cuda_weight_upload": (C.c_int, [C.c_int, C.c_void_p, C.c_int, C.c_int, C.POINTER(C.c_int)]),
     "cwen_cuda_gemvb": (C.c_int, [C.c_int, C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_int, C.c_void_p]),
     "cwen_cuda_gemvb_host": (C.c_int, [C.c_int, C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_int]),
+    "cwen_cuda_model_config": (C.c_int, [C.POINTER(Dims)]),
+    "cwen_cuda_upload": (C.c_int, [C.c_char_p, C.c_int, C.c_void_p, C.c_int, C.c_int]),
+    "cwen_cuda_model_finalize": (C.c_int, []),
+    "cwen_cuda_reset": (C.c_int, []),
+    "cwen_cuda_n_past": (C.c_int, []),
+    "cwen_cuda_forward_block": (C.c_int, [C.c_void_p, C.c_int, C.c_int]),
+    "cwen_cuda_accept": (C.c_int, [C.POINTER(C.c_int), C.POINTER(C.c_int), C.c_void_p]),
+    "cwen_cuda_commit": (C.c_int, [C.c_int]),
+    "cwen_cuda_forward_serial": (C.c_int, [C.c_int, C.c_int, C.POINTER(C.c_int)]),
+    "cwen_cuda_logits": (C.c_int, [C.c_int, C.c_void_p]),
+    "cwen_cuda_hidden": (C.c_int, [C.c_int, C.c_void_p]),
+    "cwen_cuda_dump_layers": (C.c_int, [C.c_int]),
+    "cwen_cuda_dump_read": (C.c_int, [C.c_int, C.c_int, C.c_void_p]),
+    "cwen_cuda_gdn_state": (C.c_int, [C.c_int, C.c_void_p, C.c_void_p]),
+    "cwen_cuda_ctx": (C.c_int, []),
+    "cwen_load_gguf": (C.c_int, [C.c_char_p]),
+    "cwen_load_synth": (C.c_int, [C.c_uint64, C.POINTER(Dims), C.c_int]),
+    "cwen_dims_reference": (None, [C.POINTER(Dims)]),
+    "cwen_dims_small": (None, [C.POINTER(Dims)]),
+    "cwen_spec_defaults": (None, [C.POINTER(SpecCfg)]),
+    "cwen_spec_from_env": (C.c_int, [C.POINTER(SpecCfg)]),
+    "cwen_generate": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.POINTER(SpecCfg),
+                                C.POINTER(SpecStats)]),
+    "cwen_ngram_draft": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_int]),
     "cwen_cuda_profile": (C.c_int, [C.c_int]),
     "cwen_cuda_profile_read": (C.c_int, [C.POINTER(C.c_double), C.POINTER(C.c_double),
                                          C.POINTER(C.c_longlong), C.POINTER(C.c_longlong)]),
@@ -67,3 +99,30 @@ def ptr(a) -> C.c_void_p:
     if hasattr(a, "data_ptr"):
         return C.c_void_p(a.data_ptr())
     return a.ctypes.data_as(C.c_void_p)
+
+
+def dims(kind: str = "reference") -> Dims:
+    d = Dims()
+    (lib().cwen_dims_small if kind == "small" else lib().cwen_dims_reference)(C.byref(d))
+    return d
+
+
+def spec_cfg(**kw) -> SpecCfg:
+    c = SpecCfg()
+    lib().cwen_spec_defaults(C.byref(c))
+    for k, v in kw.items():
+        setattr(c, k, int(v))
+    return c
+
+
+def generate(tokens, n_gen: int, cfg: SpecCfg | None = None):
+    """Prefill `tokens` and greedily generate n_gen ids through the C host
+    driver (serial, or speculative when cfg.spec)."""
+    import numpy as np
+    t = np.ascontiguousarray(tokens, dtype=np.int32)
+    out = np.zeros(max(n_gen, 1), dtype=np.int32)
+    st = SpecStats()
+    n = lib().cwen_generate(ptr(t), len(t), n_gen, ptr(out), C.byref(cfg) if cfg else None, C.byref(st))
+    if n < 0:
+        check(n, "cwen_generate")
+    return out[:n], st

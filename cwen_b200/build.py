@@ -18,6 +18,7 @@ PKG = Path(__file__).resolve().parent
 ROOT = PKG.parent
 BUILD = PKG / "_build"
 LIB = PKG / "libcwen_cuda.so"
+CLI = PKG / "cwen"
 NVCC = shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVFLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xptxas", "-v",
@@ -56,6 +57,8 @@ def build(verbose: bool = False) -> Path:
         if _stale(obj, src, deps):
             jobs.append(([NVCC, *ARCH, *NVFLAGS, "-c", str(src), "-o", str(obj)], BUILD / (src.stem + ".log")))
     for src in sorted((PKG / "host").glob("*.c")):
+        if src.stem.endswith("_main"):
+            continue
         obj = BUILD / (src.stem + ".o")
         objs.append(obj)
         if _stale(obj, src, deps):
@@ -64,6 +67,11 @@ def build(verbose: bool = False) -> Path:
         list(ex.map(lambda j: _run(*j), jobs))
     if jobs or not LIB.exists() or any(o.stat().st_mtime > LIB.stat().st_mtime for o in objs):
         _run([NVCC, *ARCH, "-shared", "-o", str(LIB), *map(str, objs), "-lpthread", "-lm"], BUILD / "link.log")
+    main_src = PKG / "host" / "cwen_main.c"
+    if main_src.exists() and (not CLI.exists() or CLI.stat().st_mtime < max(LIB.stat().st_mtime,
+                                                                             main_src.stat().st_mtime)):
+        _run(["gcc", *CFLAGS, "-o", str(CLI), str(main_src), "-L" + str(PKG), "-lcwen_cuda",
+              "-Wl,-rpath,$ORIGIN"], BUILD / "cli.log")
     if verbose:
         for lg in sorted(BUILD.glob("*.log")):
             sys.stdout.write(lg.read_text())

@@ -3,6 +3,7 @@
 #include <string.h>
 
 #include "engine.cuh"
+#include "model.cuh"
 
 namespace cw {
 
@@ -45,7 +46,7 @@ int ensure_io(size_t floats) {
   return CWEN_OK;
 }
 
-static int upload_qmat(int type, const void *host, int ne0, int ne1, QMat &m, int mt_off, int mt_stride) {
+int upload_qmat_rows(int type, const void *host, int ne0, int ne1, QMat &m, int mt_off, int mt_stride) {
   Engine &E = engine();
   const size_t rb = (size_t)(ne0 / 32) * (type == CWEN_T_Q8_0 ? 34 : 18);
   const size_t bytes = rb * (size_t)ne1;
@@ -135,10 +136,13 @@ int cwen_cuda_init(int device, int ctx, int bmax) {
   return CWEN_OK;
 }
 
+int cwen_cuda_ctx(void) { return engine().live ? engine().ctx : 0; }
+
 void cwen_cuda_shutdown(void) {
   Engine &E = engine();
   if (!E.live) return;
   cudaStreamSynchronize(E.stream);
+  model_free();
   for (auto &m : E.mats) cudaFree(m.w);
   E.mats.clear();
   for (auto e : E.prof.ev) cudaEventDestroy(e);
@@ -166,7 +170,7 @@ int cwen_cuda_weight_upload(int type, const void *host, int ne0, int ne1, int *w
   QMat m;
   int rc = alloc_qmat(m, type, ne0, (ne1 + 15) / 16, ne1);
   if (rc) return rc;
-  rc = upload_qmat(type, host, ne0, ne1, m, 0, 1);
+  rc = upload_qmat_rows(type, host, ne0, ne1, m, 0, 1);
   if (rc) {
     cudaFree(m.w);
     return rc;

@@ -1,0 +1,37 @@
+// GatedDeltaNet verify step -- host interface (gdn.cu).
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace cw {
+
+struct GdnLayerArgs {
+  const float *proj;  // in_proj output rows [B][ps]: qkv | z | alpha | beta
+  int ps, B, nkh, nvh;
+  int a_off, b_off;        // columns of alpha / beta in a proj row
+  const float *convw;      // [QKV][4]
+  const float *cstate_in;  // committed conv state [QKV][3]
+  float *cstate_out;       // conv state after the block's last row
+  float *craw;             // raw (pre-conv) qkv rows [B][QKV], kept for rollback
+  const float *A, *dt;     // ssm_a, ssm_dt.bias [nvh]
+  float *gin;              // recurrence inputs [B][QKV + 2*nvh]
+  const float *S_in;       // committed state [nvh][128][128]
+  float *S_out;            // state after the last row
+  float *out;              // raw head outputs S^T q / sqrt(128) [B][nvh*128]
+  float *delta;            // per-row delta [B][nvh*128], kept for rollback
+};
+
+// Committed-state view of one GDN layer for the rollback replay.
+struct GdnLayerPtrs {
+  float *S;             // committed state (updated in place)
+  float *cstate;        // committed conv state
+  const float *gin;     // block rows
+  const float *craw;
+  const float *delta;
+};
+
+cudaError_t launch_gdn_layer(const GdnLayerArgs &a, cudaStream_t st);
+// Advance every layer's committed state by block rows 0..k.
+cudaError_t launch_gdn_replay(GdnLayerPtrs *dev_layers, int n_layers, int k, int nkh, int nvh, cudaStream_t st);
+
+}  // namespace cw

@@ -1,0 +1,204 @@
+// Row-wise kernels of the forward pass: embedding, RMSNorm -> GEMV input,
+// gated GDN norm -> GEMV input, generic row -> GEMV input, argmax.
+#include "rowops.cuh"
+#include "rowprep.cuh"
+
+namespace cw {
+
+// Dynamic shared memory above the 48 KB default needs an explicit opt-in.
+template <typename F>
+static cudaError_t smem_optin(F *fn, size_t bytes, size_t &done) {
+  if (bytes <= 48 * 1024 || bytes <= done) return cudaSuccess;
+  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+  if (e == cudaSuccess) done = bytes;
+  return e;
+}
+
+// ---- embedding (embed_token_to, Q4_0 branch run.c:1873-1881) ----
+// x[b][k] = d * (q - 8) of row toks[b] of token_embd (GGUF Q4_0 layout).
+__global__ void embed_kernel(const uint8_t *__restrict__ emb, int H, int V, const Toks16 toks, int B,
+                             float *__restrict__ x, int *__restrict__ err) {
+  const int b = blockIdx.y;
+  const int tok = toks.t[b];
+  if (tok < 0 || tok >= V) {
+    if (threadIdx.x == 0 && blockIdx.x == 0) atomicExch(err, 1);
+    return;
+  }
+  const int nb = H / 32;
+  const uint8_t *row = emb + (size_t)tok * nb * 18;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < nb * 16; i += gridDim.x * blockDim.x) {
+    const int blk = i >> 4, j = i & 15;
+    const uint8_t *p = row + blk * 18;
+    const float d = __half2float(__ushort_as_half((unsigned short)(p[0] | (p[1] << 8))));
+    const uint8_t q = p[2 + j];
+    x[(size_t)b * H + blk * 32 + j] = (float)((q & 0xF) - 8) * d;
+    x[(size_t)b * H + blk * 32 + j + 16] = (float)((q >> 4) - 8) * d;
+  }
+}
+
+cudaError_t launch_embed(const uint8_t *emb, int H, int V, const Toks16 &toks, int B, float *x, int *err,
+                         cudaStream_t st) {
+  embed_kernel<<<dim3(4, B), 256, 0, st>>>(emb, H, V, toks, B, x, err);
+  return cudaGetLastError();
+}
+
+// ---- RMSNorm (run.c:346) fused with GEMV input preparation ----
+// One CTA per column b < nt*8; optional copy of the normed row to `out`.
+__global__ void __launch_bounds__(PREP_THREADS) norm_prep_kernel(const float *__restrict__ x, const float *__restrict__ w,
+                                                                 int H, int B, int nt, uint4 *__restrict__ xf,
+                                                                 int *__restrict__ xexp, float *__restrict__ out) {
+  extern __shared__ float v[];
+  __shared__ float red[32];
+  const int b = blockIdx.x;
+  const bool live = b < B;
+  float ss = 0.f;
+  if (live)
+    for (int k = threadIdx.x; k < H; k += blockDim.x) {
+      const float t = x[(size_t)b * H + k];
+      v[k] = t;
+      ss = fmaf(t, t, ss);
+    }
+  ss = block_sum(ss, red);
+  const float s = 1.f / sqrtf(ss / (float)H + 1e-6f);
+  if (live)
+    for (int k = threadIdx.x; k < H; k += blockDim.x) {
+      const float o = w[k] * v[k] * s;
+      v[k] = o;
+      if (out) out[(size_t)b * H + k] = o;
+    }
+  __syncthreads();
+  emit_xfrag(v, H, b, nt, xf, xexp, red, live);
+}
+
+cudaError_t launch_norm_prep(const float *x, const float *w, int H, int B, GemvScratch &s, float *out,
+                             cudaStream_t st) {
+  const int nt = (B + 7) / 8;
+  const size_t smem = (size_t)H * sizeof(float);
+  static size_t done = 0;
+  cudaError_t e = smem_optin(norm_prep_kernel, smem, done);
+  if (e != cudaSuccess) return e;
+  norm_prep_kernel<<<nt * 8, PREP_THREADS, smem, st>>>(x, w, H, B, nt, s.xf, s.xexp, out);
+  return cudaGetLastError();
+}
+
+// ---- plain row -> GEMV input (e.g. the SwiGLU output feeding ffn_down) ----
+__global__ void __launch_bounds__(PREP_THREADS) row_prep_kernel(const float *__restrict__ x, int xs, int K, int B,
+                                                                int nt, uint4 *__restrict__ xf,
+                                                                int *__restrict__ xexp) {
+  extern __shared__ float v[];
+  __shared__ float red[32];
+  const int b = blockIdx.x;
+  const bool live = b < B;
+  if (live)
+    for (int k = threadIdx.x; k < K; k += blockDim.x) v[k] = x[(size_t)b * xs + k];
+  __syncthreads();
+  emit_xfrag(v, K, b, nt, xf, xexp, red, live);
+}
+
+cudaError_t launch_row_prep(const float *x, int xs, int K, int B, GemvScratch &s, cudaStream_t st) {
+  const int nt = (B + 7) / 8;
+  static size_t done = 0;
+  cudaError_t e = smem_optin(row_prep_kernel, (size_t)K * sizeof(float), done);
+  if (e != cudaSuccess) return e;
+  row_prep_kernel<<<nt * 8, PREP_THREADS, (size_t)K * sizeof(float), st>>>(x, xs, K, B, nt, s.xf, s.xexp);
+  return cudaGetLastError();
+}
+
+// ---- GDN gated RMSNorm (run.c:2142-2178) fused with ssm_out input prep ----
+// o: raw GDN output [B][nvh*128] (S^T q / sqrt(128)); z: gate rows (stride zs).
+// out[h][i] = wn[i] * o[h][i] * rsqrt(mean_i o^2 + eps) * silu(z[h][i]).
+__global__ void __launch_bounds__(PREP_THREADS) gated_norm_prep_kernel(const float *__restrict__ o,
+                                                                       const float *__restrict__ z, int zs,
+                                                                       const float *__restrict__ wn, int nvh, int B,
+                                                                       int nt, uint4 *__restrict__ xf,
+                                                                       int *__restrict__ xexp) {
+  extern __shared__ float v[];
+  __shared__ float red[32];
+  const int b = blockIdx.x;
+  const bool live = b < B;
+  const int K = nvh * 128;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  if (live) {
+    for (int h = warp; h < nvh; h += nw) {
+      const float *oh = o + (size_t)b * K + h * 128;
+      float t[4], ss = 0.f;
+#pragma unroll
+      for (int i = 0; i < 4; i++) {
+        t[i] = oh[lane + 32 * i];
+        ss = fmaf(t[i], t[i], ss);
+      }
+      ss = warp_sum(ss);
+      const float s = 1.f / sqrtf(ss / 128.f + 1e-6f);
+#pragma unroll
+      for (int i = 0; i < 4; i++) {
+        const int j = lane + 32 * i;
+        const float zz = z[(size_t)b * zs + h * 128 + j];
+        v[h * 128 + j] = wn[j] * t[i] * s * silu_dev(zz);
+      }
+    }
+  }
+  __syncthreads();
+  emit_xfrag(v, K, b, nt, xf, xexp, red, live);
+}
+
+cudaError_t launch_gated_norm_prep(const float *o, const float *z, int zs, const float *wn, int nvh, int B,
+                                   GemvScratch &s, cudaStream_t st) {
+  const int nt = (B + 7) / 8;
+  static size_t done = 0;
+  cudaError_t e = smem_optin(gated_norm_prep_kernel, (size_t)nvh * 128 * sizeof(float), done);
+  if (e != cudaSuccess) return e;
+  gated_norm_prep_kernel<<<nt * 8, PREP_THREADS, (size_t)nvh * 128 * sizeof(float), st>>>(o, z, zs, wn, nvh, B, nt,
+                                                                                          s.xf, s.xexp);
+  return cudaGetLastError();
+}
+
+// ---- argmax (argmax_of run.c:2647): first maximum over n logits per row ----
+// Packed key: order-preserving float bits in the high word, ~index in the low
+// word, so a 64-bit max picks the largest value and, among equal values, the
+// lowest index -- independent of the order CTAs finish.
+CW_DEV unsigned long long argmax_key(float v, int i) {
+  uint32_t u = __float_as_uint(v);
+  u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  return ((unsigned long long)u << 32) | (uint32_t)(~(uint32_t)i);
+}
+
+__global__ void argmax_kernel(const float *__restrict__ lg, int n, int ldl, unsigned long long *__restrict__ best) {
+  const int b = blockIdx.y;
+  unsigned long long k = 0;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const float v = lg[(size_t)b * ldl + i];
+    const unsigned long long kk = argmax_key(v != v ? -INFINITY : v, i);
+    k = kk > k ? kk : k;
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long t = __shfl_xor_sync(0xffffffffu, k, o);
+    k = t > k ? t : k;
+  }
+  if ((threadIdx.x & 31) == 0) atomicMax(best + b, k);
+}
+
+// Greedy walk of generate_tokens_spec (run.c:4954-4956) on device:
+// k = longest prefix with argmax(row j) == blk[j+1]; ustar = argmax(row k).
+// res = [k, ustar, argmax(row 0..B-1)].
+__global__ void walk_kernel(const unsigned long long *__restrict__ best, const Toks16 blk, int B, int E,
+                            int *__restrict__ res) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  int am[16];
+  for (int b = 0; b < B; b++) am[b] = (int)(~(uint32_t)(best[b] & 0xffffffffu));
+  int k = 0;
+  while (k < E && am[k] == blk.t[k + 1]) k++;
+  res[0] = k;
+  res[1] = am[k];
+  for (int b = 0; b < B; b++) res[2 + b] = am[b];
+}
+
+cudaError_t launch_argmax_walk(const float *lg, int n, int ldl, int B, int E, const Toks16 &blk,
+                               unsigned long long *best, int *res, cudaStream_t st) {
+  cudaError_t e = cudaMemsetAsync(best, 0, (size_t)B * sizeof(unsigned long long), st);
+  if (e != cudaSuccess) return e;
+  argmax_kernel<<<dim3(64, B), 256, 0, st>>>(lg, n, ldl, best);
+  walk_kernel<<<1, 32, 0, st>>>(best, blk, B, E, res);
+  return cudaGetLastError();
+}
+
+}  // namespace cw

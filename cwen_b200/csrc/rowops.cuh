@@ -1,0 +1,31 @@
+// Host launchers of the row-wise kernels (rowops.cu).
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "qgemv.cuh"
+
+namespace cw {
+
+// Up to 16 token ids passed by value in the kernel parameters, so a launch
+// never depends on a host staging buffer outliving it.
+struct Toks16 {
+  int t[16];
+};
+
+cudaError_t launch_embed(const uint8_t *emb, int H, int V, const Toks16 &toks, int B, float *x, int *err,
+                         cudaStream_t st);
+// x [B][H] -> rmsnorm(x) * w as GEMV input (and optionally into out [B][H]).
+cudaError_t launch_norm_prep(const float *x, const float *w, int H, int B, GemvScratch &s, float *out,
+                             cudaStream_t st);
+// rows x [B][xs], first K values -> GEMV input.
+cudaError_t launch_row_prep(const float *x, int xs, int K, int B, GemvScratch &s, cudaStream_t st);
+// GDN gated norm of o [B][nvh*128] with gate z (row stride zs) -> GEMV input.
+cudaError_t launch_gated_norm_prep(const float *o, const float *z, int zs, const float *wn, int nvh, int B,
+                                   GemvScratch &s, cudaStream_t st);
+// First-max argmax of B rows of logits (row stride ldl) and the greedy walk
+// against blk[0..E]: res = [k, ustar, argmax rows...].
+cudaError_t launch_argmax_walk(const float *lg, int n, int ldl, int B, int E, const Toks16 &blk,
+                               unsigned long long *best, int *res, cudaStream_t st);
+
+}  // namespace cw

@@ -1,0 +1,76 @@
+// Row-wise producers of verify-GEMV inputs.
+//
+// Every GEMV input row (one per verify position b) is produced by one CTA
+// that holds the whole row in shared memory, so the norm that precedes a
+// GEMV in the reference (rmsnorm run.c:346, the GDN gated norm run.c:2142,
+// the attention gate run.c:2396) fuses with the conversion of the row into
+// the GEMV's f16 hi/lo fragments.
+#pragma once
+#include "common.cuh"
+
+namespace cw {
+
+constexpr int PREP_THREADS = 512;
+
+// Block-wide max / sum over PREP_THREADS threads (red: >= 32 floats smem).
+CW_DEV float block_max(float v, float *red) {
+  v = warp_max(v);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  v = l < (int)(blockDim.x >> 5) ? red[l] : 0.f;
+  return warp_max(v);
+}
+// Deterministic block sum: fixed per-thread strided order, fixed tree.
+CW_DEV float block_sum(float v, float *red) {
+  v = warp_sum(v);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  v = l < (int)(blockDim.x >> 5) ? red[l] : 0.f;
+  return warp_sum(v);
+}
+
+// Emit GEMV fragments for row b from v[0..K) in shared memory (b >= B rows
+// are zero padding of the n-tile).  Layout: see prep_x_kernel in qgemv.cu.
+CW_DEV void emit_xfrag(const float *v, int K, int b, int nt, uint4 *__restrict__ xf, int *__restrict__ xexp,
+                       float *red, bool live) {
+  float mx = 0.f;
+  if (live)
+    for (int k = threadIdx.x; k < K; k += blockDim.x) mx = fmaxf(mx, fabsf(v[k]));
+  mx = block_max(mx, red);
+  int e = 0;
+  if (mx > 0.f && mx <= 3.0e38f) {
+    int p;
+    frexpf(mx, &p);
+    e = 15 - p;
+    e = e < -100 ? -100 : (e > 100 ? 100 : e);
+  }
+  if (threadIdx.x == 0) xexp[b] = e;
+  const float scale = __int_as_float((127 + e) << 23);
+  const int g = b & 7, n = b >> 3, nb = K / 32;
+  for (int item = threadIdx.x; item < nb * 4; item += blockDim.x) {
+    const int kb = item >> 2, t = item & 3;
+    const float *r = v + kb * 32;
+    const int js[8] = {4 * t, 4 * t + 2, 4 * t + 1, 4 * t + 3, 4 * t + 16, 4 * t + 18, 4 * t + 17, 4 * t + 19};
+    uint32_t hi[4], lo[4];
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      const float v0 = live ? r[js[2 * i]] * scale : 0.f, v1 = live ? r[js[2 * i + 1]] * scale : 0.f;
+      const half h0 = __float2half_rn(v0), h1 = __float2half_rn(v1);
+      const half l0 = __float2half_rn(v0 - __half2float(h0)), l1 = __float2half_rn(v1 - __half2float(h1));
+      hi[i] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
+      lo[i] = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
+    }
+    const size_t o = ((size_t)(kb * nt + n) * 2) * 32 + g * 4 + t;
+    xf[o] = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+    xf[o + 32] = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+  }
+}
+
+CW_DEV float silu_dev(float x) { return x * (1.f / (1.f + expf(-x))); }
+CW_DEV float sigmoid_dev(float x) { return 1.f / (1.f + expf(-x)); }
+
+}  // namespace cw

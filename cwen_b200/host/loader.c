@@ -1,0 +1,299 @@
+/* Model loading for the C host: GGUF files and the seeded synthetic model.
+ *
+ * The GGUF reader follows the checks of the reference's load_gguf
+ * (run.c:3230-3303): version 2 or 3, at most 4 dims, no zero or int-overflowing
+ * dims, every tensor extent inside the mapping, 32-byte aligned data section
+ * (or general.alignment when the file declares it).  Unlike the reference it
+ * derives the model geometry from the tensor shapes instead of compiling it
+ * in, and hands each tensor to the engine's upload call.
+ */
+#define _GNU_SOURCE
+#include <fcntl.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
+
+#include "cwen_host.h"
+#include "synth.h"
+
+#define GG_MAX_TENSORS 4096
+
+typedef struct {
+  char name[96];
+  int type;
+  int n_dims;
+  uint64_t ne[4];
+  uint64_t off;
+  const uint8_t *data;
+} gg_tensor;
+
+typedef struct {
+  const uint8_t *p, *end;
+  int bad;
+  char why[160];
+} gg_cur;
+
+static void gg_fail(gg_cur *c, const char *why) {
+  if (!c->bad) snprintf(c->why, sizeof c->why, "%s", why);
+  c->bad = 1;
+}
+static const uint8_t *gg_take(gg_cur *c, uint64_t n) {
+  if (c->bad || (uint64_t)(c->end - c->p) < n) {
+    gg_fail(c, "truncated");
+    return NULL;
+  }
+  const uint8_t *q = c->p;
+  c->p += n;
+  return q;
+}
+static uint64_t gg_u64(gg_cur *c) {
+  const uint8_t *q = gg_take(c, 8);
+  uint64_t v = 0;
+  if (q) memcpy(&v, q, 8);
+  return v;
+}
+static uint32_t gg_u32(gg_cur *c) {
+  const uint8_t *q = gg_take(c, 4);
+  uint32_t v = 0;
+  if (q) memcpy(&v, q, 4);
+  return v;
+}
+static void gg_str(gg_cur *c, char *buf, size_t cap) {
+  uint64_t n = gg_u64(c);
+  if (c->bad) return;
+  if (n >= cap) {
+    gg_fail(c, "string too long");
+    return;
+  }
+  const uint8_t *q = gg_take(c, n);
+  if (!q) return;
+  memcpy(buf, q, n);
+  buf[n] = 0;
+}
+/* Skip one KV value; returns the value when it is a u32/i32 (alignment). */
+static uint64_t gg_skip(gg_cur *c, uint32_t t, int depth) {
+  if (depth > 64) {
+    gg_fail(c, "kv nesting too deep");
+    return 0;
+  }
+  uint64_t v = 0;
+  switch (t) {
+    case 0: case 1: case 7: gg_take(c, 1); break;
+    case 2: case 3: gg_take(c, 2); break;
+    case 4: case 5: v = gg_u32(c); break;
+    case 6: gg_take(c, 4); break;
+    case 8: { uint64_t n = gg_u64(c); gg_take(c, n); } break;
+    case 9: {
+      uint32_t at = gg_u32(c);
+      uint64_t n = gg_u64(c);
+      for (uint64_t i = 0; i < n && !c->bad; i++) gg_skip(c, at, depth + 1);
+    } break;
+    case 10: case 11: case 12: gg_take(c, 8); break;
+    default: gg_fail(c, "unknown kv type");
+  }
+  return v;
+}
+
+static size_t gg_nbytes(int type, uint64_t ne0, uint64_t rows) {
+  switch (type) {
+    case CWEN_T_F32: return (size_t)(ne0 * rows * 4);
+    case CWEN_T_Q4_0: return (size_t)(ne0 / 32 * 18 * rows);
+    case CWEN_T_Q8_0: return (size_t)(ne0 / 32 * 34 * rows);
+    default: return 0;
+  }
+}
+
+static const gg_tensor *gg_find(const gg_tensor *t, int n, const char *name) {
+  for (int i = 0; i < n; i++)
+    if (!strcmp(t[i].name, name)) return &t[i];
+  return NULL;
+}
+
+/* Geometry from shapes: see the file comment. */
+static int gg_dims(const gg_tensor *t, int n, cwen_dims *d, char *why, size_t wl) {
+  memset(d, 0, sizeof *d);
+  d->head_dim = 256; d->n_rot = 64; d->ssm_d = 128; d->conv_k = 4;
+  const gg_tensor *e = gg_find(t, n, "token_embd.weight");
+  if (!e) { snprintf(why, wl, "missing token_embd.weight"); return -1; }
+  d->n_embd = (int)e->ne[0];
+  d->n_vocab = (int)e->ne[1];
+  int mtp_layer = -1, max_layer = -1, first_full = -1;
+  for (int i = 0; i < n; i++) {
+    int l = -1, off = 0;
+    if (sscanf(t[i].name, "blk.%d.%n", &l, &off) != 1 || off == 0) continue;
+    if (!strcmp(t[i].name + off, "nextn.eh_proj.weight")) mtp_layer = l;
+    if (!strcmp(t[i].name + off, "ffn_gate.weight") && l > max_layer) max_layer = l;
+  }
+  if (max_layer < 0) { snprintf(why, wl, "no blk.*.ffn_gate.weight"); return -1; }
+  d->n_layer = mtp_layer == max_layer ? max_layer : max_layer + 1;
+  d->has_mtp = mtp_layer == d->n_layer;
+  char nm[96];
+  for (int l = 0; l < d->n_layer; l++) {
+    snprintf(nm, sizeof nm, "blk.%d.attn_q.weight", l);
+    const gg_tensor *q = gg_find(t, n, nm);
+    if (q && first_full < 0) {
+      first_full = l;
+      d->n_head = (int)(q->ne[1] / 512);
+      snprintf(nm, sizeof nm, "blk.%d.attn_k.weight", l);
+      const gg_tensor *k = gg_find(t, n, nm);
+      d->n_head_kv = k ? (int)(k->ne[1] / 256) : 0;
+    }
+  }
+  d->full_interval = first_full >= 0 ? first_full + 1 : d->n_layer + 1;
+  snprintf(nm, sizeof nm, "blk.0.ffn_gate.weight");
+  const gg_tensor *g = gg_find(t, n, nm);
+  d->n_ff = g ? (int)g->ne[1] : 0;
+  for (int l = 0; l < d->n_layer; l++) {
+    snprintf(nm, sizeof nm, "blk.%d.attn_gate.weight", l);
+    const gg_tensor *z = gg_find(t, n, nm);
+    snprintf(nm, sizeof nm, "blk.%d.attn_qkv.weight", l);
+    const gg_tensor *qkv = gg_find(t, n, nm);
+    if (z && qkv) {
+      d->ssm_n_vh = (int)(z->ne[1] / 128);
+      d->ssm_n_kh = (int)((qkv->ne[1] / 128 - (uint64_t)d->ssm_n_vh) / 2);
+      break;
+    }
+  }
+  if (!d->n_head) { d->n_head = 1; d->n_head_kv = 1; }
+  if (!d->ssm_n_vh) { d->ssm_n_vh = 1; d->ssm_n_kh = 1; }
+  return 0;
+}
+
+int cwen_load_gguf(const char *path) {
+  int fd = open(path, O_RDONLY);
+  if (fd < 0) {
+    perror(path);
+    return CWEN_EINVAL;
+  }
+  struct stat st;
+  if (fstat(fd, &st) || st.st_size < 20) {
+    close(fd);
+    fprintf(stderr, "gguf: %s: not a gguf file\n", path);
+    return CWEN_EINVAL;
+  }
+  size_t len = (size_t)st.st_size;
+  uint8_t *map = (uint8_t *)mmap(NULL, len, PROT_READ, MAP_PRIVATE, fd, 0);
+  close(fd);
+  if (map == MAP_FAILED) {
+    perror("mmap");
+    return CWEN_ENOMEM;
+  }
+  gg_cur c = {map, map + len, 0, {0}};
+  gg_tensor *t = NULL;
+  int rc = CWEN_EINVAL, nt = 0;
+  const uint8_t *magic = gg_take(&c, 4);
+  if (!magic || memcmp(magic, "GGUF", 4)) { gg_fail(&c, "bad magic"); goto out; }
+  uint32_t ver = gg_u32(&c);
+  if (ver < 2 || ver > 3) { gg_fail(&c, "unsupported gguf version"); goto out; }
+  uint64_t n_t = gg_u64(&c), n_kv = gg_u64(&c);
+  if (n_t > GG_MAX_TENSORS) { gg_fail(&c, "too many tensors"); goto out; }
+  uint64_t align = 32;
+  for (uint64_t i = 0; i < n_kv && !c.bad; i++) {
+    char key[256];
+    gg_str(&c, key, sizeof key);
+    uint32_t ty = gg_u32(&c);
+    uint64_t v = gg_skip(&c, ty, 0);
+    if (!c.bad && !strcmp(key, "general.alignment") && (ty == 4 || ty == 5)) align = v;
+  }
+  if (align == 0 || (align & (align - 1))) { gg_fail(&c, "bad general.alignment"); goto out; }
+  t = (gg_tensor *)calloc(n_t ? n_t : 1, sizeof *t);
+  if (!t) { rc = CWEN_ENOMEM; goto out; }
+  nt = (int)n_t;
+  for (int i = 0; i < nt && !c.bad; i++) {
+    gg_str(&c, t[i].name, sizeof t[i].name);
+    uint32_t nd = gg_u32(&c);
+    if (nd < 1 || nd > 4) { gg_fail(&c, "n_dims outside 1..4"); break; }
+    t[i].n_dims = (int)nd;
+    t[i].ne[0] = t[i].ne[1] = t[i].ne[2] = t[i].ne[3] = 1;
+    for (uint32_t k = 0; k < nd; k++) {
+      t[i].ne[k] = gg_u64(&c);
+      if (t[i].ne[k] == 0 || t[i].ne[k] > 0x7fffffffull) { gg_fail(&c, "dim zero or beyond INT_MAX"); break; }
+    }
+    t[i].type = (int)gg_u32(&c);
+    t[i].off = gg_u64(&c);
+  }
+  if (c.bad) goto out;
+  {
+    uint64_t data_off = (uint64_t)(c.p - map);
+    data_off = (data_off + align - 1) & ~(align - 1);
+    for (int i = 0; i < nt; i++) {
+      if (data_off >= len || t[i].off >= len - data_off) { gg_fail(&c, "tensor offset out of file"); goto out; }
+      t[i].data = map + data_off + t[i].off;
+      const uint64_t rows = t[i].ne[1] * t[i].ne[2] * t[i].ne[3];
+      const size_t nb = gg_nbytes(t[i].type, t[i].ne[0], rows);
+      if (nb && nb > len - data_off - t[i].off) {
+        snprintf(c.why, sizeof c.why, "%s: extent beyond file", t[i].name);
+        c.bad = 1;
+        goto out;
+      }
+    }
+  }
+  {
+    cwen_dims d;
+    char why[160];
+    if (gg_dims(t, nt, &d, why, sizeof why)) {
+      snprintf(c.why, sizeof c.why, "%s", why);
+      c.bad = 1;
+      goto out;
+    }
+    rc = cwen_cuda_model_config(&d);
+    if (rc) goto out_engine;
+    for (int i = 0; i < nt; i++) {
+      const gg_tensor *x = &t[i];
+      if (x->type != CWEN_T_F32 && x->type != CWEN_T_Q4_0 && x->type != CWEN_T_Q8_0) continue;
+      const uint64_t rows = x->ne[1] * x->ne[2] * x->ne[3];
+      if (rows > 0x7fffffffull) continue;
+      rc = cwen_cuda_upload(x->name, x->type, x->data, (int)x->ne[0], (int)rows);
+      if (rc) goto out_engine;
+    }
+    rc = cwen_cuda_model_finalize();
+    if (!rc) fprintf(stderr, "loaded %d tensors from %s\n", nt, path);
+  }
+out_engine:
+  if (rc) fprintf(stderr, "gguf: %s\n", cwen_cuda_last_error());
+out:
+  if (c.bad) fprintf(stderr, "gguf: %s: %s\n", path, c.why);
+  free(t);
+  munmap(map, len);
+  return c.bad ? CWEN_EINVAL : rc;
+}
+
+void cwen_dims_reference(cwen_dims *d) {
+  cw_dims s;
+  cw_dims_full(&s);
+  memcpy(d, &s, sizeof *d);
+}
+void cwen_dims_small(cwen_dims *d) {
+  cw_dims s;
+  cw_dims_tiny(&s);
+  memcpy(d, &s, sizeof *d);
+}
+
+int cwen_load_synth(uint64_t seed, const cwen_dims *dims, int threads) {
+  cw_dims d;
+  memcpy(&d, dims, sizeof d);
+  int rc = cwen_cuda_model_config(dims);
+  if (rc) return rc;
+  const int n = cw_model_tensor_count(&d);
+  size_t cap = 0;
+  for (int i = 0; i < n; i++) {
+    cw_tensor_desc td;
+    cw_model_tensor_desc(&d, i, &td);
+    size_t nb = cw_tensor_nbytes(td.type, td.ne0, td.ne1);
+    if (nb > cap) cap = nb;
+  }
+  void *buf = malloc(cap);
+  if (!buf) return CWEN_ENOMEM;
+  for (int i = 0; i < n && !rc; i++) {
+    cw_tensor_desc td;
+    cw_model_tensor_desc(&d, i, &td);
+    cw_synth_tensor(seed, &td, buf, threads);
+    rc = cwen_cuda_upload(td.name, td.type, buf, td.ne0, td.ne1);
+  }
+  free(buf);
+  if (rc) return rc;
+  return cwen_cuda_model_finalize();
+}

@@ -55,6 +55,8 @@ const char *cwen_cuda_last_error(void);
 int cwen_cuda_init(int device, int ctx, int bmax);
 /* Free everything (process exit in the reference). */
 void cwen_cuda_shutdown(void);
+/* Context window the engine was initialised with (0 before init). */
+int cwen_cuda_ctx(void);
 
 /* ---- stand-alone verify GEMV (gemvb, run.c:1577) ---- */
 /* Upload one GGUF Q4_0/Q8_0 matrix (ne0 = K row length, ne1 = M rows) from
@@ -66,6 +68,49 @@ int cwen_cuda_weight_upload(int type, const void *host, int ne0, int ne1, int *w
 int cwen_cuda_gemvb(int wid, const float *dX, int xs, float *dY, int ys, int B, void *stream);
 /* The same with host buffers: copies X in, runs, copies Y out, synchronizes. */
 int cwen_cuda_gemvb_host(int wid, const float *hX, int xs, float *hY, int ys, int B);
+
+/* ---- the model ---- */
+/* Declare the geometry (run.c:83-91 constants) before any upload. */
+int cwen_cuda_model_config(const cwen_dims *dims);
+/* Upload one GGUF tensor by its GGUF name ("token_embd.weight",
+ * "blk.<l>.ffn_gate.weight", "blk.<n_layer>.nextn.eh_proj.weight", ...),
+ * validating type and shape like rebind_layers_from_tens (run.c:3366-3465).
+ * Matrices are repacked on the device (fused where they share an input);
+ * names the path does not use are accepted and ignored. */
+int cwen_cuda_upload(const char *name, int type, const void *host, int ne0, int ne1);
+/* Check every required tensor is bound and allocate the decode state:
+ * alloc_state (run.c:3928); KV cache only for the attention layers. */
+int cwen_cuda_model_finalize(void);
+/* Fresh sequence: zero the GDN/conv state, rewind (reset_state, run.c:4011). */
+int cwen_cuda_reset(void);
+/* Tokens in the committed state (the reference's pos_n + 1). */
+int cwen_cuda_n_past(void);
+/* Score toks[0..B) at slots n_past..n_past+B-1 (forward_block, run.c:2752).
+ * nlogits in [0,B]: logits + argmax for rows 0..nlogits-1; -1: last row only
+ * (the prefill convention of run.c:4850-4854).  The block stays pending until
+ * cwen_cuda_commit.  Row j's argmax is compared with toks[j+1] on the device
+ * (the greedy walk of run.c:4954-4956). */
+int cwen_cuda_forward_block(const int *toks, int B, int nlogits);
+/* Result of the fused argmax + greedy walk of the pending block:
+ * k = accepted drafts, ustar = bonus token, argmax_out[0..nlogits) (optional).
+ * Synchronizes. */
+int cwen_cuda_accept(int *k_out, int *ustar_out, int *argmax_out);
+/* Keep rows 0..k of the pending block: pointer swap when k is the last row,
+ * otherwise a replay of the stored per-row GDN updates (snap_load + replay of
+ * run.c:4975-4988 without a second weight sweep). */
+int cwen_cuda_commit(int k);
+/* One token at slot n_past, committed (forward_ex, run.c:2594); with
+ * need_logits the argmax of its logits goes to *argmax_out. */
+int cwen_cuda_forward_serial(int token, int need_logits, int *argmax_out);
+/* Copies of device rows for parity checks: logits row (n_vocab floats), the
+ * residual stream after the last layer (n_embd), per-layer residual streams
+ * (the CWEN_DUMP layerNN files, run.c:2601-2629) while dumps are on, and a
+ * GDN layer's committed state [n_vh][128][128] + conv state [qkv][3]. */
+int cwen_cuda_logits(int row, float *host);
+int cwen_cuda_hidden(int row, float *host);
+int cwen_cuda_dump_layers(int on);
+int cwen_cuda_dump_read(int layer, int row, float *host);
+int cwen_cuda_gdn_state(int layer, float *S_host, float *conv_host);
 
 /* ---- instrumentation (the reference's CWEN_SPEC_DEBUG timers, run.c:3133) ---- */
 /* Reset counters and turn per-launch CUDA-event timing of the verify-GEMV

@@ -1,0 +1,63 @@
+/* cwen_host.h -- the C host side kept from the reference (maci0/cwen run.c):
+ * model loading (GGUF, or the seeded synthetic model), the n-gram drafter,
+ * and the serial / speculative decode drivers.  They run on the CPU and call
+ * the GPU engine only through include/cwen_cuda.h.
+ */
+#ifndef CWEN_HOST_H
+#define CWEN_HOST_H
+#include <stdint.h>
+
+#include "cwen_cuda.h"
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- loading ---- */
+/* Parse a GGUF v2/v3 file (bounds-checked like load_gguf, run.c:3230-3303),
+ * derive the geometry from the tensor shapes, upload every tensor and
+ * finalize.  The engine must be initialised (cwen_cuda_init). */
+int cwen_load_gguf(const char *path);
+/* The seeded random-init model of the benchmark configurations: every tensor
+ * generated on the host (`threads` threads, <= 0: all cores) and uploaded. */
+int cwen_load_synth(uint64_t seed, const cwen_dims *dims, int threads);
+/* Geometry of the reference (run.c:83-91) and the small test geometry. */
+void cwen_dims_reference(cwen_dims *d);
+void cwen_dims_small(cwen_dims *d);
+
+/* ---- speculation knobs (spec_config_init, run.c:4021-4053) ---- */
+typedef struct {
+  int spec;       /* CWEN_SPEC: block speculation on */
+  int use_mtp;    /* CWEN_MTP: draft with the blk.<L> nextn head when present */
+  int max_draft;  /* CWEN_SPEC_MAX_DRAFT / -d: drafts per block, 1..15 */
+  int min_draft;  /* CWEN_SPEC_MIN_DRAFT: smaller proposals run a plain step */
+  int n_key;      /* CWEN_SPEC_NGRAM_N: n-gram key length, 2..256 */
+  int cooldown;   /* CWEN_SPEC_COOLDOWN: plain steps after 3 short walks */
+  int debug;      /* CWEN_SPEC_DEBUG: per-cycle trace on stderr */
+} cwen_spec_cfg;
+void cwen_spec_defaults(cwen_spec_cfg *c);
+/* Apply the CWEN_SPEC* / CWEN_MTP environment with the reference's strict
+ * parsing; returns CWEN_EINVAL (message in cwen_cuda_last_error) on a bad
+ * value instead of exiting. */
+int cwen_spec_from_env(cwen_spec_cfg *c);
+
+typedef struct {
+  long long cycles, drafted, full, shortw, kept;  /* the "spec:" stats line */
+  long long plain_steps;
+} cwen_spec_stats;
+
+/* Prefill tokens[0..n_tok) and greedily generate up to n_gen ids into out
+ * (generate_tokens run.c:5027 / generate_tokens_spec run.c:4882).  Returns the
+ * number emitted (< n_gen only when the context window fills), or a negative
+ * CWEN_E* code.  Speculative output is identical to serial output. */
+int cwen_generate(const int32_t *tokens, int n_tok, int n_gen, int32_t *out, const cwen_spec_cfg *cfg,
+                  cwen_spec_stats *stats);
+
+/* ---- drafters (the contract of run.c:4527-4532) ---- */
+/* Prompt-lookup scan (ngram_draft, run.c:4533): propose up to max_d ids that
+ * followed the most useful earlier match of the last n_key ids. */
+int cwen_ngram_draft(const int32_t *hist, int hn, int32_t *out, int n_key, int max_d);
+
+#ifdef __cplusplus
+}
+#endif
+#endif
