@@ -1,7 +1,16 @@
 """Benchmark of the cwen B200 verify-decode engine (one JSON line on rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload gemv]
+                    [--workload decode|gemv]
+
+Workload `decode` (default; BASELINE configs 2 and 3): the random-init 27B
+hybrid (64 layers, Q4_0 weights with scales |N(0,0.01)|, norms 1, seeded),
+greedy decode of one sequence after a 512-id random prompt.  A step is one
+decoded token: the forward pass of the previous token at the next slot plus
+its argmax back on the host (cwen_cuda_forward_serial).  value = tok/s over
+K timed steps (CUDA events on the engine stream).  The same run also times
+config 3: n-gram speculative decode, draft depth 8, 2048-id motif prompt,
+512 new tokens, checked token-for-token against serial decode.
 
 Workload `gemv`: the B=8 Q4_0 verify GEMV, W 17408x5120,
 X fp32 8x5120 ~N(0,1), scales |N(0,0.01)|, nibbles uniform.  A step is one
@@ -35,6 +44,10 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 sys.path.insert(0, str(ROOT / "tests"))
 
+DEC_SEED = 1
+PROMPT_LEN, N_GEN = 512, 256          # config 2
+SPEC_PROMPT, SPEC_GEN = 2048, 512     # config 3
+DEC_CTX = 4096
 GEMV_K, GEMV_M, GEMV_B = 5120, 17408, 8
 GEMV_BYTES = (GEMV_K // 32) * 18 * GEMV_M + GEMV_B * GEMV_K * 4 + GEMV_B * GEMV_M * 4  # 50,855,936
 RING = 8
@@ -253,18 +266,207 @@ def run_gemv_ours(args, ws, rank, local):
     return ms, kern, e2e_s, clk, W, X
 
 
+# ---------------- decode (configs 2 / 3) ----------------
+def synth_ids(n, seed, stream, V):
+    from oracle_lib import load_oracle, vp
+    out = np.zeros(n, np.int32)
+    load_oracle().cw_synth_ids(seed, stream.encode(), V, vp(out), n)
+    return out
+
+
+def motif_prompt(n, V, seed=3):
+    """2048 ids: a seed-random 37-token motif repeated, 5% uniform substitutions."""
+    rng = np.random.default_rng(seed)
+    motif = rng.integers(0, V, size=37)
+    p = np.resize(motif, n).astype(np.int32)
+    sub = rng.random(n) < 0.05
+    p[sub] = rng.integers(0, V, size=int(sub.sum()))
+    return p
+
+
+def run_decode_ours(args, ws, rank, local):
+    import torch
+
+    import cwen_b200
+    from cwen_b200 import build
+    build.build()
+    L = cwen_b200.lib()
+    cwen_b200.check(L.cwen_cuda_init(local, DEC_CTX, 16), "init")
+    d = cwen_b200.dims("reference")
+    t0 = time.perf_counter()
+    cwen_b200.check(L.cwen_load_synth(DEC_SEED, C.byref(d), 0), "load_synth")
+    load_s = time.perf_counter() - t0
+    V = d.n_vocab
+    prompt = synth_ids(PROMPT_LEN, DEC_SEED, "bench.prompt", V)
+    serial = cwen_b200.spec_cfg(spec=0)
+    first, _ = cwen_b200.generate(prompt, 1, serial)
+    tok = int(first[0])
+    nxt = C.c_int(0)
+    stream = torch.cuda.ExternalStream(L.cwen_cuda_stream(), device=torch.device("cuda", local))
+
+    def steps(n, tok):
+        for _ in range(n):
+            cwen_b200.check(L.cwen_cuda_forward_serial(tok, 1, C.byref(nxt)), "forward_serial")
+            tok = nxt.value
+        return tok
+
+    tok = steps(args.warmup, tok)
+    torch.cuda.synchronize()
+    barrier(ws)
+    clocks = ClockSampler(local)
+    clocks.start()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    tok = steps(args.steps, tok)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = ev0.elapsed_time(ev1) / args.steps
+    ms = barrier_max(ws, ms)
+    # GEMV roofline pass: per-launch CUDA events around every GEMV (not in the headline number)
+    kp = max(4, min(args.steps, 16))
+    cwen_b200.check(L.cwen_cuda_profile(1), "profile")
+    tok = steps(kp, tok)
+    gm, gb, gc, nl = C.c_double(), C.c_double(), C.c_longlong(), C.c_longlong()
+    cwen_b200.check(L.cwen_cuda_profile_read(C.byref(gm), C.byref(gb), C.byref(gc), C.byref(nl)), "profile_read")
+    cwen_b200.check(L.cwen_cuda_profile(0), "profile")
+    kern = {"gemv_ms_per_token": gm.value / kp, "gemv_bytes_per_token": gb.value / kp,
+            "gemv_calls_per_token": gc.value / kp, "launches_per_token": nl.value / kp}
+    # end to end through the public host API (bench_toks method): (t(n) - t(1)) / (n - 1)
+    t0 = time.perf_counter()
+    cwen_b200.generate(prompt, 1, serial)
+    t1 = time.perf_counter() - t0
+    t0 = time.perf_counter()
+    out_ser, _ = cwen_b200.generate(prompt, N_GEN, serial)
+    tn = time.perf_counter() - t0
+    e2e_tps = (N_GEN - 1) / (tn - t1)
+    # config 3: n-gram speculation, depth 8, motif prompt; stream must equal serial
+    mp = motif_prompt(SPEC_PROMPT, V)
+    t0 = time.perf_counter()
+    cwen_b200.generate(mp, 1, serial)
+    s1 = time.perf_counter() - t0
+    t0 = time.perf_counter()
+    ref_stream, _ = cwen_b200.generate(mp, SPEC_GEN, serial)
+    sn = time.perf_counter() - t0
+    spec_cfg = cwen_b200.spec_cfg(spec=1, max_draft=8)
+    t0 = time.perf_counter()
+    spec_stream, st = cwen_b200.generate(mp, SPEC_GEN, spec_cfg)
+    pn = time.perf_counter() - t0
+    spec = {"workload": "config3: n-gram spec d=8, 2048-id motif prompt, 512 new",
+            "tok_s": round((SPEC_GEN - 1) / (pn - s1), 2), "serial_tok_s": round((SPEC_GEN - 1) / (sn - s1), 2),
+            "identical_to_serial": bool(np.array_equal(ref_stream, spec_stream)),
+            "cycles": st.cycles, "drafted": st.drafted, "full_accept": st.full, "short": st.shortw,
+            "avg_kept": round(st.kept / st.drafted, 3) if st.drafted else 0.0}
+    L.cwen_cuda_shutdown()
+    return ms, kern, e2e_tps, clk, spec, load_s, prompt
+
+
+def cpu_decode_baseline(prompt, budget_s: float = 20.0):
+    """The reference's own greedy decode (generate_tokens, run.c:5027) on the
+    seeded model in host memory, all host cores: (t(1+n) - t(1)) / n on a
+    4-id prefix of the bench prompt."""
+    path, variant = ref_lib_path()
+    if not path.exists():
+        return None
+    os.environ.setdefault("OMP_NUM_THREADS", str(host_cores()))
+    os.environ.setdefault("OMP_PROC_BIND", "close")
+    os.environ.setdefault("OMP_PLACES", "cores")
+    ref = C.CDLL(str(path))
+    ref.cwref_threads.restype = C.c_int
+    vp = lambda a: a.ctypes.data_as(C.c_void_p)
+    t0 = time.perf_counter()
+    if ref.cwref_load_synth(C.c_uint64(DEC_SEED), 0, 0):
+        return None
+    load_s = time.perf_counter() - t0
+    ref.cwref_alloc_state(64, 0, 0)
+    p4 = np.ascontiguousarray(prompt[:4], np.int32)
+    out = np.zeros(64, np.int32)
+    t0 = time.perf_counter()
+    ref.cwref_generate(vp(p4), 4, 1, vp(out))
+    t1 = time.perf_counter() - t0
+    n = int(max(2, min(24, budget_s / max(t1 / 2.0, 1e-3))))
+    t0 = time.perf_counter()
+    ref.cwref_generate(vp(p4), 4, 1 + n, vp(out))
+    tn = time.perf_counter() - t0
+    tps = n / max(tn - t1, 1e-9)
+    return tps, {"kind": "reference", "cores": int(ref.cwref_threads()), "variant": variant,
+                 "sample": f"reference generate_tokens on the same seeded 27B model: 4-id prompt, "
+                           f"(t({1 + n}) - t(1))/{n} decode steps ({tn:.1f} s; model synth {load_s:.0f} s)"}
+
+
+def main_decode(args, ws, rank, local):
+    hbm, bf16, peak_kind = peaks()
+    config = {"workload": "config2: serial greedy decode, random-init 27B hybrid (64 layers, Q4_0, "
+                          "scales |N(0,0.01)|), prompt 512 random ids",
+              "model": "cwen qwen35-style hybrid 27B (GDN:attention 3:1), synthetic weights",
+              "prompt": PROMPT_LEN, "ctx": DEC_CTX, "batch": 1,
+              "l2": "every step streams 14.4 GB of weights (>> 126 MB L2)",
+              "parallelism": f"replicas{ws} (independent sequence per GPU)" if ws > 1 else "single"}
+    metric = "decode tok/s (serial greedy, config 2)"
+    if args.impl == "reference":
+        if rank != 0:
+            return 0
+        from oracle_lib import load_oracle  # noqa: F401  (synth ids)
+        prompt = synth_ids(PROMPT_LEN, DEC_SEED, "bench.prompt", 248320)
+        res = cpu_decode_baseline(prompt, budget_s=max(5.0, min(60.0, 1.0 * args.steps)))
+        if res is None:
+            print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref reference build missing"}))
+            return 0
+        tps, info = res
+        print(json.dumps({"impl": "reference", "metric": metric, "value": round(tps, 4), "unit": "tok/s",
+                          "n_gpus": 0, "steps": args.steps, "warmup": args.warmup,
+                          "ms_per_step": round(1000.0 / tps, 3), "higher_is_better": True, "scaling": "weak",
+                          "vs_baseline": None, "dtype": "q4_0 weights, fp32 activations", "data": "synthetic (seeded)",
+                          "config": config, "cpu_baseline": {**info, "value": round(tps, 4), "unit": "tok/s"},
+                          "e2e": {"value": round(tps, 4), "unit": "tok/s", "h2d_bytes_per_step": 0,
+                                  "d2h_bytes_per_step": 0}}))
+        return 0
+    ms, kern, e2e_tps, clk, spec, load_s, prompt = run_decode_ours(args, ws, rank, local)
+    tps = 1000.0 / ms
+    gemv_ms = kern["gemv_ms_per_token"] / max(kern["gemv_calls_per_token"], 1)
+    gemv_bytes = kern["gemv_bytes_per_token"] / max(kern["gemv_calls_per_token"], 1)
+    ach = kern["gemv_bytes_per_token"] / (kern["gemv_ms_per_token"] * 1e-3) / 1e9
+    line = {"metric": metric, "value": round(tps * ws, 3), "unit": "tok/s", "n_gpus": ws, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "q4_0 weights, fp32 activations (f16 hi+lo MMA, fp32 accumulate)",
+            "data": "synthetic (seeded random-init weights, random prompt ids)", "config": config,
+            "gpu_launches": int(round(kern["launches_per_token"] * args.steps)), "clocks": clk,
+            "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": hbm, "unit": "GB/s",
+                         "frac": round(ach / hbm, 4), "peak_kind": peak_kind, "traffic": None,
+                         "kernel": "qgemv_kernel (all verify-GEMV launches of a decode step)",
+                         "launches_per_token": round(kern["gemv_calls_per_token"], 1),
+                         "avg_launch_ms": round(gemv_ms, 5), "avg_launch_bytes": round(gemv_bytes),
+                         "gemv_share_of_step": round(kern["gemv_ms_per_token"] / ms, 3)},
+            "e2e": {"value": round(e2e_tps * ws, 3), "unit": "tok/s", "h2d_bytes_per_step": 4,
+                    "d2h_bytes_per_step": 12, "method": "cwen_generate (C host driver): (t(256)-t(1))/255"},
+            "spec_d8": spec, "model_load_s": round(load_s, 1)}
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+        res = cpu_decode_baseline(prompt)
+        if res:
+            line["cpu_baseline"] = {**res[1], "value": round(res[0], 4), "unit": "tok/s"}
+    if rank == 0:
+        print(json.dumps(line))
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=32)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="gemv", choices=["gemv"])
+    ap.add_argument("--workload", default="decode", choices=["decode", "gemv"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     ws, rank, local = dist_init(args)
+    if args.workload == "decode":
+        rc = main_decode(args, ws, rank, local)
+        if ws > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+        return rc
     hbm, bf16, peak_kind = peaks()
     config = {"workload": "config0: Q4_0 verify GEMV W[17408x5120], X fp32[8x5120], Y[8x17408]",
               "B": GEMV_B, "K": GEMV_K, "M": GEMV_M,

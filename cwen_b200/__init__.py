@@ -59,6 +59,7 @@ _SIGS = {
     "cwen_cuda_dump_read": (C.c_int, [C.c_int, C.c_int, C.c_void_p]),
     "cwen_cuda_gdn_state": (C.c_int, [C.c_int, C.c_void_p, C.c_void_p]),
     "cwen_cuda_ctx": (C.c_int, []),
+    "cwen_cuda_stream": (C.c_void_p, []),
     "cwen_load_gguf": (C.c_int, [C.c_char_p]),
     "cwen_load_synth": (C.c_int, [C.c_uint64, C.POINTER(Dims), C.c_int]),
     "cwen_dims_reference": (None, [C.POINTER(Dims)]),

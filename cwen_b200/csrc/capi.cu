@@ -137,6 +137,7 @@ int cwen_cuda_init(int device, int ctx, int bmax) {
 }
 
 int cwen_cuda_ctx(void) { return engine().live ? engine().ctx : 0; }
+void *cwen_cuda_stream(void) { return engine().live ? (void *)engine().stream : nullptr; }
 
 void cwen_cuda_shutdown(void) {
   Engine &E = engine();

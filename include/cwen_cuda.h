@@ -57,6 +57,9 @@ int cwen_cuda_init(int device, int ctx, int bmax);
 void cwen_cuda_shutdown(void);
 /* Context window the engine was initialised with (0 before init). */
 int cwen_cuda_ctx(void);
+/* The engine's CUDA stream (a cudaStream_t), for callers that time or order
+ * their own work against it. */
+void *cwen_cuda_stream(void);
 
 /* ---- stand-alone verify GEMV (gemvb, run.c:1577) ---- */
 /* Upload one GGUF Q4_0/Q8_0 matrix (ne0 = K row length, ne1 = M rows) from
