@@ -69,6 +69,10 @@ _SIGS = {
     "cwen_generate": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.POINTER(SpecCfg),
                                 C.POINTER(SpecStats)]),
     "cwen_ngram_draft": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_int]),
+    "cw_synth_q4_0": (None, [C.c_uint64, C.c_char_p, C.c_int, C.c_int, C.c_void_p, C.c_int]),
+    "cw_synth_q8_0": (None, [C.c_uint64, C.c_char_p, C.c_int, C.c_int, C.c_void_p, C.c_int]),
+    "cw_synth_normal": (None, [C.c_uint64, C.c_char_p, C.c_float, C.c_float, C.c_void_p, C.c_size_t]),
+    "cw_synth_ids": (None, [C.c_uint64, C.c_char_p, C.c_int, C.c_void_p, C.c_size_t]),
     "cwen_cuda_profile": (C.c_int, [C.c_int]),
     "cwen_cuda_profile_read": (C.c_int, [C.POINTER(C.c_double), C.POINTER(C.c_double),
                                          C.POINTER(C.c_longlong), C.POINTER(C.c_longlong)]),
@@ -127,3 +131,28 @@ def generate(tokens, n_gen: int, cfg: SpecCfg | None = None):
     if n < 0:
         check(n, "cwen_generate")
     return out[:n], st
+
+
+# ---- seeded synthetic inputs (host/synth.c, the generator behind cwen_load_synth) ----
+def synth_q(seed: int, stream: str, typ: int, K: int, M: int):
+    """Seeded GGUF Q4_0 (typ 2) or Q8_0 (typ 8) matrix of M rows x K: scales
+    |N(0, 0.01)| as f16, nibbles / int8 uniform."""
+    import numpy as np
+    W = np.zeros((K // 32) * (18 if typ == CWEN_T_Q4_0 else 34) * M, np.uint8)
+    fn = lib().cw_synth_q4_0 if typ == CWEN_T_Q4_0 else lib().cw_synth_q8_0
+    fn(seed, stream.encode(), K, M, ptr(W), 0)
+    return W
+
+
+def synth_normal(seed: int, stream: str, n: int, mean: float = 0.0, std: float = 1.0):
+    import numpy as np
+    v = np.zeros(n, np.float32)
+    lib().cw_synth_normal(seed, stream.encode(), mean, std, ptr(v), n)
+    return v
+
+
+def synth_ids(seed: int, stream: str, V: int, n: int):
+    import numpy as np
+    v = np.zeros(n, np.int32)
+    lib().cw_synth_ids(seed, stream.encode(), V, ptr(v), n)
+    return v
