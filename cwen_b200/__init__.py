@@ -43,6 +43,7 @@ _SIGS = {
     "cwen_cuda_shutdown": (None, []),
     "cwen_cuda_weight_upload": (C.c_int, [C.c_int, C.c_void_p, C.c_int, C.c_int, C.POINTER(C.c_int)]),
     "cwen_cuda_gemvb": (C.c_int, [C.c_int, C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_int, C.c_void_p]),
+    "cwen_cuda_gemvb_static": (C.c_int, [C.c_int, C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_int, C.c_void_p]),
     "cwen_cuda_gemvb_host": (C.c_int, [C.c_int, C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_int]),
     "cwen_cuda_model_config": (C.c_int, [C.POINTER(Dims)]),
     "cwen_cuda_upload": (C.c_int, [C.c_char_p, C.c_int, C.c_void_p, C.c_int, C.c_int]),

@@ -1,0 +1,104 @@
+// Verify GEMV whose scratch lives in statically allocated device memory.
+//
+// cwen_cuda_gemvb needs the split-K partials, the per-tile arrival counters
+// and the prepared X tiles of the engine's scratch, which cwen_cuda_init
+// allocates.  This variant runs the same two kernels (X preparation and the
+// GEMV) on file-scope __device__ arrays instead, so that a call allocates
+// nothing.  It is meant for callers that must not call cudaMalloc on their
+// per-call path: a host framework whose caching allocator already reserved
+// the device memory (a cudaMalloc there fails or fragments its pool), and
+// latency-critical loops where cudaMalloc / cudaFree would synchronize the
+// device and stall the other streams.
+//
+// Limits (the arrays are sized for them; every GPU that loads the library
+// holds about 12 MiB of them until the process exits):
+//   K <= 32768, B <= 16, at most 4096 tiles of 256 rows (M <= 1,048,576),
+//   at most 320 CTAs of split-K partials.
+#include "engine.cuh"
+#include "qgemv.cuh"
+
+namespace cw {
+namespace {
+
+constexpr int NA_KMAX = 32768;
+constexpr int NA_MAX_CTAS = 320;
+constexpr int NA_MAX_TILES = 4096;
+constexpr int NA_MAX_DEVICES = 64;
+constexpr size_t NA_XF_UINT4 = (size_t)(NA_KMAX / 32) * 2 * 2 * 32;  // X tiles for K <= NA_KMAX, 2 column tiles
+constexpr size_t NA_WS_FLOATS = (size_t)NA_MAX_CTAS * 2 * QG_TILE_MT * 16 * 16;
+
+static __device__ __align__(256) uint4 g_na_xf[NA_XF_UINT4];
+static __device__ __align__(256) int g_na_xexp[QG_MAXB];
+static __device__ __align__(256) float g_na_ws[NA_WS_FLOATS];
+static __device__ __align__(256) int g_na_cnt[NA_MAX_TILES];
+
+struct NaDevice {
+  bool ready = false;
+  GemvScratch s;
+};
+NaDevice g_na[NA_MAX_DEVICES];
+
+// Device addresses of the static arrays, looked up once per device with that
+// device current.  The array names are host-side stand-ins in host code; only
+// these addresses may be handed to kernels.
+int na_setup(int device, int n_sm) {
+  NaDevice &D = g_na[device];
+  if (D.ready) return CWEN_OK;
+  int cur = -1;
+  CW_CHECK(cudaGetDevice(&cur));
+  if (cur != device) CW_CHECK(cudaSetDevice(device));
+  GemvScratch s;
+  CW_CHECK(cudaGetSymbolAddress((void **)&s.xf, g_na_xf));
+  CW_CHECK(cudaGetSymbolAddress((void **)&s.xexp, g_na_xexp));
+  CW_CHECK(cudaGetSymbolAddress((void **)&s.ws, g_na_ws));
+  CW_CHECK(cudaGetSymbolAddress((void **)&s.cnt, g_na_cnt));
+  if (cur != device) CW_CHECK(cudaSetDevice(cur));
+  s.kmax = NA_KMAX;
+  s.G = 2 * n_sm < NA_MAX_CTAS ? 2 * n_sm : NA_MAX_CTAS;  // the engine's grid when it fits
+  s.max_tiles = NA_MAX_TILES;
+  D.s = s;
+  D.ready = true;
+  return CWEN_OK;
+}
+
+}  // namespace
+}  // namespace cw
+
+using namespace cw;
+
+extern "C" int cwen_cuda_gemvb_static(int wid, const float *dX, int xs, float *dY, int ys, int B, void *stream) {
+  Engine &E = engine();
+  if (!E.live) {
+    set_error("cwen_cuda_gemvb_static: engine not initialised");
+    return CWEN_ESTATE;
+  }
+  if (wid < 0 || wid >= (int)E.mats.size()) {
+    set_error("cwen_cuda_gemvb_static: bad weight handle %d", wid);
+    return CWEN_EINVAL;
+  }
+  const QMat &m = E.mats[wid];
+  if (B < 1 || B > QG_MAXB || !dX || !dY || xs < m.K || ys < m.M) {
+    set_error("cwen_cuda_gemvb_static: need 1 <= B <= %d, xs >= K, ys >= M, non-null X and Y", QG_MAXB);
+    return CWEN_EINVAL;
+  }
+  const int n_tiles = (m.n_mt + QG_TILE_MT - 1) / QG_TILE_MT;
+  if (m.K > NA_KMAX || n_tiles > NA_MAX_TILES) {
+    set_error("cwen_cuda_gemvb_static: K=%d, M=%d exceed the static scratch (K <= %d, M <= %d)", m.K, m.M, NA_KMAX,
+              NA_MAX_TILES * QG_TILE_MT * 16);
+    return CWEN_EINVAL;
+  }
+  if (E.device < 0 || E.device >= NA_MAX_DEVICES) {
+    set_error("cwen_cuda_gemvb_static: device %d beyond %d", E.device, NA_MAX_DEVICES);
+    return CWEN_EINVAL;
+  }
+  const int rc = na_setup(E.device, E.n_sm);
+  if (rc) return rc;
+  GemvScratch &s = g_na[E.device].s;
+  cudaStream_t st = stream ? (cudaStream_t)stream : E.stream;
+  // The arrival counters reset themselves at the end of a complete call; clear
+  // the ones this call uses in case an earlier call stopped part-way.
+  CW_CHECK(cudaMemsetAsync(s.cnt, 0, (size_t)n_tiles * sizeof(int), st));
+  CW_CHECK(gemv_prep_x(dX, xs, B, m.K, s, st));
+  CW_CHECK(gemv_run(m, B, dY, ys, EPI_STORE, s, st));
+  return CWEN_OK;
+}

@@ -72,6 +72,22 @@ int cwen_cuda_gemvb(int wid, const float *dX, int xs, float *dY, int ys, int B, 
 /* The same with host buffers: copies X in, runs, copies Y out, synchronizes. */
 int cwen_cuda_gemvb_host(int wid, const float *hX, int xs, float *hY, int ys, int B);
 
+/* The same GEMV with no allocation at all: its scratch (prepared X, split-K
+ * partials, tile counters) is a fixed array of device memory inside the
+ * library (about 12 MiB on every GPU that loads it, held until exit) instead
+ * of the engine's.  No counterpart in the reference, which has no device
+ * memory.  For callers that must not call cudaMalloc while they run -- a
+ * framework whose caching allocator already holds the device memory, or a
+ * latency-critical loop where cudaMalloc/cudaFree would synchronize the device.
+ * Weights come from cwen_cuda_weight_upload at set-up; X and Y are the
+ * caller's device buffers.  Limits: K <= 32768, M <= 1,048,576, B <= 16;
+ * larger shapes return CWEN_EINVAL.  The first call on a device looks up the
+ * array's device address (no allocation); make that first call before any
+ * stream capture.  All calls share the one array: calls that overlap on the
+ * GPU (different streams, no ordering between them) race and corrupt each
+ * other's results.  Output matches cwen_cuda_gemvb. */
+int cwen_cuda_gemvb_static(int wid, const float *dX, int xs, float *dY, int ys, int B, void *stream);
+
 /* ---- the model ---- */
 /* Declare the geometry (run.c:83-91 constants) before any upload. */
 int cwen_cuda_model_config(const cwen_dims *dims);
