@@ -507,7 +507,7 @@ def main():
     ach = kern["bytes"] / (kern_ms * 1e-3) / 1e9
     line["roofline"] = {"bound": "hbm", "achieved": round(ach, 1), "peak": hbm, "unit": "GB/s",
                         "frac": round(ach / hbm, 4), "peak_kind": peak_kind, "traffic": GEMV_NCU_TRAFFIC,
-                        "kernel": "qgemv_kernel<Q4_0,NT=1>", "kernel_ms": round(kern_ms, 5)}
+                        "kernel": "qgemv_kernel<Q4_0, 2 n-tiles of 4 columns>", "kernel_ms": round(kern_ms, 5)}
     e2e_gbs = GEMV_BYTES / e2e_s / 1e9
     line["e2e"] = {"value": round(e2e_gbs * ws, 2), "unit": "GB/s", "h2d_bytes_per_step": GEMV_B * GEMV_K * 4,
                    "d2h_bytes_per_step": GEMV_B * GEMV_M * 4,

@@ -191,13 +191,22 @@ cudaError_t launch_attention(const AttnArgs &a, GemvScratch &s, cudaStream_t st)
   }
   attn_chunk_kernel<<<dim3(a.nkv, nch), 256, smem, st>>>(a.qbuf, a.Kc, a.Vc, a.nh, a.nkv, a.pos0, a.B, a.t0,
                                                          a.nch_max, a.part);
-  const int nt = (a.B + 7) / 8;
-  attn_combine_kernel<<<nt * 8, PREP_THREADS, (size_t)a.nh * HD * sizeof(float), st>>>(
+  const int nt = gemv_ntiles(a.B);
+  attn_combine_kernel<<<nt * 4, PREP_THREADS, (size_t)a.nh * HD * sizeof(float), st>>>(
       a.part, a.proj, a.ps, a.nh, a.pos0, a.B, a.t0, a.nch_max, nt, s.xf, s.xexp, a.yout);
   return cudaGetLastError();
 }
 
 int attn_chunk_slots() { return ACH; }
 size_t attn_part_floats(int bmax, int nh, int nch_max) { return (size_t)bmax * nh * nch_max * PART; }
+
+// One-time kernel attributes (called at engine set-up).
+cudaError_t attn_configure() {
+  cudaError_t e;
+  if ((e = carveout_max(attn_prep_kernel)) != cudaSuccess) return e;
+  if ((e = carveout_max(attn_chunk_kernel)) != cudaSuccess) return e;
+  if ((e = carveout_max(attn_combine_kernel)) != cudaSuccess) return e;
+  return cudaSuccess;
+}
 
 }  // namespace cw

@@ -25,4 +25,7 @@ cudaError_t launch_attention(const AttnArgs &a, GemvScratch &s, cudaStream_t st)
 int attn_chunk_slots();
 size_t attn_part_floats(int bmax, int nh, int nch_max);
 
+// Kernel attributes set once per process (shared-memory carveout).
+cudaError_t attn_configure();
+
 }  // namespace cw

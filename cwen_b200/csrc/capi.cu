@@ -3,7 +3,10 @@
 #include <string.h>
 
 #include "engine.cuh"
+#include "attn.cuh"
+#include "gdn.cuh"
 #include "model.cuh"
+#include "rowops.cuh"
 
 namespace cw {
 
@@ -88,6 +91,20 @@ cudaError_t timed_gemv(const QMat &m, int B, float *Y, int ys, int epi, cudaStre
   return r;
 }
 
+// Error flag of the GEMV's bounded waits; read after a synchronize.  A set
+// flag means a kernel gave up on a wait (the arrival counters may be stale,
+// so they are cleared too).
+int gemv_status() {
+  Engine &E = engine();
+  int err = 0;
+  CW_CHECK(cudaMemcpy(&err, E.gs.err, sizeof(int), cudaMemcpyDeviceToHost));
+  if (!err) return CWEN_OK;
+  CW_CHECK(cudaMemset(E.gs.err, 0, sizeof(int)));
+  CW_CHECK(cudaMemset(E.gs.cnt, 0, (size_t)E.gs.max_tiles * sizeof(int)));
+  set_error("verify GEMV: a bounded device wait gave up (code %d)", err);
+  return CWEN_ETIMEOUT;
+}
+
 int alloc_qmat(QMat &m, int type, int K, int n_mt, int M) {
   m.type = type;
   m.K = K;
@@ -118,6 +135,10 @@ int cwen_cuda_init(int device, int ctx, int bmax) {
     return CWEN_EINVAL;
   }
   CW_CHECK(cudaSetDevice(device));
+  CW_CHECK(qgemv_configure());
+  CW_CHECK(rowops_configure());
+  CW_CHECK(attn_configure());
+  CW_CHECK(gdn_configure());
   E.device = device;
   E.ctx = ctx;
   E.bmax = bmax;
@@ -125,13 +146,15 @@ int cwen_cuda_init(int device, int ctx, int bmax) {
   CW_CHECK(cudaStreamCreateWithFlags(&E.stream, cudaStreamNonBlocking));
   GemvScratch &s = E.gs;
   s.kmax = 32768;
-  s.G = 2 * E.n_sm;
+  s.G = E.n_sm;  // one persistent CTA per SM
   s.max_tiles = 1 << 16;
   CW_CHECK(cudaMalloc(&s.xf, (size_t)(s.kmax / 32) * 2 * 2 * 32 * sizeof(uint4)));
   CW_CHECK(cudaMalloc(&s.xexp, QG_MAXB * sizeof(int)));
   CW_CHECK(cudaMalloc(&s.ws, gemv_scratch_ws_floats(s.G) * sizeof(float)));
   CW_CHECK(cudaMalloc(&s.cnt, (size_t)s.max_tiles * sizeof(int)));
   CW_CHECK(cudaMemset(s.cnt, 0, (size_t)s.max_tiles * sizeof(int)));
+  CW_CHECK(cudaMalloc(&s.err, sizeof(int)));
+  CW_CHECK(cudaMemset(s.err, 0, sizeof(int)));
   E.live = true;
   return CWEN_OK;
 }
@@ -151,6 +174,7 @@ void cwen_cuda_shutdown(void) {
   cudaFree(E.gs.xexp);
   cudaFree(E.gs.ws);
   cudaFree(E.gs.cnt);
+  cudaFree(E.gs.err);
   if (E.staging) cudaFree(E.staging);
   if (E.io) cudaFree(E.io);
   cudaStreamDestroy(E.stream);
@@ -255,7 +279,7 @@ int cwen_cuda_gemvb_host(int wid, const float *hX, int xs, float *hY, int ys, in
   if (rc) return rc;
   CW_CHECK(cudaMemcpyAsync(hY, dY, ny * sizeof(float), cudaMemcpyDeviceToHost, E.stream));
   CW_CHECK(cudaStreamSynchronize(E.stream));
-  return CWEN_OK;
+  return gemv_status();
 }
 
 }  // extern "C"

@@ -8,6 +8,15 @@
 
 namespace cw {
 
+// Prefer the largest shared-memory carveout for a kernel.  With every kernel
+// of the decode step on the same carveout, an SM never reconfigures its
+// L1/shared split between consecutive kernels (measured ~1.5 us per switch).
+template <class F>
+inline cudaError_t carveout_max(F *fn) {
+  return cudaFuncSetAttribute(reinterpret_cast<const void *>(fn), cudaFuncAttributePreferredSharedMemoryCarveout,
+                              (int)cudaSharedmemCarveoutMaxShared);
+}
+
 // 16-byte / 8-byte global loads through the read-only path without L1
 // allocation: weights are streamed exactly once per sweep.
 CW_DEV uint4 ldg_stream_u4(const void *p) {

@@ -40,6 +40,8 @@ struct Engine {
 cudaError_t timed_gemv(const QMat &m, int B, float *Y, int ys, int epi, cudaStream_t st);
 
 Engine &engine();
+// CWEN_OK, or CWEN_ETIMEOUT when a GEMV gave up on a bounded wait (synchronous).
+int gemv_status();
 void set_error(const char *fmt, ...);
 int cuda_fail(cudaError_t e, const char *what);
 

@@ -196,4 +196,13 @@ cudaError_t launch_gdn_replay(GdnLayerPtrs *dev_layers, int n_layers, int k, int
   return cudaGetLastError();
 }
 
+// One-time kernel attributes (called at engine set-up).
+cudaError_t gdn_configure() {
+  cudaError_t e;
+  if ((e = carveout_max(gdn_conv_kernel)) != cudaSuccess) return e;
+  if ((e = carveout_max(gdn_recur_kernel)) != cudaSuccess) return e;
+  if ((e = carveout_max(gdn_replay_kernel)) != cudaSuccess) return e;
+  return cudaSuccess;
+}
+
 }  // namespace cw

@@ -34,4 +34,7 @@ cudaError_t launch_gdn_layer(const GdnLayerArgs &a, cudaStream_t st);
 // Advance every layer's committed state by block rows 0..k.
 cudaError_t launch_gdn_replay(GdnLayerPtrs *dev_layers, int n_layers, int k, int nkh, int nvh, cudaStream_t st);
 
+// Kernel attributes set once per process (shared-memory carveout).
+cudaError_t gdn_configure();
+
 }  // namespace cw

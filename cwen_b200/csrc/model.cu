@@ -547,6 +547,8 @@ int cwen_cuda_accept(int *k_out, int *ustar_out, int *argmax_out) {
     set_error("device reported a token id out of range");
     return CWEN_ERANGE;
   }
+  rc = gemv_status();
+  if (rc) return rc;
   if (k_out) *k_out = M.h_walk[0];
   if (ustar_out) *ustar_out = M.h_walk[1];
   if (argmax_out) memcpy(argmax_out, M.h_walk + 2, (size_t)M.pending_nlog * sizeof(int));

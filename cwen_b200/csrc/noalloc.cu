@@ -12,7 +12,7 @@
 //
 // Limits (the arrays are sized for them; every GPU that loads the library
 // holds about 12 MiB of them until the process exits):
-//   K <= 32768, B <= 16, at most 4096 tiles of 256 rows (M <= 1,048,576),
+//   K <= 32768, B <= 16, at most 2048 tiles of 512 rows (M <= 1,048,576),
 //   at most 320 CTAs of split-K partials.
 #include "engine.cuh"
 #include "qgemv.cuh"
@@ -22,15 +22,16 @@ namespace {
 
 constexpr int NA_KMAX = 32768;
 constexpr int NA_MAX_CTAS = 320;
-constexpr int NA_MAX_TILES = 4096;
+constexpr int NA_MAX_TILES = 2048;
 constexpr int NA_MAX_DEVICES = 64;
 constexpr size_t NA_XF_UINT4 = (size_t)(NA_KMAX / 32) * 2 * 2 * 32;  // X tiles for K <= NA_KMAX, 2 column tiles
-constexpr size_t NA_WS_FLOATS = (size_t)NA_MAX_CTAS * 2 * QG_TILE_MT * 16 * 16;
+constexpr size_t NA_WS_FLOATS = (size_t)NA_MAX_CTAS * 2 * WS_TILE_FLOATS;
 
 static __device__ __align__(256) uint4 g_na_xf[NA_XF_UINT4];
 static __device__ __align__(256) int g_na_xexp[QG_MAXB];
 static __device__ __align__(256) float g_na_ws[NA_WS_FLOATS];
 static __device__ __align__(256) int g_na_cnt[NA_MAX_TILES];
+static __device__ __align__(256) int g_na_err[1];
 
 struct NaDevice {
   bool ready = false;
@@ -52,9 +53,10 @@ int na_setup(int device, int n_sm) {
   CW_CHECK(cudaGetSymbolAddress((void **)&s.xexp, g_na_xexp));
   CW_CHECK(cudaGetSymbolAddress((void **)&s.ws, g_na_ws));
   CW_CHECK(cudaGetSymbolAddress((void **)&s.cnt, g_na_cnt));
+  CW_CHECK(cudaGetSymbolAddress((void **)&s.err, g_na_err));
   if (cur != device) CW_CHECK(cudaSetDevice(cur));
   s.kmax = NA_KMAX;
-  s.G = 2 * n_sm < NA_MAX_CTAS ? 2 * n_sm : NA_MAX_CTAS;  // the engine's grid when it fits
+  s.G = n_sm < NA_MAX_CTAS ? n_sm : NA_MAX_CTAS;  // the engine's grid when it fits
   s.max_tiles = NA_MAX_TILES;
   D.s = s;
   D.ready = true;
@@ -96,8 +98,10 @@ extern "C" int cwen_cuda_gemvb_static(int wid, const float *dX, int xs, float *d
   GemvScratch &s = g_na[E.device].s;
   cudaStream_t st = stream ? (cudaStream_t)stream : E.stream;
   // The arrival counters reset themselves at the end of a complete call; clear
-  // the ones this call uses in case an earlier call stopped part-way.
+  // the ones this call uses, and the wait-timeout flag, in case an earlier
+  // call stopped part-way.
   CW_CHECK(cudaMemsetAsync(s.cnt, 0, (size_t)n_tiles * sizeof(int), st));
+  CW_CHECK(cudaMemsetAsync(s.err, 0, sizeof(int), st));
   CW_CHECK(gemv_prep_x(dX, xs, B, m.K, s, st));
   CW_CHECK(gemv_run(m, B, dY, ys, EPI_STORE, s, st));
   return CWEN_OK;

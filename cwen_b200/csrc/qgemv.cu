@@ -9,28 +9,38 @@
 // B = 8 columns at 28 FLOP/byte is beyond what the CUDA cores can do at HBM
 // speed, so the block dot runs on the tensor cores: (q - 8) is exact in f16,
 // and X is split into f16 hi + lo parts (x = hi + lo to ~2^-22 relative) after
-// a per-column power-of-two scale that keeps it inside f16 range.  Per block:
-//   c = A*Xhi(k0..15) + A*Xlo(k0..15) + A*Xhi(k16..31) + A*Xlo(k16..31)
-// (fp32 accumulate inside the MMA), then acc = fma(d, c, acc) on the CUDA
-// cores -- the reference's per-block scale, applied to an fp32 partial.
+// a per-column power-of-two scale that keeps it inside f16 range.  One
+// m16n8k16 B operand carries the hi parts of 4 columns and their lo parts,
+// so per 16 rows x 32 weights x 4 columns two MMAs give
+//   c_hi = A*Xhi(k0..15) + A*Xhi(k16..31),  c_lo = the same with Xlo
+// (fp32 accumulate inside the MMA), then acc_hi = fma(d, c_hi, acc_hi) and
+// acc_lo likewise on the CUDA cores -- the reference's per-block scale,
+// applied to fp32 partials; y = (acc_hi + acc_lo) * 2^-e at the end.
 //
 // Batch invariance.  Column b of any call depends only on column b of X: the
-// n-tile of 8 columns a column falls in runs the same MMA/FMA chain whether
+// n-tile of 4 columns a column falls in runs the same MMA/FMA chain whether
 // or not another n-tile runs, and the K partition (below) depends on the
 // matrix shape and grid only, never on B.  So a B-row verify block produces
 // the same bits as B single-row calls.
 //
-// Work split.  A fixed persistent grid of G CTAs (8 warps, 2 m-tiles = 32
-// rows per warp, so 256 rows per CTA tile) takes an equal contiguous share
-// of the (tile, k-pair) space ("stream-K").  A tile cut between CTAs is
-// reduced by the last CTA to arrive, summing the partials in k order, so
-// the result does not depend on arrival order.
+// Work split.  A fixed persistent grid of G <= #SM CTAs, one per SM, takes
+// equal contiguous shares of the (512-row tile, k-pair) space ("stream-K").
+// A tile cut between CTAs is reduced by the last CTA to arrive, summing the
+// partials in k order, so the result does not depend on arrival order.
 //
-// Memory.  Weights stream HBM -> shared memory through a 6-stage per-warp
-// cp.async ring (16-byte LDGSTS, no L1 allocation); X fragments (small,
-// shared by every warp) come through L1.
+// Memory.  The weights of one (tile, k-pair) -- 32 m-tiles of 16 rows, one
+// contiguous 18 KB (Q4_0) / 34 KB (Q8_0) block in the repacked layout -- and
+// the X fragments of that k-pair stream HBM -> shared memory as two bulk
+// (TMA) copies per stage into an 8-stage (Q8_0: 5) ring, issued by one
+// producer thread; 16 consumer warps (two m-tiles each) compute from shared
+// memory and release each stage through an mbarrier.  Large copies matter:
+// the issue cost of a bulk copy is nearly independent of its size up to
+// ~9 KB.  Every wait is bounded in time; a timeout raises an error flag and
+// the CTA finishes without touching memory further.
 #include "common.cuh"
 #include "qgemv.cuh"
+#include "rowprep.cuh"
+#include "sm100.cuh"
 
 namespace cw {
 
@@ -84,7 +94,8 @@ __global__ void repack_kernel(uint8_t *dst, int dst_kp, const uint8_t *src, int 
     const int g = lane >> 2, t = lane & 3;
     const int dmt = mt_off + smt * mt_stride;
     const size_t chunk = (size_t)(TYPE == 8 ? 1088 : 576);
-    uint8_t *c = dst + ((size_t)dmt * dst_kp + p) * chunk;
+    // [tile][k-pair][m-tile within tile]: one (tile, k-pair) is contiguous
+    uint8_t *c = dst + (((size_t)(dmt / QG_TILE_MT) * dst_kp + p) * QG_TILE_MT + dmt % QG_TILE_MT) * chunk;
     const int r0 = smt * 16 + g, r1 = r0 + 8;
     uint32_t words[8];
     uint16_t sc[4];
@@ -151,68 +162,37 @@ cudaError_t qmat_repack(const QMat &dst, const uint8_t *src, int M, int mt_off, 
 }
 
 // ---- X preparation ----
-// One CTA per column b < nt*8: exponent e with max|x|*2^e in [2^14, 2^15),
-// then per (32-block, lane) the f16 hi/lo fragment words in the K order the
-// A fragments use: lane (g,t) of n-tile b/8 (g = b%8) holds
-//   (x[4t], x[4t+2]) (x[4t+1], x[4t+3]) (x[4t+16], x[4t+18]) (x[4t+17], x[4t+19]).
+// One CTA per column b < nt*4: exponent e with max|x|*2^e in [2^14, 2^15),
+// then per 32-block the f16 hi and lo parts of the scaled column.  Columns
+// come in n-tiles of 4; in the m16n8k16 B operand of n-tile b/4, B column
+// b%4 holds the hi parts and B column b%4 + 4 the lo parts, so one MMA
+// multiplies a weight tile with both.  Lane (g, t) of a B operand holds, in
+// the K order the A fragments use,
+//   (x[4t], x[4t+2]) (x[4t+1], x[4t+3]) (x[4t+16], x[4t+18]) (x[4t+17], x[4t+19])
+// of B column g; one uint4 per (32-block, n-tile, lane).
 __global__ void prep_x_kernel(const float *__restrict__ X, int xs, int B, int K, int nt, uint4 *__restrict__ xf,
                               int *__restrict__ xexp) {
-  const int b = blockIdx.x;
+  extern __shared__ __align__(16) float row[];
   __shared__ float red[32];
-  __shared__ int s_e;
-  float mx = 0.f;
-  if (b < B)
-    for (int k = threadIdx.x; k < K; k += blockDim.x) mx = fmaxf(mx, fabsf(X[(size_t)b * xs + k]));
-  mx = warp_max(mx);
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
+  const int b = blockIdx.x;
+  const bool live = b < B;
+  if (live)
+    for (int k = threadIdx.x; k < K; k += blockDim.x) row[k] = X[(size_t)b * xs + k];
   __syncthreads();
-  if (threadIdx.x < 32) {
-    float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
-    v = warp_max(v);
-    if (threadIdx.x == 0) {
-      int e = 0;
-      if (v > 0.f && v <= 3.0e38f) {
-        int p;
-        frexpf(v, &p);  // v = m * 2^p, m in [0.5, 1)
-        e = 15 - p;
-        e = e < -100 ? -100 : (e > 100 ? 100 : e);
-      }
-      s_e = e;
-      xexp[b] = e;
-    }
-  }
-  __syncthreads();
-  const int e = s_e;
-  const float scale = __int_as_float((127 + e) << 23);
-  const int g = b & 7, n = b >> 3, nb = K / 32;
-  for (int item = threadIdx.x; item < nb * 4; item += blockDim.x) {
-    const int kb = item >> 2, t = item & 3;
-    const int base = kb * 32;
-    const int js[8] = {4 * t, 4 * t + 2, 4 * t + 1, 4 * t + 3, 4 * t + 16, 4 * t + 18, 4 * t + 17, 4 * t + 19};
-    uint32_t hi[4], lo[4];
-#pragma unroll
-    for (int i = 0; i < 4; i++) {
-      float v0 = 0.f, v1 = 0.f;
-      if (b < B) {
-        v0 = X[(size_t)b * xs + base + js[2 * i]] * scale;
-        v1 = X[(size_t)b * xs + base + js[2 * i + 1]] * scale;
-      }
-      const half h0 = __float2half_rn(v0), h1 = __float2half_rn(v1);
-      const half l0 = __float2half_rn(v0 - __half2float(h0)), l1 = __float2half_rn(v1 - __half2float(h1));
-      hi[i] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
-      lo[i] = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
-    }
-    const int lane = g * 4 + t;
-    const size_t o = ((size_t)(kb * nt + n) * 2) * 32 + lane;
-    xf[o] = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-    xf[o + 32] = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-  }
+  emit_xfrag(row, K, b, nt, xf, xexp, red, live);
 }
 
 cudaError_t gemv_prep_x(const float *X, int xs, int B, int K, GemvScratch &s, cudaStream_t st) {
   if (B < 1 || B > QG_MAXB || K % 64 || K > s.kmax) return cudaErrorInvalidValue;
-  const int nt = (B + 7) / 8;
-  prep_x_kernel<<<nt * 8, 256, 0, st>>>(X, xs, B, K, nt, s.xf, s.xexp);
+  const int nt = gemv_ntiles(B);
+  const size_t smem = (size_t)K * sizeof(float);
+  static size_t configured = 48 * 1024;
+  if (smem > configured) {
+    cudaError_t e = cudaFuncSetAttribute(prep_x_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    configured = smem;
+  }
+  prep_x_kernel<<<nt * 4, PREP_THREADS, smem, st>>>(X, xs, B, K, nt, s.xf, s.xexp);
   return cudaGetLastError();
 }
 
@@ -227,20 +207,36 @@ struct GemvArgs {
   int ys, epi;
   float *ws;
   int *cnt;
+  int *err;
   int G;
   long long units;
 };
 
 CW_DEV float silu_f(float x) { return x * (1.f / (1.f + expf(-x))); }
 
-// Apply the epilogue for one warp's accumulators (rows of m-tiles mt0, mt0+1).
+// Fold the lo-part accumulators into the hi-part ones: lane (g, t < 2) holds
+// B columns 2t, 2t+1 (hi parts), lane (g, t + 2) the same columns' lo parts.
+// Afterwards lanes t < 2 hold the sums (hi + lo, in that order).
+template <int NT>
+CW_DEV void fold_lo(float (&acc)[2][NT][4]) {
+#pragma unroll
+  for (int mt = 0; mt < 2; mt++)
+#pragma unroll
+    for (int n = 0; n < NT; n++)
+#pragma unroll
+      for (int i = 0; i < 4; i++) acc[mt][n][i] += __shfl_xor_sync(0xffffffffu, acc[mt][n][i], 2);
+}
+
+// Apply the epilogue for one warp's folded accumulators (rows of m-tiles
+// mt0, mt0+1; lanes t < 2 carry the columns n*4 + 2t + {0, 1}).
 template <int NT>
 CW_DEV void gemv_epilogue(const GemvArgs &a, int mt0, bool has1, const float (&acc)[2][NT][4], int g, int t) {
+  if (t >= 2) return;
 #pragma unroll
   for (int n = 0; n < NT; n++) {
 #pragma unroll
     for (int i = 0; i < 4; i++) {
-      const int col = n * 8 + 2 * t + (i & 1);
+      const int col = n * 4 + 2 * t + (i & 1);
       if (col >= a.B) continue;
       const float sc = __int_as_float((127 - __ldg(a.xexp + col)) << 23);
       const int rr = g + ((i >> 1) << 3);
@@ -267,20 +263,96 @@ CW_DEV void gemv_epilogue(const GemvArgs &a, int mt0, bool has1, const float (&a
 }
 
 template <int TYPE, int NT>
-__global__ void __launch_bounds__(QG_WARPS * 32, 2) qgemv_kernel(GemvArgs a) {
-  constexpr int CHUNK = TYPE == 8 ? 1088 : 576;
-  constexpr int QB = TYPE == 8 ? 1024 : 512;
-  constexpr int STAGE = 2 * CHUNK;
-  extern __shared__ __align__(16) uint8_t smem[];
-  __shared__ int s_last;
+struct QgLayout {
+  static constexpr int CHUNK = TYPE == 8 ? 1088 : 576;       // one m-tile x one k-pair
+  static constexpr int QB = TYPE == 8 ? 1024 : 512;          // its quant bytes (scales follow)
+  static constexpr int WB = QG_TILE_MT * CHUNK;              // weights of one (tile, k-pair)
+  static constexpr int XB = NT * 1024;                       // X fragments of one k-pair
+  static constexpr int STAGE = WB + XB;
+  static constexpr int STAGES = TYPE == 8 ? 5 : 8;
+  static constexpr int BAR_OFF = STAGES * STAGE;
+  static constexpr int SMEM = BAR_OFF + 256;
+  static_assert(WB % 16 == 0 && XB % 16 == 0 && STAGE % 16 == 0, "bulk copies need 16-byte multiples");
+  static_assert(SMEM <= 227 * 1024, "shared memory");
+};
+
+// Persistent stream-K GEMV: warps 0..15 consume (warp w owns m-tiles 2w, 2w+1
+// of the current 512-row tile), warp 16 lane 0 produces.
+template <int TYPE, int NT>
+__global__ void __launch_bounds__(QG_THREADS, 1) qgemv_kernel(GemvArgs a) {
+  using Lay = QgLayout<TYPE, NT>;
+  constexpr int S = Lay::STAGES;
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + Lay::BAR_OFF);
+  uint64_t *empty = full + S;
+  volatile int *abort_p = reinterpret_cast<volatile int *>(empty + S);
+  int *last_p = const_cast<int *>(abort_p) + 1;
+
   const int c = blockIdx.x;
   const long long u_begin = (long long)c * a.units / a.G, u_end = (long long)(c + 1) * a.units / a.G;
-  if (u_begin >= u_end) return;
+  if (u_begin >= u_end) return;  // whole CTA, before any barrier
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int g = lane >> 2, t = lane & 3;
-  uint8_t *ring = smem + warp * QG_STAGES * STAGE;
-  const float zero4[4] = {0.f, 0.f, 0.f, 0.f};
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S; i++) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], QG_CONS_WARPS);
+    }
+    *abort_p = 0;
+    mbar_fence_init();
+  }
+  __syncthreads();
 
+  if (warp == QG_CONS_WARPS) {
+    // ---------------- producer ----------------
+    // Consecutive units are consecutive (tile, k-pair) blocks of the repacked
+    // weights, so the source pointer just advances; no divisions in the loop
+    // (this thread shares its issue slots with four busy consumer warps).
+    if (lane == 0) {
+      const int n = (int)(u_end - u_begin);
+      const uint8_t *wsrc = a.w + (size_t)u_begin * Lay::WB;
+      const uint8_t *xbase = reinterpret_cast<const uint8_t *>(a.xf);
+      int k = (int)(u_begin % a.kp);
+      int st = 0;
+      uint32_t ph = 0;
+      int issued = 0;
+      bool ok = true;
+      for (; issued < n; issued++) {
+        if (!mbar_wait(&empty[st], ph ^ 1, abort_p)) {
+          ok = false;
+          break;
+        }
+        if (*abort_p) break;  // consumers gave up: issue nothing more
+        uint8_t *dst = smem + st * Lay::STAGE;
+        mbar_expect_tx(&full[st], Lay::STAGE);
+        bulk_g2s(dst, wsrc, Lay::WB, &full[st]);
+        bulk_g2s(dst + Lay::WB, xbase + (size_t)k * Lay::XB, Lay::XB, &full[st]);
+        wsrc += Lay::WB;
+        if (++k == a.kp) k = 0;
+        if (++st == S) {
+          st = 0;
+          ph ^= 1;
+        }
+      }
+      if (!ok) {
+        atomicExch(a.err, 1);
+        *abort_p = 1;
+      }
+      // never leave bulk copies in flight: wait (bounded) for the last stages issued
+      for (int i = issued > S ? issued - S : 0; i < issued; i++) {
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(&full[i % S], (uint32_t)((i / S) & 1)) && globaltimer_ns() - t0 < MBAR_TIMEOUT_NS) {
+        }
+      }
+    }
+    return;  // the producer takes part in no later barrier
+  }
+
+  // ---------------- consumers ----------------
+  const int g = lane >> 2, t = lane & 3;
+  const float zero4[4] = {0.f, 0.f, 0.f, 0.f};
+  bool ok = true;
+  int st = 0;        // ring position, advanced identically by every consumer warp and the producer
+  uint32_t ph = 0;   // its phase parity
   long long u = u_begin;
   bool first_seg = true;
   while (u < u_end) {
@@ -300,52 +372,26 @@ __global__ void __launch_bounds__(QG_WARPS * 32, 2) qgemv_kernel(GemvArgs a) {
 #pragma unroll
         for (int i = 0; i < 4; i++) acc[mt][n][i] = 0.f;
 
-    if (has0) {
-      const uint8_t *w0 = a.w + (size_t)mt0 * a.kp * CHUNK;
-      const uint8_t *w1 = w0 + (size_t)a.kp * CHUNK;
-      auto issue = [&](int i) {
-        if (i < nk) {
-          const int k = ka + i;
-          uint8_t *dst = ring + (i % QG_STAGES) * STAGE;
-          const uint8_t *s0 = w0 + (size_t)k * CHUNK, *s1 = w1 + (size_t)k * CHUNK;
-#pragma unroll
-          for (int q = 0; q < QB / 512; q++) {
-            cp_async16(dst + q * 512 + lane * 16, s0 + q * 512 + lane * 16);
-            if (has1) cp_async16(dst + CHUNK + q * 512 + lane * 16, s1 + q * 512 + lane * 16);
-          }
-          if (lane < 4) cp_async16(dst + QB + lane * 16, s0 + QB + lane * 16);
-          else if (lane < 8 && has1) cp_async16(dst + CHUNK + QB + (lane - 4) * 16, s1 + QB + (lane - 4) * 16);
+    for (int i = 0; i < nk; i++) {
+      if (ok && !mbar_wait(&full[st], ph, abort_p)) {
+        ok = false;
+        atomicExch(a.err, 2);
+        *abort_p = 1;
+      }
+      if (ok && has0) {
+        const uint8_t *stg = smem + st * Lay::STAGE;
+        const uint4 *xs = reinterpret_cast<const uint4 *>(stg + Lay::WB);
+        // one n-tile: both m-tiles share the X loads; more: reload (registers)
+        uint4 xv1[2];
+        if (NT == 1) {
+          xv1[0] = xs[lane];
+          xv1[1] = xs[32 + lane];
         }
-        cp_async_commit();
-      };
-#pragma unroll
-      for (int i = 0; i < QG_STAGES - 1; i++) issue(i);
-
-      // X fragments for k-pair k: [kb 2][n NT][hi/lo 2] uint4 at lane.
-      auto load_x = [&](int k, uint4 (&xr)[2][NT][2]) {
-#pragma unroll
-        for (int kbi = 0; kbi < 2; kbi++)
-#pragma unroll
-          for (int n = 0; n < NT; n++) {
-            const size_t o = ((size_t)((2 * k + kbi) * NT + n) * 2) * 32 + lane;
-            xr[kbi][n][0] = ldg_u4(a.xf + o);
-            xr[kbi][n][1] = ldg_u4(a.xf + o + 32);
-          }
-      };
-      uint4 xcur[2][NT][2], xnext[2][NT][2];
-      load_x(ka, xcur);
-
-      for (int i = 0; i < nk; i++) {
-        issue(i + QG_STAGES - 1);
-        if (i + 1 < nk) load_x(ka + i + 1, xnext);
-        cp_async_wait<QG_STAGES - 1>();
-        __syncwarp();
-        const uint8_t *stg = ring + (i % QG_STAGES) * STAGE;
 #pragma unroll
         for (int mt = 0; mt < 2; mt++) {
           if (mt == 1 && !has1) break;
-          const uint8_t *ch = stg + mt * CHUNK;
-          const uint2 scw = *reinterpret_cast<const uint2 *>(ch + QB + g * 8);
+          const uint8_t *ch = stg + (warp * 2 + mt) * Lay::CHUNK;
+          const uint2 scw = *reinterpret_cast<const uint2 *>(ch + Lay::QB + g * 8);
 #pragma unroll
           for (int kbi = 0; kbi < 2; kbi++) {
             uint32_t a0s0, a1s0, a2s0, a3s0, a0s1, a1s1, a2s1, a3s1;
@@ -366,12 +412,10 @@ __global__ void __launch_bounds__(QG_WARPS * 32, 2) qgemv_kernel(GemvArgs a) {
             const float dg8 = __half2float(__ushort_as_half((unsigned short)(dw >> 16)));
 #pragma unroll
             for (int n = 0; n < NT; n++) {
-              const uint4 xh = xcur[kbi][n][0], xl = xcur[kbi][n][1];
+              const uint4 xv = NT == 1 ? xv1[kbi] : xs[(kbi * NT + n) * 32 + lane];
               float cc[4];
-              mma_16816(cc, a0s0, a1s0, a2s0, a3s0, xh.x, xh.y, zero4);
-              mma_16816(cc, a0s0, a1s0, a2s0, a3s0, xl.x, xl.y, cc);
-              mma_16816(cc, a0s1, a1s1, a2s1, a3s1, xh.z, xh.w, cc);
-              mma_16816(cc, a0s1, a1s1, a2s1, a3s1, xl.z, xl.w, cc);
+              mma_16816(cc, a0s0, a1s0, a2s0, a3s0, xv.x, xv.y, zero4);
+              mma_16816(cc, a0s1, a1s1, a2s1, a3s1, xv.z, xv.w, cc);
               acc[mt][n][0] = fmaf(dg, cc[0], acc[mt][n][0]);
               acc[mt][n][1] = fmaf(dg, cc[1], acc[mt][n][1]);
               acc[mt][n][2] = fmaf(dg8, cc[2], acc[mt][n][2]);
@@ -379,47 +423,45 @@ __global__ void __launch_bounds__(QG_WARPS * 32, 2) qgemv_kernel(GemvArgs a) {
             }
           }
         }
-        __syncwarp();
-#pragma unroll
-        for (int kbi = 0; kbi < 2; kbi++)
-#pragma unroll
-          for (int n = 0; n < NT; n++) {
-            xcur[kbi][n][0] = xnext[kbi][n][0];
-            xcur[kbi][n][1] = xnext[kbi][n][1];
-          }
       }
-      cp_async_wait<0>();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[st]);
+      if (++st == S) {
+        st = 0;
+        ph ^= 1;
+      }
     }
 
-    const bool full = (ka == 0 && kb_end == a.kp);
-    if (full) {
-      if (has0) gemv_epilogue<NT>(a, mt0, has1, acc, g, t);
+    fold_lo<NT>(acc);
+    const bool full_tile = (ka == 0 && kb_end == a.kp);
+    if (full_tile) {
+      if (ok && has0) gemv_epilogue<NT>(a, mt0, has1, acc, g, t);
     } else {
       // Partial tile: park this segment's sums, last CTA to arrive reduces.
       const int slot = first_seg ? 0 : 1;
-      float *mine = a.ws + ((size_t)c * 2 + slot) * (QG_TILE_MT * 16 * 16);
-      if (has0) {
+      float *mine = a.ws + ((size_t)c * 2 + slot) * WS_TILE_FLOATS;
+      if (has0 && t < 2) {
 #pragma unroll
         for (int mt = 0; mt < 2; mt++)
 #pragma unroll
           for (int n = 0; n < NT; n++)
 #pragma unroll
             for (int h = 0; h < 2; h++) {
-              float *p = mine + ((warp * 2 + mt) * 16 + g + 8 * h) * 16 + n * 8 + 2 * t;
+              float *p = mine + ((warp * 2 + mt) * 16 + g + 8 * h) * 16 + n * 4 + 2 * t;
               *reinterpret_cast<float2 *>(p) = make_float2(acc[mt][n][2 * h], acc[mt][n][2 * h + 1]);
             }
       }
       __threadfence();
-      __syncthreads();
+      named_bar(1, QG_CONS_WARPS * 32);
       const long long tu0 = (long long)tile * a.kp, tu1 = tu0 + a.kp - 1;
       const int c_first = (int)(((tu0 + 1) * a.G - 1) / a.units);
       const int c_last = (int)(((tu1 + 1) * a.G - 1) / a.units);
       if (threadIdx.x == 0) {
-        const int old = atomicAdd(a.cnt + tile, 1);
-        s_last = (old == c_last - c_first);
+        const int old = ok ? atomicAdd(a.cnt + tile, 1) : -1;
+        *last_p = (old == c_last - c_first);
       }
-      __syncthreads();
-      if (s_last) {
+      named_bar(1, QG_CONS_WARPS * 32);
+      if (*last_p) {
         __threadfence();
         if (has0) {
           float sum[2][NT][4];
@@ -429,17 +471,18 @@ __global__ void __launch_bounds__(QG_WARPS * 32, 2) qgemv_kernel(GemvArgs a) {
             for (int n = 0; n < NT; n++)
 #pragma unroll
               for (int i = 0; i < 4; i++) sum[mt][n][i] = 0.f;
+          if (t < 2)
           for (int cc = c_first; cc <= c_last; cc++) {
             const long long cu0 = (long long)cc * a.units / a.G;
             const int sl = cu0 >= tu0 ? 0 : 1;
-            const float *src = a.ws + ((size_t)cc * 2 + sl) * (QG_TILE_MT * 16 * 16);
+            const float *src = a.ws + ((size_t)cc * 2 + sl) * WS_TILE_FLOATS;
 #pragma unroll
             for (int mt = 0; mt < 2; mt++)
 #pragma unroll
               for (int n = 0; n < NT; n++)
 #pragma unroll
                 for (int h = 0; h < 2; h++) {
-                  const float *p = src + ((warp * 2 + mt) * 16 + g + 8 * h) * 16 + n * 8 + 2 * t;
+                  const float *p = src + ((warp * 2 + mt) * 16 + g + 8 * h) * 16 + n * 4 + 2 * t;
                   const float2 v = __ldcg(reinterpret_cast<const float2 *>(p));
                   sum[mt][n][2 * h] += v.x;
                   sum[mt][n][2 * h + 1] += v.y;
@@ -449,31 +492,31 @@ __global__ void __launch_bounds__(QG_WARPS * 32, 2) qgemv_kernel(GemvArgs a) {
         }
         if (threadIdx.x == 0) a.cnt[tile] = 0;
       }
-      __syncthreads();
+      named_bar(1, QG_CONS_WARPS * 32);
     }
     u += nk;
     first_seg = false;
   }
 }
 
-size_t gemv_scratch_ws_floats(int G) { return (size_t)G * 2 * QG_TILE_MT * 16 * 16; }
+size_t gemv_scratch_ws_floats(int G) { return (size_t)G * 2 * WS_TILE_FLOATS; }
 
 template <int TYPE, int NT>
 static cudaError_t launch_t(const GemvArgs &a, cudaStream_t st) {
-  constexpr int CHUNK = TYPE == 8 ? 1088 : 576;
-  const int smem = QG_WARPS * QG_STAGES * 2 * CHUNK;
+  using Lay = QgLayout<TYPE, NT>;
   static bool configured = false;
   if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(qgemv_kernel<TYPE, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaError_t e = cudaFuncSetAttribute(qgemv_kernel<TYPE, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         Lay::SMEM);
     if (e != cudaSuccess) return e;
     configured = true;
   }
-  qgemv_kernel<TYPE, NT><<<a.G, QG_WARPS * 32, smem, st>>>(a);
+  qgemv_kernel<TYPE, NT><<<a.G, QG_THREADS, Lay::SMEM, st>>>(a);
   return cudaGetLastError();
 }
 
 cudaError_t gemv_run(const QMat &m, int B, float *Y, int ys, int epi, GemvScratch &s, cudaStream_t st) {
-  if (B < 1 || B > QG_MAXB || m.K % 64 || m.K > s.kmax || !m.w) return cudaErrorInvalidValue;
+  if (B < 1 || B > QG_MAXB || m.K % 64 || m.K > s.kmax || !m.w || !s.err) return cudaErrorInvalidValue;
   if (epi == EPI_SWIGLU && (m.n_mt % 2)) return cudaErrorInvalidValue;
   GemvArgs a;
   a.w = m.w;
@@ -488,14 +531,40 @@ cudaError_t gemv_run(const QMat &m, int B, float *Y, int ys, int epi, GemvScratc
   a.epi = epi;
   a.ws = s.ws;
   a.cnt = s.cnt;
+  a.err = s.err;
   const int n_tiles = (m.n_mt + QG_TILE_MT - 1) / QG_TILE_MT;
   if (n_tiles > s.max_tiles) return cudaErrorInvalidValue;
   a.units = (long long)n_tiles * a.kp;
   // Grid: a function of the shape only (never of B), >= 4 k-pairs per CTA.
   long long g = (a.units + 3) / 4;
   a.G = (int)(g < s.G ? g : s.G);
-  if (m.type == 8) return B > 8 ? launch_t<8, 2>(a, st) : launch_t<8, 1>(a, st);
-  return B > 8 ? launch_t<2, 2>(a, st) : launch_t<2, 1>(a, st);
+  switch (gemv_ntiles(B) * 16 + m.type) {
+    case 16 + 8: return launch_t<8, 1>(a, st);
+    case 32 + 8: return launch_t<8, 2>(a, st);
+    case 48 + 8: return launch_t<8, 3>(a, st);
+    case 64 + 8: return launch_t<8, 4>(a, st);
+    case 16 + 2: return launch_t<2, 1>(a, st);
+    case 32 + 2: return launch_t<2, 2>(a, st);
+    case 48 + 2: return launch_t<2, 3>(a, st);
+    default: return launch_t<2, 4>(a, st);
+  }
+}
+
+// One-time kernel attributes (called at engine set-up).
+cudaError_t qgemv_configure() {
+  cudaError_t e;
+  if ((e = carveout_max(repack_kernel<2>)) != cudaSuccess) return e;
+  if ((e = carveout_max(repack_kernel<8>)) != cudaSuccess) return e;
+  if ((e = carveout_max(prep_x_kernel)) != cudaSuccess) return e;
+  if ((e = carveout_max(qgemv_kernel<2, 1>)) != cudaSuccess) return e;
+  if ((e = carveout_max(qgemv_kernel<2, 2>)) != cudaSuccess) return e;
+  if ((e = carveout_max(qgemv_kernel<2, 3>)) != cudaSuccess) return e;
+  if ((e = carveout_max(qgemv_kernel<2, 4>)) != cudaSuccess) return e;
+  if ((e = carveout_max(qgemv_kernel<8, 1>)) != cudaSuccess) return e;
+  if ((e = carveout_max(qgemv_kernel<8, 2>)) != cudaSuccess) return e;
+  if ((e = carveout_max(qgemv_kernel<8, 3>)) != cudaSuccess) return e;
+  if ((e = carveout_max(qgemv_kernel<8, 4>)) != cudaSuccess) return e;
+  return cudaSuccess;
 }
 
 }  // namespace cw

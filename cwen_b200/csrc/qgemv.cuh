@@ -11,14 +11,16 @@
 namespace cw {
 
 // Device layout of one (possibly fused) weight matrix: rows grouped in
-// 16-row m-tiles; per (m-tile, pair of 32-blocks) one 576-byte chunk
-// [512 B nibbles in mma A-fragment order | 64 B f16 scales].
-// Q8_0 uses 1088-byte chunks [1024 B int8 | 64 B scales].
+// 16-row m-tiles, m-tiles in 512-row tiles of 32; per (m-tile, pair of
+// 32-blocks) one 576-byte chunk [512 B nibbles in mma A-fragment order |
+// 64 B f16 scales] (Q8_0: 1088 B [1024 B int8 | 64 B scales]), stored
+// [tile][k-pair][m-tile in tile] so that one (tile, k-pair) is contiguous.
+// The m-tile count is padded to whole tiles (zero padding).
 struct QMat {
   uint8_t *w = nullptr;  // device
   int type = 0;          // 2 = Q4_0, 8 = Q8_0
   int K = 0;             // row length
-  int n_mt = 0;          // m-tiles (16 rows)
+  int n_mt = 0;          // m-tiles (16 rows) holding rows; storage is padded to QG_TILE_MT
   int M = 0;             // valid rows (n_mt*16 >= M)
   size_t bytes = 0;
 };
@@ -26,20 +28,29 @@ struct QMat {
 enum { EPI_STORE = 0, EPI_ADD = 1, EPI_SWIGLU = 2 };
 
 constexpr int QG_MAXB = 16;
-constexpr int QG_WARPS = 8;
-constexpr int QG_TILE_MT = 2 * QG_WARPS;  // m-tiles per CTA tile
-constexpr int QG_STAGES = 6;
+constexpr int QG_CONS_WARPS = 16;                    // consumer warps, two m-tiles each
+constexpr int QG_THREADS = (QG_CONS_WARPS + 1) * 32;  // + one producer warp
+constexpr int QG_TILE_MT = 2 * QG_CONS_WARPS;         // m-tiles per CTA tile (512 rows)
+constexpr int WS_TILE_FLOATS = QG_TILE_MT * 16 * 16;   // split-K partials of one tile (16 columns)
+
+// GEMV input columns come in n-tiles of 4 (one m16n8k16 B operand holds the
+// f16 hi parts of 4 columns and their lo parts): 1 to 4 n-tiles.
+inline int gemv_ntiles(int B) { return (B + 3) / 4; }
 
 inline size_t qmat_chunk_bytes(int type) { return type == 8 ? 1088 : 576; }
-inline size_t qmat_bytes(int type, int K, int n_mt) { return qmat_chunk_bytes(type) * (size_t)(K / 64) * (size_t)n_mt; }
+inline size_t qmat_bytes(int type, int K, int n_mt) {
+  const size_t tiles = (size_t)(n_mt + QG_TILE_MT - 1) / QG_TILE_MT;
+  return qmat_chunk_bytes(type) * (size_t)(K / 64) * tiles * QG_TILE_MT;
+}
 
 // Scratch the GEMV needs (owned by the caller, reused across calls on one stream).
 struct GemvScratch {
-  uint4 *xf = nullptr;   // X fragments, >= (Kmax/32) * 2 ntiles * 2 * 32 uint4
+  uint4 *xf = nullptr;   // X fragments, >= (Kmax/32) * 4 ntiles * 32 uint4
   int *xexp = nullptr;   // [16] per-column exponents
-  float *ws = nullptr;   // split-K partials [G][2][16*16*16]
-  int *cnt = nullptr;    // per CTA-tile arrival counters (zeroed once)
-  int G = 0;             // persistent grid size (CTAs)
+  float *ws = nullptr;   // split-K partials [G][2][WS_TILE_FLOATS]
+  int *cnt = nullptr;    // per CTA-tile arrival counters (zero, self-resetting)
+  int *err = nullptr;    // set when a bounded wait gave up (0 = fine)
+  int G = 0;             // persistent grid size (CTAs), at most one per SM
   int kmax = 0;
   int max_tiles = 0;
 };
@@ -55,7 +66,8 @@ cudaError_t gemv_prep_x(const float *X, int xs, int B, int K, GemvScratch &s, cu
 // GEMV over prepared X.  epi selects the output: store, add into Y
 // (residual), or SiLU(gate)*up of an interleaved gate/up matrix.
 cudaError_t gemv_run(const QMat &m, int B, float *Y, int ys, int epi, GemvScratch &s, cudaStream_t st);
-// Kernel-count helper for bench bookkeeping.
-inline int gemv_launches() { return 2; }
+
+// Kernel attributes set once per process (shared-memory carveout).
+cudaError_t qgemv_configure();
 
 }  // namespace cw

@@ -72,12 +72,12 @@ __global__ void __launch_bounds__(PREP_THREADS) norm_prep_kernel(const float *__
 
 cudaError_t launch_norm_prep(const float *x, const float *w, int H, int B, GemvScratch &s, float *out,
                              cudaStream_t st) {
-  const int nt = (B + 7) / 8;
+  const int nt = gemv_ntiles(B);
   const size_t smem = (size_t)H * sizeof(float);
   static size_t done = 0;
   cudaError_t e = smem_optin(norm_prep_kernel, smem, done);
   if (e != cudaSuccess) return e;
-  norm_prep_kernel<<<nt * 8, PREP_THREADS, smem, st>>>(x, w, H, B, nt, s.xf, s.xexp, out);
+  norm_prep_kernel<<<nt * 4, PREP_THREADS, smem, st>>>(x, w, H, B, nt, s.xf, s.xexp, out);
   return cudaGetLastError();
 }
 
@@ -96,11 +96,11 @@ __global__ void __launch_bounds__(PREP_THREADS) row_prep_kernel(const float *__r
 }
 
 cudaError_t launch_row_prep(const float *x, int xs, int K, int B, GemvScratch &s, cudaStream_t st) {
-  const int nt = (B + 7) / 8;
+  const int nt = gemv_ntiles(B);
   static size_t done = 0;
   cudaError_t e = smem_optin(row_prep_kernel, (size_t)K * sizeof(float), done);
   if (e != cudaSuccess) return e;
-  row_prep_kernel<<<nt * 8, PREP_THREADS, (size_t)K * sizeof(float), st>>>(x, xs, K, B, nt, s.xf, s.xexp);
+  row_prep_kernel<<<nt * 4, PREP_THREADS, (size_t)K * sizeof(float), st>>>(x, xs, K, B, nt, s.xf, s.xexp);
   return cudaGetLastError();
 }
 
@@ -143,11 +143,11 @@ __global__ void __launch_bounds__(PREP_THREADS) gated_norm_prep_kernel(const flo
 
 cudaError_t launch_gated_norm_prep(const float *o, const float *z, int zs, const float *wn, int nvh, int B,
                                    GemvScratch &s, cudaStream_t st) {
-  const int nt = (B + 7) / 8;
+  const int nt = gemv_ntiles(B);
   static size_t done = 0;
   cudaError_t e = smem_optin(gated_norm_prep_kernel, (size_t)nvh * 128 * sizeof(float), done);
   if (e != cudaSuccess) return e;
-  gated_norm_prep_kernel<<<nt * 8, PREP_THREADS, (size_t)nvh * 128 * sizeof(float), st>>>(o, z, zs, wn, nvh, B, nt,
+  gated_norm_prep_kernel<<<nt * 4, PREP_THREADS, (size_t)nvh * 128 * sizeof(float), st>>>(o, z, zs, wn, nvh, B, nt,
                                                                                           s.xf, s.xexp);
   return cudaGetLastError();
 }
@@ -199,6 +199,18 @@ cudaError_t launch_argmax_walk(const float *lg, int n, int ldl, int B, int E, co
   argmax_kernel<<<dim3(64, B), 256, 0, st>>>(lg, n, ldl, best);
   walk_kernel<<<1, 32, 0, st>>>(best, blk, B, E, res);
   return cudaGetLastError();
+}
+
+// One-time kernel attributes (called at engine set-up).
+cudaError_t rowops_configure() {
+  cudaError_t e;
+  if ((e = carveout_max(embed_kernel)) != cudaSuccess) return e;
+  if ((e = carveout_max(norm_prep_kernel)) != cudaSuccess) return e;
+  if ((e = carveout_max(row_prep_kernel)) != cudaSuccess) return e;
+  if ((e = carveout_max(gated_norm_prep_kernel)) != cudaSuccess) return e;
+  if ((e = carveout_max(argmax_kernel)) != cudaSuccess) return e;
+  if ((e = carveout_max(walk_kernel)) != cudaSuccess) return e;
+  return cudaSuccess;
 }
 
 }  // namespace cw

@@ -28,4 +28,7 @@ cudaError_t launch_gated_norm_prep(const float *o, const float *z, int zs, const
 cudaError_t launch_argmax_walk(const float *lg, int n, int ldl, int B, int E, const Toks16 &blk,
                                unsigned long long *best, int *res, cudaStream_t st);
 
+// Kernel attributes set once per process (shared-memory carveout).
+cudaError_t rowops_configure();
+
 }  // namespace cw

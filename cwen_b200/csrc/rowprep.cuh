@@ -33,8 +33,8 @@ CW_DEV float block_sum(float v, float *red) {
   return warp_sum(v);
 }
 
-// Emit GEMV fragments for row b from v[0..K) in shared memory (b >= B rows
-// are zero padding of the n-tile).  Layout: see prep_x_kernel in qgemv.cu.
+// Emit GEMV fragments for column b from v[0..K) in shared memory (columns
+// b >= B are zero padding of the n-tile).  Layout: see prep_x_kernel in qgemv.cu.
 CW_DEV void emit_xfrag(const float *v, int K, int b, int nt, uint4 *__restrict__ xf, int *__restrict__ xexp,
                        float *red, bool live) {
   float mx = 0.f;
@@ -50,7 +50,7 @@ CW_DEV void emit_xfrag(const float *v, int K, int b, int nt, uint4 *__restrict__
   }
   if (threadIdx.x == 0) xexp[b] = e;
   const float scale = __int_as_float((127 + e) << 23);
-  const int g = b & 7, n = b >> 3, nb = K / 32;
+  const int g = b & 3, n = b >> 2, nb = K / 32;
   for (int item = threadIdx.x; item < nb * 4; item += blockDim.x) {
     const int kb = item >> 2, t = item & 3;
     const float *r = v + kb * 32;
@@ -64,9 +64,9 @@ CW_DEV void emit_xfrag(const float *v, int K, int b, int nt, uint4 *__restrict__
       hi[i] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
       lo[i] = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
     }
-    const size_t o = ((size_t)(kb * nt + n) * 2) * 32 + g * 4 + t;
-    xf[o] = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-    xf[o + 32] = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+    uint4 *o = xf + (size_t)(kb * nt + n) * 32;
+    o[g * 4 + t] = make_uint4(hi[0], hi[1], hi[2], hi[3]);        // B column g: hi part
+    o[(g + 4) * 4 + t] = make_uint4(lo[0], lo[1], lo[2], lo[3]);  // B column g + 4: lo part
   }
 }
 

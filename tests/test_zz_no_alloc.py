@@ -69,7 +69,7 @@ def test_static_scratch_rejects_oversize(eng, orc):
 
     import cwen_b200
     L = eng
-    # 4097 tiles of 256 rows: accepted by the engine, one tile beyond the static scratch
+    # 1,048,832 rows: accepted by the engine, beyond the static scratch's 1,048,576
     K, M = 64, 4097 * 256
     W = gen_q(orc, 23, "na_big", 2, K, M)
     wid = C.c_int(-1)
