@@ -25,6 +25,8 @@ __global__ void __launch_bounds__(HD) attn_prep_kernel(const float *__restrict__
                                                        const float2 *__restrict__ rope, int pos0,
                                                        float *__restrict__ qbuf, float *__restrict__ Kc,
                                                        float *__restrict__ Vc) {
+  pdl_trigger();
+  pdl_wait();
   const int y = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
   const int pos = pos0 + b;
   const float *row = proj + (size_t)b * ps;
@@ -61,6 +63,8 @@ __global__ void __launch_bounds__(HD) attn_prep_kernel(const float *__restrict__
 __global__ void __launch_bounds__(256) attn_chunk_kernel(const float *__restrict__ qbuf, const float *__restrict__ Kc,
                                                          const float *__restrict__ Vc, int nh, int nkv, int pos0,
                                                          int B, int t0, int nch_max, float *__restrict__ part) {
+  pdl_trigger();
+  pdl_wait();
   extern __shared__ float sm[];
   float *Ks = sm;                       // [ACH][KPAD]
   float *Vs = Ks + ACH * KPAD;          // [ACH][HD]
@@ -148,6 +152,8 @@ __global__ void __launch_bounds__(PREP_THREADS) attn_combine_kernel(const float 
                                                                     int pos0, int B, int t0, int nch_max, int nt,
                                                                     uint4 *__restrict__ xf, int *__restrict__ xexp,
                                                                     float *__restrict__ yout) {
+  pdl_trigger();
+  pdl_wait();
   extern __shared__ float v[];
   __shared__ float red[32];
   const int b = blockIdx.x;
@@ -177,8 +183,8 @@ __global__ void __launch_bounds__(PREP_THREADS) attn_combine_kernel(const float 
 }
 
 cudaError_t launch_attention(const AttnArgs &a, GemvScratch &s, cudaStream_t st) {
-  attn_prep_kernel<<<dim3(a.nh + 2 * a.nkv, a.B), HD, 0, st>>>(a.proj, a.ps, a.nh, a.nkv, a.qn, a.kn, a.rope, a.pos0,
-                                                               a.qbuf, a.Kc, a.Vc);
+  CW_TRY(launch_pdl(attn_prep_kernel, dim3(a.nh + 2 * a.nkv, a.B), HD, 0, st, a.proj, a.ps, a.nh, a.nkv, a.qn, a.kn, a.rope, a.pos0,
+                                                               a.qbuf, a.Kc, a.Vc));
   const int last = a.pos0 + a.B - 1;
   const int nch = last / ACH + 1;
   if (nch > a.nch_max) return cudaErrorInvalidValue;
@@ -189,11 +195,11 @@ cudaError_t launch_attention(const AttnArgs &a, GemvScratch &s, cudaStream_t st)
     if (e != cudaSuccess) return e;
     configured = true;
   }
-  attn_chunk_kernel<<<dim3(a.nkv, nch), 256, smem, st>>>(a.qbuf, a.Kc, a.Vc, a.nh, a.nkv, a.pos0, a.B, a.t0,
-                                                         a.nch_max, a.part);
+  CW_TRY(launch_pdl(attn_chunk_kernel, dim3(a.nkv, nch), 256, smem, st, a.qbuf, a.Kc, a.Vc, a.nh, a.nkv, a.pos0, a.B, a.t0,
+                                                         a.nch_max, a.part));
   const int nt = gemv_ntiles(a.B);
-  attn_combine_kernel<<<nt * 4, PREP_THREADS, (size_t)a.nh * HD * sizeof(float), st>>>(
-      a.part, a.proj, a.ps, a.nh, a.pos0, a.B, a.t0, a.nch_max, nt, s.xf, s.xexp, a.yout);
+  CW_TRY(launch_pdl(attn_combine_kernel, nt * 4, PREP_THREADS, (size_t)a.nh * HD * sizeof(float), st, 
+      a.part, a.proj, a.ps, a.nh, a.pos0, a.B, a.t0, a.nch_max, nt, s.xf, s.xexp, a.yout));
   return cudaGetLastError();
 }
 

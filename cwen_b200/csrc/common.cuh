@@ -4,9 +4,44 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 #define CW_DEV __device__ __forceinline__
 
 namespace cw {
+
+// Programmatic dependent launch (PDL).  Every decode-step kernel is launched
+// with programmatic stream serialization: it may start while the previous
+// kernel of the stream still runs.  Each kernel therefore calls pdl_wait()
+// before it touches any memory an earlier kernel writes or reads (the wait
+// returns once the previous grid has completed and its writes are visible;
+// that grid itself waited on its predecessor, so the chain is ordered), and
+// calls pdl_trigger() early so that its successor's launch overlaps its run.
+CW_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+CW_DEV void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args &&...args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+// Return the error of a launch from a launcher that returns cudaError_t.
+#define CW_TRY(expr)                  \
+  do {                                \
+    cudaError_t _e = (expr);          \
+    if (_e != cudaSuccess) return _e; \
+  } while (0)
 
 // Prefer the largest shared-memory carveout for a kernel.  With every kernel
 // of the decode step on the same carveout, an SM never reconfigures its

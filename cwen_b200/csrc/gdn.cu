@@ -28,6 +28,8 @@ __global__ void __launch_bounds__(128) gdn_conv_kernel(const float *__restrict__
                                                        float *__restrict__ cstate_out, float *__restrict__ craw,
                                                        const float *__restrict__ A, const float *__restrict__ dt,
                                                        float *__restrict__ gin) {
+  pdl_trigger();
+  pdl_wait();
   const int QKV = (2 * nkh + nvh) * 128;
   const int GS = QKV + 2 * nvh;
   const int grp = blockIdx.x;
@@ -81,6 +83,8 @@ constexpr int GDN_T = 256;
 __global__ void __launch_bounds__(GDN_T) gdn_recur_kernel(const float *__restrict__ Sin, float *__restrict__ Sout,
                                                           const float *__restrict__ gin, int B, int nkh, int nvh,
                                                           float *__restrict__ out, float *__restrict__ delta) {
+  pdl_trigger();
+  pdl_wait();
   const int hv = blockIdx.x >> 1, half = blockIdx.x & 1;
   const int hk = hv % nkh;
   const int col = threadIdx.x & 63, q4 = threadIdx.x >> 6;
@@ -141,6 +145,8 @@ __global__ void __launch_bounds__(GDN_T) gdn_recur_kernel(const float *__restric
 // place; conv state <- last three raw inputs. One CTA per (layer, head, half)
 // for S, plus conv CTAs. ----
 __global__ void __launch_bounds__(GDN_T) gdn_replay_kernel(GdnLayerPtrs *__restrict__ lp, int k, int nkh, int nvh) {
+  pdl_trigger();
+  pdl_wait();
   const int layer = blockIdx.y;
   const GdnLayerPtrs P = lp[layer];
   const int QKV = (2 * nkh + nvh) * 128;
@@ -183,16 +189,16 @@ __global__ void __launch_bounds__(GDN_T) gdn_replay_kernel(GdnLayerPtrs *__restr
 
 cudaError_t launch_gdn_layer(const GdnLayerArgs &a, cudaStream_t st) {
   const int QKV = (2 * a.nkh + a.nvh) * 128;
-  gdn_conv_kernel<<<QKV / 128 + 1, 128, 0, st>>>(a.proj, a.ps, a.B, a.nkh, a.nvh, a.a_off, a.b_off, a.convw,
-                                                  a.cstate_in, a.cstate_out, a.craw, a.A, a.dt, a.gin);
-  gdn_recur_kernel<<<a.nvh * 2, GDN_T, 0, st>>>(a.S_in, a.S_out, a.gin, a.B, a.nkh, a.nvh, a.out, a.delta);
+  CW_TRY(launch_pdl(gdn_conv_kernel, QKV / 128 + 1, 128, 0, st, a.proj, a.ps, a.B, a.nkh, a.nvh, a.a_off, a.b_off, a.convw,
+                                                  a.cstate_in, a.cstate_out, a.craw, a.A, a.dt, a.gin));
+  CW_TRY(launch_pdl(gdn_recur_kernel, a.nvh * 2, GDN_T, 0, st, a.S_in, a.S_out, a.gin, a.B, a.nkh, a.nvh, a.out, a.delta));
   return cudaGetLastError();
 }
 
 cudaError_t launch_gdn_replay(GdnLayerPtrs *dev_layers, int n_layers, int k, int nkh, int nvh, cudaStream_t st) {
   const int QKV = (2 * nkh + nvh) * 128;
   dim3 grid(nvh * 2 + (QKV + GDN_T - 1) / GDN_T, n_layers);
-  gdn_replay_kernel<<<grid, GDN_T, 0, st>>>(dev_layers, k, nkh, nvh);
+  CW_TRY(launch_pdl(gdn_replay_kernel, grid, GDN_T, 0, st, dev_layers, k, nkh, nvh));
   return cudaGetLastError();
 }
 

@@ -172,6 +172,8 @@ cudaError_t qmat_repack(const QMat &dst, const uint8_t *src, int M, int mt_off, 
 // of B column g; one uint4 per (32-block, n-tile, lane).
 __global__ void prep_x_kernel(const float *__restrict__ X, int xs, int B, int K, int nt, uint4 *__restrict__ xf,
                               int *__restrict__ xexp) {
+  pdl_trigger();
+  pdl_wait();
   extern __shared__ __align__(16) float row[];
   __shared__ float red[32];
   const int b = blockIdx.x;
@@ -192,7 +194,7 @@ cudaError_t gemv_prep_x(const float *X, int xs, int B, int K, GemvScratch &s, cu
     if (e != cudaSuccess) return e;
     configured = smem;
   }
-  prep_x_kernel<<<nt * 4, PREP_THREADS, smem, st>>>(X, xs, B, K, nt, s.xf, s.xexp);
+  CW_TRY(launch_pdl(prep_x_kernel, nt * 4, PREP_THREADS, smem, st, X, xs, B, K, nt, s.xf, s.xexp));
   return cudaGetLastError();
 }
 
@@ -292,6 +294,7 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemv_kernel(GemvArgs a) {
   const long long u_begin = (long long)c * a.units / a.G, u_end = (long long)(c + 1) * a.units / a.G;
   if (u_begin >= u_end) return;  // whole CTA, before any barrier
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  pdl_trigger();
   if (threadIdx.x == 0) {
     for (int i = 0; i < S; i++) {
       mbar_init(&full[i], 1);
@@ -309,24 +312,34 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemv_kernel(GemvArgs a) {
     // (this thread shares its issue slots with four busy consumer warps).
     if (lane == 0) {
       const int n = (int)(u_end - u_begin);
-      const uint8_t *wsrc = a.w + (size_t)u_begin * Lay::WB;
+      const uint8_t *wbase = a.w + (size_t)u_begin * Lay::WB;
       const uint8_t *xbase = reinterpret_cast<const uint8_t *>(a.xf);
+      // The weights are not written by any kernel of the decode step: fetch
+      // the first stages before waiting for the previous kernel (PDL), so the
+      // ring fills while that kernel finishes.  X is its output: after.
+      const int pre = n < S ? n : S;
+      for (int i = 0; i < pre; i++) {
+        mbar_expect_tx(&full[i], Lay::STAGE);
+        bulk_g2s(smem + i * Lay::STAGE, wbase + (size_t)i * Lay::WB, Lay::WB, &full[i]);
+      }
+      pdl_wait();
       int k = (int)(u_begin % a.kp);
       int st = 0;
       uint32_t ph = 0;
       int issued = 0;
       bool ok = true;
       for (; issued < n; issued++) {
-        if (!mbar_wait(&empty[st], ph ^ 1, abort_p)) {
-          ok = false;
-          break;
-        }
-        if (*abort_p) break;  // consumers gave up: issue nothing more
         uint8_t *dst = smem + st * Lay::STAGE;
-        mbar_expect_tx(&full[st], Lay::STAGE);
-        bulk_g2s(dst, wsrc, Lay::WB, &full[st]);
+        if (issued >= pre) {
+          if (!mbar_wait(&empty[st], ph ^ 1, abort_p)) {
+            ok = false;
+            break;
+          }
+          if (*abort_p) break;  // consumers gave up: issue nothing more
+          mbar_expect_tx(&full[st], Lay::STAGE);
+          bulk_g2s(dst, wbase + (size_t)issued * Lay::WB, Lay::WB, &full[st]);
+        }
         bulk_g2s(dst + Lay::WB, xbase + (size_t)k * Lay::XB, Lay::XB, &full[st]);
-        wsrc += Lay::WB;
         if (++k == a.kp) k = 0;
         if (++st == S) {
           st = 0;
@@ -338,7 +351,8 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemv_kernel(GemvArgs a) {
         *abort_p = 1;
       }
       // never leave bulk copies in flight: wait (bounded) for the last stages issued
-      for (int i = issued > S ? issued - S : 0; i < issued; i++) {
+      const int hi = issued > pre ? issued : pre;
+      for (int i = hi > S ? hi - S : 0; i < hi; i++) {
         const uint64_t t0 = globaltimer_ns();
         while (!mbar_try_wait(&full[i % S], (uint32_t)((i / S) & 1)) && globaltimer_ns() - t0 < MBAR_TIMEOUT_NS) {
         }
@@ -348,6 +362,7 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemv_kernel(GemvArgs a) {
   }
 
   // ---------------- consumers ----------------
+  pdl_wait();  // before touching Y, the split-K partials or the tile counters
   const int g = lane >> 2, t = lane & 3;
   const float zero4[4] = {0.f, 0.f, 0.f, 0.f};
   bool ok = true;
@@ -511,8 +526,7 @@ static cudaError_t launch_t(const GemvArgs &a, cudaStream_t st) {
     if (e != cudaSuccess) return e;
     configured = true;
   }
-  qgemv_kernel<TYPE, NT><<<a.G, QG_THREADS, Lay::SMEM, st>>>(a);
-  return cudaGetLastError();
+  return launch_pdl(qgemv_kernel<TYPE, NT>, a.G, QG_THREADS, Lay::SMEM, st, a);
 }
 
 cudaError_t gemv_run(const QMat &m, int B, float *Y, int ys, int epi, GemvScratch &s, cudaStream_t st) {

@@ -18,6 +18,8 @@ static cudaError_t smem_optin(F *fn, size_t bytes, size_t &done) {
 // x[b][k] = d * (q - 8) of row toks[b] of token_embd (GGUF Q4_0 layout).
 __global__ void embed_kernel(const uint8_t *__restrict__ emb, int H, int V, const Toks16 toks, int B,
                              float *__restrict__ x, int *__restrict__ err) {
+  pdl_trigger();
+  pdl_wait();
   const int b = blockIdx.y;
   const int tok = toks.t[b];
   if (tok < 0 || tok >= V) {
@@ -38,7 +40,7 @@ __global__ void embed_kernel(const uint8_t *__restrict__ emb, int H, int V, cons
 
 cudaError_t launch_embed(const uint8_t *emb, int H, int V, const Toks16 &toks, int B, float *x, int *err,
                          cudaStream_t st) {
-  embed_kernel<<<dim3(4, B), 256, 0, st>>>(emb, H, V, toks, B, x, err);
+  CW_TRY(launch_pdl(embed_kernel, dim3(4, B), 256, 0, st, emb, H, V, toks, B, x, err));
   return cudaGetLastError();
 }
 
@@ -47,6 +49,8 @@ cudaError_t launch_embed(const uint8_t *emb, int H, int V, const Toks16 &toks, i
 __global__ void __launch_bounds__(PREP_THREADS) norm_prep_kernel(const float *__restrict__ x, const float *__restrict__ w,
                                                                  int H, int B, int nt, uint4 *__restrict__ xf,
                                                                  int *__restrict__ xexp, float *__restrict__ out) {
+  pdl_trigger();
+  pdl_wait();
   extern __shared__ float v[];
   __shared__ float red[32];
   const int b = blockIdx.x;
@@ -77,7 +81,7 @@ cudaError_t launch_norm_prep(const float *x, const float *w, int H, int B, GemvS
   static size_t done = 0;
   cudaError_t e = smem_optin(norm_prep_kernel, smem, done);
   if (e != cudaSuccess) return e;
-  norm_prep_kernel<<<nt * 4, PREP_THREADS, smem, st>>>(x, w, H, B, nt, s.xf, s.xexp, out);
+  CW_TRY(launch_pdl(norm_prep_kernel, nt * 4, PREP_THREADS, smem, st, x, w, H, B, nt, s.xf, s.xexp, out));
   return cudaGetLastError();
 }
 
@@ -85,6 +89,8 @@ cudaError_t launch_norm_prep(const float *x, const float *w, int H, int B, GemvS
 __global__ void __launch_bounds__(PREP_THREADS) row_prep_kernel(const float *__restrict__ x, int xs, int K, int B,
                                                                 int nt, uint4 *__restrict__ xf,
                                                                 int *__restrict__ xexp) {
+  pdl_trigger();
+  pdl_wait();
   extern __shared__ float v[];
   __shared__ float red[32];
   const int b = blockIdx.x;
@@ -100,7 +106,7 @@ cudaError_t launch_row_prep(const float *x, int xs, int K, int B, GemvScratch &s
   static size_t done = 0;
   cudaError_t e = smem_optin(row_prep_kernel, (size_t)K * sizeof(float), done);
   if (e != cudaSuccess) return e;
-  row_prep_kernel<<<nt * 4, PREP_THREADS, (size_t)K * sizeof(float), st>>>(x, xs, K, B, nt, s.xf, s.xexp);
+  CW_TRY(launch_pdl(row_prep_kernel, nt * 4, PREP_THREADS, (size_t)K * sizeof(float), st, x, xs, K, B, nt, s.xf, s.xexp));
   return cudaGetLastError();
 }
 
@@ -112,6 +118,8 @@ __global__ void __launch_bounds__(PREP_THREADS) gated_norm_prep_kernel(const flo
                                                                        const float *__restrict__ wn, int nvh, int B,
                                                                        int nt, uint4 *__restrict__ xf,
                                                                        int *__restrict__ xexp) {
+  pdl_trigger();
+  pdl_wait();
   extern __shared__ float v[];
   __shared__ float red[32];
   const int b = blockIdx.x;
@@ -147,8 +155,8 @@ cudaError_t launch_gated_norm_prep(const float *o, const float *z, int zs, const
   static size_t done = 0;
   cudaError_t e = smem_optin(gated_norm_prep_kernel, (size_t)nvh * 128 * sizeof(float), done);
   if (e != cudaSuccess) return e;
-  gated_norm_prep_kernel<<<nt * 4, PREP_THREADS, (size_t)nvh * 128 * sizeof(float), st>>>(o, z, zs, wn, nvh, B, nt,
-                                                                                          s.xf, s.xexp);
+  CW_TRY(launch_pdl(gated_norm_prep_kernel, nt * 4, PREP_THREADS, (size_t)nvh * 128 * sizeof(float), st, o, z, zs, wn, nvh, B, nt,
+                                                                                          s.xf, s.xexp));
   return cudaGetLastError();
 }
 
@@ -163,6 +171,8 @@ CW_DEV unsigned long long argmax_key(float v, int i) {
 }
 
 __global__ void argmax_kernel(const float *__restrict__ lg, int n, int ldl, unsigned long long *__restrict__ best) {
+  pdl_trigger();
+  pdl_wait();
   const int b = blockIdx.y;
   unsigned long long k = 0;
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
@@ -182,6 +192,8 @@ __global__ void argmax_kernel(const float *__restrict__ lg, int n, int ldl, unsi
 // res = [k, ustar, argmax(row 0..B-1)].
 __global__ void walk_kernel(const unsigned long long *__restrict__ best, const Toks16 blk, int B, int E,
                             int *__restrict__ res) {
+  pdl_trigger();
+  pdl_wait();
   if (threadIdx.x != 0 || blockIdx.x != 0) return;
   int am[16];
   for (int b = 0; b < B; b++) am[b] = (int)(~(uint32_t)(best[b] & 0xffffffffu));
@@ -196,8 +208,8 @@ cudaError_t launch_argmax_walk(const float *lg, int n, int ldl, int B, int E, co
                                unsigned long long *best, int *res, cudaStream_t st) {
   cudaError_t e = cudaMemsetAsync(best, 0, (size_t)B * sizeof(unsigned long long), st);
   if (e != cudaSuccess) return e;
-  argmax_kernel<<<dim3(64, B), 256, 0, st>>>(lg, n, ldl, best);
-  walk_kernel<<<1, 32, 0, st>>>(best, blk, B, E, res);
+  CW_TRY(launch_pdl(argmax_kernel, dim3(64, B), 256, 0, st, lg, n, ldl, best));
+  CW_TRY(launch_pdl(walk_kernel, 1, 32, 0, st, best, blk, B, E, res));
   return cudaGetLastError();
 }
 
