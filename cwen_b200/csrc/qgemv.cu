@@ -279,7 +279,8 @@ struct QgLayout {
 };
 
 // Persistent stream-K GEMV: warps 0..15 consume (warp w owns m-tiles 2w, 2w+1
-// of the current 512-row tile), warp 16 lane 0 produces.
+// of the current 512-row tile); lane 0 of warp 16 streams the weights and
+// lane 0 of warp 17 the X fragments.
 template <int TYPE, int NT>
 __global__ void __launch_bounds__(QG_THREADS, 1) qgemv_kernel(GemvArgs a) {
   using Lay = QgLayout<TYPE, NT>;
@@ -288,7 +289,7 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemv_kernel(GemvArgs a) {
   uint64_t *full = reinterpret_cast<uint64_t *>(smem + Lay::BAR_OFF);
   uint64_t *empty = full + S;
   volatile int *abort_p = reinterpret_cast<volatile int *>(empty + S);
-  int *last_p = const_cast<int *>(abort_p) + 1;
+  int *last_p = const_cast<int *>(abort_p) + 1;  // [2]
 
   const int c = blockIdx.x;
   const long long u_begin = (long long)c * a.units / a.G, u_end = (long long)(c + 1) * a.units / a.G;
@@ -297,7 +298,7 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemv_kernel(GemvArgs a) {
   pdl_trigger();
   if (threadIdx.x == 0) {
     for (int i = 0; i < S; i++) {
-      mbar_init(&full[i], 1);
+      mbar_init(&full[i], 2);  // the weight and the X producer
       mbar_init(&empty[i], QG_CONS_WARPS);
     }
     *abort_p = 0;
@@ -305,42 +306,43 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemv_kernel(GemvArgs a) {
   }
   __syncthreads();
 
-  if (warp == QG_CONS_WARPS) {
-    // ---------------- producer ----------------
+  if (warp >= QG_CONS_WARPS) {
+    // ---------------- producers ----------------
+    // Two producer threads in two warps, one for the weights and one for X:
+    // a bulk copy occupies its issuing thread for ~0.3 us whatever its size,
+    // so one thread issuing both copies of a stage would cap the stream.
     // Consecutive units are consecutive (tile, k-pair) blocks of the repacked
-    // weights, so the source pointer just advances; no divisions in the loop
-    // (this thread shares its issue slots with four busy consumer warps).
+    // weights, so the weight source just advances; no divisions in the loops.
     if (lane == 0) {
+      const bool wprod = warp == QG_CONS_WARPS;
       const int n = (int)(u_end - u_begin);
-      const uint8_t *wbase = a.w + (size_t)u_begin * Lay::WB;
+      const uint8_t *wsrc = a.w + (size_t)u_begin * Lay::WB;
       const uint8_t *xbase = reinterpret_cast<const uint8_t *>(a.xf);
-      // The weights are not written by any kernel of the decode step: fetch
-      // the first stages before waiting for the previous kernel (PDL), so the
-      // ring fills while that kernel finishes.  X is its output: after.
-      const int pre = n < S ? n : S;
-      for (int i = 0; i < pre; i++) {
-        mbar_expect_tx(&full[i], Lay::STAGE);
-        bulk_g2s(smem + i * Lay::STAGE, wbase + (size_t)i * Lay::WB, Lay::WB, &full[i]);
-      }
-      pdl_wait();
+      // Weights are not written by any kernel of the decode step: the weight
+      // producer never waits for the previous kernel (PDL), so the ring fills
+      // while that kernel finishes.  X is that kernel's output.
+      if (!wprod) pdl_wait();
       int k = (int)(u_begin % a.kp);
       int st = 0;
       uint32_t ph = 0;
       int issued = 0;
       bool ok = true;
       for (; issued < n; issued++) {
-        uint8_t *dst = smem + st * Lay::STAGE;
-        if (issued >= pre) {
-          if (!mbar_wait(&empty[st], ph ^ 1, abort_p)) {
-            ok = false;
-            break;
-          }
-          if (*abort_p) break;  // consumers gave up: issue nothing more
-          mbar_expect_tx(&full[st], Lay::STAGE);
-          bulk_g2s(dst, wbase + (size_t)issued * Lay::WB, Lay::WB, &full[st]);
+        if (!mbar_wait(&empty[st], ph ^ 1, abort_p)) {
+          ok = false;
+          break;
         }
-        bulk_g2s(dst + Lay::WB, xbase + (size_t)k * Lay::XB, Lay::XB, &full[st]);
-        if (++k == a.kp) k = 0;
+        if (*abort_p) break;  // consumers gave up: issue nothing more
+        uint8_t *dst = smem + st * Lay::STAGE;
+        if (wprod) {
+          mbar_expect_tx(&full[st], Lay::WB);
+          bulk_g2s(dst, wsrc, Lay::WB, &full[st]);
+          wsrc += Lay::WB;
+        } else {
+          mbar_expect_tx(&full[st], Lay::XB);
+          bulk_g2s(dst + Lay::WB, xbase + (size_t)k * Lay::XB, Lay::XB, &full[st]);
+          if (++k == a.kp) k = 0;
+        }
         if (++st == S) {
           st = 0;
           ph ^= 1;
@@ -350,15 +352,15 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemv_kernel(GemvArgs a) {
         atomicExch(a.err, 1);
         *abort_p = 1;
       }
-      // never leave bulk copies in flight: wait (bounded) for the last stages issued
-      const int hi = issued > pre ? issued : pre;
-      for (int i = hi > S ? hi - S : 0; i < hi; i++) {
-        const uint64_t t0 = globaltimer_ns();
+      // never leave bulk copies in flight: wait (bounded, one deadline) for
+      // the last stages issued
+      const uint64_t t0 = globaltimer_ns();
+      for (int i = issued > S ? issued - S : 0; i < issued; i++) {
         while (!mbar_try_wait(&full[i % S], (uint32_t)((i / S) & 1)) && globaltimer_ns() - t0 < MBAR_TIMEOUT_NS) {
         }
       }
     }
-    return;  // the producer takes part in no later barrier
+    return;  // the producers take part in no later barrier
   }
 
   // ---------------- consumers ----------------
@@ -370,6 +372,8 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemv_kernel(GemvArgs a) {
   uint32_t ph = 0;   // its phase parity
   long long u = u_begin;
   bool first_seg = true;
+  int ptile[2];  // split tiles of this CTA (its first and last segments), uniform across the CTA
+  int np = 0;
   while (u < u_end) {
     const int tile = (int)(u / a.kp);
     const int ka = (int)(u % a.kp);
@@ -452,7 +456,8 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemv_kernel(GemvArgs a) {
     if (full_tile) {
       if (ok && has0) gemv_epilogue<NT>(a, mt0, has1, acc, g, t);
     } else {
-      // Partial tile: park this segment's sums, last CTA to arrive reduces.
+      // Partial tile: park this segment's sums; the arrival count and the
+      // reduction wait until this CTA's last segment, so the stream never stalls.
       const int slot = first_seg ? 0 : 1;
       float *mine = a.ws + ((size_t)c * 2 + slot) * WS_TILE_FLOATS;
       if (has0 && t < 2) {
@@ -466,51 +471,105 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemv_kernel(GemvArgs a) {
               *reinterpret_cast<float2 *>(p) = make_float2(acc[mt][n][2 * h], acc[mt][n][2 * h + 1]);
             }
       }
-      __threadfence();
-      named_bar(1, QG_CONS_WARPS * 32);
-      const long long tu0 = (long long)tile * a.kp, tu1 = tu0 + a.kp - 1;
-      const int c_first = (int)(((tu0 + 1) * a.G - 1) / a.units);
-      const int c_last = (int)(((tu1 + 1) * a.G - 1) / a.units);
-      if (threadIdx.x == 0) {
-        const int old = ok ? atomicAdd(a.cnt + tile, 1) : -1;
-        *last_p = (old == c_last - c_first);
-      }
-      named_bar(1, QG_CONS_WARPS * 32);
-      if (*last_p) {
-        __threadfence();
-        if (has0) {
-          float sum[2][NT][4];
-#pragma unroll
-          for (int mt = 0; mt < 2; mt++)
-#pragma unroll
-            for (int n = 0; n < NT; n++)
-#pragma unroll
-              for (int i = 0; i < 4; i++) sum[mt][n][i] = 0.f;
-          if (t < 2)
-          for (int cc = c_first; cc <= c_last; cc++) {
-            const long long cu0 = (long long)cc * a.units / a.G;
-            const int sl = cu0 >= tu0 ? 0 : 1;
-            const float *src = a.ws + ((size_t)cc * 2 + sl) * WS_TILE_FLOATS;
-#pragma unroll
-            for (int mt = 0; mt < 2; mt++)
-#pragma unroll
-              for (int n = 0; n < NT; n++)
-#pragma unroll
-                for (int h = 0; h < 2; h++) {
-                  const float *p = src + ((warp * 2 + mt) * 16 + g + 8 * h) * 16 + n * 4 + 2 * t;
-                  const float2 v = __ldcg(reinterpret_cast<const float2 *>(p));
-                  sum[mt][n][2 * h] += v.x;
-                  sum[mt][n][2 * h + 1] += v.y;
-                }
-          }
-          gemv_epilogue<NT>(a, mt0, has1, sum, g, t);
-        }
-        if (threadIdx.x == 0) a.cnt[tile] = 0;
-      }
-      named_bar(1, QG_CONS_WARPS * 32);
+      ptile[np++] = tile;
     }
     u += nk;
     first_seg = false;
+  }
+
+  // ---- split tiles: every contributor reduces a share of the rows ----
+  // All contributors of a split tile are resident (one CTA per SM, G <= SMs,
+  // and PDL successors start only after every CTA of this grid started), and
+  // each first counts itself in for all its split tiles and only then waits,
+  // so the waits below end; they are bounded all the same.  The counter of a
+  // tile goes 0 -> n (partials parked) -> 2n (shares reduced) -> 0.
+  if (np == 0) return;
+  __threadfence();
+  named_bar(1, QG_CONS_WARPS * 32);
+  if (threadIdx.x == 0)
+    for (int j = 0; j < np; j++) atomicAdd(a.cnt + ptile[j], 1);
+  for (int j = 0; j < np; j++) {
+    const int tile = ptile[j];
+    const long long tu0 = (long long)tile * a.kp, tu1 = tu0 + a.kp - 1;
+    const int c_first = (int)(((tu0 + 1) * a.G - 1) / a.units);
+    const int c_last = (int)(((tu1 + 1) * a.G - 1) / a.units);
+    const int ncon = c_last - c_first + 1, r = c - c_first;
+    if (threadIdx.x == 0) {
+      const uint64_t t0 = globaltimer_ns();
+      while (ok && *(volatile int *)(a.cnt + tile) < ncon) {
+        if (globaltimer_ns() - t0 > MBAR_TIMEOUT_NS) {
+          atomicExch(a.err, 3);
+          ok = false;
+        }
+      }
+      last_p[0] = ok;
+    }
+    named_bar(1, QG_CONS_WARPS * 32);
+    const bool go = last_p[0] != 0;
+    __threadfence();
+    // warp w's two m-tiles are reduced by contributor w % ncon: lane l sums
+    // row l & 15 of m-tile l >> 4, four columns per n-tile (one float4 per
+    // contributor and n-tile), over all contributors in CTA order.
+    const int mt0 = tile * QG_TILE_MT + warp * 2;
+    const int mt = lane >> 4, row = lane & 15;
+    if (go && warp % ncon == r && mt0 + mt < a.n_mt) {
+      float4 sum[NT];
+#pragma unroll
+      for (int n = 0; n < NT; n++) sum[n] = make_float4(0.f, 0.f, 0.f, 0.f);
+      const size_t off = (size_t)((warp * 2 + mt) * 16 + row) * 16;
+      constexpr int CH = NT == 1 ? 8 : (NT == 2 ? 4 : 2);  // independent loads in flight per lane
+      for (int c0 = c_first; c0 <= c_last; c0 += CH) {
+        float4 v[CH][NT];
+#pragma unroll
+        for (int q = 0; q < CH; q++) {
+          const int cc = c0 + q;
+          if (cc > c_last) break;
+          const long long cu0 = (long long)cc * a.units / a.G;
+          const float *src = a.ws + ((size_t)cc * 2 + (cu0 >= tu0 ? 0 : 1)) * WS_TILE_FLOATS + off;
+#pragma unroll
+          for (int n = 0; n < NT; n++) v[q][n] = __ldcg(reinterpret_cast<const float4 *>(src + 4 * n));
+        }
+#pragma unroll
+        for (int q = 0; q < CH; q++) {
+          if (c0 + q > c_last) break;
+#pragma unroll
+          for (int n = 0; n < NT; n++) {
+            sum[n].x += v[q][n].x;
+            sum[n].y += v[q][n].y;
+            sum[n].z += v[q][n].z;
+            sum[n].w += v[q][n].w;
+          }
+        }
+      }
+#pragma unroll
+      for (int n = 0; n < NT; n++) {
+        const float e4[4] = {sum[n].x, sum[n].y, sum[n].z, sum[n].w};
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+          const int col = n * 4 + j;
+          if (col >= a.B) continue;
+          const float sc = __int_as_float((127 - __ldg(a.xexp + col)) << 23);
+          if (a.epi == EPI_SWIGLU) {
+            const float up = __shfl_down_sync(0x0000ffffu, e4[j], 16, 32);
+            if (mt == 0) {
+              const int orow = (mt0 >> 1) * 16 + row;
+              if (orow * 2 < a.M) a.y[(size_t)col * a.ys + orow] = silu_f(e4[j] * sc) * (up * sc);
+            }
+          } else {
+            const int grow = (mt0 + mt) * 16 + row;
+            if (grow < a.M) {
+              float *p = a.y + (size_t)col * a.ys + grow;
+              if (a.epi == EPI_ADD) *p += e4[j] * sc;
+              else *p = e4[j] * sc;
+            }
+          }
+        }
+      }
+    }
+    named_bar(1, QG_CONS_WARPS * 32);  // every read of the partials of this tile is done
+    if (threadIdx.x == 0 && go) {
+      if (atomicAdd(a.cnt + tile, 1) == 2 * ncon - 1) a.cnt[tile] = 0;
+    }
   }
 }
 
@@ -550,8 +609,15 @@ cudaError_t gemv_run(const QMat &m, int B, float *Y, int ys, int epi, GemvScratc
   if (n_tiles > s.max_tiles) return cudaErrorInvalidValue;
   a.units = (long long)n_tiles * a.kp;
   // Grid: a function of the shape only (never of B), >= 4 k-pairs per CTA.
+  // When the tiles are fewer than the CTAs, take a multiple of the tile count:
+  // every tile is then split evenly between the same number of CTAs and
+  // every CTA holds exactly one segment (one split tile at most), instead of
+  // the arbitrary cuts of stream-K that give some CTAs two split tiles and
+  // two reductions.
   long long g = (a.units + 3) / 4;
-  a.G = (int)(g < s.G ? g : s.G);
+  if (g > s.G) g = s.G;
+  if (n_tiles <= g) g = g / n_tiles * n_tiles;
+  a.G = (int)g;
   switch (gemv_ntiles(B) * 16 + m.type) {
     case 16 + 8: return launch_t<8, 1>(a, st);
     case 32 + 8: return launch_t<8, 2>(a, st);

@@ -29,7 +29,7 @@ enum { EPI_STORE = 0, EPI_ADD = 1, EPI_SWIGLU = 2 };
 
 constexpr int QG_MAXB = 16;
 constexpr int QG_CONS_WARPS = 16;                    // consumer warps, two m-tiles each
-constexpr int QG_THREADS = (QG_CONS_WARPS + 1) * 32;  // + one producer warp
+constexpr int QG_THREADS = (QG_CONS_WARPS + 2) * 32;  // + two producer warps
 constexpr int QG_TILE_MT = 2 * QG_CONS_WARPS;         // m-tiles per CTA tile (512 rows)
 constexpr int WS_TILE_FLOATS = QG_TILE_MT * 16 * 16;   // split-K partials of one tile (16 columns)
 
