@@ -58,6 +58,9 @@ _SIGS = {
     "cwen_cuda_hidden": (C.c_int, [C.c_int, C.c_void_p]),
     "cwen_cuda_dump_layers": (C.c_int, [C.c_int]),
     "cwen_cuda_dump_read": (C.c_int, [C.c_int, C.c_int, C.c_void_p]),
+    "cwen_cuda_mtp_ready": (C.c_int, []),
+    "cwen_cuda_mtp_commit": (C.c_int, [C.c_int, C.c_int, C.c_int]),
+    "cwen_cuda_mtp_draft": (C.c_int, [C.c_int, C.c_void_p, C.c_int]),
     "cwen_cuda_gdn_state": (C.c_int, [C.c_int, C.c_void_p, C.c_void_p]),
     "cwen_cuda_ctx": (C.c_int, []),
     "cwen_cuda_stream": (C.c_void_p, []),

@@ -253,7 +253,7 @@ static int alloc_state() {
     if ((rc = A(M.mtp_hprev, (size_t)H)) || (rc = A(M.mtp_x, (size_t)bm * H)) || (rc = A(M.mtp_cat, (size_t)2 * H)) ||
         (rc = A(M.mtp_out, (size_t)bm * H)))
       return rc;
-    CW_CHECK(cudaMalloc(&M.mtp_draft, (size_t)(bm + 1) * sizeof(int)));
+    CW_CHECK(cudaMalloc(&M.mtp_draft, (size_t)3 * (bm + 1) * sizeof(int)));  // walk results per draft step
     CW_CHECK(cudaMallocHost(&M.h_draft, (size_t)(bm + 1) * sizeof(int)));
   }
   return CWEN_OK;
@@ -302,6 +302,41 @@ static int run_layer_block(int l, int B, int pos0, cudaStream_t st) {
   if (M.dump_on)
     CW_CHECK(cudaMemcpyAsync(M.dump + (size_t)l * E.bmax * H, M.x, (size_t)B * H * sizeof(float),
                              cudaMemcpyDeviceToDevice, st));
+  return CWEN_OK;
+}
+
+// ---- MTP (nextn) drafter ----
+// One nextn step (mtp_step, run.c:3098-3131) at slot pos: the input token is
+// `token` or, when dtok is set, the device int it points to; hin is the
+// predecessor hidden [H] (device).  Writes K/V at pos of the nextn cache, the
+// shared-head-normed hidden to hout, and leaves hout as the pending GEMV input
+// (for the shared lm_head of a draft step).
+static int mtp_step_dev(int pos, int token, const int *dtok, const float *hin, float *hout, cudaStream_t st) {
+  Model &M = g_model;
+  Engine &E = engine();
+  const cwen_dims &d = M.d;
+  MtpW &w = M.mtp;
+  const int H = d.n_embd, I = d.n_ff;
+  Toks16 tk;
+  memset(&tk, 0, sizeof tk);
+  tk.t[0] = token;
+  CW_CHECK(launch_embed(M.tok_embd, H, d.n_vocab, tk, 1, M.mtp_cat, M.err, st, dtok));
+  CW_CHECK(launch_cat_norm_prep(M.mtp_cat, hin, w.enorm, w.hnorm, H, E.gs, st));
+  CW_CHECK(timed_gemv(w.eh_proj, 1, M.mtp_x, H, EPI_STORE, st));
+  CW_CHECK(launch_norm_prep(M.mtp_x, w.attn_norm, H, 1, E.gs, nullptr, st));
+  CW_CHECK(timed_gemv(w.in_proj, 1, M.proj, M.PS, EPI_STORE, st));
+  AttnArgs a;
+  a.proj = M.proj; a.ps = M.PS; a.nh = d.n_head; a.nkv = d.n_head_kv; a.B = 1;
+  a.qn = w.q_norm; a.kn = w.k_norm; a.rope = M.rope; a.pos0 = pos; a.t0 = 1;  // the nextn stream starts at slot 1
+  a.qbuf = M.qbuf; a.Kc = M.mtp_K; a.Vc = M.mtp_V; a.part = M.attn_part; a.nch_max = M.nch_max; a.yout = nullptr;
+  CW_CHECK(launch_attention(a, E.gs, st));
+  CW_CHECK(timed_gemv(w.out_proj, 1, M.mtp_x, H, EPI_ADD, st));
+  CW_CHECK(launch_norm_prep(M.mtp_x, w.post_norm, H, 1, E.gs, nullptr, st));
+  CW_CHECK(timed_gemv(w.gate_up, 1, M.h, I, EPI_SWIGLU, st));
+  CW_CHECK(launch_row_prep(M.h, I, I, 1, E.gs, st));
+  CW_CHECK(timed_gemv(w.down, 1, M.mtp_x, H, EPI_ADD, st));
+  CW_CHECK(launch_norm_prep(M.mtp_x, w.shared_head_norm, H, 1, E.gs, hout, st));
+  E.prof.launches += 12;
   return CWEN_OK;
 }
 
@@ -621,6 +656,81 @@ int cwen_cuda_dump_read(int layer, int row, float *host) {
   CW_CHECK(cudaMemcpy(host, M.dump + ((size_t)layer * engine().bmax + row) * M.d.n_embd,
                       (size_t)M.d.n_embd * sizeof(float), cudaMemcpyDeviceToHost));
   return CWEN_OK;
+}
+
+int cwen_cuda_mtp_ready(void) { return engine().live && g_model.finalized && g_model.mtp_on ? 1 : 0; }
+
+int cwen_cuda_mtp_commit(int pos, int token, int row) {
+  Model &M = g_model;
+  Engine &E = engine();
+  int rc = check_ready("cwen_cuda_mtp_commit");
+  if (rc) return rc;
+  if (!M.mtp_on) {
+    set_error("cwen_cuda_mtp_commit: the model has no MTP block (blk.%d.nextn.*)", M.d.n_layer);
+    return CWEN_ESTATE;
+  }
+  if (row < 0 || row >= E.bmax || pos < 0 || pos >= E.ctx) {
+    set_error("cwen_cuda_mtp_commit: need 0 <= row < %d and 0 <= pos < ctx %d", E.bmax, E.ctx);
+    return CWEN_EINVAL;
+  }
+  if (token < 0 || token >= M.d.n_vocab) {
+    set_error("token id %d out of range [0,%d)", token, M.d.n_vocab);
+    return CWEN_ERANGE;
+  }
+  const int H = M.d.n_embd;
+  cudaStream_t st = E.stream;
+  // a step at pos when pos-1 is parked; its output is not needed (scratch half of mtp_out)
+  if (pos >= 1 && M.mtp_hpos == pos - 1) {
+    rc = mtp_step_dev(pos, token, nullptr, M.mtp_hprev, M.mtp_out, st);
+    if (rc) return rc;
+  }
+  CW_CHECK(launch_norm_prep(M.x + (size_t)row * H, M.output_norm, H, 1, E.gs, M.mtp_hprev, st));
+  E.prof.launches++;
+  M.mtp_hpos = pos;
+  return CWEN_OK;
+}
+
+int cwen_cuda_mtp_draft(int pend, int *out, int max_d) {
+  Model &M = g_model;
+  Engine &E = engine();
+  int rc = check_ready("cwen_cuda_mtp_draft");
+  if (rc) return rc;
+  const int pos_n = M.n_past - 1;
+  if (!M.mtp_on || M.mtp_hpos != pos_n || max_d <= 0 || M.pending) return 0;
+  if (!out || pend < 0 || pend >= M.d.n_vocab) {
+    set_error("cwen_cuda_mtp_draft: need out and a pending token in [0,%d)", M.d.n_vocab);
+    return CWEN_EINVAL;
+  }
+  int n = max_d < E.bmax ? max_d : E.bmax;
+  if (pos_n + n >= E.ctx) n = E.ctx - 1 - pos_n;
+  if (n <= 0) return 0;
+  const int H = M.d.n_embd, V = M.d.n_vocab;
+  cudaStream_t st = E.stream;
+  const float *hin = M.mtp_hprev;
+  Toks16 none;
+  memset(&none, 0, sizeof none);
+  for (int t = 0; t < n; t++) {
+    float *hout = M.mtp_out + (size_t)(t & 1) * H;
+    rc = mtp_step_dev(pos_n + 1 + t, pend, t ? M.mtp_draft + 3 * (t - 1) + 1 : nullptr, hin, hout, st);
+    if (rc) return rc;
+    CW_CHECK(timed_gemv(M.lm_head, 1, M.logits, V, EPI_STORE, st));
+    CW_CHECK(launch_argmax_walk(M.logits, V, V, 1, 0, none, M.best, M.mtp_draft + 3 * t, st));
+    E.prof.launches += 2;
+    hin = hout;
+  }
+  int res[3 * 16];
+  CW_CHECK(cudaMemcpyAsync(res, M.mtp_draft, (size_t)3 * n * sizeof(int), cudaMemcpyDeviceToHost, st));
+  CW_CHECK(cudaStreamSynchronize(st));
+  int err = 0;
+  CW_CHECK(cudaMemcpy(&err, M.err, sizeof(int), cudaMemcpyDeviceToHost));
+  if (err) {
+    set_error("device reported a token id out of range");
+    return CWEN_ERANGE;
+  }
+  rc = gemv_status();
+  if (rc) return rc;
+  for (int t = 0; t < n; t++) out[t] = res[3 * t + 1];
+  return n;
 }
 
 int cwen_cuda_gdn_state(int layer, float *S_host, float *conv_host) {

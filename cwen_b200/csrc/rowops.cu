@@ -16,12 +16,14 @@ static cudaError_t smem_optin(F *fn, size_t bytes, size_t &done) {
 
 // ---- embedding (embed_token_to, Q4_0 branch run.c:1873-1881) ----
 // x[b][k] = d * (q - 8) of row toks[b] of token_embd (GGUF Q4_0 layout).
-__global__ void embed_kernel(const uint8_t *__restrict__ emb, int H, int V, const Toks16 toks, int B,
-                             float *__restrict__ x, int *__restrict__ err) {
+// The token ids come from `toks` or, when dtok is set, from device memory
+// (a drafted token produced by an earlier kernel).
+__global__ void embed_kernel(const uint8_t *__restrict__ emb, int H, int V, const Toks16 toks, const int *dtok,
+                             int B, float *__restrict__ x, int *__restrict__ err) {
   pdl_trigger();
   pdl_wait();
   const int b = blockIdx.y;
-  const int tok = toks.t[b];
+  const int tok = dtok ? dtok[b] : toks.t[b];
   if (tok < 0 || tok >= V) {
     if (threadIdx.x == 0 && blockIdx.x == 0) atomicExch(err, 1);
     return;
@@ -39,8 +41,49 @@ __global__ void embed_kernel(const uint8_t *__restrict__ emb, int H, int V, cons
 }
 
 cudaError_t launch_embed(const uint8_t *emb, int H, int V, const Toks16 &toks, int B, float *x, int *err,
-                         cudaStream_t st) {
-  CW_TRY(launch_pdl(embed_kernel, dim3(4, B), 256, 0, st, emb, H, V, toks, B, x, err));
+                         cudaStream_t st, const int *dtok) {
+  CW_TRY(launch_pdl(embed_kernel, dim3(4, B), 256, 0, st, emb, H, V, toks, dtok, B, x, err));
+  return cudaGetLastError();
+}
+
+// ---- MTP input: [rmsnorm(e, enorm) | rmsnorm(h, hnorm)] -> GEMV input (run.c:3100-3102) ----
+// One row (column 0 of an n-tile; the other three columns are not read by
+// anything: a GEMV column depends only on its own X column).
+__global__ void __launch_bounds__(PREP_THREADS) cat_norm_prep_kernel(const float *__restrict__ e,
+                                                                     const float *__restrict__ h,
+                                                                     const float *__restrict__ we,
+                                                                     const float *__restrict__ wh, int H,
+                                                                     uint4 *__restrict__ xf, int *__restrict__ xexp) {
+  pdl_trigger();
+  pdl_wait();
+  extern __shared__ __align__(16) float v[];
+  __shared__ float red[32];
+  float se = 0.f, sh = 0.f;
+  for (int k = threadIdx.x; k < H; k += blockDim.x) {
+    const float a = e[k], c = h[k];
+    v[k] = a;
+    v[H + k] = c;
+    se = fmaf(a, a, se);
+    sh = fmaf(c, c, sh);
+  }
+  se = block_sum(se, red);
+  sh = block_sum(sh, red);
+  const float re = 1.f / sqrtf(se / (float)H + 1e-6f), rh = 1.f / sqrtf(sh / (float)H + 1e-6f);
+  for (int k = threadIdx.x; k < H; k += blockDim.x) {
+    v[k] = we[k] * v[k] * re;
+    v[H + k] = wh[k] * v[H + k] * rh;
+  }
+  __syncthreads();
+  emit_xfrag(v, 2 * H, 0, 1, xf, xexp, red, true);
+}
+
+cudaError_t launch_cat_norm_prep(const float *e, const float *h, const float *we, const float *wh, int H,
+                                 GemvScratch &s, cudaStream_t st) {
+  const size_t smem = (size_t)2 * H * sizeof(float);
+  static size_t done = 0;
+  cudaError_t err = smem_optin(cat_norm_prep_kernel, smem, done);
+  if (err != cudaSuccess) return err;
+  CW_TRY(launch_pdl(cat_norm_prep_kernel, 1, PREP_THREADS, smem, st, e, h, we, wh, H, s.xf, s.xexp));
   return cudaGetLastError();
 }
 
@@ -222,6 +265,7 @@ cudaError_t rowops_configure() {
   if ((e = carveout_max(gated_norm_prep_kernel)) != cudaSuccess) return e;
   if ((e = carveout_max(argmax_kernel)) != cudaSuccess) return e;
   if ((e = carveout_max(walk_kernel)) != cudaSuccess) return e;
+  if ((e = carveout_max(cat_norm_prep_kernel)) != cudaSuccess) return e;
   return cudaSuccess;
 }
 

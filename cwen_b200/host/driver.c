@@ -227,7 +227,19 @@ static void ng_free(ngmap *m) {
 
 /* Prefill: slot 0 alone, then batched chunks; the last chunk's last row gets
    logits.  Returns the argmax after the prompt in *first. */
-static int prefill(const int32_t *tokens, int n_tok, int *first) {
+/* Fold committed slots pos0..pos0+n-1 (tokens t[0..n), rows 0..n-1 of the
+   last forward) into the MTP stream (mtp_commit per committed position,
+   run.c:4830-4849, 4948, 4987-4994). */
+static int mtp_fold(int use_mtp, int pos0, const int32_t *t, int n) {
+  if (!use_mtp) return 0;
+  for (int b = 0; b < n; b++) {
+    int rc = cwen_cuda_mtp_commit(pos0 + b, t[b], b);
+    if (rc) return rc;
+  }
+  return 0;
+}
+
+static int prefill(const int32_t *tokens, int n_tok, int *first, int use_mtp) {
   int rc = cwen_cuda_reset();
   if (rc) return rc;
   int i = 0;
@@ -241,6 +253,8 @@ static int prefill(const int32_t *tokens, int n_tok, int *first) {
       if (rc) return rc;
     }
     rc = cwen_cuda_commit(B - 1);
+    if (rc) return rc;
+    rc = mtp_fold(use_mtp, i, tokens + i, B);
     if (rc) return rc;
     i += B;
   }
@@ -257,7 +271,9 @@ int cwen_generate(const int32_t *tokens, int n_tok, int n_gen, int32_t *out, con
     cfg = &def;
   }
   if (n_tok < 1 || n_gen < 0 || !tokens || (!out && n_gen)) return CWEN_EINVAL;
-  int pend = 0, rc = prefill(tokens, n_tok, &pend);
+  /* the MTP head drafts only in speculative mode (run.c:5195) */
+  const int use_mtp = cfg->spec && cfg->use_mtp && cwen_cuda_mtp_ready();
+  int pend = 0, rc = prefill(tokens, n_tok, &pend, use_mtp);
   if (rc) return rc;
   const int ctx = cwen_cuda_ctx();
   int n = 0;
@@ -303,7 +319,10 @@ int cwen_generate(const int32_t *tokens, int n_tok, int n_gen, int32_t *out, con
     } else {
       const int room = ctx - 1 - n_past;
       int cap = E_cap < room ? E_cap : room;
-      if (cap > 0) {
+      if (cap > 0 && use_mtp) {
+        E = cwen_cuda_mtp_draft(hist[hn - 1], blk + 1, cap);
+        if (E < 0) { rc = E; goto fail; }
+      } else if (cap > 0) {
         if (use_map) {
           E = ng_draft_map(&ngm, hist, hn, blk + 1, cap);
           int esc = cwen_ngram_draft(hist, hn, scan, cfg->n_key, cap);
@@ -321,6 +340,8 @@ int cwen_generate(const int32_t *tokens, int n_tok, int n_gen, int32_t *out, con
     st.cycles++;
     if (E == 0) {
       rc = cwen_cuda_forward_serial(blk[0], 1, &ustar);
+      if (rc) goto fail;
+      rc = mtp_fold(use_mtp, n_past, blk, 1);
       if (rc) goto fail;
       st.plain_steps++;
     } else {
@@ -340,6 +361,10 @@ int cwen_generate(const int32_t *tokens, int n_tok, int n_gen, int32_t *out, con
         E_cap = k > cfg->min_draft ? k : cfg->min_draft;
       }
       rc = cwen_cuda_commit(k);
+      if (rc) goto fail;
+      /* rows 0..k became context; the verify rows are the rows a re-score
+         of pend + the kept drafts would give (batch invariance) */
+      rc = mtp_fold(use_mtp, n_past, blk, k + 1);
       if (rc) goto fail;
     }
     for (int i = 0; i < k; i++) hist[hn++] = blk[i + 1];

@@ -121,6 +121,21 @@ int cwen_cuda_commit(int k);
 /* One token at slot n_past, committed (forward_ex, run.c:2594); with
  * need_logits the argmax of its logits goes to *argmax_out. */
 int cwen_cuda_forward_serial(int token, int need_logits, int *argmax_out);
+/* ---- MTP (nextn) drafter, blk.<n_layer> of the GGUF ---- */
+/* 1 when the model carries the MTP block (all 15 nextn tensors bound). */
+int cwen_cuda_mtp_ready(void);
+/* Fold the token committed at slot pos into the nextn stream and park the
+ * normed hidden of row `row` of the last forward (its residual stream before
+ * output_norm) for slot pos+1.  Call once per committed slot, in order
+ * (mtp_commit, run.c:3147-3159). */
+int cwen_cuda_mtp_commit(int pos, int token, int row);
+/* Draft up to max_d tokens after the last committed slot from the pending
+ * token `pend`: a chain of nextn steps, each scored by the shared lm_head and
+ * argmax'ed on the device; one synchronization at the end.  Returns the
+ * number drafted (0 when the stream is not at the last committed slot), or a
+ * negative CWEN_E* code (mtp_draft, run.c:3166-3187). */
+int cwen_cuda_mtp_draft(int pend, int *out, int max_d);
+
 /* Copies of device rows for parity checks: logits row (n_vocab floats), the
  * residual stream after the last layer (n_embd), per-layer residual streams
  * (the CWEN_DUMP layerNN files, run.c:2601-2629) while dumps are on, and a

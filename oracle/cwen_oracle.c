@@ -234,9 +234,20 @@ typedef struct {
   int t_gate, t_up, t_down, t_qkv, t_gz, t_al, t_be, t_out, t_q, t_k, t_v, t_o;
 } or_layer;
 
+/* the nextn (MTP) block, blk.<n_layer> (run.c:3098-3131) */
+typedef struct {
+  const void *eh_proj, *enorm, *hnorm, *shn;
+  int t_eh, t_q, t_k, t_v, t_o, t_gate, t_up, t_down;
+  float *K, *V;                 /* own KV cache [ctx][n_head_kv * head_dim] */
+  float *hprev;                 /* NHprev: parked normed hidden */
+  int hpos;                     /* mtp_hpos */
+  float *emb, *cat, *resid, *ln, *qfull, *qh, *gq, *kh, *vh, *ao, *op, *ffg, *ffu, *oh, *lg;
+} or_mtp;
+
 struct or_model {
   cw_dims d;
   int ctx;
+  or_mtp mtp;
   void *blobs[2048];
   int nblobs;
   const void *tok_embd, *output, *output_norm;
@@ -257,11 +268,10 @@ or_model *or_model_synth(const cw_dims *d, uint64_t seed, int ctx, int threads) 
   or_model *m = (or_model *)calloc(1, sizeof *m);
   if (!m) return NULL;
   m->d = *d;
-  m->d.has_mtp = 0;
   m->ctx = ctx;
   const int H = d->n_embd, I = d->n_ff, V = d->n_vocab, QKV = cw_qkv_dim(d);
   const int Z = d->ssm_n_vh * d->ssm_d, QO = d->n_head * d->head_dim, KO = d->n_head_kv * d->head_dim;
-  m->L = (or_layer *)or_alloc(m, sizeof(or_layer) * (size_t)d->n_layer);
+  m->L = (or_layer *)or_alloc(m, sizeof(or_layer) * (size_t)(d->n_layer + 1));  /* + the MTP block */
   m->lin_idx = (int *)or_alloc(m, sizeof(int) * (size_t)d->n_layer);
   m->full_idx = (int *)or_alloc(m, sizeof(int) * (size_t)d->n_layer);
   int nlin = 0, nfull = 0;
@@ -294,6 +304,30 @@ or_model *or_model_synth(const cw_dims *d, uint64_t seed, int ctx, int threads) 
     B("attn_q.weight", wq); B("attn_k.weight", wk); B("attn_v.weight", wv); B("attn_output.weight", wo);
     B("attn_q_norm.weight", q_norm); B("attn_k_norm.weight", k_norm);
 #undef B
+    if (l == d->n_layer) {
+      or_mtp *n = &m->mtp;
+      if (!strcmp(suf, "nextn.eh_proj.weight")) { n->eh_proj = buf; n->t_eh = t.type; }
+      else if (!strcmp(suf, "nextn.enorm.weight")) n->enorm = buf;
+      else if (!strcmp(suf, "nextn.hnorm.weight")) n->hnorm = buf;
+      else if (!strcmp(suf, "nextn.shared_head_norm.weight")) n->shn = buf;
+      else if (!strcmp(suf, "attn_q.weight")) n->t_q = t.type;
+      else if (!strcmp(suf, "attn_k.weight")) n->t_k = t.type;
+      else if (!strcmp(suf, "attn_v.weight")) n->t_v = t.type;
+      else if (!strcmp(suf, "attn_output.weight")) n->t_o = t.type;
+      else if (!strcmp(suf, "ffn_gate.weight")) n->t_gate = t.type;
+      else if (!strcmp(suf, "ffn_up.weight")) n->t_up = t.type;
+      else if (!strcmp(suf, "ffn_down.weight")) n->t_down = t.type;
+    }
+  }
+  if (d->has_mtp) {
+    or_mtp *n = &m->mtp;
+    n->K = (float *)or_alloc(m, sizeof(float) * (size_t)ctx * KO);
+    n->V = (float *)or_alloc(m, sizeof(float) * (size_t)ctx * KO);
+#define A_(f, cnt) n->f = (float *)or_alloc(m, sizeof(float) * (size_t)(cnt))
+    A_(hprev, H); A_(emb, H); A_(cat, 2 * H); A_(resid, H); A_(ln, H); A_(qfull, 2 * QO); A_(qh, QO);
+    A_(gq, QO); A_(kh, KO); A_(vh, KO); A_(ao, QO); A_(op, H); A_(ffg, I); A_(ffu, I); A_(oh, H); A_(lg, V);
+#undef A_
+    n->hpos = -1;
   }
   m->S = (float *)or_alloc(m, sizeof(float) * (size_t)nlin * d->ssm_n_vh * d->ssm_d * d->ssm_d);
   m->conv = (float *)or_alloc(m, sizeof(float) * (size_t)nlin * QKV * 3);
@@ -319,6 +353,7 @@ void or_model_free(or_model *m) {
 
 void or_reset(or_model *m) {
   const cw_dims *d = &m->d;
+  m->mtp.hpos = -1;
   int nlin = 0;
   for (int l = 0; l < d->n_layer; l++) nlin += cw_is_linear(d, l);
   memset(m->S, 0, sizeof(float) * (size_t)nlin * d->ssm_n_vh * d->ssm_d * d->ssm_d);
@@ -408,6 +443,80 @@ const float *or_layer_out(const or_model *m, int l) { return m->layer_out + (siz
 const float *or_gdn_state(const or_model *m, int layer) {
   return m->S + (size_t)m->lin_idx[layer] * m->d.ssm_n_vh * m->d.ssm_d * m->d.ssm_d;
 }
+/* ---- MTP (nextn) drafter ---- */
+/* mtp_step (run.c:3098-3131): one nextn step at slot pos with input token and
+   predecessor hidden h_target; writes K/V at pos of the nextn cache and the
+   shared-head-normed hidden into out_h. */
+void or_mtp_step(or_model *m, int token, int pos, const float *h_target, float *out_h) {
+  const cw_dims *d = &m->d;
+  or_mtp *n = &m->mtp;
+  const or_layer *w = &m->L[d->n_layer];
+  const int H = d->n_embd, I = d->n_ff, HD = d->head_dim, NH = d->n_head, NKV = d->n_head_kv;
+  const int QO = NH * HD, KO = NKV * HD;
+  or_embed_q4_0(m->tok_embd, H, token, n->emb);
+  or_rmsnorm(n->cat, n->emb, (const float *)n->enorm, H);
+  or_rmsnorm(n->cat + H, h_target, (const float *)n->hnorm, H);
+  or_gemv(n->t_eh, n->eh_proj, 2 * H, H, n->cat, n->resid);
+  or_rmsnorm(n->ln, n->resid, (const float *)w->attn_norm, H);
+  or_gemv(n->t_q, w->wq, H, 2 * QO, n->ln, n->qfull);
+  for (int h = 0; h < NH; h++) {
+    memcpy(n->qh + (size_t)h * HD, n->qfull + (size_t)h * HD * 2, HD * sizeof(float));
+    memcpy(n->gq + (size_t)h * HD, n->qfull + (size_t)h * HD * 2 + HD, HD * sizeof(float));
+  }
+  or_gemv(n->t_k, w->wk, H, KO, n->ln, n->kh);
+  or_gemv(n->t_v, w->wv, H, KO, n->ln, n->vh);
+  for (int h = 0; h < NH; h++) or_rmsnorm(n->qh + (size_t)h * HD, n->qh + (size_t)h * HD, (const float *)w->q_norm, HD);
+  for (int h = 0; h < NKV; h++) or_rmsnorm(n->kh + (size_t)h * HD, n->kh + (size_t)h * HD, (const float *)w->k_norm, HD);
+  or_rope(n->qh, NH, HD, pos);
+  or_rope(n->kh, NKV, HD, pos);
+  memcpy(n->K + (size_t)pos * KO, n->kh, KO * sizeof(float));
+  memcpy(n->V + (size_t)pos * KO, n->vh, KO * sizeof(float));
+  or_attention(d, n->K, n->V, 1, pos, n->qh, n->gq, n->ao);   /* the nextn stream starts at slot 1 */
+  or_gemv(n->t_o, w->wo, QO, H, n->ao, n->op);
+  or_resadd(n->resid, n->op, H);
+  or_rmsnorm(n->ln, n->resid, (const float *)w->post_norm, H);
+  or_gemv(n->t_gate, w->ffn_gate, H, I, n->ln, n->ffg);
+  or_gemv(n->t_up, w->ffn_up, H, I, n->ln, n->ffu);
+  for (int i = 0; i < I; i++) n->ffg[i] = or_silu(n->ffg[i]) * n->ffu[i];
+  or_gemv(n->t_down, w->ffn_down, I, H, n->ffg, n->op);
+  or_resadd(n->resid, n->op, H);
+  or_rmsnorm(out_h, n->resid, (const float *)n->shn, H);
+}
+/* mtp_commit (run.c:3147-3159): fold the token scored at pos into the nextn
+   stream (a step at pos when the previous position was parked), then park
+   rmsnorm(x_pre, output_norm) for the next slot. */
+void or_mtp_commit(or_model *m, int pos, int token, const float *x_pre) {
+  or_mtp *n = &m->mtp;
+  if (!m->d.has_mtp) return;
+  if (pos >= 1 && n->hpos == pos - 1) or_mtp_step(m, token, pos, n->hprev, n->oh);
+  or_rmsnorm(n->hprev, x_pre, (const float *)m->output_norm, m->d.n_embd);
+  n->hpos = pos;
+}
+/* mtp_draft (run.c:3166-3187) after the last committed slot pos_n: chain of
+   nextn steps from the pending token, each scored by the shared lm_head. */
+int or_mtp_draft(or_model *m, int pos_n, int pend, int32_t *out, int max_d) {
+  or_mtp *n = &m->mtp;
+  const int H = m->d.n_embd, V = m->d.n_vocab;
+  if (!m->d.has_mtp || n->hpos != pos_n || max_d <= 0) return 0;
+  int cnt = max_d;
+  if (pos_n + cnt >= m->ctx) cnt = m->ctx - 1 - pos_n;
+  if (cnt <= 0) return 0;
+  float *hprev = (float *)malloc(sizeof(float) * (size_t)H);
+  memcpy(hprev, n->hprev, sizeof(float) * (size_t)H);
+  int tok = pend;
+  for (int t = 0; t < cnt; t++) {
+    or_mtp_step(m, tok, pos_n + 1 + t, hprev, n->oh);
+    or_gemv(CW_T_Q4_0, m->output, H, V, n->oh, n->lg);
+    out[t] = or_argmax(n->lg, V);
+    tok = out[t];
+    memcpy(hprev, n->oh, sizeof(float) * (size_t)H);
+  }
+  free(hprev);
+  return cnt;
+}
+const float *or_mtp_hprev(const or_model *m) { return m->mtp.hprev; }
+const float *or_mtp_logits(const or_model *m) { return m->mtp.lg; }
+
 /* Serial greedy decode (generate_tokens, run.c:5027-5045): token g is the
    argmax after the prompt and the g previous tokens. */
 int or_generate(or_model *m, const int32_t *tokens, int n_tok, int n_gen, int32_t *out) {

@@ -41,6 +41,13 @@ const float *or_hidden(const or_model *m);
 /* Residual stream after layer l of the last or_forward (per-layer dump). */
 const float *or_layer_out(const or_model *m, int l);
 const float *or_gdn_state(const or_model *m, int layer);
+/* MTP (nextn) drafter of a model with d.has_mtp (run.c:3098-3187). */
+void or_mtp_step(or_model *m, int token, int pos, const float *h_target, float *out_h);
+void or_mtp_commit(or_model *m, int pos, int token, const float *x_pre);
+int or_mtp_draft(or_model *m, int pos_n, int pend, int32_t *out, int max_d);
+const float *or_mtp_hprev(const or_model *m);
+/* logits of the last draft step */
+const float *or_mtp_logits(const or_model *m);
 /* Serial greedy decode: prefill tokens[0..n_tok), then n_gen argmax tokens. */
 int or_generate(or_model *m, const int32_t *tokens, int n_tok, int n_gen, int32_t *out);
 

@@ -1,0 +1,101 @@
+"""MTP (nextn) drafter on the device vs the CPU oracle, small seeded model
+with the MTP block (blk.<n_layer>, Q8_0 matrices), through the C ABI.
+
+- after a prompt folded into the nextn stream, the device drafts the same
+  tokens as the oracle's mtp_draft (run.c:3166-3187) and the last draft
+  step's logits agree to rel L2 <= 1e-4 (fp32 math, X split f16 hi+lo);
+- speculative generation with the MTP drafter emits exactly the serial
+  stream (drafts only decide what is verified, never what is emitted).
+"""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+from oracle_lib import CwDims, rel_l2, vp
+
+pytestmark = pytest.mark.gpu
+
+SEED = 5
+CTX = 256
+
+
+@pytest.fixture(scope="module")
+def mtp_model():
+    import cwen_b200
+    from cwen_b200 import build
+    build.build()
+    L = cwen_b200.lib()
+    cwen_b200.check(L.cwen_cuda_init(0, CTX, 16), "init")
+    d = cwen_b200.dims("small")
+    d.has_mtp = 1
+    cwen_b200.check(L.cwen_load_synth(SEED, C.byref(d), 0), "load_synth")
+    yield L, d
+    L.cwen_cuda_shutdown()
+
+
+def _oracle(orc):
+    orc.or_mtp_commit.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_void_p]
+    orc.or_mtp_draft.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_int]
+    orc.or_mtp_draft.restype = C.c_int
+    orc.or_mtp_logits.argtypes = [C.c_void_p]
+    orc.or_mtp_logits.restype = C.POINTER(C.c_float)
+    d = CwDims()
+    orc.cw_dims_tiny(C.byref(d))
+    d.has_mtp = 1
+    m = orc.or_model_synth(C.byref(d), SEED, CTX, 0)
+    assert m
+    return d, m
+
+
+def test_mtp_ready(mtp_model):
+    L, _ = mtp_model
+    assert L.cwen_cuda_mtp_ready() == 1
+
+
+def test_mtp_draft_matches_oracle(mtp_model, orc):
+    import cwen_b200
+    L, d = mtp_model
+    od, om = _oracle(orc)
+    try:
+        toks = np.random.default_rng(3).integers(0, d.n_vocab, size=10).astype(np.int32)
+        # engine: prefill as one verify block, fold every slot into the nextn stream
+        cwen_b200.check(L.cwen_cuda_reset())
+        cwen_b200.check(L.cwen_cuda_forward_block(vp(toks), len(toks), -1), "forward_block")
+        pend = C.c_int(-1)
+        cwen_b200.check(L.cwen_cuda_accept(None, C.byref(pend), None), "accept")
+        cwen_b200.check(L.cwen_cuda_commit(len(toks) - 1), "commit")
+        for p, t in enumerate(toks):
+            cwen_b200.check(L.cwen_cuda_mtp_commit(p, int(t), p), "mtp_commit")
+        # oracle: serial forward + mtp_commit per slot
+        orc.or_reset(om)
+        for p, t in enumerate(toks):
+            orc.or_forward(om, int(t), p, 1)
+            orc.or_mtp_commit(om, p, int(t), orc.or_hidden(om))
+        opend = int(np.argmax(np.ctypeslib.as_array(orc.or_logits(om), shape=(d.n_vocab,))))
+        assert pend.value == opend
+        for nd in (1, 4):
+            out = np.zeros(16, np.int32)
+            n = L.cwen_cuda_mtp_draft(pend.value, vp(out), nd)
+            assert n == nd, cwen_b200.lib().cwen_cuda_last_error()
+            oout = np.zeros(16, np.int32)
+            on = orc.or_mtp_draft(om, len(toks) - 1, opend, vp(oout), nd)
+            assert on == nd
+            assert list(out[:n]) == list(oout[:on])
+            lg = np.zeros(d.n_vocab, np.float32)
+            cwen_b200.check(L.cwen_cuda_logits(0, vp(lg)), "logits")
+            olg = np.ctypeslib.as_array(orc.or_mtp_logits(om), shape=(d.n_vocab,))
+            assert rel_l2(lg, olg) <= 1e-4, rel_l2(lg, olg)
+    finally:
+        orc.or_model_free(om)
+
+
+def test_mtp_spec_equals_serial(mtp_model):
+    import cwen_b200
+    L, d = mtp_model
+    prompt = np.random.default_rng(9).integers(0, d.n_vocab, size=24).astype(np.int32)
+    serial, _ = cwen_b200.generate(prompt, 48, cwen_b200.spec_cfg(spec=0))
+    for md in (3, 8):
+        spec, st = cwen_b200.generate(prompt, 48, cwen_b200.spec_cfg(spec=1, use_mtp=1, max_draft=md))
+        assert np.array_equal(serial, spec), md
+        assert st.drafted > 0
