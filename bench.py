@@ -47,6 +47,7 @@ sys.path.insert(0, str(ROOT / "tests"))
 DEC_SEED = 1
 PROMPT_LEN, N_GEN = 512, 256          # config 2
 SPEC_PROMPT, SPEC_GEN = 2048, 512     # config 3
+MTP_GEN = 128
 DEC_CTX = 4096
 GEMV_K, GEMV_M, GEMV_B = 5120, 17408, 8
 GEMV_BYTES = (GEMV_K // 32) * 18 * GEMV_M + GEMV_B * GEMV_K * 4 + GEMV_B * GEMV_M * 4  # 50,855,936
@@ -109,6 +110,11 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(self.rows)}
 
 
+def _backend() -> str:
+    # NCCL on the GPU box; gloo lets the multi-rank plumbing run on CPU (tests)
+    return os.environ.get("CWEN_DIST_BACKEND", "nccl")
+
+
 def dist_init(args):
     ws = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -118,17 +124,19 @@ def dist_init(args):
 
         import torch
         import torch.distributed as dist
-        torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+        if _backend() == "nccl":
+            torch.cuda.set_device(local)
+        dist.init_process_group(_backend(), timeout=datetime.timedelta(seconds=120))
     return ws, rank, local
 
 
 def barrier_max(ws, value: float) -> float:
+    """Max over ranks (every multi-GPU time is the slowest rank's)."""
     if ws == 1:
         return value
     import torch
     import torch.distributed as dist
-    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    t = torch.tensor([value], dtype=torch.float64, device="cuda" if _backend() == "nccl" else "cpu")
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
 
@@ -296,6 +304,7 @@ def run_decode_ours(args, ws, rank, local):
     L = cwen_b200.lib()
     cwen_b200.check(L.cwen_cuda_init(local, DEC_CTX, 16), "init")
     d = cwen_b200.dims("reference")
+    d.has_mtp = 1  # blk.64 nextn block (Q8_0), used only by the MTP-drafted run below
     t0 = time.perf_counter()
     cwen_b200.check(L.cwen_load_synth(DEC_SEED, C.byref(d), 0), "load_synth")
     load_s = time.perf_counter() - t0
@@ -353,7 +362,7 @@ def run_decode_ours(args, ws, rank, local):
     t0 = time.perf_counter()
     ref_stream, _ = cwen_b200.generate(mp, SPEC_GEN, serial)
     sn = time.perf_counter() - t0
-    spec_cfg = cwen_b200.spec_cfg(spec=1, max_draft=8)
+    spec_cfg = cwen_b200.spec_cfg(spec=1, use_mtp=0, max_draft=8)
     t0 = time.perf_counter()
     spec_stream, st = cwen_b200.generate(mp, SPEC_GEN, spec_cfg)
     pn = time.perf_counter() - t0
@@ -362,6 +371,22 @@ def run_decode_ours(args, ws, rank, local):
             "identical_to_serial": bool(np.array_equal(ref_stream, spec_stream)),
             "cycles": st.cycles, "drafted": st.drafted, "full_accept": st.full, "short": st.shortw,
             "avg_kept": round(st.kept / st.drafted, 3) if st.drafted else 0.0}
+    # MTP-drafted speculation, depth 8, on the config-2 prompt (a 512-slot
+    # context, not config 4's 32k prefill); stream checked against serial
+    mtp_cfg = cwen_b200.spec_cfg(spec=1, use_mtp=1, max_draft=8)
+    t0 = time.perf_counter()
+    cwen_b200.generate(prompt, 1, mtp_cfg)
+    m1 = time.perf_counter() - t0
+    t0 = time.perf_counter()
+    mtp_stream, mst = cwen_b200.generate(prompt, MTP_GEN, mtp_cfg)
+    mn = time.perf_counter() - t0
+    mtp = {"workload": f"MTP (blk.64 nextn, Q8_0) drafter, depth 8, config-2 prompt, {MTP_GEN} new",
+           "tok_s": round((MTP_GEN - 1) / (mn - m1), 2),
+           "identical_to_serial": bool(np.array_equal(out_ser[:MTP_GEN], mtp_stream)),
+           "cycles": mst.cycles, "drafted": mst.drafted, "full_accept": mst.full, "short": mst.shortw,
+           "avg_kept": round(mst.kept / mst.drafted, 3) if mst.drafted else 0.0,
+           "note": "random-init weights: the nextn head is not trained on the target, so few drafts are kept"}
+    spec["mtp_d8"] = mtp
     L.cwen_cuda_shutdown()
     return ms, kern, e2e_tps, clk, spec, load_s, prompt
 
@@ -445,7 +470,7 @@ def main_decode(args, ws, rank, local):
                          "gemv_share_of_step": round(kern["gemv_ms_per_token"] / ms, 3)},
             "e2e": {"value": round(e2e_tps * ws, 3), "unit": "tok/s", "h2d_bytes_per_step": 4,
                     "d2h_bytes_per_step": 12, "method": "cwen_generate (C host driver): (t(256)-t(1))/255"},
-            "spec_d8": spec, "model_load_s": round(load_s, 1)}
+            "spec_d8": spec, "mtp_d8": spec.pop("mtp_d8", None), "model_load_s": round(load_s, 1)}
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
         res = cpu_decode_baseline(prompt)
         if res:
