@@ -145,41 +145,58 @@ __global__ void __launch_bounds__(256) attn_chunk_kernel(const float *__restrict
   }
 }
 
-// Merge the chunks of each (row, head) in chunk order, apply the sigmoid gate
-// (run.c:2396-2406) and emit the wo GEMV input.
-__global__ void __launch_bounds__(PREP_THREADS) attn_combine_kernel(const float *__restrict__ part,
-                                                                    const float *__restrict__ proj, int ps, int nh,
-                                                                    int pos0, int B, int t0, int nch_max, int nt,
-                                                                    uint4 *__restrict__ xf, int *__restrict__ xexp,
-                                                                    float *__restrict__ yout) {
+// Merge the chunks of each (row, head), apply the sigmoid gate
+// (run.c:2396-2406) and emit the wo GEMV input.  One thread-block cluster per
+// row (blockIdx.y); each CTA owns whole heads: per head one warp turns the
+// chunk maxima into chunk weights w_c = exp(m_c - M) and l = sum l_c w_c, then
+// every element sums its chunks' weighted partials in chunk order.
+constexpr int COMB_THREADS = 256;
+__global__ void __launch_bounds__(COMB_THREADS) attn_combine_kernel(const float *__restrict__ part,
+                                                                   const float *__restrict__ proj, int ps, int nh,
+                                                                   int pos0, int t0, int nch_max, int nt,
+                                                                   uint4 *__restrict__ xf, int *__restrict__ xexp,
+                                                                   float *__restrict__ yout) {
   pdl_trigger();
   pdl_wait();
-  extern __shared__ float v[];
-  __shared__ float red[32];
-  const int b = blockIdx.x;
-  const bool live = b < B;
-  const int K = nh * HD;
-  if (live) {
-    const int p = pos0 + b;
-    const int cf = t0 / ACH, cl = p / ACH;
-    for (int i = threadIdx.x; i < K; i += blockDim.x) {
-      const int h = i / HD, d = i % HD;
-      const float *ph = part + ((size_t)b * nh + h) * nch_max * PART;
-      float M = -INFINITY;
-      for (int c = cf; c <= cl; c++) M = fmaxf(M, ph[(size_t)c * PART]);
-      float l = 0.f, a = 0.f;
-      for (int c = cf; c <= cl; c++) {
-        const float w = expf(ph[(size_t)c * PART] - M);
-        l = fmaf(ph[(size_t)c * PART + 1], w, l);
-        a = fmaf(ph[(size_t)c * PART + 4 + d], w, a);
-      }
-      const float o = (a / l) * sigmoid_dev(proj[(size_t)b * ps + h * 2 * HD + HD + d]);
-      v[i] = o;
-      if (yout) yout[(size_t)b * K + i] = o;
+  extern __shared__ __align__(16) float sm[];
+  __shared__ float red[32], slot, linv[32];
+  const int b = blockIdx.y, r = blockIdx.x, hper = nh / gridDim.x, h0 = r * hper;
+  float *v = sm;                    // [hper][HD]
+  float *wts = sm + hper * HD;      // [hper][nch_max]
+  const int p = pos0 + b, cf = t0 / ACH, cl = p / ACH, nc = cl - cf + 1;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  for (int hl = warp; hl < hper; hl += nw) {
+    const float *ph = part + ((size_t)b * nh + h0 + hl) * nch_max * PART;
+    float M = -INFINITY;
+    for (int c = cf + lane; c <= cl; c += 32) M = fmaxf(M, ph[(size_t)c * PART]);
+    M = warp_max(M);
+    float l = 0.f;
+    for (int c = cf + lane; c <= cl; c += 32) {
+      const float w = expf(ph[(size_t)c * PART] - M);
+      wts[hl * nch_max + (c - cf)] = w;
+      l = fmaf(ph[(size_t)c * PART + 1], w, l);
     }
+    l = warp_sum(l);
+    if (lane == 0) linv[hl] = l;
   }
   __syncthreads();
-  emit_xfrag(v, K, b, nt, xf, xexp, red, live);
+  float mx = 0.f;
+  for (int i = threadIdx.x; i < hper * HD; i += blockDim.x) {
+    const int hl = i / HD, d = i % HD, h = h0 + hl;
+    const float *ph = part + ((size_t)b * nh + h) * nch_max * PART + 4 + d;
+    const float *wh = wts + hl * nch_max;
+    float a = 0.f;
+#pragma unroll 4
+    for (int c = 0; c < nc; c++) a = fmaf(ph[(size_t)(cf + c) * PART], wh[c], a);
+    const float o = (a / linv[hl]) * sigmoid_dev(proj[(size_t)b * ps + h * 2 * HD + HD + d]);
+    v[i] = o;
+    mx = fmaxf(mx, fabsf(o));
+    if (yout) yout[(size_t)b * nh * HD + h * HD + d] = o;
+  }
+  mx = cluster_reduce<true>(block_max(mx, red), &slot);
+  const int e = xfrag_exponent(mx);
+  if (r == 0 && threadIdx.x == 0) xexp[b] = e;
+  emit_xfrag_blocks(v, h0 * (HD / 32), hper * (HD / 32), b, nt, xf, __int_as_float((127 + e) << 23), true);
 }
 
 cudaError_t launch_attention(const AttnArgs &a, GemvScratch &s, cudaStream_t st) {
@@ -197,9 +214,17 @@ cudaError_t launch_attention(const AttnArgs &a, GemvScratch &s, cudaStream_t st)
   }
   CW_TRY(launch_pdl(attn_chunk_kernel, dim3(a.nkv, nch), 256, smem, st, a.qbuf, a.Kc, a.Vc, a.nh, a.nkv, a.pos0, a.B, a.t0,
                                                          a.nch_max, a.part));
-  const int nt = gemv_ntiles(a.B);
-  CW_TRY(launch_pdl(attn_combine_kernel, nt * 4, PREP_THREADS, (size_t)a.nh * HD * sizeof(float), st, 
-      a.part, a.proj, a.ps, a.nh, a.pos0, a.B, a.t0, a.nch_max, nt, s.xf, s.xexp, a.yout));
+  const int cl = cluster_split(a.nh);
+  if (a.nh / cl > 32) return cudaErrorInvalidValue;  // per-CTA heads must fit linv[32]
+  const size_t csmem = (size_t)(a.nh / cl) * (HD + a.nch_max) * sizeof(float);
+  static size_t cdone = 48 * 1024;
+  if (csmem > cdone) {
+    cudaError_t e = cudaFuncSetAttribute(attn_combine_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)csmem);
+    if (e != cudaSuccess) return e;
+    cdone = csmem;
+  }
+  CW_TRY(launch_pdl_cluster(attn_combine_kernel, dim3(cl, a.B), COMB_THREADS, csmem, st, cl, a.part, a.proj, a.ps,
+                            a.nh, a.pos0, a.t0, a.nch_max, gemv_ntiles(a.B), s.xf, s.xexp, a.yout));
   return cudaGetLastError();
 }
 

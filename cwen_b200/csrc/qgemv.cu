@@ -39,6 +39,7 @@
 // the CTA finishes without touching memory further.
 #include "common.cuh"
 #include "qgemv.cuh"
+#include "rowops.cuh"
 #include "rowprep.cuh"
 #include "sm100.cuh"
 
@@ -161,41 +162,18 @@ cudaError_t qmat_repack(const QMat &dst, const uint8_t *src, int M, int mt_off, 
   return cudaGetLastError();
 }
 
-// ---- X preparation ----
-// One CTA per column b < nt*4: exponent e with max|x|*2^e in [2^14, 2^15),
-// then per 32-block the f16 hi and lo parts of the scaled column.  Columns
+// ---- X preparation (launch_row_prep: one thread-block cluster per column) ----
+// Per column b: exponent e with max|x|*2^e in [2^14, 2^15), then per 32-block
+// the f16 hi and lo parts of the scaled column.  Columns
 // come in n-tiles of 4; in the m16n8k16 B operand of n-tile b/4, B column
 // b%4 holds the hi parts and B column b%4 + 4 the lo parts, so one MMA
 // multiplies a weight tile with both.  Lane (g, t) of a B operand holds, in
 // the K order the A fragments use,
 //   (x[4t], x[4t+2]) (x[4t+1], x[4t+3]) (x[4t+16], x[4t+18]) (x[4t+17], x[4t+19])
 // of B column g; one uint4 per (32-block, n-tile, lane).
-__global__ void prep_x_kernel(const float *__restrict__ X, int xs, int B, int K, int nt, uint4 *__restrict__ xf,
-                              int *__restrict__ xexp) {
-  pdl_trigger();
-  pdl_wait();
-  extern __shared__ __align__(16) float row[];
-  __shared__ float red[32];
-  const int b = blockIdx.x;
-  const bool live = b < B;
-  if (live)
-    for (int k = threadIdx.x; k < K; k += blockDim.x) row[k] = X[(size_t)b * xs + k];
-  __syncthreads();
-  emit_xfrag(row, K, b, nt, xf, xexp, red, live);
-}
-
 cudaError_t gemv_prep_x(const float *X, int xs, int B, int K, GemvScratch &s, cudaStream_t st) {
   if (B < 1 || B > QG_MAXB || K % 64 || K > s.kmax) return cudaErrorInvalidValue;
-  const int nt = gemv_ntiles(B);
-  const size_t smem = (size_t)K * sizeof(float);
-  static size_t configured = 48 * 1024;
-  if (smem > configured) {
-    cudaError_t e = cudaFuncSetAttribute(prep_x_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
-    configured = smem;
-  }
-  CW_TRY(launch_pdl(prep_x_kernel, nt * 4, PREP_THREADS, smem, st, X, xs, B, K, nt, s.xf, s.xexp));
-  return cudaGetLastError();
+  return launch_row_prep(X, xs, K, B, s, st);
 }
 
 // ---- the GEMV ----
@@ -635,7 +613,6 @@ cudaError_t qgemv_configure() {
   cudaError_t e;
   if ((e = carveout_max(repack_kernel<2>)) != cudaSuccess) return e;
   if ((e = carveout_max(repack_kernel<8>)) != cudaSuccess) return e;
-  if ((e = carveout_max(prep_x_kernel)) != cudaSuccess) return e;
   if ((e = carveout_max(qgemv_kernel<2, 1>)) != cudaSuccess) return e;
   if ((e = carveout_max(qgemv_kernel<2, 2>)) != cudaSuccess) return e;
   if ((e = carveout_max(qgemv_kernel<2, 3>)) != cudaSuccess) return e;

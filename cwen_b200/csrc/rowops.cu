@@ -87,119 +87,128 @@ cudaError_t launch_cat_norm_prep(const float *e, const float *h, const float *we
   return cudaGetLastError();
 }
 
+// Row kernels below run one thread-block cluster of CL CTAs per row (blockIdx.y
+// = row b < B, cluster rank = blockIdx.x): each CTA owns a contiguous slice of
+// the row; row-wide sums and maxima go through distributed shared memory in
+// cluster-rank order (deterministic, independent of B), and each CTA emits the
+// GEMV fragments of its own slice.  Only live rows run: a GEMV column depends
+// only on its own X column, so stale padding columns are never read into a
+// live result.
+constexpr int ROW_THREADS = 256;
+
 // ---- RMSNorm (run.c:346) fused with GEMV input preparation ----
-// One CTA per column b < nt*8; optional copy of the normed row to `out`.
-__global__ void __launch_bounds__(PREP_THREADS) norm_prep_kernel(const float *__restrict__ x, const float *__restrict__ w,
-                                                                 int H, int B, int nt, uint4 *__restrict__ xf,
-                                                                 int *__restrict__ xexp, float *__restrict__ out) {
+// Optional copy of the normed row to `out`.
+__global__ void __launch_bounds__(ROW_THREADS) norm_prep_kernel(const float *__restrict__ x, const float *__restrict__ w,
+                                                                int H, int nt, uint4 *__restrict__ xf,
+                                                                int *__restrict__ xexp, float *__restrict__ out) {
   pdl_trigger();
   pdl_wait();
-  extern __shared__ float v[];
-  __shared__ float red[32];
-  const int b = blockIdx.x;
-  const bool live = b < B;
+  extern __shared__ __align__(16) float v[];
+  __shared__ float red[32], slot;
+  const int b = blockIdx.y, r = blockIdx.x, n = H / gridDim.x, k0 = r * n;
   float ss = 0.f;
-  if (live)
-    for (int k = threadIdx.x; k < H; k += blockDim.x) {
-      const float t = x[(size_t)b * H + k];
-      v[k] = t;
-      ss = fmaf(t, t, ss);
-    }
-  ss = block_sum(ss, red);
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float t = x[(size_t)b * H + k0 + i];
+    v[i] = t;
+    ss = fmaf(t, t, ss);
+  }
+  ss = cluster_reduce<false>(block_sum(ss, red), &slot);
   const float s = 1.f / sqrtf(ss / (float)H + 1e-6f);
-  if (live)
-    for (int k = threadIdx.x; k < H; k += blockDim.x) {
-      const float o = w[k] * v[k] * s;
-      v[k] = o;
-      if (out) out[(size_t)b * H + k] = o;
-    }
-  __syncthreads();
-  emit_xfrag(v, H, b, nt, xf, xexp, red, live);
+  float mx = 0.f;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float o = w[k0 + i] * v[i] * s;
+    v[i] = o;
+    mx = fmaxf(mx, fabsf(o));
+    if (out) out[(size_t)b * H + k0 + i] = o;
+  }
+  mx = cluster_reduce<true>(block_max(mx, red), &slot);
+  const int e = xfrag_exponent(mx);
+  if (r == 0 && threadIdx.x == 0) xexp[b] = e;
+  emit_xfrag_blocks(v, k0 / 32, n / 32, b, nt, xf, __int_as_float((127 + e) << 23), true);
 }
 
 cudaError_t launch_norm_prep(const float *x, const float *w, int H, int B, GemvScratch &s, float *out,
                              cudaStream_t st) {
-  const int nt = gemv_ntiles(B);
-  const size_t smem = (size_t)H * sizeof(float);
-  static size_t done = 0;
-  cudaError_t e = smem_optin(norm_prep_kernel, smem, done);
-  if (e != cudaSuccess) return e;
-  CW_TRY(launch_pdl(norm_prep_kernel, nt * 4, PREP_THREADS, smem, st, x, w, H, B, nt, s.xf, s.xexp, out));
+  const int cl = cluster_split(H / 32);
+  CW_TRY(launch_pdl_cluster(norm_prep_kernel, dim3(cl, B), ROW_THREADS, (size_t)(H / cl) * sizeof(float), st, cl, x, w,
+                            H, gemv_ntiles(B), s.xf, s.xexp, out));
   return cudaGetLastError();
 }
 
 // ---- plain row -> GEMV input (e.g. the SwiGLU output feeding ffn_down) ----
-__global__ void __launch_bounds__(PREP_THREADS) row_prep_kernel(const float *__restrict__ x, int xs, int K, int B,
-                                                                int nt, uint4 *__restrict__ xf,
-                                                                int *__restrict__ xexp) {
+__global__ void __launch_bounds__(ROW_THREADS) row_prep_kernel(const float *__restrict__ x, int xs, int K, int nt,
+                                                               uint4 *__restrict__ xf, int *__restrict__ xexp) {
   pdl_trigger();
   pdl_wait();
-  extern __shared__ float v[];
-  __shared__ float red[32];
-  const int b = blockIdx.x;
-  const bool live = b < B;
-  if (live)
-    for (int k = threadIdx.x; k < K; k += blockDim.x) v[k] = x[(size_t)b * xs + k];
-  __syncthreads();
-  emit_xfrag(v, K, b, nt, xf, xexp, red, live);
+  extern __shared__ __align__(16) float v[];
+  __shared__ float red[32], slot;
+  const int b = blockIdx.y, r = blockIdx.x, n = K / gridDim.x, k0 = r * n;
+  float mx = 0.f;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float t = x[(size_t)b * xs + k0 + i];
+    v[i] = t;
+    mx = fmaxf(mx, fabsf(t));
+  }
+  mx = cluster_reduce<true>(block_max(mx, red), &slot);
+  const int e = xfrag_exponent(mx);
+  if (r == 0 && threadIdx.x == 0) xexp[b] = e;
+  emit_xfrag_blocks(v, k0 / 32, n / 32, b, nt, xf, __int_as_float((127 + e) << 23), true);
 }
 
 cudaError_t launch_row_prep(const float *x, int xs, int K, int B, GemvScratch &s, cudaStream_t st) {
-  const int nt = gemv_ntiles(B);
-  static size_t done = 0;
-  cudaError_t e = smem_optin(row_prep_kernel, (size_t)K * sizeof(float), done);
-  if (e != cudaSuccess) return e;
-  CW_TRY(launch_pdl(row_prep_kernel, nt * 4, PREP_THREADS, (size_t)K * sizeof(float), st, x, xs, K, B, nt, s.xf, s.xexp));
+  const int cl = cluster_split(K / 32);
+  CW_TRY(launch_pdl_cluster(row_prep_kernel, dim3(cl, B), ROW_THREADS, (size_t)(K / cl) * sizeof(float), st, cl, x, xs,
+                            K, gemv_ntiles(B), s.xf, s.xexp));
   return cudaGetLastError();
 }
 
 // ---- GDN gated RMSNorm (run.c:2142-2178) fused with ssm_out input prep ----
 // o: raw GDN output [B][nvh*128] (S^T q / sqrt(128)); z: gate rows (stride zs).
 // out[h][i] = wn[i] * o[h][i] * rsqrt(mean_i o^2 + eps) * silu(z[h][i]).
-__global__ void __launch_bounds__(PREP_THREADS) gated_norm_prep_kernel(const float *__restrict__ o,
-                                                                       const float *__restrict__ z, int zs,
-                                                                       const float *__restrict__ wn, int nvh, int B,
-                                                                       int nt, uint4 *__restrict__ xf,
-                                                                       int *__restrict__ xexp) {
+// Each CTA of the cluster owns whole heads.
+__global__ void __launch_bounds__(ROW_THREADS) gated_norm_prep_kernel(const float *__restrict__ o,
+                                                                      const float *__restrict__ z, int zs,
+                                                                      const float *__restrict__ wn, int nvh, int nt,
+                                                                      uint4 *__restrict__ xf,
+                                                                      int *__restrict__ xexp) {
   pdl_trigger();
   pdl_wait();
-  extern __shared__ float v[];
-  __shared__ float red[32];
-  const int b = blockIdx.x;
-  const bool live = b < B;
+  extern __shared__ __align__(16) float v[];
+  __shared__ float red[32], slot;
+  const int b = blockIdx.y, r = blockIdx.x, hper = nvh / gridDim.x, h0 = r * hper;
   const int K = nvh * 128;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-  if (live) {
-    for (int h = warp; h < nvh; h += nw) {
-      const float *oh = o + (size_t)b * K + h * 128;
-      float t[4], ss = 0.f;
+  float mx = 0.f;
+  for (int hl = warp; hl < hper; hl += nw) {
+    const int h = h0 + hl;
+    const float *oh = o + (size_t)b * K + h * 128;
+    float t[4], ss = 0.f;
 #pragma unroll
-      for (int i = 0; i < 4; i++) {
-        t[i] = oh[lane + 32 * i];
-        ss = fmaf(t[i], t[i], ss);
-      }
-      ss = warp_sum(ss);
-      const float s = 1.f / sqrtf(ss / 128.f + 1e-6f);
+    for (int i = 0; i < 4; i++) {
+      t[i] = oh[lane + 32 * i];
+      ss = fmaf(t[i], t[i], ss);
+    }
+    ss = warp_sum(ss);
+    const float s = 1.f / sqrtf(ss / 128.f + 1e-6f);
 #pragma unroll
-      for (int i = 0; i < 4; i++) {
-        const int j = lane + 32 * i;
-        const float zz = z[(size_t)b * zs + h * 128 + j];
-        v[h * 128 + j] = wn[j] * t[i] * s * silu_dev(zz);
-      }
+    for (int i = 0; i < 4; i++) {
+      const int j = lane + 32 * i;
+      const float val = wn[j] * t[i] * s * silu_dev(z[(size_t)b * zs + h * 128 + j]);
+      v[hl * 128 + j] = val;
+      mx = fmaxf(mx, fabsf(val));
     }
   }
-  __syncthreads();
-  emit_xfrag(v, K, b, nt, xf, xexp, red, live);
+  mx = cluster_reduce<true>(block_max(mx, red), &slot);
+  const int e = xfrag_exponent(mx);
+  if (r == 0 && threadIdx.x == 0) xexp[b] = e;
+  emit_xfrag_blocks(v, h0 * 4, hper * 4, b, nt, xf, __int_as_float((127 + e) << 23), true);
 }
 
 cudaError_t launch_gated_norm_prep(const float *o, const float *z, int zs, const float *wn, int nvh, int B,
                                    GemvScratch &s, cudaStream_t st) {
-  const int nt = gemv_ntiles(B);
-  static size_t done = 0;
-  cudaError_t e = smem_optin(gated_norm_prep_kernel, (size_t)nvh * 128 * sizeof(float), done);
-  if (e != cudaSuccess) return e;
-  CW_TRY(launch_pdl(gated_norm_prep_kernel, nt * 4, PREP_THREADS, (size_t)nvh * 128 * sizeof(float), st, o, z, zs, wn, nvh, B, nt,
-                                                                                          s.xf, s.xexp));
+  const int cl = cluster_split(nvh);
+  CW_TRY(launch_pdl_cluster(gated_norm_prep_kernel, dim3(cl, B), ROW_THREADS, (size_t)(nvh / cl) * 128 * sizeof(float),
+                            st, cl, o, z, zs, wn, nvh, gemv_ntiles(B), s.xf, s.xexp));
   return cudaGetLastError();
 }
 

@@ -6,6 +6,8 @@
 // the attention gate run.c:2396) fuses with the conversion of the row into
 // the GEMV's f16 hi/lo fragments.
 #pragma once
+#include <cooperative_groups.h>
+
 #include "common.cuh"
 
 namespace cw {
@@ -33,14 +35,9 @@ CW_DEV float block_sum(float v, float *red) {
   return warp_sum(v);
 }
 
-// Emit GEMV fragments for column b from v[0..K) in shared memory (columns
-// b >= B are zero padding of the n-tile).  Layout: see prep_x_kernel in qgemv.cu.
-CW_DEV void emit_xfrag(const float *v, int K, int b, int nt, uint4 *__restrict__ xf, int *__restrict__ xexp,
-                       float *red, bool live) {
-  float mx = 0.f;
-  if (live)
-    for (int k = threadIdx.x; k < K; k += blockDim.x) mx = fmaxf(mx, fabsf(v[k]));
-  mx = block_max(mx, red);
+// Exponent of a column whose largest magnitude is mx: max|x| * 2^e in
+// [2^14, 2^15), so that the f16 hi part holds 11 bits and the lo part the next 11.
+CW_DEV int xfrag_exponent(float mx) {
   int e = 0;
   if (mx > 0.f && mx <= 3.0e38f) {
     int p;
@@ -48,12 +45,18 @@ CW_DEV void emit_xfrag(const float *v, int K, int b, int nt, uint4 *__restrict__
     e = 15 - p;
     e = e < -100 ? -100 : (e > 100 ? 100 : e);
   }
-  if (threadIdx.x == 0) xexp[b] = e;
-  const float scale = __int_as_float((127 + e) << 23);
-  const int g = b & 3, n = b >> 2, nb = K / 32;
-  for (int item = threadIdx.x; item < nb * 4; item += blockDim.x) {
-    const int kb = item >> 2, t = item & 3;
-    const float *r = v + kb * 32;
+  return e;
+}
+
+// Emit GEMV fragments of column b for the 32-blocks [kb0, kb0 + nkb) from
+// v (v[0] is element 32*kb0 of the column), already scaled by nothing: the
+// power-of-two `scale` is applied here.  Layout: see prep comments in qgemv.cu.
+CW_DEV void emit_xfrag_blocks(const float *v, int kb0, int nkb, int b, int nt, uint4 *__restrict__ xf, float scale,
+                              bool live) {
+  const int g = b & 3, n = b >> 2;
+  for (int item = threadIdx.x; item < nkb * 4; item += blockDim.x) {
+    const int kbl = item >> 2, t = item & 3;
+    const float *r = v + kbl * 32;
     const int js[8] = {4 * t, 4 * t + 2, 4 * t + 1, 4 * t + 3, 4 * t + 16, 4 * t + 18, 4 * t + 17, 4 * t + 19};
     uint32_t hi[4], lo[4];
 #pragma unroll
@@ -64,10 +67,42 @@ CW_DEV void emit_xfrag(const float *v, int K, int b, int nt, uint4 *__restrict__
       hi[i] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
       lo[i] = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
     }
-    uint4 *o = xf + (size_t)(kb * nt + n) * 32;
+    uint4 *o = xf + (size_t)((kb0 + kbl) * nt + n) * 32;
     o[g * 4 + t] = make_uint4(hi[0], hi[1], hi[2], hi[3]);        // B column g: hi part
     o[(g + 4) * 4 + t] = make_uint4(lo[0], lo[1], lo[2], lo[3]);  // B column g + 4: lo part
   }
+}
+
+// Emit GEMV fragments for column b from v[0..K) in shared memory (one CTA
+// holds the whole column; columns b >= B are zero padding of the n-tile).
+CW_DEV void emit_xfrag(const float *v, int K, int b, int nt, uint4 *__restrict__ xf, int *__restrict__ xexp,
+                       float *red, bool live) {
+  float mx = 0.f;
+  if (live)
+    for (int k = threadIdx.x; k < K; k += blockDim.x) mx = fmaxf(mx, fabsf(v[k]));
+  mx = block_max(mx, red);
+  const int e = xfrag_exponent(mx);
+  if (threadIdx.x == 0) xexp[b] = e;
+  emit_xfrag_blocks(v, 0, K / 32, b, nt, xf, __int_as_float((127 + e) << 23), live);
+}
+
+// One float per CTA reduced over the thread-block cluster through distributed
+// shared memory, in cluster-rank order (deterministic); every CTA gets the
+// result.  `slot` is one float of this CTA's shared memory.
+template <bool MAX>
+CW_DEV float cluster_reduce(float v, float *slot) {
+  namespace cg = cooperative_groups;
+  cg::cluster_group cl = cg::this_cluster();
+  if (threadIdx.x == 0) *slot = v;
+  cl.sync();
+  float r = 0.f;
+  const unsigned n = cl.num_blocks();
+  for (unsigned i = 0; i < n; i++) {
+    const float o = *cl.map_shared_rank(slot, i);
+    r = MAX ? fmaxf(r, o) : (i == 0 ? o : r + o);
+  }
+  cl.sync();  // every CTA has read every slot before any slot is reused
+  return r;
 }
 
 CW_DEV float silu_dev(float x) { return x * (1.f / (1.f + expf(-x))); }
