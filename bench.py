@@ -1,7 +1,7 @@
 """Benchmark of the cwen B200 verify-decode engine (one JSON line on rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload decode|gemv]
+                    [--workload decode|gemv|mtp]
 
 Workload `decode` (default; BASELINE configs 2 and 3): the random-init 27B
 hybrid (64 layers, Q4_0 weights with scales |N(0,0.01)|, norms 1, seeded),
@@ -16,6 +16,10 @@ Workload `gemv`: the B=8 Q4_0 verify GEMV, W 17408x5120,
 X fp32 8x5120 ~N(0,1), scales |N(0,0.01)|, nibbles uniform.  A step is one
 call over a weight copy from a ring of 8 distinct copies (400 MB > 126 MB L2),
 so every step streams W from HBM.  value = algorithmic bytes / device time.
+
+Workload `mtp`: the hybrid plus the blk.64 MTP block,
+a 32767-id prefill, 256 new tokens drafted by the MTP head and verified;
+MTP spec tok/s, prefill rate, stream checked against serial decode.
 
 Multi-GPU: one process per GPU (torchrun); the GEMV has no exchange, each
 rank runs the same per-GPU work ("scaling": "weak"), the barrier-bracketed
@@ -480,20 +484,85 @@ def main_decode(args, ws, rank, local):
     return 0
 
 
+# ---------------- config 4: MTP speculation after a 32k prefill ----------------
+# The context window is the reference's maximum (CWEN_CTX <= 32768); the prompt
+# leaves room for the 256 new tokens and a full verify block after them.
+MTP_CTX, MTP_NEW = 32768, 256
+MTP_PROMPT = MTP_CTX - MTP_NEW - 17
+
+
+def main_mtp(args, ws, rank, local):
+    """the hybrid plus the blk.64 MTP block (Q8_0), a 32k
+    context pre-filled with random ids, 256 new tokens drafted by the MTP head
+    (depth 8) and verified; the stream must equal serial decode.  value =
+    (t(256) - t(1)) / 255 through cwen_generate; the prefill rate (blocks of
+    16 verify rows plus the nextn fold of every slot) is reported beside it."""
+    metric = "MTP spec decode tok/s (config 4: 32k prefill, depth 8)"
+    config = {"workload": f"config4: random-init 27B hybrid + blk.64 MTP (Q8_0), {MTP_PROMPT}-id random prompt "
+                          f"in a {MTP_CTX} context, {MTP_NEW} new",
+              "ctx": MTP_CTX, "parallelism": f"replicas{ws}" if ws > 1 else "single"}
+    if args.impl == "reference":
+        if rank == 0:
+            print(json.dumps({"impl": "reference", "unavailable": "config 4 needs a 32767-token CPU prefill "
+                                                                  "(about an hour on the reference)"}))
+        return 0
+    import torch
+
+    import cwen_b200
+    from cwen_b200 import build
+    build.build()
+    L = cwen_b200.lib()
+    cwen_b200.check(L.cwen_cuda_init(local, MTP_CTX, 16), "init")
+    d = cwen_b200.dims("reference")
+    d.has_mtp = 1
+    cwen_b200.check(L.cwen_load_synth(DEC_SEED, C.byref(d), 0), "load_synth")
+    prompt = synth_ids(MTP_PROMPT, DEC_SEED, "bench.mtp.prompt", d.n_vocab)
+    mtp_cfg = cwen_b200.spec_cfg(spec=1, use_mtp=1, max_draft=8)
+    barrier(ws)
+    clocks = ClockSampler(local)
+    clocks.start()
+    t0 = time.perf_counter()
+    cwen_b200.generate(prompt, 1, mtp_cfg)
+    t1 = time.perf_counter() - t0
+    t0 = time.perf_counter()
+    spec_stream, st = cwen_b200.generate(prompt, MTP_NEW, mtp_cfg)
+    tn = time.perf_counter() - t0
+    clk = clocks.stop()
+    serial, _ = cwen_b200.generate(prompt, MTP_NEW, cwen_b200.spec_cfg(spec=0))
+    L.cwen_cuda_shutdown()
+    tps = (MTP_NEW - 1) / max(tn - t1, 1e-9)
+    tps = 1.0 / barrier_max(ws, 1.0 / tps)
+    if rank == 0:
+        print(json.dumps({
+            "metric": metric, "value": round(tps * ws, 3), "unit": "tok/s", "n_gpus": ws, "steps": MTP_NEW,
+            "warmup": 1, "ms_per_step": round(1000.0 / tps, 3), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "q4_0 / q8_0 weights, fp32 activations", "data": "synthetic (seeded)",
+            "config": config, "clocks": clk,
+            "prefill": {"tokens": MTP_PROMPT, "seconds": round(t1, 2), "tok_s": round(MTP_PROMPT / t1, 1),
+                        "note": "blocks of 16 verify rows + one nextn step per slot; includes the first token"},
+            "identical_to_serial": bool(np.array_equal(serial, spec_stream)),
+            "mtp": {"cycles": st.cycles, "drafted": st.drafted, "full_accept": st.full, "short": st.shortw,
+                    "avg_kept": round(st.kept / st.drafted, 3) if st.drafted else 0.0,
+                    "note": "random-init weights: the nextn head is not trained on the target"},
+            "e2e": {"value": round(tps * ws, 3), "unit": "tok/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 12,
+                    "method": "cwen_generate (C host driver): (t(256)-t(1))/255"}}))
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=32)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="decode", choices=["decode", "gemv"])
+    ap.add_argument("--workload", default="decode", choices=["decode", "gemv", "mtp"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     ws, rank, local = dist_init(args)
-    if args.workload == "decode":
-        rc = main_decode(args, ws, rank, local)
+    if args.workload in ("decode", "mtp"):
+        rc = (main_decode if args.workload == "decode" else main_mtp)(args, ws, rank, local)
         if ws > 1:
             import torch.distributed as dist
             dist.destroy_process_group()

@@ -60,9 +60,11 @@ __global__ void __launch_bounds__(HD) attn_prep_kernel(const float *__restrict__
 }
 
 // Partial attention of every (row, head of kv group) against one chunk.
+// Grid (kv head, chunk, row group): rows [z*rb, z*rb + rb) of the block, so a
+// verify block spreads over rb-times more CTAs than a single row.
 __global__ void __launch_bounds__(256) attn_chunk_kernel(const float *__restrict__ qbuf, const float *__restrict__ Kc,
                                                          const float *__restrict__ Vc, int nh, int nkv, int pos0,
-                                                         int B, int t0, int nch_max, float *__restrict__ part) {
+                                                         int B, int t0, int nch_max, int rb, float *__restrict__ part) {
   pdl_trigger();
   pdl_wait();
   extern __shared__ float sm[];
@@ -70,8 +72,9 @@ __global__ void __launch_bounds__(256) attn_chunk_kernel(const float *__restrict
   float *Vs = Ks + ACH * KPAD;          // [ACH][HD]
   float *Qs = Vs + ACH * HD;            // [8 warps][HD]
   const int hkv = blockIdx.x, c = blockIdx.y;
+  const int b0 = blockIdx.z * rb, b1 = min(B, b0 + rb);
   const int c0 = c * ACH;
-  const int last = pos0 + B - 1;
+  const int last = pos0 + b1 - 1;
   if (c0 > last) return;
   const int tmax = min(c0 + ACH - 1, last);
   // stage the chunk (slots beyond the last row are zero-filled and masked)
@@ -90,8 +93,8 @@ __global__ void __launch_bounds__(256) attn_chunk_kernel(const float *__restrict
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   float *q = Qs + warp * HD;
   const float scale = 1.f / sqrtf((float)HD);
-  for (int qi = warp; qi < B * G; qi += 8) {
-    const int b = qi / G, h = hkv * G + qi % G;
+  for (int qi = warp; qi < (b1 - b0) * G; qi += 8) {
+    const int b = b0 + qi / G, h = hkv * G + qi % G;
     const int p = pos0 + b;
     if (c0 > p || c0 + ACH - 1 < t0) continue;  // warp-uniform
     __syncwarp();
@@ -212,8 +215,9 @@ cudaError_t launch_attention(const AttnArgs &a, GemvScratch &s, cudaStream_t st)
     if (e != cudaSuccess) return e;
     configured = true;
   }
-  CW_TRY(launch_pdl(attn_chunk_kernel, dim3(a.nkv, nch), 256, smem, st, a.qbuf, a.Kc, a.Vc, a.nh, a.nkv, a.pos0, a.B, a.t0,
-                                                         a.nch_max, a.part));
+  const int G = a.nh / a.nkv, rb = G >= 8 ? 1 : 8 / G;  // rows per CTA: about one (row, head) item per warp
+  CW_TRY(launch_pdl(attn_chunk_kernel, dim3(a.nkv, nch, (a.B + rb - 1) / rb), 256, smem, st, a.qbuf, a.Kc, a.Vc, a.nh,
+                    a.nkv, a.pos0, a.B, a.t0, a.nch_max, rb, a.part));
   const int cl = cluster_split(a.nh);
   if (a.nh / cl > 32) return cudaErrorInvalidValue;  // per-CTA heads must fit linv[32]
   const size_t csmem = (size_t)(a.nh / cl) * (HD + a.nch_max) * sizeof(float);
