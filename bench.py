@@ -539,7 +539,7 @@ def main_mtp(args, ws, rank, local):
             "vs_baseline": None, "dtype": "q4_0 / q8_0 weights, fp32 activations", "data": "synthetic (seeded)",
             "config": config, "clocks": clk,
             "prefill": {"tokens": MTP_PROMPT, "seconds": round(t1, 2), "tok_s": round(MTP_PROMPT / t1, 1),
-                        "note": "blocks of 16 verify rows + one nextn step per slot; includes the first token"},
+                        "note": "blocks of 16 verify rows, each folded into the nextn stream in one 16-row MTP pass; includes the first token"},
             "identical_to_serial": bool(np.array_equal(serial, spec_stream)),
             "mtp": {"cycles": st.cycles, "drafted": st.drafted, "full_accept": st.full, "short": st.shortw,
                     "avg_kept": round(st.kept / st.drafted, 3) if st.drafted else 0.0,

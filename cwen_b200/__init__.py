@@ -60,6 +60,7 @@ _SIGS = {
     "cwen_cuda_dump_read": (C.c_int, [C.c_int, C.c_int, C.c_void_p]),
     "cwen_cuda_mtp_ready": (C.c_int, []),
     "cwen_cuda_mtp_commit": (C.c_int, [C.c_int, C.c_int, C.c_int]),
+    "cwen_cuda_mtp_commit_block": (C.c_int, [C.c_int, C.c_void_p, C.c_int]),
     "cwen_cuda_mtp_draft": (C.c_int, [C.c_int, C.c_void_p, C.c_int]),
     "cwen_cuda_gdn_state": (C.c_int, [C.c_int, C.c_void_p, C.c_void_p]),
     "cwen_cuda_ctx": (C.c_int, []),

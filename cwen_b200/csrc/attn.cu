@@ -215,7 +215,22 @@ cudaError_t launch_attention(const AttnArgs &a, GemvScratch &s, cudaStream_t st)
     if (e != cudaSuccess) return e;
     configured = true;
   }
-  const int G = a.nh / a.nkv, rb = G >= 8 ? 1 : 8 / G;  // rows per CTA: about one (row, head) item per warp
+  // Rows per CTA: split the block's rows over more CTAs only while the
+  // (kv head, chunk) grid alone is short of two CTAs per SM -- each extra row
+  // group stages the chunk's K/V again, which long contexts cannot afford.
+  static int n_sm = 0;
+  if (!n_sm) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev);
+    if (n_sm <= 0) n_sm = 148;
+  }
+  const int G = a.nh / a.nkv, base = a.nkv * nch;
+  const int min_rb = G >= 8 ? 1 : 8 / G;                       // about one (row, head) item per warp
+  int groups = (2 * n_sm + base - 1) / base;
+  const int max_groups = (a.B + min_rb - 1) / min_rb;
+  groups = groups < 1 ? 1 : (groups > max_groups ? max_groups : groups);
+  const int rb = (a.B + groups - 1) / groups;
   CW_TRY(launch_pdl(attn_chunk_kernel, dim3(a.nkv, nch, (a.B + rb - 1) / rb), 256, smem, st, a.qbuf, a.Kc, a.Vc, a.nh,
                     a.nkv, a.pos0, a.B, a.t0, a.nch_max, rb, a.part));
   const int cl = cluster_split(a.nh);

@@ -69,6 +69,7 @@ void model_free() {
   for (auto p : M.Kc) F(p);
   for (auto p : M.Vc) F(p);
   F(M.mtp_K); F(M.mtp_V); F(M.mtp_hprev); F(M.mtp_x); F(M.mtp_cat); F(M.mtp_out); F(M.mtp_draft);
+  F(M.mtp_emb); F(M.mtp_hin);
   if (M.h_walk) cudaFreeHost(M.h_walk);
   if (M.h_toks) cudaFreeHost(M.h_toks);
   if (M.h_draft) cudaFreeHost(M.h_draft);
@@ -251,7 +252,7 @@ static int alloc_state() {
     CW_CHECK(cudaMalloc(&M.mtp_K, (size_t)ctx * KO * sizeof(float)));
     CW_CHECK(cudaMalloc(&M.mtp_V, (size_t)ctx * KO * sizeof(float)));
     if ((rc = A(M.mtp_hprev, (size_t)H)) || (rc = A(M.mtp_x, (size_t)bm * H)) || (rc = A(M.mtp_cat, (size_t)2 * H)) ||
-        (rc = A(M.mtp_out, (size_t)bm * H)))
+        (rc = A(M.mtp_out, (size_t)bm * H)) || (rc = A(M.mtp_emb, (size_t)bm * H)) || (rc = A(M.mtp_hin, (size_t)bm * H)))
       return rc;
     CW_CHECK(cudaMalloc(&M.mtp_draft, (size_t)3 * (bm + 1) * sizeof(int)));  // walk results per draft step
     CW_CHECK(cudaMallocHost(&M.h_draft, (size_t)(bm + 1) * sizeof(int)));
@@ -306,36 +307,36 @@ static int run_layer_block(int l, int B, int pos0, cudaStream_t st) {
 }
 
 // ---- MTP (nextn) drafter ----
-// One nextn step (mtp_step, run.c:3098-3131) at slot pos: the input token is
-// `token` or, when dtok is set, the device int it points to; hin is the
-// predecessor hidden [H] (device).  Writes K/V at pos of the nextn cache, the
-// shared-head-normed hidden to hout, and leaves hout as the pending GEMV input
-// (for the shared lm_head of a draft step).
-static int mtp_step_dev(int pos, int token, const int *dtok, const float *hin, float *hout, cudaStream_t st) {
+// nextn steps (mtp_step, run.c:3098-3131) for B consecutive slots pos0.. at
+// once: row j takes token toks.t[j] (or, for a single row, the device int at
+// dtok) and the predecessor hidden hin + j*H (device); each row writes K/V at
+// its slot of the nextn cache and its shared-head-normed hidden to hout + j*H,
+// and hout stays the pending GEMV input (for the shared lm_head of a draft).
+// Row j attends slots [1, pos0 + j] -- the rows before it in the same call
+// included -- so B rows give the bits of B single-row steps in order.
+static int mtp_step_dev(int pos0, int B, const Toks16 &toks, const int *dtok, const float *hin, float *hout,
+                        cudaStream_t st) {
   Model &M = g_model;
   Engine &E = engine();
   const cwen_dims &d = M.d;
   MtpW &w = M.mtp;
   const int H = d.n_embd, I = d.n_ff;
-  Toks16 tk;
-  memset(&tk, 0, sizeof tk);
-  tk.t[0] = token;
-  CW_CHECK(launch_embed(M.tok_embd, H, d.n_vocab, tk, 1, M.mtp_cat, M.err, st, dtok));
-  CW_CHECK(launch_cat_norm_prep(M.mtp_cat, hin, w.enorm, w.hnorm, H, E.gs, st));
-  CW_CHECK(timed_gemv(w.eh_proj, 1, M.mtp_x, H, EPI_STORE, st));
-  CW_CHECK(launch_norm_prep(M.mtp_x, w.attn_norm, H, 1, E.gs, nullptr, st));
-  CW_CHECK(timed_gemv(w.in_proj, 1, M.proj, M.PS, EPI_STORE, st));
+  CW_CHECK(launch_embed(M.tok_embd, H, d.n_vocab, toks, B, M.mtp_emb, M.err, st, dtok));
+  CW_CHECK(launch_cat_norm_prep(M.mtp_emb, hin, w.enorm, w.hnorm, H, B, E.gs, st));
+  CW_CHECK(timed_gemv(w.eh_proj, B, M.mtp_x, H, EPI_STORE, st));
+  CW_CHECK(launch_norm_prep(M.mtp_x, w.attn_norm, H, B, E.gs, nullptr, st));
+  CW_CHECK(timed_gemv(w.in_proj, B, M.proj, M.PS, EPI_STORE, st));
   AttnArgs a;
-  a.proj = M.proj; a.ps = M.PS; a.nh = d.n_head; a.nkv = d.n_head_kv; a.B = 1;
-  a.qn = w.q_norm; a.kn = w.k_norm; a.rope = M.rope; a.pos0 = pos; a.t0 = 1;  // the nextn stream starts at slot 1
+  a.proj = M.proj; a.ps = M.PS; a.nh = d.n_head; a.nkv = d.n_head_kv; a.B = B;
+  a.qn = w.q_norm; a.kn = w.k_norm; a.rope = M.rope; a.pos0 = pos0; a.t0 = 1;  // the nextn stream starts at slot 1
   a.qbuf = M.qbuf; a.Kc = M.mtp_K; a.Vc = M.mtp_V; a.part = M.attn_part; a.nch_max = M.nch_max; a.yout = nullptr;
   CW_CHECK(launch_attention(a, E.gs, st));
-  CW_CHECK(timed_gemv(w.out_proj, 1, M.mtp_x, H, EPI_ADD, st));
-  CW_CHECK(launch_norm_prep(M.mtp_x, w.post_norm, H, 1, E.gs, nullptr, st));
-  CW_CHECK(timed_gemv(w.gate_up, 1, M.h, I, EPI_SWIGLU, st));
-  CW_CHECK(launch_row_prep(M.h, I, I, 1, E.gs, st));
-  CW_CHECK(timed_gemv(w.down, 1, M.mtp_x, H, EPI_ADD, st));
-  CW_CHECK(launch_norm_prep(M.mtp_x, w.shared_head_norm, H, 1, E.gs, hout, st));
+  CW_CHECK(timed_gemv(w.out_proj, B, M.mtp_x, H, EPI_ADD, st));
+  CW_CHECK(launch_norm_prep(M.mtp_x, w.post_norm, H, B, E.gs, nullptr, st));
+  CW_CHECK(timed_gemv(w.gate_up, B, M.h, I, EPI_SWIGLU, st));
+  CW_CHECK(launch_row_prep(M.h, I, I, B, E.gs, st));
+  CW_CHECK(timed_gemv(w.down, B, M.mtp_x, H, EPI_ADD, st));
+  CW_CHECK(launch_norm_prep(M.mtp_x, w.shared_head_norm, H, B, E.gs, hout, st));
   E.prof.launches += 12;
   return CWEN_OK;
 }
@@ -679,14 +680,66 @@ int cwen_cuda_mtp_commit(int pos, int token, int row) {
   }
   const int H = M.d.n_embd;
   cudaStream_t st = E.stream;
-  // a step at pos when pos-1 is parked; its output is not needed (scratch half of mtp_out)
+  // a step at pos when pos-1 is parked; its output is not needed
   if (pos >= 1 && M.mtp_hpos == pos - 1) {
-    rc = mtp_step_dev(pos, token, nullptr, M.mtp_hprev, M.mtp_out, st);
+    Toks16 tk;
+    memset(&tk, 0, sizeof tk);
+    tk.t[0] = token;
+    rc = mtp_step_dev(pos, 1, tk, nullptr, M.mtp_hprev, M.mtp_out, st);
     if (rc) return rc;
   }
   CW_CHECK(launch_norm_prep(M.x + (size_t)row * H, M.output_norm, H, 1, E.gs, M.mtp_hprev, st));
   E.prof.launches++;
   M.mtp_hpos = pos;
+  return CWEN_OK;
+}
+
+int cwen_cuda_mtp_commit_block(int pos0, const int *toks, int n) {
+  Model &M = g_model;
+  Engine &E = engine();
+  int rc = check_ready("cwen_cuda_mtp_commit_block");
+  if (rc) return rc;
+  if (!M.mtp_on) {
+    set_error("cwen_cuda_mtp_commit_block: the model has no MTP block (blk.%d.nextn.*)", M.d.n_layer);
+    return CWEN_ESTATE;
+  }
+  if (!toks || n < 1 || n > E.bmax || pos0 < 0 || pos0 + n > E.ctx) {
+    set_error("cwen_cuda_mtp_commit_block: need 1 <= n <= %d rows inside the context", E.bmax);
+    return CWEN_EINVAL;
+  }
+  for (int j = 0; j < n; j++)
+    if (toks[j] < 0 || toks[j] >= M.d.n_vocab) {
+      set_error("token id %d out of range [0,%d)", toks[j], M.d.n_vocab);
+      return CWEN_ERANGE;
+    }
+  if (pos0 >= 1 && M.mtp_hpos != pos0 - 1) {
+    // not contiguous with the parked slot: fold row by row (steps where the reference steps)
+    for (int j = 0; j < n; j++) {
+      rc = cwen_cuda_mtp_commit(pos0 + j, toks[j], j);
+      if (rc) return rc;
+    }
+    return CWEN_OK;
+  }
+  const int H = M.d.n_embd;
+  cudaStream_t st = E.stream;
+  // predecessor hiddens: slot pos0 + j steps on rmsnorm(x_pre of slot pos0 + j - 1)
+  // -- the parked one for j = 0, row j - 1 of the last forward otherwise
+  const int j0 = pos0 == 0 ? 1 : 0;  // slot 0 only parks (no attendable slot yet)
+  if (n > 1) {
+    CW_CHECK(launch_norm_prep(M.x, M.output_norm, H, n - 1, E.gs, M.mtp_hin + H, st));
+    E.prof.launches++;
+  }
+  if (j0 == 0) CW_CHECK(cudaMemcpyAsync(M.mtp_hin, M.mtp_hprev, (size_t)H * sizeof(float), cudaMemcpyDeviceToDevice, st));
+  if (n > j0) {
+    Toks16 tk;
+    memset(&tk, 0, sizeof tk);
+    for (int j = j0; j < n; j++) tk.t[j - j0] = toks[j];
+    rc = mtp_step_dev(pos0 + j0, n - j0, tk, nullptr, M.mtp_hin + (size_t)j0 * H, M.mtp_out, st);
+    if (rc) return rc;
+  }
+  CW_CHECK(launch_norm_prep(M.x + (size_t)(n - 1) * H, M.output_norm, H, 1, E.gs, M.mtp_hprev, st));
+  E.prof.launches++;
+  M.mtp_hpos = pos0 + n - 1;
   return CWEN_OK;
 }
 
@@ -711,7 +764,10 @@ int cwen_cuda_mtp_draft(int pend, int *out, int max_d) {
   memset(&none, 0, sizeof none);
   for (int t = 0; t < n; t++) {
     float *hout = M.mtp_out + (size_t)(t & 1) * H;
-    rc = mtp_step_dev(pos_n + 1 + t, pend, t ? M.mtp_draft + 3 * (t - 1) + 1 : nullptr, hin, hout, st);
+    Toks16 tk;
+    memset(&tk, 0, sizeof tk);
+    tk.t[0] = pend;
+    rc = mtp_step_dev(pos_n + 1 + t, 1, tk, t ? M.mtp_draft + 3 * (t - 1) + 1 : nullptr, hin, hout, st);
     if (rc) return rc;
     CW_CHECK(timed_gemv(M.lm_head, 1, M.logits, V, EPI_STORE, st));
     CW_CHECK(launch_argmax_walk(M.logits, V, V, 1, 0, none, M.best, M.mtp_draft + 3 * t, st));

@@ -67,6 +67,7 @@ struct Model {
   float *mtp_hprev = nullptr;   // parked normed hidden [H]
   int mtp_hpos = -1;
   float *mtp_x = nullptr, *mtp_cat = nullptr, *mtp_out = nullptr;
+  float *mtp_emb = nullptr, *mtp_hin = nullptr;  // [bmax][H]: embeddings and predecessor hiddens of a block
   int *mtp_draft = nullptr, *h_draft = nullptr;
 };
 

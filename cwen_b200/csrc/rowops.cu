@@ -47,17 +47,20 @@ cudaError_t launch_embed(const uint8_t *emb, int H, int V, const Toks16 &toks, i
 }
 
 // ---- MTP input: [rmsnorm(e, enorm) | rmsnorm(h, hnorm)] -> GEMV input (run.c:3100-3102) ----
-// One row (column 0 of an n-tile; the other three columns are not read by
-// anything: a GEMV column depends only on its own X column).
+// One CTA per row b < B (column b; padding columns are not read into any
+// live result: a GEMV column depends only on its own X column).
 __global__ void __launch_bounds__(PREP_THREADS) cat_norm_prep_kernel(const float *__restrict__ e,
                                                                      const float *__restrict__ h,
                                                                      const float *__restrict__ we,
-                                                                     const float *__restrict__ wh, int H,
+                                                                     const float *__restrict__ wh, int H, int nt,
                                                                      uint4 *__restrict__ xf, int *__restrict__ xexp) {
   pdl_trigger();
   pdl_wait();
   extern __shared__ __align__(16) float v[];
   __shared__ float red[32];
+  const int b = blockIdx.x;
+  e += (size_t)b * H;
+  h += (size_t)b * H;
   float se = 0.f, sh = 0.f;
   for (int k = threadIdx.x; k < H; k += blockDim.x) {
     const float a = e[k], c = h[k];
@@ -74,16 +77,16 @@ __global__ void __launch_bounds__(PREP_THREADS) cat_norm_prep_kernel(const float
     v[H + k] = wh[k] * v[H + k] * rh;
   }
   __syncthreads();
-  emit_xfrag(v, 2 * H, 0, 1, xf, xexp, red, true);
+  emit_xfrag(v, 2 * H, b, nt, xf, xexp, red, true);
 }
 
-cudaError_t launch_cat_norm_prep(const float *e, const float *h, const float *we, const float *wh, int H,
+cudaError_t launch_cat_norm_prep(const float *e, const float *h, const float *we, const float *wh, int H, int B,
                                  GemvScratch &s, cudaStream_t st) {
   const size_t smem = (size_t)2 * H * sizeof(float);
   static size_t done = 0;
   cudaError_t err = smem_optin(cat_norm_prep_kernel, smem, done);
   if (err != cudaSuccess) return err;
-  CW_TRY(launch_pdl(cat_norm_prep_kernel, 1, PREP_THREADS, smem, st, e, h, we, wh, H, s.xf, s.xexp));
+  CW_TRY(launch_pdl(cat_norm_prep_kernel, B, PREP_THREADS, smem, st, e, h, we, wh, H, gemv_ntiles(B), s.xf, s.xexp));
   return cudaGetLastError();
 }
 

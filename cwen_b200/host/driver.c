@@ -232,11 +232,7 @@ static void ng_free(ngmap *m) {
    run.c:4830-4849, 4948, 4987-4994). */
 static int mtp_fold(int use_mtp, int pos0, const int32_t *t, int n) {
   if (!use_mtp) return 0;
-  for (int b = 0; b < n; b++) {
-    int rc = cwen_cuda_mtp_commit(pos0 + b, t[b], b);
-    if (rc) return rc;
-  }
-  return 0;
+  return cwen_cuda_mtp_commit_block(pos0, (const int *)t, n);
 }
 
 static int prefill(const int32_t *tokens, int n_tok, int *first, int use_mtp) {

@@ -129,6 +129,12 @@ int cwen_cuda_mtp_ready(void);
  * output_norm) for slot pos+1.  Call once per committed slot, in order
  * (mtp_commit, run.c:3147-3159). */
 int cwen_cuda_mtp_commit(int pos, int token, int row);
+/* The same for rows 0..n-1 of the last forward at slots pos0..pos0+n-1
+ * (tokens toks[0..n)) in one pass over the nextn weights instead of n: the
+ * rows' steps attend causally over the nextn cache, so the result is the bits
+ * of n cwen_cuda_mtp_commit calls in order (the prefill and verify-cycle folds
+ * of run.c:4830-4849, 4987-4994). */
+int cwen_cuda_mtp_commit_block(int pos0, const int *toks, int n);
 /* Draft up to max_d tokens after the last committed slot from the pending
  * token `pend`: a chain of nextn steps, each scored by the shared lm_head and
  * argmax'ed on the device; one synchronization at the end.  Returns the

@@ -99,3 +99,45 @@ def test_mtp_spec_equals_serial(mtp_model):
         spec, st = cwen_b200.generate(prompt, 48, cwen_b200.spec_cfg(spec=1, use_mtp=1, max_draft=md))
         assert np.array_equal(serial, spec), md
         assert st.drafted > 0
+
+
+def _fold_and_draft(L, toks, cuts, blockwise, nd=4):
+    """Prefill `toks` as verify blocks split at `cuts`, folding each block
+    into the nextn stream row by row or in one block commit; return the
+    draft tokens and the last draft step's logits."""
+    import cwen_b200
+    cwen_b200.check(L.cwen_cuda_reset())
+    pend = C.c_int(-1)
+    edges = [0] + list(cuts) + [len(toks)]
+    for a, b in zip(edges[:-1], edges[1:]):
+        blk = np.ascontiguousarray(toks[a:b])
+        cwen_b200.check(L.cwen_cuda_forward_block(vp(blk), b - a, -1), "forward_block")
+        cwen_b200.check(L.cwen_cuda_accept(None, C.byref(pend), None), "accept")
+        cwen_b200.check(L.cwen_cuda_commit(b - a - 1), "commit")
+        if blockwise:
+            cwen_b200.check(L.cwen_cuda_mtp_commit_block(a, vp(blk), b - a), "mtp_commit_block")
+        else:
+            for j in range(b - a):
+                cwen_b200.check(L.cwen_cuda_mtp_commit(a + j, int(blk[j]), j), "mtp_commit")
+    out = np.zeros(16, np.int32)
+    n = L.cwen_cuda_mtp_draft(pend.value, vp(out), nd)
+    assert n == nd, L.cwen_cuda_last_error()
+    return out[:n].copy(), pend.value
+
+
+def test_mtp_commit_block_equals_rows(mtp_model):
+    """One block commit gives the bits of n row commits in order: the nextn
+    steps are batch-invariant and attend causally over the nextn cache."""
+    import cwen_b200
+    L, d = mtp_model
+    toks = np.random.default_rng(11).integers(0, d.n_vocab, size=16).astype(np.int32)
+    for cuts in ((), (9,), (1, 5, 12)):
+        res = []
+        for blockwise in (False, True):
+            dr, pend = _fold_and_draft(L, toks, cuts, blockwise)
+            lg = np.zeros(d.n_vocab, np.float32)
+            cwen_b200.check(L.cwen_cuda_logits(0, vp(lg)), "logits")
+            res.append((dr, pend, lg))
+        (d0, p0, l0), (d1, p1, l1) = res
+        assert p0 == p1 and list(d0) == list(d1), cuts
+        assert np.array_equal(l0.view(np.uint32), l1.view(np.uint32)), cuts
