@@ -332,9 +332,9 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemv_kernel(GemvArgs a) {
       }
       // never leave bulk copies in flight: wait (bounded, one deadline) for
       // the last stages issued
-      const uint64_t t0 = globaltimer_ns();
+      const long long t0 = cycles_now();
       for (int i = issued > S ? issued - S : 0; i < issued; i++) {
-        while (!mbar_try_wait(&full[i % S], (uint32_t)((i / S) & 1)) && globaltimer_ns() - t0 < MBAR_TIMEOUT_NS) {
+        while (!mbar_try_wait(&full[i % S], (uint32_t)((i / S) & 1)) && !spin_expired(t0)) {
         }
       }
     }
@@ -473,9 +473,9 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemv_kernel(GemvArgs a) {
     const int c_last = (int)(((tu1 + 1) * a.G - 1) / a.units);
     const int ncon = c_last - c_first + 1, r = c - c_first;
     if (threadIdx.x == 0) {
-      const uint64_t t0 = globaltimer_ns();
+      const long long t0 = cycles_now();
       while (ok && *(volatile int *)(a.cnt + tile) < ncon) {
-        if (globaltimer_ns() - t0 > MBAR_TIMEOUT_NS) {
+        if (spin_expired(t0)) {
           atomicExch(a.err, 3);
           ok = false;
         }

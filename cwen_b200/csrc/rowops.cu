@@ -107,25 +107,28 @@ __global__ void __launch_bounds__(ROW_THREADS) norm_prep_kernel(const float *__r
   pdl_trigger();
   pdl_wait();
   extern __shared__ __align__(16) float v[];
-  __shared__ float red[32], slot;
+  __shared__ float red[64];
+  __shared__ float2 slot;
   const int b = blockIdx.y, r = blockIdx.x, n = H / gridDim.x, k0 = r * n;
-  float ss = 0.f;
+  // one pass: sum x^2 and max |w x|; one cluster exchange for both.
+  // max |(w x) s| = max |w x| * s exactly: s > 0 and rounding is monotonic.
+  float ss = 0.f, m = 0.f;
   for (int i = threadIdx.x; i < n; i += blockDim.x) {
     const float t = x[(size_t)b * H + k0 + i];
-    v[i] = t;
+    const float wt = w[k0 + i] * t;
+    v[i] = wt;
     ss = fmaf(t, t, ss);
+    m = fmaxf(m, fabsf(wt));
   }
-  ss = cluster_reduce<false>(block_sum(ss, red), &slot);
-  const float s = 1.f / sqrtf(ss / (float)H + 1e-6f);
-  float mx = 0.f;
+  const float2 sm = cluster_reduce_sum_max(block_sum_max(ss, m, red), &slot);
+  const float s = 1.f / sqrtf(sm.x / (float)H + 1e-6f);
   for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    const float o = w[k0 + i] * v[i] * s;
+    const float o = v[i] * s;  // (w x) s, the reference's order
     v[i] = o;
-    mx = fmaxf(mx, fabsf(o));
     if (out) out[(size_t)b * H + k0 + i] = o;
   }
-  mx = cluster_reduce<true>(block_max(mx, red), &slot);
-  const int e = xfrag_exponent(mx);
+  __syncthreads();
+  const int e = xfrag_exponent(sm.y * s);
   if (r == 0 && threadIdx.x == 0) xexp[b] = e;
   emit_xfrag_blocks(v, k0 / 32, n / 32, b, nt, xf, __int_as_float((127 + e) << 23), true);
 }

@@ -86,22 +86,50 @@ CW_DEV void emit_xfrag(const float *v, int K, int b, int nt, uint4 *__restrict__
   emit_xfrag_blocks(v, 0, K / 32, b, nt, xf, __int_as_float((127 + e) << 23), live);
 }
 
-// One float per CTA reduced over the thread-block cluster through distributed
-// shared memory, in cluster-rank order (deterministic); every CTA gets the
-// result.  `slot` is one float of this CTA's shared memory.
+// One float per CTA reduced over the thread-block cluster (<= 32 CTAs)
+// through distributed shared memory; every CTA gets the result.  Each warp
+// reads the CTAs' slots in parallel (lane i <- rank i) and reduces them with a
+// fixed xor tree, so the result is deterministic and the same in every CTA.
+// `slot` is one float of this CTA's shared memory.
 template <bool MAX>
 CW_DEV float cluster_reduce(float v, float *slot) {
   namespace cg = cooperative_groups;
   cg::cluster_group cl = cg::this_cluster();
   if (threadIdx.x == 0) *slot = v;
   cl.sync();
-  float r = 0.f;
-  const unsigned n = cl.num_blocks();
-  for (unsigned i = 0; i < n; i++) {
-    const float o = *cl.map_shared_rank(slot, i);
-    r = MAX ? fmaxf(r, o) : (i == 0 ? o : r + o);
-  }
+  const unsigned l = threadIdx.x & 31;
+  float o = l < cl.num_blocks() ? *cl.map_shared_rank(slot, l) : 0.f;  // 0: identity of the sum and of the max of |.|
+  o = MAX ? warp_max(o) : warp_sum(o);
   cl.sync();  // every CTA has read every slot before any slot is reused
+  return o;
+}
+
+// Block-wide (sum, max) pair in one exchange (red: >= 64 floats smem).
+CW_DEV float2 block_sum_max(float v, float m, float *red) {
+  v = warp_sum(v);
+  m = warp_max(m);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) {
+    red[w] = v;
+    red[32 + w] = m;
+  }
+  __syncthreads();
+  const bool in = l < (int)(blockDim.x >> 5);
+  return make_float2(warp_sum(in ? red[l] : 0.f), warp_max(in ? red[32 + l] : 0.f));
+}
+
+// (sum, max) pair per CTA reduced over the thread-block cluster in one
+// exchange, like cluster_reduce.  `slot` is one float2 of this CTA's shared memory.
+CW_DEV float2 cluster_reduce_sum_max(float2 v, float2 *slot) {
+  namespace cg = cooperative_groups;
+  cg::cluster_group cl = cg::this_cluster();
+  if (threadIdx.x == 0) *slot = v;
+  cl.sync();
+  const unsigned l = threadIdx.x & 31;
+  const float2 o = l < cl.num_blocks() ? *cl.map_shared_rank(slot, l) : make_float2(0.f, 0.f);
+  const float2 r = make_float2(warp_sum(o.x), warp_max(o.y));
+  cl.sync();  // every CTA has read every slot before any CTA leaves
   return r;
 }
 

@@ -30,22 +30,24 @@ CW_DEV bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-CW_DEV uint64_t globaltimer_ns() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
-  return t;
-}
+// Time bound for the spin-waits, in SM clock cycles: %clock64 is read in a
+// few cycles, whereas a %globaltimer read takes a fraction of a microsecond,
+// which a wait loop that reads it on its first miss pays on every stage.
+// 4e9 cycles is ~2 s at the 1965 MHz maximum clock -- far beyond any
+// legitimate wait -- and proportionally longer at lower clocks.
+constexpr long long SPIN_TIMEOUT_CYCLES = 4000000000ll;
+CW_DEV long long cycles_now() { return clock64(); }
+CW_DEV bool spin_expired(long long t0) { return clock64() - t0 > SPIN_TIMEOUT_CYCLES; }
 // Bounded wait for the phase of `parity` to complete.  Gives up (returns
-// false) after MBAR_TIMEOUT_NS of wall time -- far beyond any legitimate
-// wait -- or as soon as another thread of the CTA raised *abort.
-constexpr uint64_t MBAR_TIMEOUT_NS = 2000000000ull;
+// false) after SPIN_TIMEOUT_CYCLES or as soon as another thread of the CTA
+// raised *abort.
 CW_DEV bool mbar_wait(uint64_t *bar, uint32_t parity, const volatile int *abort) {
   if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = globaltimer_ns();
+  const long long t0 = cycles_now();
   for (uint32_t it = 1;; it++) {
     if (mbar_try_wait(bar, parity)) return true;
     if (*abort) return false;
-    if ((it & 255u) == 0 && globaltimer_ns() - t0 > MBAR_TIMEOUT_NS) return false;
+    if ((it & 63u) == 0 && spin_expired(t0)) return false;
   }
 }
 
