@@ -190,9 +190,16 @@ struct GemvArgs {
   int *err;
   int G;
   long long units;
+  int cl;  // > 1: the contributors of each split tile form one thread-block cluster of cl CTAs
 };
 
 CW_DEV float silu_f(float x) { return x * (1.f / (1.f + expf(-x))); }
+
+// Thread-block cluster barrier (every thread of every CTA of the cluster),
+// release / acquire at cluster scope.
+CW_DEV void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
 
 // Fold the lo-part accumulators into the hi-part ones: lane (g, t < 2) holds
 // B columns 2t, 2t+1 (hi parts), lane (g, t + 2) the same columns' lo parts.
@@ -236,6 +243,37 @@ CW_DEV void gemv_epilogue(const GemvArgs &a, int mt0, bool has1, const float (&a
           float *p = a.y + (size_t)col * a.ys + row;
           if (a.epi == EPI_ADD) *p += v;
           else *p = v;
+        }
+      }
+    }
+  }
+}
+
+// Epilogue of a reduced split-tile share: lane (mt, row) holds row `row` of
+// m-tile mt0 + mt, four columns per n-tile.  The whole warp calls it (the
+// SwiGLU pairs gate and up rows across the warp's halves).
+template <int NT>
+CW_DEV void split_epilogue(const GemvArgs &a, int mt0, int mt, int row, bool live, const float4 (&sum)[NT]) {
+#pragma unroll
+  for (int n = 0; n < NT; n++) {
+    const float e4[4] = {sum[n].x, sum[n].y, sum[n].z, sum[n].w};
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      const int col = n * 4 + j;
+      if (col >= a.B) continue;
+      const float sc = __int_as_float((127 - __ldg(a.xexp + col)) << 23);
+      if (a.epi == EPI_SWIGLU) {
+        const float up = __shfl_down_sync(0xffffffffu, e4[j], 16);
+        if (live && mt == 0) {
+          const int orow = (mt0 >> 1) * 16 + row;
+          if (orow * 2 < a.M) a.y[(size_t)col * a.ys + orow] = silu_f(e4[j] * sc) * (up * sc);
+        }
+      } else if (live) {
+        const int grow = (mt0 + mt) * 16 + row;
+        if (grow < a.M) {
+          float *p = a.y + (size_t)col * a.ys + grow;
+          if (a.epi == EPI_ADD) *p += e4[j] * sc;
+          else *p = e4[j] * sc;
         }
       }
     }
@@ -338,7 +376,11 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemv_kernel(GemvArgs a) {
         }
       }
     }
-    return;  // the producers take part in no later barrier
+    if (a.cl > 1) {  // the two cluster barriers of the split-tile reduction
+      cluster_sync_all();
+      cluster_sync_all();
+    }
+    return;  // the producers take part in no later CTA barrier
   }
 
   // ---------------- consumers ----------------
@@ -436,8 +478,11 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemv_kernel(GemvArgs a) {
     } else {
       // Partial tile: park this segment's sums; the arrival count and the
       // reduction wait until this CTA's last segment, so the stream never stalls.
+      // In cluster mode the CTA holds its one segment in its own shared
+      // memory (the drained ring), read by the other CTAs of the cluster.
       const int slot = first_seg ? 0 : 1;
-      float *mine = a.ws + ((size_t)c * 2 + slot) * WS_TILE_FLOATS;
+      float *mine = a.cl > 1 ? reinterpret_cast<float *>(smem) : a.ws + ((size_t)c * 2 + slot) * WS_TILE_FLOATS;
+      if (a.cl > 1) named_bar(1, QG_CONS_WARPS * 32);  // every warp is done with the ring
       if (has0 && t < 2) {
 #pragma unroll
         for (int mt = 0; mt < 2; mt++)
@@ -455,17 +500,65 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemv_kernel(GemvArgs a) {
     first_seg = false;
   }
 
-  // ---- split tiles: every contributor reduces a share of the rows ----
-  // All contributors of a split tile are resident (one CTA per SM, G <= SMs,
-  // and PDL successors start only after every CTA of this grid started), and
-  // each first counts itself in for all its split tiles and only then waits,
-  // so the waits below end; they are bounded all the same.  The counter of a
-  // tile goes 0 -> n (partials parked) -> 2n (shares reduced) -> 0.
   if (np == 0) return;
-  __threadfence();
+  // ---- split tiles: every contributor reduces a share of the rows ----
+  // warp w's two m-tiles are reduced by contributor w % ncon: lane l sums row
+  // l & 15 of m-tile l >> 4, four columns per n-tile (one float4 per
+  // contributor and n-tile), over all contributors in CTA order.
+  const int mt = lane >> 4, row = lane & 15;
+  if (a.cl > 1) {
+    // Cluster mode: the tile's contributors are the cluster's CTAs (ranks 0..cl-1
+    // in CTA order); partials are read from their shared memory.  Both cluster
+    // barriers are hardware barriers that every thread of the cluster reaches
+    // (all earlier waits are bounded).
+    namespace cg = cooperative_groups;
+    cg::cluster_group cluster = cg::this_cluster();
+    cluster_sync_all();  // every CTA's partials are in its shared memory
+    const int tile = ptile[0], r = (int)cluster.block_rank();
+    const int mt0 = tile * QG_TILE_MT + warp * 2;
+    if (__all_sync(0xffffffffu, ok) && warp % a.cl == r) {  // warp-uniform: split_epilogue shuffles
+      const bool live = mt0 + mt < a.n_mt;
+      float4 sum[NT];
+#pragma unroll
+      for (int n = 0; n < NT; n++) sum[n] = make_float4(0.f, 0.f, 0.f, 0.f);
+      const int off = ((warp * 2 + mt) * 16 + row) * 16;
+      if (live) {
+        float4 v[4][NT];
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+          if (q >= a.cl) break;
+          const float *src = cluster.map_shared_rank(reinterpret_cast<float *>(smem), q) + off;
+#pragma unroll
+          for (int n = 0; n < NT; n++) v[q][n] = *reinterpret_cast<const float4 *>(src + 4 * n);
+        }
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+          if (q >= a.cl) break;
+#pragma unroll
+          for (int n = 0; n < NT; n++) {
+            sum[n].x += v[q][n].x;
+            sum[n].y += v[q][n].y;
+            sum[n].z += v[q][n].z;
+            sum[n].w += v[q][n].w;
+          }
+        }
+      }
+      split_epilogue<NT>(a, mt0, mt, row, live, sum);
+    }
+    cluster_sync_all();  // no CTA leaves while another reads its shared memory
+    return;
+  }
+  // Global mode.  All contributors of a split tile are resident (one CTA per
+  // SM, G <= SMs, and PDL successors start only after every CTA of this grid
+  // started), and each first counts itself in for all its split tiles and
+  // only then waits, so the waits below end; they are bounded all the same.
+  // The counter of a tile goes 0 -> n (partials parked) -> 2n (shares
+  // reduced) -> 0.
   named_bar(1, QG_CONS_WARPS * 32);
-  if (threadIdx.x == 0)
+  if (threadIdx.x == 0) {
+    __threadfence();  // the CTA's partials (ordered before by the barrier), before the arrival
     for (int j = 0; j < np; j++) atomicAdd(a.cnt + ptile[j], 1);
+  }
   for (int j = 0; j < np; j++) {
     const int tile = ptile[j];
     const long long tu0 = (long long)tile * a.kp, tu1 = tu0 + a.kp - 1;
@@ -480,69 +573,45 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemv_kernel(GemvArgs a) {
           ok = false;
         }
       }
+      __threadfence();  // the other contributors' partials, after their arrivals
       last_p[0] = ok;
     }
     named_bar(1, QG_CONS_WARPS * 32);
     const bool go = last_p[0] != 0;
-    __threadfence();
-    // warp w's two m-tiles are reduced by contributor w % ncon: lane l sums
-    // row l & 15 of m-tile l >> 4, four columns per n-tile (one float4 per
-    // contributor and n-tile), over all contributors in CTA order.
     const int mt0 = tile * QG_TILE_MT + warp * 2;
-    const int mt = lane >> 4, row = lane & 15;
-    if (go && warp % ncon == r && mt0 + mt < a.n_mt) {
+    if (go && warp % ncon == r) {
+      const bool live = mt0 + mt < a.n_mt;
       float4 sum[NT];
 #pragma unroll
       for (int n = 0; n < NT; n++) sum[n] = make_float4(0.f, 0.f, 0.f, 0.f);
       const size_t off = (size_t)((warp * 2 + mt) * 16 + row) * 16;
       constexpr int CH = NT == 1 ? 8 : (NT == 2 ? 4 : 2);  // independent loads in flight per lane
-      for (int c0 = c_first; c0 <= c_last; c0 += CH) {
-        float4 v[CH][NT];
+      if (live) {
+        for (int c0 = c_first; c0 <= c_last; c0 += CH) {
+          float4 v[CH][NT];
 #pragma unroll
-        for (int q = 0; q < CH; q++) {
-          const int cc = c0 + q;
-          if (cc > c_last) break;
-          const long long cu0 = (long long)cc * a.units / a.G;
-          const float *src = a.ws + ((size_t)cc * 2 + (cu0 >= tu0 ? 0 : 1)) * WS_TILE_FLOATS + off;
+          for (int q = 0; q < CH; q++) {
+            const int cc = c0 + q;
+            if (cc > c_last) break;
+            const long long cu0 = (long long)cc * a.units / a.G;
+            const float *src = a.ws + ((size_t)cc * 2 + (cu0 >= tu0 ? 0 : 1)) * WS_TILE_FLOATS + off;
 #pragma unroll
-          for (int n = 0; n < NT; n++) v[q][n] = __ldcg(reinterpret_cast<const float4 *>(src + 4 * n));
-        }
-#pragma unroll
-        for (int q = 0; q < CH; q++) {
-          if (c0 + q > c_last) break;
-#pragma unroll
-          for (int n = 0; n < NT; n++) {
-            sum[n].x += v[q][n].x;
-            sum[n].y += v[q][n].y;
-            sum[n].z += v[q][n].z;
-            sum[n].w += v[q][n].w;
+            for (int n = 0; n < NT; n++) v[q][n] = __ldcg(reinterpret_cast<const float4 *>(src + 4 * n));
           }
-        }
-      }
 #pragma unroll
-      for (int n = 0; n < NT; n++) {
-        const float e4[4] = {sum[n].x, sum[n].y, sum[n].z, sum[n].w};
+          for (int q = 0; q < CH; q++) {
+            if (c0 + q > c_last) break;
 #pragma unroll
-        for (int j = 0; j < 4; j++) {
-          const int col = n * 4 + j;
-          if (col >= a.B) continue;
-          const float sc = __int_as_float((127 - __ldg(a.xexp + col)) << 23);
-          if (a.epi == EPI_SWIGLU) {
-            const float up = __shfl_down_sync(0x0000ffffu, e4[j], 16, 32);
-            if (mt == 0) {
-              const int orow = (mt0 >> 1) * 16 + row;
-              if (orow * 2 < a.M) a.y[(size_t)col * a.ys + orow] = silu_f(e4[j] * sc) * (up * sc);
-            }
-          } else {
-            const int grow = (mt0 + mt) * 16 + row;
-            if (grow < a.M) {
-              float *p = a.y + (size_t)col * a.ys + grow;
-              if (a.epi == EPI_ADD) *p += e4[j] * sc;
-              else *p = e4[j] * sc;
+            for (int n = 0; n < NT; n++) {
+              sum[n].x += v[q][n].x;
+              sum[n].y += v[q][n].y;
+              sum[n].z += v[q][n].z;
+              sum[n].w += v[q][n].w;
             }
           }
         }
       }
+      split_epilogue<NT>(a, mt0, mt, row, live, sum);
     }
     named_bar(1, QG_CONS_WARPS * 32);  // every read of the partials of this tile is done
     if (threadIdx.x == 0 && go) {
@@ -553,8 +622,37 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemv_kernel(GemvArgs a) {
 
 size_t gemv_scratch_ws_floats(int G) { return (size_t)G * 2 * WS_TILE_FLOATS; }
 
+// Thread-block clusters of cl CTAs of this kernel that can be resident at once
+// (0: none / not queryable).
 template <int TYPE, int NT>
-static cudaError_t launch_t(const GemvArgs &a, cudaStream_t st) {
+static int max_clusters(int cl) {
+  using Lay = QgLayout<TYPE, NT>;
+  static int cache[5] = {-1, -1, -1, -1, -1};
+  if (cl < 2 || cl > 4) return 0;
+  if (cache[cl] < 0) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(cl * 64);
+    cfg.blockDim = dim3(QG_THREADS);
+    cfg.dynamicSmemBytes = Lay::SMEM;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = cl;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, qgemv_kernel<TYPE, NT>, &cfg) != cudaSuccess) {
+      (void)cudaGetLastError();
+      n = 0;
+    }
+    cache[cl] = n;
+  }
+  return cache[cl];
+}
+
+template <int TYPE, int NT>
+static cudaError_t launch_t(GemvArgs a, cudaStream_t st) {
   using Lay = QgLayout<TYPE, NT>;
   static bool configured = false;
   if (!configured) {
@@ -563,6 +661,11 @@ static cudaError_t launch_t(const GemvArgs &a, cudaStream_t st) {
     if (e != cudaSuccess) return e;
     configured = true;
   }
+  // Split tiles reduced inside thread-block clusters only when every tile's
+  // cluster can be resident at once (the grid is one wave); the sums are the
+  // same as the global path's (contributors in CTA order).
+  if (a.cl > 1 && max_clusters<TYPE, NT>(a.cl) < a.G / a.cl) a.cl = 1;
+  if (a.cl > 1) return launch_pdl_cluster(qgemv_kernel<TYPE, NT>, a.G, QG_THREADS, Lay::SMEM, st, a.cl, a);
   return launch_pdl(qgemv_kernel<TYPE, NT>, a.G, QG_THREADS, Lay::SMEM, st, a);
 }
 
@@ -596,6 +699,10 @@ cudaError_t gemv_run(const QMat &m, int B, float *Y, int ys, int epi, GemvScratc
   if (g > s.G) g = s.G;
   if (n_tiles <= g) g = g / n_tiles * n_tiles;
   a.G = (int)g;
+  // 2 to 4 contributors per tile: reduce inside a thread-block cluster
+  // (distributed shared memory) instead of through global scratch
+  a.cl = 1;
+  if (n_tiles <= g && g / n_tiles >= 2 && g / n_tiles <= 4) a.cl = (int)(g / n_tiles);
   switch (gemv_ntiles(B) * 16 + m.type) {
     case 16 + 8: return launch_t<8, 1>(a, st);
     case 32 + 8: return launch_t<8, 2>(a, st);
