@@ -68,11 +68,12 @@ int upload_qmat_rows(int type, const void *host, int ne0, int ne1, QMat &m, int 
   return CWEN_OK;
 }
 
-cudaError_t timed_gemv(const QMat &m, int B, float *Y, int ys, int epi, cudaStream_t st) {
+cudaError_t timed_gemv(const QMat &m, int B, float *Y, int ys, int epi, cudaStream_t st, const float *X, int xs) {
   Engine &E = engine();
   Prof &P = E.prof;
-  E.prof.launches += 1;
-  if (!P.on) return gemv_run(m, B, Y, ys, epi, E.gs, st);
+  E.prof.launches += X && !gemv_uses_local_x(m, E.gs) ? 2 : 1;
+  auto run = [&]() { return X ? gemv_run_x(m, X, xs, B, Y, ys, epi, E.gs, st) : gemv_run(m, B, Y, ys, epi, E.gs, st); };
+  if (!P.on) return run();
   if (P.used + 2 > P.ev.size()) {
     for (int i = 0; i < 256; i++) {
       cudaEvent_t e;
@@ -83,7 +84,7 @@ cudaError_t timed_gemv(const QMat &m, int B, float *Y, int ys, int epi, cudaStre
   }
   cudaEvent_t a = P.ev[P.used], b = P.ev[P.used + 1];
   cudaEventRecord(a, st);
-  cudaError_t r = gemv_run(m, B, Y, ys, epi, E.gs, st);
+  cudaError_t r = run();
   cudaEventRecord(b, st);
   P.used += 2;
   const double wbytes = (double)(m.K / 32) * (m.type == 8 ? 34 : 18) * (double)m.M;
@@ -217,9 +218,7 @@ int cwen_cuda_gemvb(int wid, const float *dX, int xs, float *dY, int ys, int B, 
     return CWEN_EINVAL;
   }
   cudaStream_t st = stream ? (cudaStream_t)stream : E.stream;
-  CW_CHECK(gemv_prep_x(dX, xs, B, m.K, E.gs, st));
-  E.prof.launches += 1;
-  CW_CHECK(timed_gemv(m, B, dY, ys, EPI_STORE, st));
+  CW_CHECK(timed_gemv(m, B, dY, ys, EPI_STORE, st, dX, xs));
   return CWEN_OK;
 }
 

@@ -37,7 +37,9 @@ struct Engine {
 };
 
 // GEMV over already-prepared X with optional event timing + launch counting.
-cudaError_t timed_gemv(const QMat &m, int B, float *Y, int ys, int epi, cudaStream_t st);
+// X != nullptr: raw fp32 X [B][xs] (gemv_run_x); otherwise prepared fragments.
+cudaError_t timed_gemv(const QMat &m, int B, float *Y, int ys, int epi, cudaStream_t st, const float *X = nullptr,
+                       int xs = 0);
 
 Engine &engine();
 // CWEN_OK, or CWEN_ETIMEOUT when a GEMV gave up on a bounded wait (synchronous).

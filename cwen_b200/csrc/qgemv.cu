@@ -191,6 +191,10 @@ struct GemvArgs {
   int G;
   long long units;
   int cl;  // > 1: the contributors of each split tile form one thread-block cluster of cl CTAs
+  // local-X variant: raw fp32 rows X (column b at xr + b*xrs), turned into
+  // fragments by each CTA for its own k-range with its own column exponents
+  const float *xr;
+  int xrs;
 };
 
 CW_DEV float silu_f(float x) { return x * (1.f / (1.f + expf(-x))); }
@@ -217,7 +221,8 @@ CW_DEV void fold_lo(float (&acc)[2][NT][4]) {
 // Apply the epilogue for one warp's folded accumulators (rows of m-tiles
 // mt0, mt0+1; lanes t < 2 carry the columns n*4 + 2t + {0, 1}).
 template <int NT>
-CW_DEV void gemv_epilogue(const GemvArgs &a, int mt0, bool has1, const float (&acc)[2][NT][4], int g, int t) {
+CW_DEV void gemv_epilogue(const GemvArgs &a, int mt0, bool has1, const float (&acc)[2][NT][4], int g, int t,
+                          const float *xun) {
   if (t >= 2) return;
 #pragma unroll
   for (int n = 0; n < NT; n++) {
@@ -225,7 +230,7 @@ CW_DEV void gemv_epilogue(const GemvArgs &a, int mt0, bool has1, const float (&a
     for (int i = 0; i < 4; i++) {
       const int col = n * 4 + 2 * t + (i & 1);
       if (col >= a.B) continue;
-      const float sc = __int_as_float((127 - __ldg(a.xexp + col)) << 23);
+      const float sc = xun ? xun[col] : __int_as_float((127 - __ldg(a.xexp + col)) << 23);
       const int rr = g + ((i >> 1) << 3);
       if (a.epi == EPI_SWIGLU) {
         const int row = (mt0 >> 1) * 16 + rr;
@@ -249,6 +254,13 @@ CW_DEV void gemv_epilogue(const GemvArgs &a, int mt0, bool has1, const float (&a
   }
 }
 
+// Power-of-two unscale of column col: the global exponent of prepared
+// fragments, or (local-X variant) 1 for partials already unscaled by the CTA
+// that computed them.
+CW_DEV float split_unscale(const GemvArgs &a, int col) {
+  return a.xr ? 1.f : __int_as_float((127 - __ldg(a.xexp + col)) << 23);
+}
+
 // Epilogue of a reduced split-tile share: lane (mt, row) holds row `row` of
 // m-tile mt0 + mt, four columns per n-tile.  The whole warp calls it (the
 // SwiGLU pairs gate and up rows across the warp's halves).
@@ -261,7 +273,7 @@ CW_DEV void split_epilogue(const GemvArgs &a, int mt0, int mt, int row, bool liv
     for (int j = 0; j < 4; j++) {
       const int col = n * 4 + j;
       if (col >= a.B) continue;
-      const float sc = __int_as_float((127 - __ldg(a.xexp + col)) << 23);
+      const float sc = split_unscale(a, col);
       if (a.epi == EPI_SWIGLU) {
         const float up = __shfl_down_sync(0xffffffffu, e4[j], 16);
         if (live && mt == 0) {
@@ -280,16 +292,20 @@ CW_DEV void split_epilogue(const GemvArgs &a, int mt0, int mt, int row, bool liv
   }
 }
 
-template <int TYPE, int NT>
+template <int TYPE, int NT, bool XL = false>
 struct QgLayout {
   static constexpr int CHUNK = TYPE == 8 ? 1088 : 576;       // one m-tile x one k-pair
   static constexpr int QB = TYPE == 8 ? 1024 : 512;          // its quant bytes (scales follow)
   static constexpr int WB = QG_TILE_MT * CHUNK;              // weights of one (tile, k-pair)
-  static constexpr int XB = NT * 1024;                       // X fragments of one k-pair
+  static constexpr int XB = XL ? 0 : NT * 1024;              // X fragments of one k-pair (streamed)
   static constexpr int STAGE = WB + XB;
   static constexpr int STAGES = TYPE == 8 ? 5 : 8;
   static constexpr int BAR_OFF = STAGES * STAGE;
-  static constexpr int SMEM = BAR_OFF + 256;
+  // local-X variant: the CTA's k-range of X fragments, resident (<= QG_XL_KP k-pairs x 4 n-tiles)
+  static constexpr int XL_OFF = BAR_OFF + 256;
+  static constexpr int XL_BYTES = XL ? QG_XL_KP * 4 * 1024 : 0;
+  static constexpr int XE_OFF = XL_OFF + XL_BYTES;  // per column: 2^-e [16] floats, scratch [16][16] floats
+  static constexpr int SMEM = XE_OFF + (XL ? 64 + 16 * 16 * 4 : 0);
   static_assert(WB % 16 == 0 && XB % 16 == 0 && STAGE % 16 == 0, "bulk copies need 16-byte multiples");
   static_assert(SMEM <= 227 * 1024, "shared memory");
 };
@@ -297,14 +313,77 @@ struct QgLayout {
 // Persistent stream-K GEMV: warps 0..15 consume (warp w owns m-tiles 2w, 2w+1
 // of the current 512-row tile); lane 0 of warp 16 streams the weights and
 // lane 0 of warp 17 the X fragments.
-template <int TYPE, int NT>
+// Local X (run by the 16 consumer warps once, after pdl_wait): the CTA's
+// k-range [64*ka0, 64*(ka0+nkp)) of every column of the raw rows X becomes
+// f16 hi/lo fragments in shared memory, scaled by the CTA's own power of two
+// 2^e (max |x| over the range in [2^14, 2^15)); xun[col] = 2^-e unscales the
+// CTA's results.  The fragments hold the same values and layout gemv_prep_x
+// emits, except for the exponent's range.  Warp b owns column b; lane l holds
+// the 32-blocks l and l + 32 of the range in registers (one load round trip),
+// so 2 * nkp <= 64.
+template <int NT>
+CW_DEV void x_local_prologue(const GemvArgs &a, uint4 *xl, float *xun, int ka0, int nkp) {
+  constexpr int NTH = QG_CONS_WARPS * 32;
+  const int lane = threadIdx.x & 31, b = threadIdx.x >> 5;
+  const int nblk = 2 * nkp;
+  if (b < a.B) {
+    const float4 *x = reinterpret_cast<const float4 *>(a.xr + (size_t)b * a.xrs + (size_t)ka0 * 64);
+    float4 v[2][8];
+    float m = 0.f;
+#pragma unroll
+    for (int j = 0; j < 2; j++) {
+      const int kb = lane + 32 * j;
+      if (kb < nblk) {
+#pragma unroll
+        for (int q = 0; q < 8; q++) v[j][q] = __ldg(x + kb * 8 + q);
+#pragma unroll
+        for (int q = 0; q < 8; q++)
+          m = fmaxf(m, fmaxf(fmaxf(fabsf(v[j][q].x), fabsf(v[j][q].y)), fmaxf(fabsf(v[j][q].z), fabsf(v[j][q].w))));
+      }
+    }
+    m = warp_max(m);
+    const int e = xfrag_exponent(m);
+    const float sc = __int_as_float((127 + e) << 23);
+    if (lane == 0) xun[b] = __int_as_float((127 - e) << 23);
+#pragma unroll
+    for (int j = 0; j < 2; j++) {
+      const int kb = lane + 32 * j;
+      if (kb < nblk) {
+        const float *r = reinterpret_cast<const float *>(v[j]);
+        // B operand lane (col & 3, t): (x[4t], x[4t+2]) (x[4t+1], x[4t+3]) (x[4t+16], x[4t+18]) (x[4t+17], x[4t+19])
+#pragma unroll
+        for (int t = 0; t < 4; t++) {
+          const int js[8] = {4 * t, 4 * t + 2, 4 * t + 1, 4 * t + 3, 4 * t + 16, 4 * t + 18, 4 * t + 17, 4 * t + 19};
+          uint32_t hw[4], lw[4];
+#pragma unroll
+          for (int i = 0; i < 4; i++) {
+            const float v0 = r[js[2 * i]] * sc, v1 = r[js[2 * i + 1]] * sc;
+            const half h0 = __float2half_rn(v0), h1 = __float2half_rn(v1);
+            const half l0 = __float2half_rn(v0 - __half2float(h0)), l1 = __float2half_rn(v1 - __half2float(h1));
+            hw[i] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
+            lw[i] = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
+          }
+          uint4 *o = xl + ((size_t)kb * NT + (b >> 2)) * 32 + (b & 3) * 4 + t;
+          o[0] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+          o[16] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+        }
+      }
+    }
+  } else if (lane == 0 && b < 16) {
+    xun[b] = 1.f;  // padding column
+  }
+  named_bar(1, NTH);
+}
+
+template <int TYPE, int NT, bool XL>
 __global__ void __launch_bounds__(QG_THREADS, 1) qgemv_kernel(GemvArgs a) {
-  using Lay = QgLayout<TYPE, NT>;
+  using Lay = QgLayout<TYPE, NT, XL>;
   constexpr int S = Lay::STAGES;
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t *full = reinterpret_cast<uint64_t *>(smem + Lay::BAR_OFF);
   uint64_t *empty = full + S;
-  volatile int *abort_p = reinterpret_cast<volatile int *>(empty + S);
+  uint64_t *xready = empty + S;  // local X: the prologue's fragments are in shared memory
+  volatile int *abort_p = reinterpret_cast<volatile int *>(xready + 1);
   int *last_p = const_cast<int *>(abort_p) + 1;  // [2]
 
   const int c = blockIdx.x;
@@ -314,9 +393,10 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemv_kernel(GemvArgs a) {
   pdl_trigger();
   if (threadIdx.x == 0) {
     for (int i = 0; i < S; i++) {
-      mbar_init(&full[i], 2);  // the weight and the X producer
+      mbar_init(&full[i], XL ? 1 : 2);  // the weight and the X producer
       mbar_init(&empty[i], QG_CONS_WARPS);
     }
+    mbar_init(xready, 1);
     *abort_p = 0;
     mbar_fence_init();
   }
@@ -329,7 +409,7 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemv_kernel(GemvArgs a) {
     // so one thread issuing both copies of a stage would cap the stream.
     // Consecutive units are consecutive (tile, k-pair) blocks of the repacked
     // weights, so the weight source just advances; no divisions in the loops.
-    if (lane == 0) {
+    if (lane == 0 && (!XL || warp == QG_CONS_WARPS)) {  // local X: no X copies
       const bool wprod = warp == QG_CONS_WARPS;
       const int n = (int)(u_end - u_begin);
       const uint8_t *wsrc = a.w + (size_t)u_begin * Lay::WB;
@@ -349,6 +429,12 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemv_kernel(GemvArgs a) {
           break;
         }
         if (*abort_p) break;  // consumers gave up: issue nothing more
+        // Local X: two weight stages go ahead, the rest after the prologue has
+        // read X -- its loads would otherwise queue behind a full ring of weights.
+        if (XL && wprod && issued == 2 && !mbar_wait(xready, 0, abort_p)) {
+          ok = false;
+          break;
+        }
         uint8_t *dst = smem + st * Lay::STAGE;
         if (wprod) {
           mbar_expect_tx(&full[st], Lay::WB);
@@ -386,6 +472,12 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemv_kernel(GemvArgs a) {
   // ---------------- consumers ----------------
   pdl_wait();  // before touching Y, the split-K partials or the tile counters
   const int g = lane >> 2, t = lane & 3;
+  const int ka0 = (int)(u_begin % a.kp);  // local X: the CTA's one segment starts here
+  float *xun = XL ? reinterpret_cast<float *>(smem + Lay::XE_OFF) : nullptr;
+  if (XL) {
+    x_local_prologue<NT>(a, reinterpret_cast<uint4 *>(smem + Lay::XL_OFF), xun, ka0, (int)(u_end - u_begin));
+    if (threadIdx.x == 0) mbar_arrive(xready);
+  }
   const float zero4[4] = {0.f, 0.f, 0.f, 0.f};
   bool ok = true;
   int st = 0;        // ring position, advanced identically by every consumer warp and the producer
@@ -419,7 +511,8 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemv_kernel(GemvArgs a) {
       }
       if (ok && has0) {
         const uint8_t *stg = smem + st * Lay::STAGE;
-        const uint4 *xs = reinterpret_cast<const uint4 *>(stg + Lay::WB);
+        const uint4 *xs = XL ? reinterpret_cast<const uint4 *>(smem + Lay::XL_OFF) + (size_t)(ka + i - ka0) * (2 * NT * 32)
+                             : reinterpret_cast<const uint4 *>(stg + Lay::WB);
         // one n-tile: both m-tiles share the X loads; more: reload (registers)
         uint4 xv1[2];
         if (NT == 1) {
@@ -474,7 +567,7 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemv_kernel(GemvArgs a) {
     fold_lo<NT>(acc);
     const bool full_tile = (ka == 0 && kb_end == a.kp);
     if (full_tile) {
-      if (ok && has0) gemv_epilogue<NT>(a, mt0, has1, acc, g, t);
+      if (ok && has0) gemv_epilogue<NT>(a, mt0, has1, acc, g, t, xun);
     } else {
       // Partial tile: park this segment's sums; the arrival count and the
       // reduction wait until this CTA's last segment, so the stream never stalls.
@@ -491,7 +584,12 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemv_kernel(GemvArgs a) {
 #pragma unroll
             for (int h = 0; h < 2; h++) {
               float *p = mine + ((warp * 2 + mt) * 16 + g + 8 * h) * 16 + n * 4 + 2 * t;
-              *reinterpret_cast<float2 *>(p) = make_float2(acc[mt][n][2 * h], acc[mt][n][2 * h + 1]);
+              float2 v = make_float2(acc[mt][n][2 * h], acc[mt][n][2 * h + 1]);
+              if (XL) {  // local exponents differ between contributors: unscale before the sum (exact)
+                v.x *= xun[n * 4 + 2 * t];
+                v.y *= xun[n * 4 + 2 * t + 1];
+              }
+              *reinterpret_cast<float2 *>(p) = v;
             }
       }
       ptile[np++] = tile;
@@ -624,9 +722,9 @@ size_t gemv_scratch_ws_floats(int G) { return (size_t)G * 2 * WS_TILE_FLOATS; }
 
 // Thread-block clusters of cl CTAs of this kernel that can be resident at once
 // (0: none / not queryable).
-template <int TYPE, int NT>
+template <int TYPE, int NT, bool XL>
 static int max_clusters(int cl) {
-  using Lay = QgLayout<TYPE, NT>;
+  using Lay = QgLayout<TYPE, NT, XL>;
   static int cache[5] = {-1, -1, -1, -1, -1};
   if (cl < 2 || cl > 4) return 0;
   if (cache[cl] < 0) {
@@ -642,7 +740,7 @@ static int max_clusters(int cl) {
     cfg.attrs = at;
     cfg.numAttrs = 1;
     int n = 0;
-    if (cudaOccupancyMaxActiveClusters(&n, qgemv_kernel<TYPE, NT>, &cfg) != cudaSuccess) {
+    if (cudaOccupancyMaxActiveClusters(&n, qgemv_kernel<TYPE, NT, XL>, &cfg) != cudaSuccess) {
       (void)cudaGetLastError();
       n = 0;
     }
@@ -651,25 +749,55 @@ static int max_clusters(int cl) {
   return cache[cl];
 }
 
-template <int TYPE, int NT>
+template <int TYPE, int NT, bool XL>
 static cudaError_t launch_t(GemvArgs a, cudaStream_t st) {
-  using Lay = QgLayout<TYPE, NT>;
+  using Lay = QgLayout<TYPE, NT, XL>;
   static bool configured = false;
   if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(qgemv_kernel<TYPE, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaError_t e = cudaFuncSetAttribute(qgemv_kernel<TYPE, NT, XL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          Lay::SMEM);
+    if (e != cudaSuccess) return e;
+    e = carveout_max(qgemv_kernel<TYPE, NT, XL>);
     if (e != cudaSuccess) return e;
     configured = true;
   }
   // Split tiles reduced inside thread-block clusters only when every tile's
   // cluster can be resident at once (the grid is one wave); the sums are the
   // same as the global path's (contributors in CTA order).
-  if (a.cl > 1 && max_clusters<TYPE, NT>(a.cl) < a.G / a.cl) a.cl = 1;
-  if (a.cl > 1) return launch_pdl_cluster(qgemv_kernel<TYPE, NT>, a.G, QG_THREADS, Lay::SMEM, st, a.cl, a);
-  return launch_pdl(qgemv_kernel<TYPE, NT>, a.G, QG_THREADS, Lay::SMEM, st, a);
+  if (a.cl > 1 && max_clusters<TYPE, NT, XL>(a.cl) < a.G / a.cl) a.cl = 1;
+  if (a.cl > 1) return launch_pdl_cluster(qgemv_kernel<TYPE, NT, XL>, a.G, QG_THREADS, Lay::SMEM, st, a.cl, a);
+  return launch_pdl(qgemv_kernel<TYPE, NT, XL>, a.G, QG_THREADS, Lay::SMEM, st, a);
 }
 
-cudaError_t gemv_run(const QMat &m, int B, float *Y, int ys, int epi, GemvScratch &s, cudaStream_t st) {
+// Grid of a GEMV: a function of the shape only (never of B), >= 4 k-pairs per
+// CTA.  When the tiles are fewer than the CTAs, a multiple of the tile count:
+// every tile is then split evenly between the same number of CTAs and every
+// CTA holds exactly one segment (one split tile at most), instead of the
+// arbitrary cuts of stream-K that give some CTAs two split tiles and two
+// reductions.
+static long long gemv_grid(const QMat &m, const GemvScratch &s, int &n_tiles, long long &units) {
+  n_tiles = (m.n_mt + QG_TILE_MT - 1) / QG_TILE_MT;
+  units = (long long)n_tiles * (m.K / 64);
+  long long g = (units + 3) / 4;
+  if (g > s.G) g = s.G;
+  if (n_tiles <= g) g = g / n_tiles * n_tiles;
+  return g;
+}
+
+// The local-X variant applies when the grid is tile-aligned and every CTA's
+// k-range holds at most QG_XL_KP k-pairs -- decided on the shape alone, so
+// that every B takes the same path (batch invariance).
+static bool gemv_local_x(const QMat &m, const GemvScratch &s) {
+  int n_tiles;
+  long long units;
+  const long long g = gemv_grid(m, s, n_tiles, units);
+  if (m.type != 2 || n_tiles > g) return false;
+  const long long ncon = g / n_tiles, kp = m.K / 64;
+  return (kp + ncon - 1) / ncon <= QG_XL_KP;
+}
+
+static cudaError_t gemv_launch(const QMat &m, int B, float *Y, int ys, int epi, GemvScratch &s, cudaStream_t st,
+                               const float *xr, int xrs) {
   if (B < 1 || B > QG_MAXB || m.K % 64 || m.K > s.kmax || !m.w || !s.err) return cudaErrorInvalidValue;
   if (epi == EPI_SWIGLU && (m.n_mt % 2)) return cudaErrorInvalidValue;
   GemvArgs a;
@@ -686,33 +814,49 @@ cudaError_t gemv_run(const QMat &m, int B, float *Y, int ys, int epi, GemvScratc
   a.ws = s.ws;
   a.cnt = s.cnt;
   a.err = s.err;
-  const int n_tiles = (m.n_mt + QG_TILE_MT - 1) / QG_TILE_MT;
+  a.xr = xr;
+  a.xrs = xrs;
+  int n_tiles;
+  const long long g = gemv_grid(m, s, n_tiles, a.units);
   if (n_tiles > s.max_tiles) return cudaErrorInvalidValue;
-  a.units = (long long)n_tiles * a.kp;
-  // Grid: a function of the shape only (never of B), >= 4 k-pairs per CTA.
-  // When the tiles are fewer than the CTAs, take a multiple of the tile count:
-  // every tile is then split evenly between the same number of CTAs and
-  // every CTA holds exactly one segment (one split tile at most), instead of
-  // the arbitrary cuts of stream-K that give some CTAs two split tiles and
-  // two reductions.
-  long long g = (a.units + 3) / 4;
-  if (g > s.G) g = s.G;
-  if (n_tiles <= g) g = g / n_tiles * n_tiles;
   a.G = (int)g;
   // 2 to 4 contributors per tile: reduce inside a thread-block cluster
   // (distributed shared memory) instead of through global scratch
   a.cl = 1;
   if (n_tiles <= g && g / n_tiles >= 2 && g / n_tiles <= 4) a.cl = (int)(g / n_tiles);
-  switch (gemv_ntiles(B) * 16 + m.type) {
-    case 16 + 8: return launch_t<8, 1>(a, st);
-    case 32 + 8: return launch_t<8, 2>(a, st);
-    case 48 + 8: return launch_t<8, 3>(a, st);
-    case 64 + 8: return launch_t<8, 4>(a, st);
-    case 16 + 2: return launch_t<2, 1>(a, st);
-    case 32 + 2: return launch_t<2, 2>(a, st);
-    case 48 + 2: return launch_t<2, 3>(a, st);
-    default: return launch_t<2, 4>(a, st);
+  const int nt = gemv_ntiles(B);
+  if (xr) {
+    switch (nt) {
+      case 1: return launch_t<2, 1, true>(a, st);
+      case 2: return launch_t<2, 2, true>(a, st);
+      case 3: return launch_t<2, 3, true>(a, st);
+      default: return launch_t<2, 4, true>(a, st);
+    }
   }
+  switch (nt * 16 + m.type) {
+    case 16 + 8: return launch_t<8, 1, false>(a, st);
+    case 32 + 8: return launch_t<8, 2, false>(a, st);
+    case 48 + 8: return launch_t<8, 3, false>(a, st);
+    case 64 + 8: return launch_t<8, 4, false>(a, st);
+    case 16 + 2: return launch_t<2, 1, false>(a, st);
+    case 32 + 2: return launch_t<2, 2, false>(a, st);
+    case 48 + 2: return launch_t<2, 3, false>(a, st);
+    default: return launch_t<2, 4, false>(a, st);
+  }
+}
+
+cudaError_t gemv_run(const QMat &m, int B, float *Y, int ys, int epi, GemvScratch &s, cudaStream_t st) {
+  return gemv_launch(m, B, Y, ys, epi, s, st, nullptr, 0);
+}
+
+bool gemv_uses_local_x(const QMat &m, const GemvScratch &s) { return gemv_local_x(m, s); }
+
+cudaError_t gemv_run_x(const QMat &m, const float *X, int xs, int B, float *Y, int ys, int epi, GemvScratch &s,
+                       cudaStream_t st) {
+  if (!X || xs < m.K) return cudaErrorInvalidValue;
+  if (gemv_local_x(m, s)) return gemv_launch(m, B, Y, ys, epi, s, st, X, xs);
+  CW_TRY(gemv_prep_x(X, xs, B, m.K, s, st));
+  return gemv_launch(m, B, Y, ys, epi, s, st, nullptr, 0);
 }
 
 // One-time kernel attributes (called at engine set-up).
@@ -720,14 +864,14 @@ cudaError_t qgemv_configure() {
   cudaError_t e;
   if ((e = carveout_max(repack_kernel<2>)) != cudaSuccess) return e;
   if ((e = carveout_max(repack_kernel<8>)) != cudaSuccess) return e;
-  if ((e = carveout_max(qgemv_kernel<2, 1>)) != cudaSuccess) return e;
-  if ((e = carveout_max(qgemv_kernel<2, 2>)) != cudaSuccess) return e;
-  if ((e = carveout_max(qgemv_kernel<2, 3>)) != cudaSuccess) return e;
-  if ((e = carveout_max(qgemv_kernel<2, 4>)) != cudaSuccess) return e;
-  if ((e = carveout_max(qgemv_kernel<8, 1>)) != cudaSuccess) return e;
-  if ((e = carveout_max(qgemv_kernel<8, 2>)) != cudaSuccess) return e;
-  if ((e = carveout_max(qgemv_kernel<8, 3>)) != cudaSuccess) return e;
-  if ((e = carveout_max(qgemv_kernel<8, 4>)) != cudaSuccess) return e;
+  if ((e = carveout_max(qgemv_kernel<2, 1, false>)) != cudaSuccess) return e;
+  if ((e = carveout_max(qgemv_kernel<2, 2, false>)) != cudaSuccess) return e;
+  if ((e = carveout_max(qgemv_kernel<2, 3, false>)) != cudaSuccess) return e;
+  if ((e = carveout_max(qgemv_kernel<2, 4, false>)) != cudaSuccess) return e;
+  if ((e = carveout_max(qgemv_kernel<8, 1, false>)) != cudaSuccess) return e;
+  if ((e = carveout_max(qgemv_kernel<8, 2, false>)) != cudaSuccess) return e;
+  if ((e = carveout_max(qgemv_kernel<8, 3, false>)) != cudaSuccess) return e;
+  if ((e = carveout_max(qgemv_kernel<8, 4, false>)) != cudaSuccess) return e;
   return cudaSuccess;
 }
 

@@ -32,6 +32,7 @@ constexpr int QG_CONS_WARPS = 16;                    // consumer warps, two m-ti
 constexpr int QG_THREADS = (QG_CONS_WARPS + 2) * 32;  // + two producer warps
 constexpr int QG_TILE_MT = 2 * QG_CONS_WARPS;         // m-tiles per CTA tile (512 rows)
 constexpr int WS_TILE_FLOATS = QG_TILE_MT * 16 * 16;   // split-K partials of one tile (16 columns)
+constexpr int QG_XL_KP = 20;  // local-X variant: at most this many k-pairs per CTA
 
 // GEMV input columns come in n-tiles of 4 (one m16n8k16 B operand holds the
 // f16 hi parts of 4 columns and their lo parts): 1 to 4 n-tiles.
@@ -66,6 +67,17 @@ cudaError_t gemv_prep_x(const float *X, int xs, int B, int K, GemvScratch &s, cu
 // GEMV over prepared X.  epi selects the output: store, add into Y
 // (residual), or SiLU(gate)*up of an interleaved gate/up matrix.
 cudaError_t gemv_run(const QMat &m, int B, float *Y, int ys, int epi, GemvScratch &s, cudaStream_t st);
+
+// GEMV over raw fp32 X [B][xs].  When the grid is tile-aligned and every
+// CTA's k-range is short (the shape decides, never B), each CTA turns its own
+// k-range of X into fragments with its own power-of-two column scale and
+// unscales its partials before the reduction -- no separate X preparation;
+// otherwise gemv_prep_x + gemv_run.
+cudaError_t gemv_run_x(const QMat &m, const float *X, int xs, int B, float *Y, int ys, int epi, GemvScratch &s,
+                       cudaStream_t st);
+// Whether gemv_run_x takes the local-X variant for this matrix (one launch) or
+// prepares X first (two).
+bool gemv_uses_local_x(const QMat &m, const GemvScratch &s);
 
 // Kernel attributes set once per process (shared-memory carveout).
 cudaError_t qgemv_configure();
