@@ -68,11 +68,18 @@ int upload_qmat_rows(int type, const void *host, int ne0, int ne1, QMat &m, int 
   return CWEN_OK;
 }
 
-cudaError_t timed_gemv(const QMat &m, int B, float *Y, int ys, int epi, cudaStream_t st, const float *X, int xs) {
+cudaError_t timed_gemv(const QMat &m, int B, float *Y, int ys, int epi, cudaStream_t st, const float *X, int xs,
+                       const float *norm_w, bool want_stats) {
   Engine &E = engine();
   Prof &P = E.prof;
-  E.prof.launches += X && !gemv_uses_local_x(m, E.gs) ? 2 : 1;
-  auto run = [&]() { return X ? gemv_run_x(m, X, xs, B, Y, ys, epi, E.gs, st) : gemv_run(m, B, Y, ys, epi, E.gs, st); };
+  if (!X) E.prof.launches += 1;
+  else if (norm_w) E.prof.launches += gemv_norm_fused(m, X, xs, B, E.gs) ? 1 : 2;
+  else E.prof.launches += gemv_uses_local_x(m, E.gs) ? 1 : 2;
+  auto run = [&]() {
+    if (!X) return gemv_run(m, B, Y, ys, epi, E.gs, st);
+    if (norm_w) return gemv_run_xn(m, X, xs, norm_w, B, Y, ys, epi, E.gs, st);
+    return gemv_run_x(m, X, xs, B, Y, ys, epi, E.gs, st, want_stats);
+  };
   if (!P.on) return run();
   if (P.used + 2 > P.ev.size()) {
     for (int i = 0; i < 256; i++) {
@@ -156,6 +163,8 @@ int cwen_cuda_init(int device, int ctx, int bmax) {
   CW_CHECK(cudaMemset(s.cnt, 0, (size_t)s.max_tiles * sizeof(int)));
   CW_CHECK(cudaMalloc(&s.err, sizeof(int)));
   CW_CHECK(cudaMemset(s.err, 0, sizeof(int)));
+  CW_CHECK(cudaMalloc(&s.stat, (size_t)160 * QG_STAT_COLS * sizeof(float)));
+  CW_CHECK(cudaMalloc(&s.stat_next, (size_t)160 * QG_STAT_COLS * sizeof(float)));
   E.live = true;
   return CWEN_OK;
 }
@@ -176,6 +185,8 @@ void cwen_cuda_shutdown(void) {
   cudaFree(E.gs.ws);
   cudaFree(E.gs.cnt);
   cudaFree(E.gs.err);
+  cudaFree(E.gs.stat);
+  cudaFree(E.gs.stat_next);
   if (E.staging) cudaFree(E.staging);
   if (E.io) cudaFree(E.io);
   cudaStreamDestroy(E.stream);

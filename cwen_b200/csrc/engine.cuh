@@ -37,9 +37,11 @@ struct Engine {
 };
 
 // GEMV over already-prepared X with optional event timing + launch counting.
-// X != nullptr: raw fp32 X [B][xs] (gemv_run_x); otherwise prepared fragments.
+// X != nullptr: raw fp32 X [B][xs] (gemv_run_x), RMSNorm(X) * norm_w with
+// norm_w (gemv_run_xn); otherwise prepared fragments.  want_stats: leave the
+// output rows' sums of squares for the next GEMV's RMSNorm.
 cudaError_t timed_gemv(const QMat &m, int B, float *Y, int ys, int epi, cudaStream_t st, const float *X = nullptr,
-                       int xs = 0);
+                       int xs = 0, const float *norm_w = nullptr, bool want_stats = false);
 
 Engine &engine();
 // CWEN_OK, or CWEN_ETIMEOUT when a GEMV gave up on a bounded wait (synchronous).

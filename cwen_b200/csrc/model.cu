@@ -268,11 +268,11 @@ static int run_layer_block(int l, int B, int pos0, cudaStream_t st) {
   LayerW &w = M.L[l];
   const int H = d.n_embd, I = d.n_ff;
   long long &nl = E.prof.launches;
-  CW_CHECK(launch_norm_prep(M.x, w.attn_norm, H, B, E.gs, nullptr, st));
-  nl++;
+  // attn_norm: inside the in_proj GEMV when the previous ffn_down left the
+  // rows' sums of squares (gemv_run_xn), else a row kernel first
   if (w.linear) {
     const int li = w.idx, nxt = M.cur ^ 1;
-    CW_CHECK(timed_gemv(w.in_proj, B, M.proj, M.PS, EPI_STORE, st));
+    CW_CHECK(timed_gemv(w.in_proj, B, M.proj, M.PS, EPI_STORE, st, M.x, H, w.attn_norm));
     GdnLayerArgs g;
     g.proj = M.proj; g.ps = M.PS; g.B = B; g.nkh = d.ssm_n_kh; g.nvh = d.ssm_n_vh;
     g.a_off = M.a_off; g.b_off = M.b_off;
@@ -285,7 +285,7 @@ static int run_layer_block(int l, int B, int pos0, cudaStream_t st) {
     nl++;
   } else {
     const int fi = w.idx;
-    CW_CHECK(timed_gemv(w.in_proj, B, M.proj, M.PS, EPI_STORE, st));
+    CW_CHECK(timed_gemv(w.in_proj, B, M.proj, M.PS, EPI_STORE, st, M.x, H, w.attn_norm));
     AttnArgs a;
     a.proj = M.proj; a.ps = M.PS; a.nh = d.n_head; a.nkv = d.n_head_kv; a.B = B;
     a.qn = w.q_norm; a.kn = w.k_norm; a.rope = M.rope; a.pos0 = pos0; a.t0 = 0;
@@ -297,7 +297,8 @@ static int run_layer_block(int l, int B, int pos0, cudaStream_t st) {
   CW_CHECK(launch_norm_prep(M.x, w.post_norm, H, B, E.gs, nullptr, st));
   nl++;
   CW_CHECK(timed_gemv(w.gate_up, B, M.h, I, EPI_SWIGLU, st));
-  CW_CHECK(timed_gemv(w.down, B, M.x, H, EPI_ADD, st, M.h, I));  // the SwiGLU rows, raw
+  // the SwiGLU rows, raw; the new residual's sums of squares for the next layer's attn_norm
+  CW_CHECK(timed_gemv(w.down, B, M.x, H, EPI_ADD, st, M.h, I, nullptr, l + 1 < d.n_layer));
   if (M.dump_on)
     CW_CHECK(cudaMemcpyAsync(M.dump + (size_t)l * E.bmax * H, M.x, (size_t)B * H * sizeof(float),
                              cudaMemcpyDeviceToDevice, st));

@@ -37,6 +37,8 @@
 // the issue cost of a bulk copy is nearly independent of its size up to
 // ~9 KB.  Every wait is bounded in time; a timeout raises an error flag and
 // the CTA finishes without touching memory further.
+#include <utility>
+
 #include "common.cuh"
 #include "qgemv.cuh"
 #include "rowops.cuh"
@@ -195,6 +197,10 @@ struct GemvArgs {
   // fragments by each CTA for its own k-range with its own column exponents
   const float *xr;
   int xrs;
+  const float *xw;     // != nullptr: X = RMSNorm(xr) * xw (run.c:346), scale from st_in
+  const float *st_in;  // sums of squares of the rows, [st_g][16] per-CTA partials of the GEMV that wrote them
+  int st_g;
+  float *st_out;       // != nullptr: this GEMV's per-CTA sums of squares of its output rows [G][16]
 };
 
 CW_DEV float silu_f(float x) { return x * (1.f / (1.f + expf(-x))); }
@@ -265,7 +271,8 @@ CW_DEV float split_unscale(const GemvArgs &a, int col) {
 // m-tile mt0 + mt, four columns per n-tile.  The whole warp calls it (the
 // SwiGLU pairs gate and up rows across the warp's halves).
 template <int NT>
-CW_DEV void split_epilogue(const GemvArgs &a, int mt0, int mt, int row, bool live, const float4 (&sum)[NT]) {
+CW_DEV void split_epilogue(const GemvArgs &a, int mt0, int mt, int row, bool live, const float4 (&sum)[NT],
+                           float *wst) {
 #pragma unroll
   for (int n = 0; n < NT; n++) {
     const float e4[4] = {sum[n].x, sum[n].y, sum[n].z, sum[n].w};
@@ -273,6 +280,16 @@ CW_DEV void split_epilogue(const GemvArgs &a, int mt0, int mt, int row, bool liv
     for (int j = 0; j < 4; j++) {
       const int col = n * 4 + j;
       if (col >= a.B) continue;
+      if (a.st_out && a.epi == EPI_ADD) {  // sums of squares of the new rows (warp order, then CTA order)
+        float v2 = 0.f;
+        const int grow = (mt0 + mt) * 16 + row;
+        if (live && grow < a.M) {
+          const float v = a.y[(size_t)col * a.ys + grow] + e4[j] * split_unscale(a, col);
+          v2 = v * v;
+        }
+        v2 = warp_sum(v2);
+        if ((threadIdx.x & 31) == 0) wst[col] += v2;
+      }
       const float sc = split_unscale(a, col);
       if (a.epi == EPI_SWIGLU) {
         const float up = __shfl_down_sync(0xffffffffu, e4[j], 16);
@@ -328,7 +345,15 @@ CW_DEV void x_local_prologue(const GemvArgs &a, uint4 *xl, float *xun, int ka0, 
   const int nblk = 2 * nkp;
   if (b < a.B) {
     const float4 *x = reinterpret_cast<const float4 *>(a.xr + (size_t)b * a.xrs + (size_t)ka0 * 64);
-    float4 v[2][8];
+    const float4 *wn = reinterpret_cast<const float4 *>(a.xw + (size_t)ka0 * 64);
+    // RMSNorm: the row's sum of squares from the per-CTA partials of the GEMV
+    // that wrote it, in slot order then a fixed xor tree (every CTA, every B)
+    float ss = 0.f;
+    if (a.xw)
+#pragma unroll
+      for (int i = 0; i < 5; i++)
+        if (lane + 32 * i < a.st_g) ss += __ldcg(a.st_in + (size_t)(lane + 32 * i) * QG_STAT_COLS + b);
+    float4 v[2][8];  // w x (RMSNorm) or x
     float m = 0.f;
 #pragma unroll
     for (int j = 0; j < 2; j++) {
@@ -336,14 +361,27 @@ CW_DEV void x_local_prologue(const GemvArgs &a, uint4 *xl, float *xun, int ka0, 
       if (kb < nblk) {
 #pragma unroll
         for (int q = 0; q < 8; q++) v[j][q] = __ldg(x + kb * 8 + q);
+        if (a.xw) {
+#pragma unroll
+          for (int q = 0; q < 8; q++) {
+            const float4 w4 = __ldg(wn + kb * 8 + q);
+            v[j][q] = make_float4(w4.x * v[j][q].x, w4.y * v[j][q].y, w4.z * v[j][q].z, w4.w * v[j][q].w);
+          }
+        }
 #pragma unroll
         for (int q = 0; q < 8; q++)
           m = fmaxf(m, fmaxf(fmaxf(fabsf(v[j][q].x), fabsf(v[j][q].y)), fmaxf(fabsf(v[j][q].z), fabsf(v[j][q].w))));
       }
     }
     m = warp_max(m);
+    float s = 1.f;
+    if (a.xw) {
+      s = 1.f / sqrtf(warp_sum(ss) / (float)(a.kp * 64) + 1e-6f);
+      m *= s;  // max |(w x) s| = max |w x| * s: s > 0 and rounding is monotonic
+    }
     const int e = xfrag_exponent(m);
-    const float sc = __int_as_float((127 + e) << 23);
+    // ((w x) s) 2^e == (w x) (s 2^e) exactly: 2^e only shifts the exponent
+    const float sc = s * __int_as_float((127 + e) << 23);
     if (lane == 0) xun[b] = __int_as_float((127 - e) << 23);
 #pragma unroll
     for (int j = 0; j < 2; j++) {
@@ -474,6 +512,8 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemv_kernel(GemvArgs a) {
   const int g = lane >> 2, t = lane & 3;
   const int ka0 = (int)(u_begin % a.kp);  // local X: the CTA's one segment starts here
   float *xun = XL ? reinterpret_cast<float *>(smem + Lay::XE_OFF) : nullptr;
+  float *wst = XL ? xun + 16 + warp * 16 : nullptr;  // this warp's output sums of squares per column
+  if (XL && a.st_out && lane < 16) wst[lane] = 0.f;
   if (XL) {
     x_local_prologue<NT>(a, reinterpret_cast<uint4 *>(smem + Lay::XL_OFF), xun, ka0, (int)(u_end - u_begin));
     if (threadIdx.x == 0) mbar_arrive(xready);
@@ -598,7 +638,7 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemv_kernel(GemvArgs a) {
     first_seg = false;
   }
 
-  if (np == 0) return;
+  if (np == 0) return;  // (sums of squares are only asked of fully split grids)
   // ---- split tiles: every contributor reduces a share of the rows ----
   // warp w's two m-tiles are reduced by contributor w % ncon: lane l sums row
   // l & 15 of m-tile l >> 4, four columns per n-tile (one float4 per
@@ -641,9 +681,15 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemv_kernel(GemvArgs a) {
           }
         }
       }
-      split_epilogue<NT>(a, mt0, mt, row, live, sum);
+      split_epilogue<NT>(a, mt0, mt, row, live, sum, wst);
     }
     cluster_sync_all();  // no CTA leaves while another reads its shared memory
+    if (XL && a.st_out && threadIdx.x < QG_STAT_COLS) {  // this CTA's slot: the warps' sums in warp order
+      const float *w0 = xun + 16;
+      float ss = 0.f;
+      for (int w = 0; w < QG_CONS_WARPS; w++) ss += w0[w * 16 + threadIdx.x];
+      a.st_out[(size_t)c * QG_STAT_COLS + threadIdx.x] = ss;
+    }
     return;
   }
   // Global mode.  All contributors of a split tile are resident (one CTA per
@@ -709,12 +755,18 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemv_kernel(GemvArgs a) {
           }
         }
       }
-      split_epilogue<NT>(a, mt0, mt, row, live, sum);
+      split_epilogue<NT>(a, mt0, mt, row, live, sum, wst);
     }
     named_bar(1, QG_CONS_WARPS * 32);  // every read of the partials of this tile is done
     if (threadIdx.x == 0 && go) {
       if (atomicAdd(a.cnt + tile, 1) == 2 * ncon - 1) a.cnt[tile] = 0;
     }
+  }
+  if (XL && a.st_out && threadIdx.x < QG_STAT_COLS) {  // this CTA's slot: the warps' sums in warp order
+    const float *w0 = xun + 16;
+    float ss = 0.f;
+    for (int w = 0; w < QG_CONS_WARPS; w++) ss += w0[w * 16 + threadIdx.x];
+    a.st_out[(size_t)c * QG_STAT_COLS + threadIdx.x] = ss;
   }
 }
 
@@ -796,8 +848,17 @@ static bool gemv_local_x(const QMat &m, const GemvScratch &s) {
   return (kp + ncon - 1) / ncon <= QG_XL_KP;
 }
 
+// Every tile split between >= 2 CTAs (each CTA one segment): the epilogue's
+// row statistics are then all taken in the split-tile reduction.
+static bool gemv_all_split(const QMat &m, const GemvScratch &s) {
+  int n_tiles;
+  long long units;
+  const long long g = gemv_grid(m, s, n_tiles, units);
+  return n_tiles <= g && g / n_tiles >= 2;
+}
+
 static cudaError_t gemv_launch(const QMat &m, int B, float *Y, int ys, int epi, GemvScratch &s, cudaStream_t st,
-                               const float *xr, int xrs) {
+                               const float *xr, int xrs, const float *norm_w = nullptr, bool want_stats = false) {
   if (B < 1 || B > QG_MAXB || m.K % 64 || m.K > s.kmax || !m.w || !s.err) return cudaErrorInvalidValue;
   if (epi == EPI_SWIGLU && (m.n_mt % 2)) return cudaErrorInvalidValue;
   GemvArgs a;
@@ -816,6 +877,16 @@ static cudaError_t gemv_launch(const QMat &m, int B, float *Y, int ys, int epi, 
   a.err = s.err;
   a.xr = xr;
   a.xrs = xrs;
+  a.xw = nullptr;
+  a.st_in = nullptr;
+  a.st_g = 0;
+  a.st_out = nullptr;
+  if (xr && norm_w) {
+    a.xw = norm_w;
+    a.st_in = s.stat;
+    a.st_g = s.stat_g;
+  }
+  if (xr && want_stats) a.st_out = s.stat_next;
   int n_tiles;
   const long long g = gemv_grid(m, s, n_tiles, a.units);
   if (n_tiles > s.max_tiles) return cudaErrorInvalidValue;
@@ -825,13 +896,25 @@ static cudaError_t gemv_launch(const QMat &m, int B, float *Y, int ys, int epi, 
   a.cl = 1;
   if (n_tiles <= g && g / n_tiles >= 2 && g / n_tiles <= 4) a.cl = (int)(g / n_tiles);
   const int nt = gemv_ntiles(B);
+  s.stat_ok = false;  // statistics describe the output of the GEMV right before
   if (xr) {
+    cudaError_t e;
     switch (nt) {
-      case 1: return launch_t<2, 1, true>(a, st);
-      case 2: return launch_t<2, 2, true>(a, st);
-      case 3: return launch_t<2, 3, true>(a, st);
-      default: return launch_t<2, 4, true>(a, st);
+      case 1: e = launch_t<2, 1, true>(a, st); break;
+      case 2: e = launch_t<2, 2, true>(a, st); break;
+      case 3: e = launch_t<2, 3, true>(a, st); break;
+      default: e = launch_t<2, 4, true>(a, st); break;
     }
+    if (e == cudaSuccess && a.st_out) {
+      std::swap(s.stat, s.stat_next);
+      s.stat_ok = true;
+      s.stat_g = a.G;
+      s.stat_y = Y;
+      s.stat_ys = ys;
+      s.stat_len = m.M;
+      s.stat_cols = B;
+    }
+    return e;
   }
   switch (nt * 16 + m.type) {
     case 16 + 8: return launch_t<8, 1, false>(a, st);
@@ -852,10 +935,25 @@ cudaError_t gemv_run(const QMat &m, int B, float *Y, int ys, int epi, GemvScratc
 bool gemv_uses_local_x(const QMat &m, const GemvScratch &s) { return gemv_local_x(m, s); }
 
 cudaError_t gemv_run_x(const QMat &m, const float *X, int xs, int B, float *Y, int ys, int epi, GemvScratch &s,
-                       cudaStream_t st) {
+                       cudaStream_t st, bool want_stats) {
   if (!X || xs < m.K) return cudaErrorInvalidValue;
-  if (gemv_local_x(m, s)) return gemv_launch(m, B, Y, ys, epi, s, st, X, xs);
+  if (gemv_local_x(m, s))
+    return gemv_launch(m, B, Y, ys, epi, s, st, X, xs, nullptr,
+                       want_stats && epi == EPI_ADD && s.stat && s.stat_next && gemv_all_split(m, s));
   CW_TRY(gemv_prep_x(X, xs, B, m.K, s, st));
+  return gemv_launch(m, B, Y, ys, epi, s, st, nullptr, 0);
+}
+
+bool gemv_norm_fused(const QMat &m, const float *X, int xs, int B, const GemvScratch &s) {
+  return gemv_local_x(m, s) && s.stat_ok && s.stat_y == X && s.stat_ys == xs && s.stat_len == m.K &&
+         s.stat_cols >= B && s.stat_g >= 1 && s.stat_g <= 160;
+}
+
+cudaError_t gemv_run_xn(const QMat &m, const float *X, int xs, const float *w, int B, float *Y, int ys, int epi,
+                        GemvScratch &s, cudaStream_t st) {
+  if (!X || !w || xs < m.K) return cudaErrorInvalidValue;
+  if (gemv_norm_fused(m, X, xs, B, s)) return gemv_launch(m, B, Y, ys, epi, s, st, X, xs, w, false);
+  CW_TRY(launch_norm_prep(X, w, m.K, B, s, nullptr, st));
   return gemv_launch(m, B, Y, ys, epi, s, st, nullptr, 0);
 }
 

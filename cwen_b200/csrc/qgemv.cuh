@@ -33,6 +33,7 @@ constexpr int QG_THREADS = (QG_CONS_WARPS + 2) * 32;  // + two producer warps
 constexpr int QG_TILE_MT = 2 * QG_CONS_WARPS;         // m-tiles per CTA tile (512 rows)
 constexpr int WS_TILE_FLOATS = QG_TILE_MT * 16 * 16;   // split-K partials of one tile (16 columns)
 constexpr int QG_XL_KP = 20;  // local-X variant: at most this many k-pairs per CTA
+constexpr int QG_STAT_COLS = 16;  // per-CTA statistics slot: one float per column
 
 // GEMV input columns come in n-tiles of 4 (one m16n8k16 B operand holds the
 // f16 hi parts of 4 columns and their lo parts): 1 to 4 n-tiles.
@@ -54,6 +55,13 @@ struct GemvScratch {
   int G = 0;             // persistent grid size (CTAs), at most one per SM
   int kmax = 0;
   int max_tiles = 0;
+  // Sums of squares of the output rows of the last GEMV, per CTA [G][16]
+  // (two buffers: a GEMV never writes the one it reads), for an RMSNorm of
+  // those rows inside the next GEMV.  Optional (nullptr: never fused).
+  float *stat = nullptr, *stat_next = nullptr;
+  bool stat_ok = false;  // stat describes the output (stat_y, stat_ys) of the GEMV right before
+  int stat_g = 0, stat_len = 0, stat_cols = 0, stat_ys = 0;
+  const float *stat_y = nullptr;
 };
 size_t gemv_scratch_ws_floats(int G);
 
@@ -73,8 +81,17 @@ cudaError_t gemv_run(const QMat &m, int B, float *Y, int ys, int epi, GemvScratc
 // k-range of X into fragments with its own power-of-two column scale and
 // unscales its partials before the reduction -- no separate X preparation;
 // otherwise gemv_prep_x + gemv_run.
+// want_stats (EPI_ADD): also leave the output rows' sums of squares for
+// gemv_run_xn of the next GEMV.
 cudaError_t gemv_run_x(const QMat &m, const float *X, int xs, int B, float *Y, int ys, int epi, GemvScratch &s,
-                       cudaStream_t st);
+                       cudaStream_t st, bool want_stats = false);
+// GEMV over RMSNorm(X) * w (run.c:346) of rows X [B][xs].  When the GEMV right
+// before wrote X with want_stats and this matrix takes the local-X variant,
+// each CTA normalises its own k-range inside the GEMV; otherwise
+// launch_norm_prep + gemv_run.  (Either way the choice is the shape's, not B's.)
+cudaError_t gemv_run_xn(const QMat &m, const float *X, int xs, const float *w, int B, float *Y, int ys, int epi,
+                        GemvScratch &s, cudaStream_t st);
+bool gemv_norm_fused(const QMat &m, const float *X, int xs, int B, const GemvScratch &s);
 // Whether gemv_run_x takes the local-X variant for this matrix (one launch) or
 // prepares X first (two).
 bool gemv_uses_local_x(const QMat &m, const GemvScratch &s);
