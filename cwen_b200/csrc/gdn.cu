@@ -2,9 +2,9 @@
 // recurrence over the B positions of a verify block, with rollback.
 //
 // Replaces conv1d_update (run.c:2183-2200), the decay/beta transform
-// (run.c:2339-2344, 2693-2699), gdn_step (run.c:2014-2180, without the
-// gated norm, which is fused into the ssm_out input prep) and the rollback
-// snapshots snap_save/snap_load (run.c:2787-2809).
+// (run.c:2339-2344, 2693-2699), gdn_step with its gated norm
+// (run.c:2014-2180) and the rollback snapshots snap_save/snap_load
+// (run.c:2787-2809).
 //
 // Rollback.  A block reads the committed state (buffer `cur`) and writes the
 // state after its last row to the other buffer.  Each row's rank-1 update
@@ -77,12 +77,20 @@ __global__ void __launch_bounds__(128) gdn_conv_kernel(const float *__restrict__
 
 // ---- the recurrence: CTA = (value head, half of the value columns),
 // 256 threads = 64 columns x 4 quarters of the key rows; each thread keeps
-// its 32x1 slice of S in registers for all B positions. ----
+// its 32x1 slice of S in registers for all B positions.  The two halves of a
+// head form a thread-block cluster of 2 for the gated RMSNorm of the head's
+// 128 outputs per row (run.c:2142-2178):
+//   out[i] = wn[i] * o[i] * rsqrt(mean_i o^2 + eps) * silu(z[i]),
+// one exchange of the halves' per-row sums of squares through distributed
+// shared memory after the last row. ----
 constexpr int GDN_T = 256;
+constexpr int GDN_MAXB = 16;
 
 __global__ void __launch_bounds__(GDN_T) gdn_recur_kernel(const float *__restrict__ Sin, float *__restrict__ Sout,
                                                           const float *__restrict__ gin, int B, int nkh, int nvh,
-                                                          float *__restrict__ out, float *__restrict__ delta) {
+                                                          float *__restrict__ out, float *__restrict__ delta,
+                                                          const float *__restrict__ z, int zs,
+                                                          const float *__restrict__ wn) {
   pdl_trigger();
   pdl_wait();
   const int hv = blockIdx.x >> 1, half = blockIdx.x & 1;
@@ -94,6 +102,8 @@ __global__ void __launch_bounds__(GDN_T) gdn_recur_kernel(const float *__restric
   __shared__ float kq[2][128];
   __shared__ float part[4][64];
   __shared__ float dl[64];
+  __shared__ float ob[GDN_MAXB][64];   // raw outputs of this half, per row
+  __shared__ float oss[GDN_MAXB];      // their sums of squares (read by the other half)
   const float *S0 = Sin + (size_t)hv * 128 * 128;
   float s[32];
 #pragma unroll
@@ -133,12 +143,32 @@ __global__ void __launch_bounds__(GDN_T) gdn_recur_kernel(const float *__restric
     __syncthreads();
     part[q4][col] = o;
     __syncthreads();
-    if (q4 == 0)
-      out[(size_t)b * nvh * 128 + hv * 128 + j] = ((part[0][col] + part[1][col]) + (part[2][col] + part[3][col])) * scale;
+    if (q4 == 0) ob[b][col] = ((part[0][col] + part[1][col]) + (part[2][col] + part[3][col])) * scale;
   }
   float *S1 = Sout + (size_t)hv * 128 * 128;
 #pragma unroll
   for (int i = 0; i < 32; i++) S1[(size_t)(q4 * 32 + i) * 128 + j] = s[i];
+  // gated RMSNorm: warp b (< 8) sums row b's 64 squares of this half (and row
+  // b + 8), then the halves' sums are added in rank order
+  namespace cg = cooperative_groups;
+  cg::cluster_group cl = cg::this_cluster();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int b = warp; b < B; b += GDN_T / 32) {
+    const float a0 = ob[b][lane], a1 = ob[b][lane + 32];
+    float ss = fmaf(a0, a0, a1 * a1);
+    ss = warp_sum(ss);
+    if (lane == 0) oss[b] = ss;
+  }
+  cl.sync();
+  const float *oth = cl.map_shared_rank(oss, half ^ 1);
+  for (int i = threadIdx.x; i < B * 64; i += GDN_T) {
+    const int b = i >> 6, c = i & 63, jj = half * 64 + c;
+    const float tot = half == 0 ? oss[b] + oth[b] : oth[b] + oss[b];
+    const float sn = 1.f / sqrtf(tot / 128.f + 1e-6f);
+    out[(size_t)b * nvh * 128 + hv * 128 + jj] =
+        wn[jj] * ob[b][c] * sn * silu_dev(z[(size_t)b * zs + hv * 128 + jj]);
+  }
+  cl.sync();  // the other half has read oss before this CTA leaves
 }
 
 // ---- rollback: replay rows 0..k (inclusive) onto the committed state in
@@ -191,7 +221,9 @@ cudaError_t launch_gdn_layer(const GdnLayerArgs &a, cudaStream_t st) {
   const int QKV = (2 * a.nkh + a.nvh) * 128;
   CW_TRY(launch_pdl(gdn_conv_kernel, QKV / 128 + 1, 128, 0, st, a.proj, a.ps, a.B, a.nkh, a.nvh, a.a_off, a.b_off, a.convw,
                                                   a.cstate_in, a.cstate_out, a.craw, a.A, a.dt, a.gin));
-  CW_TRY(launch_pdl(gdn_recur_kernel, a.nvh * 2, GDN_T, 0, st, a.S_in, a.S_out, a.gin, a.B, a.nkh, a.nvh, a.out, a.delta));
+  if (a.B < 1 || a.B > GDN_MAXB) return cudaErrorInvalidValue;
+  CW_TRY(launch_pdl_cluster(gdn_recur_kernel, a.nvh * 2, GDN_T, 0, st, 2, a.S_in, a.S_out, a.gin, a.B, a.nkh, a.nvh,
+                            a.out, a.delta, a.z, a.ps, a.wn));
   return cudaGetLastError();
 }
 

@@ -17,8 +17,10 @@ struct GdnLayerArgs {
   float *gin;              // recurrence inputs [B][QKV + 2*nvh]
   const float *S_in;       // committed state [nvh][128][128]
   float *S_out;            // state after the last row
-  float *out;              // raw head outputs S^T q / sqrt(128) [B][nvh*128]
+  float *out;              // gated-norm head outputs [B][nvh*128] (the ssm_out GEMV's rows)
   float *delta;            // per-row delta [B][nvh*128], kept for rollback
+  const float *z;          // gate rows (z of proj), stride ps
+  const float *wn;         // ssm_norm weight [128]
 };
 
 // Committed-state view of one GDN layer for the rollback replay.

@@ -279,10 +279,9 @@ static int run_layer_block(int l, int B, int pos0, cudaStream_t st) {
     g.convw = w.conv_w; g.cstate_in = M.conv[M.cur][li]; g.cstate_out = M.conv[nxt][li];
     g.craw = M.craw[li]; g.A = w.ssm_a; g.dt = w.ssm_dt; g.gin = M.gin[li];
     g.S_in = M.S[M.cur][li]; g.S_out = M.S[nxt][li]; g.out = M.gdn_out; g.delta = M.delta[li];
+    g.z = M.proj + M.QKV; g.wn = w.ssm_norm;  // gated norm of the head outputs, in the recurrence kernel
     CW_CHECK(launch_gdn_layer(g, st));
     nl += 2;
-    CW_CHECK(launch_gated_norm_prep(M.gdn_out, M.proj + M.QKV, M.PS, w.ssm_norm, d.ssm_n_vh, B, E.gs, st));
-    nl++;
   } else {
     const int fi = w.idx;
     CW_CHECK(timed_gemv(w.in_proj, B, M.proj, M.PS, EPI_STORE, st, M.x, H, w.attn_norm));
@@ -293,7 +292,9 @@ static int run_layer_block(int l, int B, int pos0, cudaStream_t st) {
     CW_CHECK(launch_attention(a, E.gs, st));
     nl += 3;
   }
-  CW_CHECK(timed_gemv(w.out_proj, B, M.x, H, EPI_ADD, st));
+  // ssm_out reads the gated-norm rows raw; wo the attention combine's fragments
+  if (w.linear) CW_CHECK(timed_gemv(w.out_proj, B, M.x, H, EPI_ADD, st, M.gdn_out, M.Z));
+  else CW_CHECK(timed_gemv(w.out_proj, B, M.x, H, EPI_ADD, st));
   CW_CHECK(launch_norm_prep(M.x, w.post_norm, H, B, E.gs, nullptr, st));
   nl++;
   CW_CHECK(timed_gemv(w.gate_up, B, M.h, I, EPI_SWIGLU, st));
