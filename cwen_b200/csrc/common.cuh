@@ -118,7 +118,7 @@ CW_DEV uint32_t lop3(uint32_t a, uint32_t b, uint32_t c) {
 // D = A(16x16 f16, row) * B(16x8 f16, col) + C, fp32 accumulate.
 CW_DEV void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
                       uint32_t b1, const float (&c)[4]) {
-  asm volatile(
+  asm(  // no side effects: the compiler may schedule it freely
       "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
       "{%10,%11,%12,%13};"
       : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])

@@ -353,24 +353,29 @@ CW_DEV void x_local_prologue(const GemvArgs &a, uint4 *xl, float *xun, int ka0, 
 #pragma unroll
       for (int i = 0; i < 5; i++)
         if (lane + 32 * i < a.st_g) ss += __ldcg(a.st_in + (size_t)(lane + 32 * i) * QG_STAT_COLS + b);
-    float4 v[2][8];  // w x (RMSNorm) or x
+    // pass 1: max |w x| (or |x|) over the range, block j = 0 kept in registers;
+    // pass 2 converts block 0 from registers and reloads block 1 (cache hits)
+    float4 v[8];
     float m = 0.f;
 #pragma unroll
     for (int j = 0; j < 2; j++) {
       const int kb = lane + 32 * j;
       if (kb < nblk) {
+        float4 u[8];
 #pragma unroll
-        for (int q = 0; q < 8; q++) v[j][q] = __ldg(x + kb * 8 + q);
+        for (int q = 0; q < 8; q++) u[q] = __ldg(x + kb * 8 + q);
         if (a.xw) {
 #pragma unroll
           for (int q = 0; q < 8; q++) {
             const float4 w4 = __ldg(wn + kb * 8 + q);
-            v[j][q] = make_float4(w4.x * v[j][q].x, w4.y * v[j][q].y, w4.z * v[j][q].z, w4.w * v[j][q].w);
+            u[q] = make_float4(w4.x * u[q].x, w4.y * u[q].y, w4.z * u[q].z, w4.w * u[q].w);
           }
         }
 #pragma unroll
-        for (int q = 0; q < 8; q++)
-          m = fmaxf(m, fmaxf(fmaxf(fabsf(v[j][q].x), fabsf(v[j][q].y)), fmaxf(fabsf(v[j][q].z), fabsf(v[j][q].w))));
+        for (int q = 0; q < 8; q++) {
+          m = fmaxf(m, fmaxf(fmaxf(fabsf(u[q].x), fabsf(u[q].y)), fmaxf(fabsf(u[q].z), fabsf(u[q].w))));
+          if (j == 0) v[q] = u[q];
+        }
       }
     }
     m = warp_max(m);
@@ -383,11 +388,22 @@ CW_DEV void x_local_prologue(const GemvArgs &a, uint4 *xl, float *xun, int ka0, 
     // ((w x) s) 2^e == (w x) (s 2^e) exactly: 2^e only shifts the exponent
     const float sc = s * __int_as_float((127 + e) << 23);
     if (lane == 0) xun[b] = __int_as_float((127 - e) << 23);
-#pragma unroll
+#pragma unroll 1
     for (int j = 0; j < 2; j++) {
       const int kb = lane + 32 * j;
       if (kb < nblk) {
-        const float *r = reinterpret_cast<const float *>(v[j]);
+        if (j == 1) {
+#pragma unroll
+          for (int q = 0; q < 8; q++) v[q] = __ldg(x + kb * 8 + q);
+          if (a.xw) {
+#pragma unroll
+            for (int q = 0; q < 8; q++) {
+              const float4 w4 = __ldg(wn + kb * 8 + q);
+              v[q] = make_float4(w4.x * v[q].x, w4.y * v[q].y, w4.z * v[q].z, w4.w * v[q].w);
+            }
+          }
+        }
+        const float *r = reinterpret_cast<const float *>(v);
         // B operand lane (col & 3, t): (x[4t], x[4t+2]) (x[4t+1], x[4t+3]) (x[4t+16], x[4t+18]) (x[4t+17], x[4t+19])
 #pragma unroll
         for (int t = 0; t < 4; t++) {
