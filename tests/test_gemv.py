@@ -43,8 +43,17 @@ def _gemv(L, wid, X, M):
     return Y
 
 
+# Work-split paths the shapes reach (one CTA per SM, 148 SMs):
+#   (2, 512, 96), (2, 1024, 48): one tile split 2 / 4 ways -> cluster reduction, local X
+#   (2, 5120, 34816): 68 tiles x 2 (gate_up) -> cluster reduction, prepared X (40 k-pairs per CTA)
+#   (2, 5120, 16480): 33 tiles x 4 (GDN in_proj) -> cluster reduction, local X
+#   (2, 17408, 5120), (2, 6144, 5120), (2, 5120, 17408): 10 / 10 / 34 tiles -> global reduction, local X
+#   (2, 512, 102400): 200 tiles > CTAs -> stream-K, prepared X
+#   (2, 256, 10240): 20 tiles, one CTA each -> no split, local X
+#   (8, ...): Q8_0 -> prepared X
 SHAPES = [(2, 512, 96), (2, 1024, 48), (8, 512, 64), (2, 5120, 64), (2, 5120, 1040), (8, 10240, 5120),
-          (2, 17408, 5120), (2, 5120, 17408), (2, 6144, 5120)]
+          (2, 17408, 5120), (2, 5120, 17408), (2, 6144, 5120), (2, 5120, 34816), (2, 5120, 16480),
+          (2, 512, 102400), (2, 256, 10240)]
 
 
 @pytest.mark.parametrize("typ,K,M", SHAPES)
@@ -73,7 +82,8 @@ def test_gemv_vs_reference_goldens(eng, orc, golden):
             assert rel_l2(got, ref) <= 1e-5, (ti, B)
 
 
-@pytest.mark.parametrize("typ,K,M", [(2, 5120, 17408), (8, 512, 64), (2, 17408, 5120)])
+@pytest.mark.parametrize("typ,K,M", [(2, 5120, 17408), (8, 512, 64), (2, 17408, 5120), (2, 5120, 34816),
+                                     (2, 5120, 16480)])
 def test_gemv_batch_invariant(eng, orc, typ, K, M):
     """Column b of a B-row call is bit-identical to a 1-row call on row b."""
     W = gen_q(orc, 5, "binv", typ, K, M)
