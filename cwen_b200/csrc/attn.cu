@@ -3,21 +3,36 @@
 // Replaces layer_full_blk's per-row head split, q/k RMSNorm, RoPE and KV
 // write (run.c:2714-2737) and attention_heads_kv (run.c:2362-2409).
 //
-// Split-K decode: the KV range [t0, pos] of a query row is cut into fixed
-// 64-slot chunks; one CTA per (kv head, chunk) scores every query row of the
-// block that reaches the chunk against one shared K/V tile in shared memory,
-// and keeps (max, sum, weighted V) per query; the combine pass merges the
-// chunks of a row in chunk order.  The chunking depends on the row's position
-// only, so a row's output does not depend on the other rows of the block.
+// Split-K decode: the KV range [t0, pos] of a query row is cut into splits of
+// S(pos) slots, the smallest power of two >= 64 with pos < 64 * S -- at most
+// 64 splits per row, so short contexts spread over many CTAs and long ones
+// leave few partials to merge.  One CTA per (kv head, slot range, row group)
+// runs an online softmax over its range in 32-slot chunks staged in shared
+// memory -- every query row of the group and every q head of the kv group
+// against one staged tile, state in registers -- and leaves (max, sum,
+// weighted V) per (row, head, split) at each of the row's split boundaries;
+// the combine pass merges a row's splits in split order.  Split boundaries
+// depend on the row's own position only (a CTA's range is S of the block's
+// last row, the largest, and holds whole splits of every smaller S), so a
+// row's output does not depend on the other rows of the block.
 #include "attn.cuh"
 #include "rowprep.cuh"
 
 namespace cw {
 
 constexpr int HD = 256;
-constexpr int ACH = 64;     // slots per chunk
+constexpr int ACH = 32;     // slots per staged chunk
+constexpr int SPS = 64;     // smallest split
+constexpr int NSPLIT = 64;  // splits per row at most
+CW_HOST_DEV int split_of(int p) {
+  int S = SPS;
+  while (p >= NSPLIT * S) S *= 2;
+  return S;
+}
 constexpr int KPAD = 260;   // padded K row (floats) in shared memory
 constexpr int PART = 4 + HD;
+constexpr int IPW = 3;      // (row, head) items per warp
+constexpr int MAXIT = 8 * IPW;
 
 // q/k RMSNorm (per head, shared 256-vector weight), RoPE on dims 0..63, KV write.
 __global__ void __launch_bounds__(HD) attn_prep_kernel(const float *__restrict__ proj, int ps, int nh, int nkv,
@@ -59,52 +74,60 @@ __global__ void __launch_bounds__(HD) attn_prep_kernel(const float *__restrict__
   else Kc[((size_t)pos * nkv + h) * HD + d] = r;
 }
 
-// Partial attention of every (row, head of kv group) against one chunk.
-// Grid (kv head, chunk, row group): rows [z*rb, z*rb + rb) of the block, so a
-// verify block spreads over rb-times more CTAs than a single row.
-__global__ void __launch_bounds__(256) attn_chunk_kernel(const float *__restrict__ qbuf, const float *__restrict__ Kc,
+// Online-softmax attention of every (row, head of the kv group) over one
+// split.  Grid (kv head, split, row group): rows [z*rb, z*rb + rb) of the
+// block (rb * G <= MAXIT items; warp w owns items w, w + 8, w + 16).
+__global__ void __launch_bounds__(256) attn_split_kernel(const float *__restrict__ qbuf, const float *__restrict__ Kc,
                                                          const float *__restrict__ Vc, int nh, int nkv, int pos0,
-                                                         int B, int t0, int nch_max, int rb, float *__restrict__ part) {
+                                                         int B, int t0, int nsp_max, int rb, int range,
+                                                         float *__restrict__ part) {
   pdl_trigger();
   pdl_wait();
   extern __shared__ float sm[];
   float *Ks = sm;                       // [ACH][KPAD]
   float *Vs = Ks + ACH * KPAD;          // [ACH][HD]
-  float *Qs = Vs + ACH * HD;            // [8 warps][HD]
-  const int hkv = blockIdx.x, c = blockIdx.y;
+  float *Qs = Vs + ACH * HD;            // [MAXIT][HD]
+  const int hkv = blockIdx.x, sp = blockIdx.y;
   const int b0 = blockIdx.z * rb, b1 = min(B, b0 + rb);
-  const int c0 = c * ACH;
-  const int last = pos0 + b1 - 1;
-  if (c0 > last) return;
-  const int tmax = min(c0 + ACH - 1, last);
-  // stage the chunk (slots beyond the last row are zero-filled and masked)
-  for (int i = threadIdx.x; i < ACH * (HD / 4); i += blockDim.x) {
-    const int t = i / (HD / 4), d4 = (i % (HD / 4)) * 4;
-    float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
-    if (c0 + t <= tmax) {
-      kv = *reinterpret_cast<const float4 *>(Kc + ((size_t)(c0 + t) * nkv + hkv) * HD + d4);
-      vv = *reinterpret_cast<const float4 *>(Vc + ((size_t)(c0 + t) * nkv + hkv) * HD + d4);
-    }
-    *reinterpret_cast<float4 *>(Ks + t * KPAD + d4) = kv;
-    *reinterpret_cast<float4 *>(Vs + t * HD + d4) = vv;
-  }
-  __syncthreads();
-  const int G = nh / nkv;
+  const int G = nh / nkv, nit = (b1 - b0) * G;
+  const int last = pos0 + b1 - 1, s0 = sp * range;
+  if (s0 > last || s0 + range - 1 < t0) return;  // no row of the group reaches the range (whole CTA)
+  const int send = min(s0 + range - 1, last);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  float *q = Qs + warp * HD;
-  const float scale = 1.f / sqrtf((float)HD);
-  for (int qi = warp; qi < (b1 - b0) * G; qi += 8) {
-    const int b = b0 + qi / G, h = hkv * G + qi % G;
-    const int p = pos0 + b;
-    if (c0 > p || c0 + ACH - 1 < t0) continue;  // warp-uniform
-    __syncwarp();
-    for (int d = lane; d < HD; d += 32) q[d] = qbuf[((size_t)b * nh + h) * HD + d];
-    __syncwarp();
-    float sc[2];
+  for (int i = threadIdx.x; i < nit * HD; i += blockDim.x) {
+    const int it = i / HD, d = i % HD;
+    Qs[i] = qbuf[((size_t)(b0 + it / G) * nh + hkv * G + it % G) * HD + d];
+  }
+  float m[IPW], l[IPW], acc[IPW][8];
 #pragma unroll
-    for (int u = 0; u < 2; u++) {
-      const int t = lane + 32 * u;
-      const float *kr = Ks + t * KPAD;
+  for (int j = 0; j < IPW; j++) {
+    m[j] = -INFINITY;
+    l[j] = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; i++) acc[j][i] = 0.f;
+  }
+  const float scale = 1.f / sqrtf((float)HD);
+  for (int c0 = s0; c0 <= send; c0 += ACH) {
+    __syncthreads();  // the previous chunk's reads (and the q stores) are done
+    for (int i = threadIdx.x; i < ACH * (HD / 4); i += blockDim.x) {
+      const int t = i / (HD / 4), d4 = (i % (HD / 4)) * 4;
+      float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
+      if (c0 + t <= send) {
+        kv = *reinterpret_cast<const float4 *>(Kc + ((size_t)(c0 + t) * nkv + hkv) * HD + d4);
+        vv = *reinterpret_cast<const float4 *>(Vc + ((size_t)(c0 + t) * nkv + hkv) * HD + d4);
+      }
+      *reinterpret_cast<float4 *>(Ks + t * KPAD + d4) = kv;
+      *reinterpret_cast<float4 *>(Vs + t * HD + d4) = vv;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int j = 0; j < IPW; j++) {
+      const int it = warp + 8 * j;
+      if (it >= nit) break;
+      const int p = pos0 + b0 + it / G;
+      if (c0 > p || c0 + ACH - 1 < t0) continue;  // warp-uniform: no slot of the chunk for this row
+      const float *q = Qs + it * HD;
+      const float *kr = Ks + lane * KPAD;
       float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
 #pragma unroll 8
       for (int d = 0; d < HD; d += 4) {
@@ -115,109 +138,111 @@ __global__ void __launch_bounds__(256) attn_chunk_kernel(const float *__restrict
         a2 = fmaf(qq.z, kk.z, a2);
         a3 = fmaf(qq.w, kk.w, a3);
       }
-      const int tt = c0 + t;
-      sc[u] = (tt >= t0 && tt <= p) ? ((a0 + a1) + (a2 + a3)) * scale : -INFINITY;
-    }
-    float m = warp_max(fmaxf(sc[0], sc[1]));
-    const float e0 = sc[0] == -INFINITY ? 0.f : expf(sc[0] - m);
-    const float e1 = sc[1] == -INFINITY ? 0.f : expf(sc[1] - m);
-    const float l = warp_sum(e0 + e1);
-    float acc[8];
+      const int tt = c0 + lane;
+      const float sc = (tt >= t0 && tt <= p) ? ((a0 + a1) + (a2 + a3)) * scale : -INFINITY;
+      const float mn = fmaxf(m[j], warp_max(sc));  // finite: the chunk holds a slot of the row
+      const float corr = m[j] == -INFINITY ? 0.f : expf(m[j] - mn);
+      const float e = sc == -INFINITY ? 0.f : expf(sc - mn);
+      l[j] = fmaf(l[j], corr, warp_sum(e));
+      m[j] = mn;
 #pragma unroll
-    for (int i = 0; i < 8; i++) acc[i] = 0.f;
-    for (int t = 0; t < ACH; t++) {
-      const float pt = __shfl_sync(0xffffffffu, t < 32 ? e0 : e1, t & 31);
-      const float4 v0 = *reinterpret_cast<const float4 *>(Vs + t * HD + lane * 8);
-      const float4 v1 = *reinterpret_cast<const float4 *>(Vs + t * HD + lane * 8 + 4);
-      acc[0] = fmaf(pt, v0.x, acc[0]);
-      acc[1] = fmaf(pt, v0.y, acc[1]);
-      acc[2] = fmaf(pt, v0.z, acc[2]);
-      acc[3] = fmaf(pt, v0.w, acc[3]);
-      acc[4] = fmaf(pt, v1.x, acc[4]);
-      acc[5] = fmaf(pt, v1.y, acc[5]);
-      acc[6] = fmaf(pt, v1.z, acc[6]);
-      acc[7] = fmaf(pt, v1.w, acc[7]);
+      for (int i = 0; i < 8; i++) acc[j][i] *= corr;
+      for (int t = 0; t < ACH; t++) {
+        const float pt = __shfl_sync(0xffffffffu, e, t);
+        const float4 v0 = *reinterpret_cast<const float4 *>(Vs + t * HD + lane * 8);
+        const float4 v1 = *reinterpret_cast<const float4 *>(Vs + t * HD + lane * 8 + 4);
+        acc[j][0] = fmaf(pt, v0.x, acc[j][0]);
+        acc[j][1] = fmaf(pt, v0.y, acc[j][1]);
+        acc[j][2] = fmaf(pt, v0.z, acc[j][2]);
+        acc[j][3] = fmaf(pt, v0.w, acc[j][3]);
+        acc[j][4] = fmaf(pt, v1.x, acc[j][4]);
+        acc[j][5] = fmaf(pt, v1.y, acc[j][5]);
+        acc[j][6] = fmaf(pt, v1.z, acc[j][6]);
+        acc[j][7] = fmaf(pt, v1.w, acc[j][7]);
+      }
     }
-    float *o = part + (((size_t)b * nh + h) * nch_max + c) * PART;
-    if (lane == 0) {
-      o[0] = m;
-      o[1] = l;
+    // the end of a row's split (or of this CTA's range): leave its partial
+#pragma unroll
+    for (int j = 0; j < IPW; j++) {
+      const int it = warp + 8 * j;
+      if (it >= nit) break;
+      const int b = b0 + it / G, S = split_of(pos0 + b);
+      if ((c0 + ACH) % S != 0 && c0 + ACH <= send) continue;
+      if (m[j] != -INFINITY) {  // the split held a slot of the row
+        float *o = part + (((size_t)b * nh + hkv * G + it % G) * nsp_max + c0 / S) * PART;
+        if (lane == 0) {
+          o[0] = m[j];
+          o[1] = l[j];
+        }
+        *reinterpret_cast<float4 *>(o + 4 + lane * 8) = make_float4(acc[j][0], acc[j][1], acc[j][2], acc[j][3]);
+        *reinterpret_cast<float4 *>(o + 4 + lane * 8 + 4) = make_float4(acc[j][4], acc[j][5], acc[j][6], acc[j][7]);
+      }
+      m[j] = -INFINITY;
+      l[j] = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; i++) acc[j][i] = 0.f;
     }
-    *reinterpret_cast<float4 *>(o + 4 + lane * 8) = make_float4(acc[0], acc[1], acc[2], acc[3]);
-    *reinterpret_cast<float4 *>(o + 4 + lane * 8 + 4) = make_float4(acc[4], acc[5], acc[6], acc[7]);
   }
 }
 
-// Merge the chunks of each (row, head), apply the sigmoid gate
-// (run.c:2396-2406) and emit the wo GEMV input.  One thread-block cluster per
-// row (blockIdx.y); each CTA owns whole heads: per head one warp turns the
-// chunk maxima into chunk weights w_c = exp(m_c - M) and l = sum l_c w_c, then
-// every element sums its chunks' weighted partials in chunk order.
-constexpr int COMB_THREADS = 256;
+// Merge the splits of each (row, head) and apply the sigmoid gate
+// (run.c:2396-2406): o = (sum_s w_s a_s) / (sum_s w_s l_s) * sigmoid(gate),
+// w_s = exp(m_s - M), splits in order.  One CTA per (head, row), one thread
+// per dimension; the rows go to the wo GEMV as raw fp32 (local X).
+constexpr int COMB_THREADS = HD;
 __global__ void __launch_bounds__(COMB_THREADS) attn_combine_kernel(const float *__restrict__ part,
                                                                    const float *__restrict__ proj, int ps, int nh,
-                                                                   int pos0, int t0, int nch_max, int nt,
-                                                                   uint4 *__restrict__ xf, int *__restrict__ xexp,
-                                                                   float *__restrict__ yout) {
+                                                                   int pos0, int t0, int nsp_max,
+                                                                   float *__restrict__ out) {
   pdl_trigger();
   pdl_wait();
-  extern __shared__ __align__(16) float sm[];
-  __shared__ float red[32], slot, linv[32];
-  const int b = blockIdx.y, r = blockIdx.x, hper = nh / gridDim.x, h0 = r * hper;
-  float *v = sm;                    // [hper][HD]
-  float *wts = sm + hper * HD;      // [hper][nch_max]
-  const int p = pos0 + b, cf = t0 / ACH, cl = p / ACH, nc = cl - cf + 1;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-  for (int hl = warp; hl < hper; hl += nw) {
-    const float *ph = part + ((size_t)b * nh + h0 + hl) * nch_max * PART;
+  extern __shared__ float wts[];  // [nsp_max]
+  __shared__ float lsum;
+  const int h = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
+  const int p = pos0 + b, S = split_of(p), sf = t0 / S, sl = p / S, ns = sl - sf + 1;
+  const float *ph = part + ((size_t)b * nh + h) * nsp_max * PART;
+  if (threadIdx.x < 32) {
+    const int lane = threadIdx.x;
     float M = -INFINITY;
-    for (int c = cf + lane; c <= cl; c += 32) M = fmaxf(M, ph[(size_t)c * PART]);
+    for (int s = sf + lane; s <= sl; s += 32) M = fmaxf(M, ph[(size_t)s * PART]);
     M = warp_max(M);
     float l = 0.f;
-    for (int c = cf + lane; c <= cl; c += 32) {
-      const float w = expf(ph[(size_t)c * PART] - M);
-      wts[hl * nch_max + (c - cf)] = w;
-      l = fmaf(ph[(size_t)c * PART + 1], w, l);
+    for (int s = sf + lane; s <= sl; s += 32) {
+      const float w = expf(ph[(size_t)s * PART] - M);
+      wts[s - sf] = w;
+      l = fmaf(ph[(size_t)s * PART + 1], w, l);
     }
     l = warp_sum(l);
-    if (lane == 0) linv[hl] = l;
+    if (lane == 0) lsum = l;
   }
   __syncthreads();
-  float mx = 0.f;
-  for (int i = threadIdx.x; i < hper * HD; i += blockDim.x) {
-    const int hl = i / HD, d = i % HD, h = h0 + hl;
-    const float *ph = part + ((size_t)b * nh + h) * nch_max * PART + 4 + d;
-    const float *wh = wts + hl * nch_max;
-    float a = 0.f;
-#pragma unroll 4
-    for (int c = 0; c < nc; c++) a = fmaf(ph[(size_t)(cf + c) * PART], wh[c], a);
-    const float o = (a / linv[hl]) * sigmoid_dev(proj[(size_t)b * ps + h * 2 * HD + HD + d]);
-    v[i] = o;
-    mx = fmaxf(mx, fabsf(o));
-    if (yout) yout[(size_t)b * nh * HD + h * HD + d] = o;
-  }
-  mx = cluster_reduce<true>(block_max(mx, red), &slot);
-  const int e = xfrag_exponent(mx);
-  if (r == 0 && threadIdx.x == 0) xexp[b] = e;
-  emit_xfrag_blocks(v, h0 * (HD / 32), hper * (HD / 32), b, nt, xf, __int_as_float((127 + e) << 23), true);
+  const float *pd = ph + (size_t)sf * PART + 4 + d;
+  float a = 0.f;
+#pragma unroll 8
+  for (int s = 0; s < ns; s++) a = fmaf(pd[(size_t)s * PART], wts[s], a);
+  out[(size_t)b * nh * HD + h * HD + d] = (a / lsum) * sigmoid_dev(proj[(size_t)b * ps + h * 2 * HD + HD + d]);
 }
 
 cudaError_t launch_attention(const AttnArgs &a, GemvScratch &s, cudaStream_t st) {
+  (void)s;
   CW_TRY(launch_pdl(attn_prep_kernel, dim3(a.nh + 2 * a.nkv, a.B), HD, 0, st, a.proj, a.ps, a.nh, a.nkv, a.qn, a.kn, a.rope, a.pos0,
                                                                a.qbuf, a.Kc, a.Vc));
   const int last = a.pos0 + a.B - 1;
-  const int nch = last / ACH + 1;
-  if (nch > a.nch_max) return cudaErrorInvalidValue;
-  const size_t smem = (size_t)(ACH * KPAD + ACH * HD + 8 * HD) * sizeof(float);
+  const int range = split_of(last);  // a CTA's slot range: the block's largest split
+  const int nsp = last / range + 1;
+  const int G = a.nh / a.nkv;
+  if (a.nch_max < NSPLIT || G > MAXIT || !a.out) return cudaErrorInvalidValue;
+  const size_t smem = (size_t)(ACH * KPAD + ACH * HD + MAXIT * HD) * sizeof(float);
   static bool configured = false;
   if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(attn_chunk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaError_t e = cudaFuncSetAttribute(attn_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     configured = true;
   }
   // Rows per CTA: split the block's rows over more CTAs only while the
-  // (kv head, chunk) grid alone is short of two CTAs per SM -- each extra row
-  // group stages the chunk's K/V again, which long contexts cannot afford.
+  // (kv head, split) grid alone is short of two CTAs per SM -- each extra row
+  // group stages the split's K/V again, which long contexts cannot afford --
+  // and at most MAXIT (row, head) items per CTA.
   static int n_sm = 0;
   if (!n_sm) {
     int dev = 0;
@@ -225,36 +250,33 @@ cudaError_t launch_attention(const AttnArgs &a, GemvScratch &s, cudaStream_t st)
     cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev);
     if (n_sm <= 0) n_sm = 148;
   }
-  const int G = a.nh / a.nkv, base = a.nkv * nch;
-  const int min_rb = G >= 8 ? 1 : 8 / G;                       // about one (row, head) item per warp
+  const int base = a.nkv * nsp;
+  const int min_rb = G >= 8 ? 1 : 8 / G;  // about one (row, head) item per warp
+  const int max_rb = MAXIT / G;
   int groups = (2 * n_sm + base - 1) / base;
   const int max_groups = (a.B + min_rb - 1) / min_rb;
   groups = groups < 1 ? 1 : (groups > max_groups ? max_groups : groups);
-  const int rb = (a.B + groups - 1) / groups;
-  CW_TRY(launch_pdl(attn_chunk_kernel, dim3(a.nkv, nch, (a.B + rb - 1) / rb), 256, smem, st, a.qbuf, a.Kc, a.Vc, a.nh,
-                    a.nkv, a.pos0, a.B, a.t0, a.nch_max, rb, a.part));
-  const int cl = cluster_split(a.nh);
-  if (a.nh / cl > 32) return cudaErrorInvalidValue;  // per-CTA heads must fit linv[32]
-  const size_t csmem = (size_t)(a.nh / cl) * (HD + a.nch_max) * sizeof(float);
-  static size_t cdone = 48 * 1024;
-  if (csmem > cdone) {
-    cudaError_t e = cudaFuncSetAttribute(attn_combine_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)csmem);
-    if (e != cudaSuccess) return e;
-    cdone = csmem;
-  }
-  CW_TRY(launch_pdl_cluster(attn_combine_kernel, dim3(cl, a.B), COMB_THREADS, csmem, st, cl, a.part, a.proj, a.ps,
-                            a.nh, a.pos0, a.t0, a.nch_max, gemv_ntiles(a.B), s.xf, s.xexp, a.yout));
+  int rb = (a.B + groups - 1) / groups;
+  if (rb > max_rb) rb = max_rb;
+  CW_TRY(launch_pdl(attn_split_kernel, dim3(a.nkv, nsp, (a.B + rb - 1) / rb), 256, smem, st, a.qbuf, a.Kc, a.Vc,
+                    a.nh, a.nkv, a.pos0, a.B, a.t0, a.nch_max, rb, range, a.part));
+  CW_TRY(launch_pdl(attn_combine_kernel, dim3(a.nh, a.B), COMB_THREADS, (size_t)a.nch_max * sizeof(float), st, a.part,
+                    a.proj, a.ps, a.nh, a.pos0, a.t0, a.nch_max, a.out));
   return cudaGetLastError();
 }
 
-int attn_chunk_slots() { return ACH; }
+// Partial slots per (row, head): at most NSPLIT splits per row.
+int attn_splits_max(int ctx) {
+  (void)ctx;
+  return NSPLIT;
+}
 size_t attn_part_floats(int bmax, int nh, int nch_max) { return (size_t)bmax * nh * nch_max * PART; }
 
 // One-time kernel attributes (called at engine set-up).
 cudaError_t attn_configure() {
   cudaError_t e;
   if ((e = carveout_max(attn_prep_kernel)) != cudaSuccess) return e;
-  if ((e = carveout_max(attn_chunk_kernel)) != cudaSuccess) return e;
+  if ((e = carveout_max(attn_split_kernel)) != cudaSuccess) return e;
   if ((e = carveout_max(attn_combine_kernel)) != cudaSuccess) return e;
   return cudaSuccess;
 }

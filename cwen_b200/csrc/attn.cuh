@@ -15,14 +15,14 @@ struct AttnArgs {
   int t0;                // first attendable slot (1 for the MTP stream)
   float *qbuf;           // [B][nh][256]
   float *Kc, *Vc;        // this layer's cache [ctx][nkv][256]
-  float *part;           // chunk partials
-  int nch_max;
-  float *yout;           // optional copy of the gated attention output [B][nh*256]
+  float *part;           // split partials [B][nh][nch_max][4 + 256]
+  int nch_max;           // partial slots per (row, head): attn_splits_max(ctx)
+  float *out;            // gated attention output [B][nh*256] (the wo GEMV's raw rows)
 };
 
-// Prep + chunked attention + combine; leaves the wo GEMV input in s.
+// Prep + split attention + combine into a.out.
 cudaError_t launch_attention(const AttnArgs &a, GemvScratch &s, cudaStream_t st);
-int attn_chunk_slots();
+int attn_splits_max(int ctx);
 size_t attn_part_floats(int bmax, int nh, int nch_max);
 
 // Kernel attributes set once per process (shared-memory carveout).

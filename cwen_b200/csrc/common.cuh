@@ -7,6 +7,7 @@
 #include <utility>
 
 #define CW_DEV __device__ __forceinline__
+#define CW_HOST_DEV __host__ __device__ __forceinline__
 
 namespace cw {
 

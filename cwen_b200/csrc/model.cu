@@ -58,6 +58,7 @@ void model_free() {
   F(T.attn_norm); F(T.post_norm); F(T.q_norm); F(T.k_norm); F(T.enorm); F(T.hnorm); F(T.shared_head_norm);
   free_qmat(T.eh_proj); free_qmat(T.in_proj); free_qmat(T.out_proj); free_qmat(T.gate_up); free_qmat(T.down);
   F(M.x); F(M.proj); F(M.gdn_out); F(M.h); F(M.qbuf); F(M.attn_part); F(M.logits); F(M.best); F(M.walk);
+  F(M.attn_o);
   F(M.toks); F(M.err); F(M.rope); F(M.dump); F(M.replay[0]); F(M.replay[1]);
   for (int i = 0; i < 2; i++) {
     for (auto p : M.S[i]) F(p);
@@ -208,8 +209,9 @@ static int alloc_state() {
       (rc = A(M.gdn_out, (size_t)bm * M.Z)) || (rc = A(M.h, (size_t)bm * I)) ||
       (rc = A(M.qbuf, (size_t)bm * d.n_head * d.head_dim)) || (rc = A(M.logits, (size_t)bm * V)))
     return rc;
-  M.nch_max = (ctx + attn_chunk_slots() - 1) / attn_chunk_slots();
+  M.nch_max = attn_splits_max(ctx);
   if ((rc = A(M.attn_part, attn_part_floats(bm, d.n_head, M.nch_max)))) return rc;
+  if ((rc = A(M.attn_o, (size_t)bm * d.n_head * 256))) return rc;
   CW_CHECK(cudaMalloc(&M.best, (size_t)bm * sizeof(unsigned long long)));
   CW_CHECK(cudaMalloc(&M.walk, (size_t)(bm + 2) * sizeof(int)));
   CW_CHECK(cudaMalloc(&M.toks, (size_t)bm * sizeof(int)));
@@ -288,13 +290,13 @@ static int run_layer_block(int l, int B, int pos0, cudaStream_t st) {
     AttnArgs a;
     a.proj = M.proj; a.ps = M.PS; a.nh = d.n_head; a.nkv = d.n_head_kv; a.B = B;
     a.qn = w.q_norm; a.kn = w.k_norm; a.rope = M.rope; a.pos0 = pos0; a.t0 = 0;
-    a.qbuf = M.qbuf; a.Kc = M.Kc[fi]; a.Vc = M.Vc[fi]; a.part = M.attn_part; a.nch_max = M.nch_max; a.yout = nullptr;
+    a.qbuf = M.qbuf; a.Kc = M.Kc[fi]; a.Vc = M.Vc[fi]; a.part = M.attn_part; a.nch_max = M.nch_max; a.out = M.attn_o;
     CW_CHECK(launch_attention(a, E.gs, st));
     nl += 3;
   }
-  // ssm_out reads the gated-norm rows raw; wo the attention combine's fragments
+  // ssm_out reads the gated-norm rows raw, wo the attention combine's rows
   if (w.linear) CW_CHECK(timed_gemv(w.out_proj, B, M.x, H, EPI_ADD, st, M.gdn_out, M.Z));
-  else CW_CHECK(timed_gemv(w.out_proj, B, M.x, H, EPI_ADD, st));
+  else CW_CHECK(timed_gemv(w.out_proj, B, M.x, H, EPI_ADD, st, M.attn_o, d.n_head * 256));
   CW_CHECK(launch_norm_prep(M.x, w.post_norm, H, B, E.gs, nullptr, st));
   nl++;
   CW_CHECK(timed_gemv(w.gate_up, B, M.h, I, EPI_SWIGLU, st));
@@ -329,9 +331,9 @@ static int mtp_step_dev(int pos0, int B, const Toks16 &toks, const int *dtok, co
   AttnArgs a;
   a.proj = M.proj; a.ps = M.PS; a.nh = d.n_head; a.nkv = d.n_head_kv; a.B = B;
   a.qn = w.q_norm; a.kn = w.k_norm; a.rope = M.rope; a.pos0 = pos0; a.t0 = 1;  // the nextn stream starts at slot 1
-  a.qbuf = M.qbuf; a.Kc = M.mtp_K; a.Vc = M.mtp_V; a.part = M.attn_part; a.nch_max = M.nch_max; a.yout = nullptr;
+  a.qbuf = M.qbuf; a.Kc = M.mtp_K; a.Vc = M.mtp_V; a.part = M.attn_part; a.nch_max = M.nch_max; a.out = M.attn_o;
   CW_CHECK(launch_attention(a, E.gs, st));
-  CW_CHECK(timed_gemv(w.out_proj, B, M.mtp_x, H, EPI_ADD, st));
+  CW_CHECK(timed_gemv(w.out_proj, B, M.mtp_x, H, EPI_ADD, st, M.attn_o, d.n_head * 256));
   CW_CHECK(launch_norm_prep(M.mtp_x, w.post_norm, H, B, E.gs, nullptr, st));
   CW_CHECK(timed_gemv(w.gate_up, B, M.h, I, EPI_SWIGLU, st));
   CW_CHECK(timed_gemv(w.down, B, M.mtp_x, H, EPI_ADD, st, M.h, I));

@@ -51,6 +51,7 @@ struct Model {
   int pending_nlog = 0;
   float *x = nullptr, *proj = nullptr, *gdn_out = nullptr, *h = nullptr, *qbuf = nullptr;
   float *attn_part = nullptr;
+  float *attn_o = nullptr;  // gated attention output rows [bmax][n_head*256]
   int nch_max = 0;
   float *logits = nullptr;
   unsigned long long *best = nullptr;
