@@ -168,56 +168,6 @@ cudaError_t launch_row_prep(const float *x, int xs, int K, int B, GemvScratch &s
   return cudaGetLastError();
 }
 
-// ---- GDN gated RMSNorm (run.c:2142-2178) fused with ssm_out input prep ----
-// o: raw GDN output [B][nvh*128] (S^T q / sqrt(128)); z: gate rows (stride zs).
-// out[h][i] = wn[i] * o[h][i] * rsqrt(mean_i o^2 + eps) * silu(z[h][i]).
-// Each CTA of the cluster owns whole heads.
-__global__ void __launch_bounds__(ROW_THREADS) gated_norm_prep_kernel(const float *__restrict__ o,
-                                                                      const float *__restrict__ z, int zs,
-                                                                      const float *__restrict__ wn, int nvh, int nt,
-                                                                      uint4 *__restrict__ xf,
-                                                                      int *__restrict__ xexp) {
-  pdl_trigger();
-  pdl_wait();
-  extern __shared__ __align__(16) float v[];
-  __shared__ float red[32], slot;
-  const int b = blockIdx.y, r = blockIdx.x, hper = nvh / gridDim.x, h0 = r * hper;
-  const int K = nvh * 128;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-  float mx = 0.f;
-  for (int hl = warp; hl < hper; hl += nw) {
-    const int h = h0 + hl;
-    const float *oh = o + (size_t)b * K + h * 128;
-    float t[4], ss = 0.f;
-#pragma unroll
-    for (int i = 0; i < 4; i++) {
-      t[i] = oh[lane + 32 * i];
-      ss = fmaf(t[i], t[i], ss);
-    }
-    ss = warp_sum(ss);
-    const float s = 1.f / sqrtf(ss / 128.f + 1e-6f);
-#pragma unroll
-    for (int i = 0; i < 4; i++) {
-      const int j = lane + 32 * i;
-      const float val = wn[j] * t[i] * s * silu_dev(z[(size_t)b * zs + h * 128 + j]);
-      v[hl * 128 + j] = val;
-      mx = fmaxf(mx, fabsf(val));
-    }
-  }
-  mx = cluster_reduce<true>(block_max(mx, red), &slot);
-  const int e = xfrag_exponent(mx);
-  if (r == 0 && threadIdx.x == 0) xexp[b] = e;
-  emit_xfrag_blocks(v, h0 * 4, hper * 4, b, nt, xf, __int_as_float((127 + e) << 23), true);
-}
-
-cudaError_t launch_gated_norm_prep(const float *o, const float *z, int zs, const float *wn, int nvh, int B,
-                                   GemvScratch &s, cudaStream_t st) {
-  const int cl = cluster_split(nvh);
-  CW_TRY(launch_pdl_cluster(gated_norm_prep_kernel, dim3(cl, B), ROW_THREADS, (size_t)(nvh / cl) * 128 * sizeof(float),
-                            st, cl, o, z, zs, wn, nvh, gemv_ntiles(B), s.xf, s.xexp));
-  return cudaGetLastError();
-}
-
 // ---- argmax (argmax_of run.c:2647): first maximum over n logits per row ----
 // Packed key: order-preserving float bits in the high word, ~index in the low
 // word, so a 64-bit max picks the largest value and, among equal values, the
@@ -277,7 +227,6 @@ cudaError_t rowops_configure() {
   if ((e = carveout_max(embed_kernel)) != cudaSuccess) return e;
   if ((e = carveout_max(norm_prep_kernel)) != cudaSuccess) return e;
   if ((e = carveout_max(row_prep_kernel)) != cudaSuccess) return e;
-  if ((e = carveout_max(gated_norm_prep_kernel)) != cudaSuccess) return e;
   if ((e = carveout_max(argmax_kernel)) != cudaSuccess) return e;
   if ((e = carveout_max(walk_kernel)) != cudaSuccess) return e;
   if ((e = carveout_max(cat_norm_prep_kernel)) != cudaSuccess) return e;

@@ -23,9 +23,6 @@ cudaError_t launch_norm_prep(const float *x, const float *w, int H, int B, GemvS
                              cudaStream_t st);
 // rows x [B][xs], first K values -> GEMV input.
 cudaError_t launch_row_prep(const float *x, int xs, int K, int B, GemvScratch &s, cudaStream_t st);
-// GDN gated norm of o [B][nvh*128] with gate z (row stride zs) -> GEMV input.
-cudaError_t launch_gated_norm_prep(const float *o, const float *z, int zs, const float *wn, int nvh, int B,
-                                   GemvScratch &s, cudaStream_t st);
 // First-max argmax of B rows of logits (row stride ldl) and the greedy walk
 // against blk[0..E]: res = [k, ustar, argmax rows...].
 cudaError_t launch_argmax_walk(const float *lg, int n, int ldl, int B, int E, const Toks16 &blk,
