@@ -6,7 +6,9 @@ seeds plus the reference outputs as small .npz files.  Inputs are
 regenerated at test time from the same seeds with the synth generator
 (cwen_b200/host/synth.c), so only outputs need storing.
 
-Run here (where /root/reference exists):  python tests/golden/make_golden.py
+Run where the reference sources are available (oracle/build_ref.sh takes
+their directory as its argument or CWEN_REFERENCE_DIR):
+    python tests/golden/make_golden.py
 """
 from __future__ import annotations
 
