@@ -1,7 +1,7 @@
 """Benchmark of the cwen B200 verify-decode engine (one JSON line on rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload decode|gemv|mtp]
+                    [--workload decode|gemv|mtp|gdn]
 
 Workload `decode` (default; BASELINE configs 2 and 3): the random-init 27B
 hybrid (64 layers, Q4_0 weights with scales |N(0,0.01)|, norms 1, seeded),
@@ -16,6 +16,11 @@ Workload `gemv`: the B=8 Q4_0 verify GEMV, W 17408x5120,
 X fp32 8x5120 ~N(0,1), scales |N(0,0.01)|, nibbles uniform.  A step is one
 call over a weight copy from a ring of 8 distinct copies (400 MB > 126 MB L2),
 so every step streams W from HBM.  value = algorithmic bytes / device time.
+
+Workload `gdn`: one GatedDeltaNet layer's verify block
+(B=8 rows) and the rollback to a rejection index uniform in 0..8, through
+cwen_cuda_gdn_verify, over a ring of 64 layers' states (253 MB > L2).
+value = us per step (CUDA events).
 
 Workload `mtp`: the hybrid plus the blk.64 MTP block,
 a 32767-id prefill, 256 new tokens drafted by the MTP head and verified;
@@ -555,20 +560,233 @@ def main_mtp(args, ws, rank, local):
     return 0
 
 
+
+# ---------------- config 1: GatedDeltaNet verify step with rollback ----------------
+GDN_NKH, GDN_NVH, GDN_D, GDN_B = 16, 48, 128, 8
+GDN_QKV = (2 * GDN_NKH + GDN_NVH) * GDN_D        # 10240 conv channels
+GDN_Z = GDN_NVH * GDN_D                          # 6144
+GDN_PS = GDN_QKV + GDN_Z + 2 * GDN_NVH           # proj row: q|k|v|z|alpha|beta
+GDN_S = GDN_NVH * GDN_D * GDN_D                  # 786,432 floats = 3,145,728 B
+GDN_RING = 64                                    # distinct layers: 64 x 3.96 MB = 253 MB > 126 MB L2
+GDN_SEED = 11
+
+
+def gdn_min_bytes(keep: int) -> int:
+    """Bytes a verify step must move at least: the block's input rows, the
+    committed state and the conv weights read once, the head outputs written
+    once, and the committed state written once when rows are kept."""
+    rd = GDN_B * GDN_PS * 4 + GDN_S * 4 + GDN_QKV * 3 * 4 + GDN_QKV * 4 * 4 + (2 * GDN_NVH + GDN_D) * 4
+    wr = GDN_B * GDN_Z * 4 + ((GDN_S + GDN_QKV * 3) * 4 if keep > 0 else 0)
+    return rd + wr
+
+
+def gdn_keeps(n: int) -> np.ndarray:
+    """Rejection indices uniform in 0..8 (rows kept of the 8-row block)."""
+    return np.random.default_rng(GDN_SEED).integers(0, GDN_B + 1, size=n)
+
+
+def make_gdn_layer(i: int):
+    """One layer's seeded inputs (config 1): state ~N(0, 0.1), conv state and
+    block rows ~N(0, 1) (q, k, v, z, alpha, beta; the kernel L2-normalises q
+    and k after the conv and applies decay = exp(-softplus(alpha)), beta =
+    sigmoid(beta): A = -1, dt = 0), conv weights ~N(0, 0.1), norm 1."""
+    import cwen_b200
+    sd = GDN_SEED * 1000 + i
+    return {"proj": cwen_b200.synth_normal(sd, "bench.gdn.proj", GDN_B * GDN_PS).reshape(GDN_B, GDN_PS),
+            "convw": cwen_b200.synth_normal(sd, "bench.gdn.convw", GDN_QKV * 4, 0.0, 0.1),
+            "S": cwen_b200.synth_normal(sd, "bench.gdn.S", GDN_S, 0.0, 0.1),
+            "conv": cwen_b200.synth_normal(sd, "bench.gdn.conv", GDN_QKV * 3)}
+
+
+def cpu_gdn_baseline(budget_s: float = 12.0):
+    """The reference's own kernels on the same step: for each of the 8 rows
+    decay/beta (run.c:2339-2344), conv1d_update + gdn_step (run.c:2183-2200,
+    2014-2180) and a snapshot of the state (the snap_save copy, run.c:2787),
+    then the state restored from the snapshot at the rejection index
+    (snap_load, run.c:2802).  Bounded by a time budget; all host cores."""
+    path, variant = ref_lib_path()
+    if not path.exists():
+        return None
+    os.environ.setdefault("OMP_NUM_THREADS", str(host_cores()))
+    os.environ.setdefault("OMP_PROC_BIND", "close")
+    os.environ.setdefault("OMP_PLACES", "cores")
+    ref = C.CDLL(str(path))
+    ref.cwref_threads.restype = C.c_int
+    vp = lambda a: a.ctypes.data_as(C.c_void_p)
+    lay = make_gdn_layer(0)
+    S, cs = lay["S"].copy(), lay["conv"].copy()
+    cw, nw = lay["convw"], np.ones(GDN_D, np.float32)
+    A, dt = -np.ones(GDN_NVH, np.float32), np.zeros(GDN_NVH, np.float32)
+    snapS = np.zeros((GDN_B + 1, GDN_S), np.float32)
+    snapC = np.zeros((GDN_B + 1, GDN_QKV * 3), np.float32)
+    out = np.zeros((GDN_B, GDN_Z), np.float32)
+    keeps = gdn_keeps(100000)
+
+    def step(keep):
+        snapS[0] = S
+        snapC[0] = cs
+        for b in range(GDN_B):
+            row = lay["proj"][b]
+            qkv = row[:GDN_QKV].copy()
+            z = row[GDN_QKV:GDN_QKV + GDN_Z].copy()
+            a = row[GDN_QKV + GDN_Z:GDN_QKV + GDN_Z + GDN_NVH].copy()
+            bt = row[GDN_QKV + GDN_Z + GDN_NVH:].copy()
+            ref.cwref_decay_beta(vp(A), vp(dt), vp(a), vp(bt), GDN_NVH)
+            ref.cwref_gdn_step(vp(S), vp(cs), vp(cw), vp(nw), vp(qkv), vp(z), vp(a), vp(bt), vp(out[b]))
+            snapS[b + 1] = S
+            snapC[b + 1] = cs
+        S[:] = snapS[keep]
+        cs[:] = snapC[keep]
+
+    step(int(keeps[0]))
+    n, t0 = 0, time.perf_counter()
+    while True:
+        step(int(keeps[n % len(keeps)]))
+        n += 1
+        el = time.perf_counter() - t0
+        if el > budget_s or n >= 20000:
+            break
+    us = el / n * 1e6
+    return us, {"kind": "reference", "cores": int(ref.cwref_threads()), "variant": variant,
+                "sample": f"{n} config-1 verify steps (8 rows of conv1d_update + gdn_step, 9 state snapshots, "
+                          f"restore at the rejection index) in {el:.1f} s"}
+
+
+def main_gdn(args, ws, rank, local):
+    """BASELINE config 1.  A step is one layer's verify block (B = 8 rows:
+    conv + decay/beta + recurrence with the gated norm) followed by the
+    rollback to a rejection index uniform in 0..8, through
+    cwen_cuda_gdn_verify on device buffers, over a ring of 64 layers' states
+    (253 MB > 126 MB L2) so every step reads its state from HBM."""
+    metric = "GDN verify step with rollback, us per step (config 1)"
+    config = {"workload": "config1: GatedDeltaNet verify step, 48 value / 16 key heads x 128, B=8, "
+                          "state ~N(0,0.1), rejection index uniform 0..8",
+              "B": GDN_B, "heads": [GDN_NVH, GDN_NKH], "head_dim": GDN_D, "conv_channels": GDN_QKV,
+              "l2": "ring of 64 layers' states and inputs (253 MB > 126 MB L2), next layer every step",
+              "parallelism": f"replicas{ws}" if ws > 1 else "single"}
+    if args.impl == "reference":
+        if rank != 0:
+            return 0
+        res = cpu_gdn_baseline(budget_s=max(4.0, min(60.0, 1.0 * args.steps)))
+        if res is None:
+            print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref reference build missing"}))
+            return 0
+        us, info = res
+        print(json.dumps({"impl": "reference", "metric": metric, "value": round(us, 3), "unit": "us",
+                          "n_gpus": 0, "steps": args.steps, "warmup": args.warmup,
+                          "ms_per_step": round(us / 1000.0, 5), "higher_is_better": False, "scaling": "weak",
+                          "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)", "config": config,
+                          "cpu_baseline": {**info, "value": round(us, 3), "unit": "us"},
+                          "e2e": {"value": round(us, 3), "unit": "us", "h2d_bytes_per_step": 0,
+                                  "d2h_bytes_per_step": 0}}))
+        return 0
+    import torch
+
+    import cwen_b200
+    from cwen_b200 import build
+    build.build()
+    L = cwen_b200.lib()
+    cwen_b200.check(L.cwen_cuda_init(local, 64, 16), "init")
+    hbm, _, peak_kind = peaks()
+    dev = torch.device("cuda", local)
+    layers = []
+    for i in range(GDN_RING):
+        lay = make_gdn_layer(i)
+        layers.append({k: torch.from_numpy(np.ascontiguousarray(v)).to(dev) for k, v in lay.items()})
+    A = torch.full((GDN_NVH,), -1.0, dtype=torch.float32, device=dev)
+    dt = torch.zeros(GDN_NVH, dtype=torch.float32, device=dev)
+    wn = torch.ones(GDN_D, dtype=torch.float32, device=dev)
+    out = torch.zeros((GDN_B, GDN_Z), dtype=torch.float32, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+    sp = C.c_void_p(stream.cuda_stream)
+    P = lambda x: C.c_void_p(x.data_ptr())
+    n_all = args.warmup + 2 * args.steps
+    keeps = gdn_keeps(n_all)
+
+    def step(i, proj=None):
+        lay = layers[i % GDN_RING]
+        cwen_b200.check(L.cwen_cuda_gdn_verify(GDN_NKH, GDN_NVH, GDN_B, P(lay["proj"] if proj is None else proj),
+                                               GDN_PS, P(lay["convw"]), P(A), P(dt), P(wn), P(lay["S"]),
+                                               P(lay["conv"]), int(keeps[i]), P(out), sp), "gdn_verify")
+
+    with torch.cuda.stream(stream):
+        for i in range(args.warmup):
+            step(i)
+    torch.cuda.synchronize()
+    barrier(ws)
+    clocks = ClockSampler(local)
+    clocks.start()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    idx = range(args.warmup, args.warmup + args.steps)
+    torch.cuda.nvtx.range_push("bench_timed")
+    ev0.record(stream)
+    for i in idx:
+        step(i)
+    ev1.record(stream)
+    torch.cuda.nvtx.range_pop()
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = ev0.elapsed_time(ev1) / args.steps
+    ms = barrier_max(ws, ms)
+    kk = [int(keeps[i]) for i in idx]
+    launches = sum(2 + (1 if 0 < k < GDN_B else 0) for k in kk)
+    min_bytes = sum(gdn_min_bytes(k) for k in kk) / args.steps
+    ach = min_bytes / (ms * 1e-3) / 1e9
+
+    # end to end: the block's rows from pinned host memory in, the head
+    # outputs back to host memory, every step (the state stays resident)
+    hproj = [torch.from_numpy(make_gdn_layer(i)["proj"]).pin_memory() for i in range(4)]
+    hout = torch.zeros((GDN_B, GDN_Z), dtype=torch.float32).pin_memory()
+    dproj = torch.empty((GDN_B, GDN_PS), dtype=torch.float32, device=dev)
+    torch.cuda.synchronize()
+    e0 = args.warmup + args.steps
+    t0 = time.perf_counter()
+    with torch.cuda.stream(stream):
+        for j, i in enumerate(range(e0, e0 + args.steps)):
+            dproj.copy_(hproj[j % 4], non_blocking=True)
+            step(i, dproj)
+            hout.copy_(out, non_blocking=True)
+            stream.synchronize()
+    e2e_s = (time.perf_counter() - t0) / args.steps
+    e2e_s = barrier_max(ws, e2e_s)
+    L.cwen_cuda_shutdown()
+    line = {"metric": metric, "value": round(ms * 1000.0, 3), "unit": "us", "n_gpus": ws, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": False, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)", "config": config,
+            "gpu_launches": launches, "clocks": clk,
+            "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": hbm, "unit": "GB/s",
+                         "frac": round(ach / hbm, 4), "peak_kind": peak_kind, "traffic": None,
+                         "kernel": "gdn_conv_kernel + gdn_recur_kernel (+ gdn_replay_kernel or a state copy)",
+                         "bytes_per_step": round(min_bytes),
+                         "bytes_note": "minimum bytes of the step (inputs, state and conv weights read once, "
+                                       "outputs written once, committed state written once when rows are kept); "
+                                       "the reference's per-position snapshots would add 8 state copies"},
+            "e2e": {"value": round(e2e_s * 1e6, 3), "unit": "us", "h2d_bytes_per_step": GDN_B * GDN_PS * 4,
+                    "d2h_bytes_per_step": GDN_B * GDN_Z * 4,
+                    "note": "pinned host rows in, head outputs out, stream synchronized every step"}}
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+        res = cpu_gdn_baseline()
+        if res:
+            line["cpu_baseline"] = {**res[1], "value": round(res[0], 3), "unit": "us"}
+    if rank == 0:
+        print(json.dumps(line))
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=32)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="decode", choices=["decode", "gemv", "mtp"])
+    ap.add_argument("--workload", default="decode", choices=["decode", "gemv", "mtp", "gdn"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     ws, rank, local = dist_init(args)
-    if args.workload in ("decode", "mtp"):
-        rc = (main_decode if args.workload == "decode" else main_mtp)(args, ws, rank, local)
+    if args.workload in ("decode", "mtp", "gdn"):
+        rc = {"decode": main_decode, "mtp": main_mtp, "gdn": main_gdn}[args.workload](args, ws, rank, local)
         if ws > 1:
             import torch.distributed as dist
             dist.destroy_process_group()

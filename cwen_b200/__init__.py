@@ -45,6 +45,9 @@ _SIGS = {
     "cwen_cuda_gemvb": (C.c_int, [C.c_int, C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_int, C.c_void_p]),
     "cwen_cuda_gemvb_static": (C.c_int, [C.c_int, C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_int, C.c_void_p]),
     "cwen_cuda_gemvb_host": (C.c_int, [C.c_int, C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_int]),
+    "cwen_cuda_gdn_verify": (C.c_int, [C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p,
+                                       C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_void_p,
+                                       C.c_void_p]),
     "cwen_cuda_model_config": (C.c_int, [C.POINTER(Dims)]),
     "cwen_cuda_upload": (C.c_int, [C.c_char_p, C.c_int, C.c_void_p, C.c_int, C.c_int]),
     "cwen_cuda_model_finalize": (C.c_int, []),

@@ -177,6 +177,7 @@ void cwen_cuda_shutdown(void) {
   if (!E.live) return;
   cudaStreamSynchronize(E.stream);
   model_free();
+  gdn_verify_free();
   for (auto &m : E.mats) cudaFree(m.w);
   E.mats.clear();
   for (auto e : E.prof.ev) cudaEventDestroy(e);

@@ -84,7 +84,6 @@ __global__ void __launch_bounds__(128) gdn_conv_kernel(const float *__restrict__
 // one exchange of the halves' per-row sums of squares through distributed
 // shared memory after the last row. ----
 constexpr int GDN_T = 256;
-constexpr int GDN_MAXB = 16;
 
 __global__ void __launch_bounds__(GDN_T) gdn_recur_kernel(const float *__restrict__ Sin, float *__restrict__ Sout,
                                                           const float *__restrict__ gin, int B, int nkh, int nvh,
@@ -174,11 +173,7 @@ __global__ void __launch_bounds__(GDN_T) gdn_recur_kernel(const float *__restric
 // ---- rollback: replay rows 0..k (inclusive) onto the committed state in
 // place; conv state <- last three raw inputs. One CTA per (layer, head, half)
 // for S, plus conv CTAs. ----
-__global__ void __launch_bounds__(GDN_T) gdn_replay_kernel(GdnLayerPtrs *__restrict__ lp, int k, int nkh, int nvh) {
-  pdl_trigger();
-  pdl_wait();
-  const int layer = blockIdx.y;
-  const GdnLayerPtrs P = lp[layer];
+__device__ __forceinline__ void replay_layer(const GdnLayerPtrs &P, int k, int nkh, int nvh) {
   const int QKV = (2 * nkh + nvh) * 128;
   const int GS = QKV + 2 * nvh;
   const int nS = nvh * 2;
@@ -217,11 +212,26 @@ __global__ void __launch_bounds__(GDN_T) gdn_replay_kernel(GdnLayerPtrs *__restr
   for (int i = 0; i < 32; i++) S[(size_t)(q4 * 32 + i) * 128 + j] = s[i];
 }
 
+// Every linear layer of the model (layer = blockIdx.y) from a device table.
+__global__ void __launch_bounds__(GDN_T) gdn_replay_kernel(GdnLayerPtrs *__restrict__ lp, int k, int nkh, int nvh) {
+  pdl_trigger();
+  pdl_wait();
+  const GdnLayerPtrs P = lp[blockIdx.y];
+  replay_layer(P, k, nkh, nvh);
+}
+
+// One layer whose pointers come as a kernel parameter (no table to upload).
+__global__ void __launch_bounds__(GDN_T) gdn_replay1_kernel(const GdnLayerPtrs P, int k, int nkh, int nvh) {
+  pdl_trigger();
+  pdl_wait();
+  replay_layer(P, k, nkh, nvh);
+}
+
 cudaError_t launch_gdn_layer(const GdnLayerArgs &a, cudaStream_t st) {
   const int QKV = (2 * a.nkh + a.nvh) * 128;
+  if (a.B < 1 || a.B > GDN_MAXB) return cudaErrorInvalidValue;
   CW_TRY(launch_pdl(gdn_conv_kernel, QKV / 128 + 1, 128, 0, st, a.proj, a.ps, a.B, a.nkh, a.nvh, a.a_off, a.b_off, a.convw,
                                                   a.cstate_in, a.cstate_out, a.craw, a.A, a.dt, a.gin));
-  if (a.B < 1 || a.B > GDN_MAXB) return cudaErrorInvalidValue;
   CW_TRY(launch_pdl_cluster(gdn_recur_kernel, a.nvh * 2, GDN_T, 0, st, 2, a.S_in, a.S_out, a.gin, a.B, a.nkh, a.nvh,
                             a.out, a.delta, a.z, a.ps, a.wn));
   return cudaGetLastError();
@@ -234,12 +244,19 @@ cudaError_t launch_gdn_replay(GdnLayerPtrs *dev_layers, int n_layers, int k, int
   return cudaGetLastError();
 }
 
+cudaError_t launch_gdn_replay1(const GdnLayerPtrs &layer, int k, int nkh, int nvh, cudaStream_t st) {
+  const int QKV = (2 * nkh + nvh) * 128;
+  CW_TRY(launch_pdl(gdn_replay1_kernel, nvh * 2 + (QKV + GDN_T - 1) / GDN_T, GDN_T, 0, st, layer, k, nkh, nvh));
+  return cudaGetLastError();
+}
+
 // One-time kernel attributes (called at engine set-up).
 cudaError_t gdn_configure() {
   cudaError_t e;
   if ((e = carveout_max(gdn_conv_kernel)) != cudaSuccess) return e;
   if ((e = carveout_max(gdn_recur_kernel)) != cudaSuccess) return e;
   if ((e = carveout_max(gdn_replay_kernel)) != cudaSuccess) return e;
+  if ((e = carveout_max(gdn_replay1_kernel)) != cudaSuccess) return e;
   return cudaSuccess;
 }
 

@@ -5,6 +5,9 @@
 
 namespace cw {
 
+// Rows of one verify block the recurrence kernel holds in shared memory.
+constexpr int GDN_MAXB = 16;
+
 struct GdnLayerArgs {
   const float *proj;  // in_proj output rows [B][ps]: qkv | z | alpha | beta
   int ps, B, nkh, nvh;
@@ -35,8 +38,12 @@ struct GdnLayerPtrs {
 cudaError_t launch_gdn_layer(const GdnLayerArgs &a, cudaStream_t st);
 // Advance every layer's committed state by block rows 0..k.
 cudaError_t launch_gdn_replay(GdnLayerPtrs *dev_layers, int n_layers, int k, int nkh, int nvh, cudaStream_t st);
+// The same for one layer given by value.
+cudaError_t launch_gdn_replay1(const GdnLayerPtrs &layer, int k, int nkh, int nvh, cudaStream_t st);
 
 // Kernel attributes set once per process (shared-memory carveout).
 cudaError_t gdn_configure();
+// Frees the scratch of the stand-alone entry point (cwen_cuda_gdn_verify).
+void gdn_verify_free();
 
 }  // namespace cw

@@ -88,6 +88,27 @@ int cwen_cuda_gemvb_host(int wid, const float *hX, int xs, float *hY, int ys, in
  * other's results.  Output matches cwen_cuda_gemvb. */
 int cwen_cuda_gemvb_static(int wid, const float *dX, int xs, float *dY, int ys, int B, void *stream);
 
+/* ---- stand-alone GatedDeltaNet verify step with rollback ---- */
+/* One linear-attention layer over the B <= 16 rows of a verify block, on
+ * caller device buffers, ordered on `stream` (NULL: the engine's stream):
+ * conv1d_update + SiLU + q/k l2norm (run.c:2183-2200, 2019-2020), the
+ * decay/beta transform (run.c:2339-2344), gdn_step with its gated RMSNorm
+ * (run.c:2014-2180) for every row; then the committed state is advanced by
+ * rows 0..keep-1 only, 0 <= keep <= B (the snap_save / snap_load rollback of
+ * a short walk, run.c:2787-2809, 4975-4988).
+ *   proj  [B][ps] rows [q nkh*128 | k nkh*128 | v nvh*128 | z nvh*128 |
+ *         alpha nvh | beta nvh] (the layer's input projections, pre-conv)
+ *   convw [QKV][4] (ssm_conv1d), A / dt [nvh] (ssm_a, ssm_dt.bias),
+ *   wn [128] (ssm_norm), QKV = (2 nkh + nvh) * 128
+ *   S [nvh][128][128], conv [QKV][3]: the committed state, updated in place
+ *   out [B][nvh*128]: the gated-norm head outputs of all B rows
+ * Value head h reads key head h % nkh.  The engine keeps one scratch for this
+ * call (the state after the block and the rows' rank-1 records, ~3.5 MB at
+ * nvh = 48): calls that overlap on the GPU race on it. */
+int cwen_cuda_gdn_verify(int nkh, int nvh, int B, const float *proj, int ps, const float *convw, const float *A,
+                         const float *dt, const float *wn, float *S, float *conv, int keep, float *out,
+                         void *stream);
+
 /* ---- the model ---- */
 /* Declare the geometry (run.c:83-91 constants) before any upload. */
 int cwen_cuda_model_config(const cwen_dims *dims);
