@@ -48,11 +48,17 @@ __global__ void __launch_bounds__(128) gdn_conv_kernel(const float *__restrict__
     return;
   }
   const int c = grp * 128 + threadIdx.x;
+  // every row's input at once: one memory round trip, not one per row
+  float raw[GDN_MAXB];
+#pragma unroll
+  for (int b = 0; b < GDN_MAXB; b++) raw[b] = b < B ? proj[(size_t)b * ps + c] : 0.f;
   const float w0 = convw[c * 4 + 0], w1 = convw[c * 4 + 1], w2 = convw[c * 4 + 2], w3 = convw[c * 4 + 3];
   float s0 = cstate_in[c * 3 + 0], s1 = cstate_in[c * 3 + 1], s2 = cstate_in[c * 3 + 2];
   const bool is_qk = grp < 2 * nkh;
-  for (int b = 0; b < B; b++) {
-    const float cur = proj[(size_t)b * ps + c];
+#pragma unroll
+  for (int b = 0; b < GDN_MAXB; b++) {
+    if (b >= B) break;
+    const float cur = raw[b];
     craw[(size_t)b * QKV + c] = cur;
     float y = s0 * w0 + s1 * w1 + s2 * w2 + cur * w3;
     s0 = s1;
@@ -60,12 +66,14 @@ __global__ void __launch_bounds__(128) gdn_conv_kernel(const float *__restrict__
     s2 = cur;
     y = silu_dev(y);
     if (is_qk) {
-      // l2norm over the 128 channels of this head (l2norm_rows run.c:401)
+      // l2norm over the 128 channels of this head (l2norm_rows run.c:401);
+      // the partial sums alternate between two slots, so one barrier per row
+      // suffices (a slot is rewritten two rows later, after the next barrier)
       float ss = warp_sum(y * y);
+      if ((threadIdx.x & 31) == 0) red[(b & 1) * 4 + (threadIdx.x >> 5)] = ss;
       __syncthreads();
-      if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
-      __syncthreads();
-      ss = (red[0] + red[1]) + (red[2] + red[3]);
+      const float *r = red + (b & 1) * 4;
+      ss = (r[0] + r[1]) + (r[2] + r[3]);
       y *= 1.f / sqrtf(ss + 1e-6f);
     }
     gin[(size_t)b * GS + c] = y;
@@ -76,14 +84,19 @@ __global__ void __launch_bounds__(128) gdn_conv_kernel(const float *__restrict__
 }
 
 // ---- the recurrence: CTA = (value head, half of the value columns),
-// 256 threads = 64 columns x 4 quarters of the key rows; each thread keeps
-// its 32x1 slice of S in registers for all B positions.  The two halves of a
-// head form a thread-block cluster of 2 for the gated RMSNorm of the head's
-// 128 outputs per row (run.c:2142-2178):
+// 256 threads; lane l of warp w owns value column w*8 + (l & 7) of the half
+// and key rows 32*(l >> 3) .. +31 (a quarter), and keeps that 32x1 slice of
+// S in registers for all B positions.  The quarters of a column sit in lanes
+// l, l^8, l^16, l^24, so S^T k and S^T q are reduced with two xor shuffles
+// ((q0 + q1) + (q2 + q3) in every lane) and the row loop has no barrier.  The
+// rows' k, q, v, gate and beta are staged in shared memory before the loop.
+// The two halves of a head form a thread-block cluster of 2 for the gated
+// RMSNorm of the head's 128 outputs per row (run.c:2142-2178):
 //   out[i] = wn[i] * o[i] * rsqrt(mean_i o^2 + eps) * silu(z[i]),
 // one exchange of the halves' per-row sums of squares through distributed
 // shared memory after the last row. ----
 constexpr int GDN_T = 256;
+constexpr int KQ_PAD = 33;  // a quarter's 32 keys + 1: the 4 quarters read 4 different banks
 
 __global__ void __launch_bounds__(GDN_T) gdn_recur_kernel(const float *__restrict__ Sin, float *__restrict__ Sout,
                                                           const float *__restrict__ gin, int B, int nkh, int nvh,
@@ -94,64 +107,67 @@ __global__ void __launch_bounds__(GDN_T) gdn_recur_kernel(const float *__restric
   pdl_wait();
   const int hv = blockIdx.x >> 1, half = blockIdx.x & 1;
   const int hk = hv % nkh;
-  const int col = threadIdx.x & 63, q4 = threadIdx.x >> 6;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int q4 = lane >> 3, col = warp * 8 + (lane & 7);
   const int j = half * 64 + col;
   const int QKV = (2 * nkh + nvh) * 128;
   const int GS = QKV + 2 * nvh;
-  __shared__ float kq[2][128];
-  __shared__ float part[4][64];
-  __shared__ float dl[64];
-  __shared__ float ob[GDN_MAXB][64];   // raw outputs of this half, per row
-  __shared__ float oss[GDN_MAXB];      // their sums of squares (read by the other half)
+  __shared__ float kq[GDN_MAXB][2][4 * KQ_PAD];  // per row: k, q of key head hk
+  __shared__ float vsh[GDN_MAXB][64];             // v of this half's columns
+  __shared__ float gb[GDN_MAXB][2];               // gate, beta
+  __shared__ float ob[GDN_MAXB][64];              // raw outputs of this half, per row
+  __shared__ float oss[GDN_MAXB];                 // their sums of squares (read by the other half)
   const float *S0 = Sin + (size_t)hv * 128 * 128;
   float s[32];
 #pragma unroll
   for (int i = 0; i < 32; i++) s[i] = S0[(size_t)(q4 * 32 + i) * 128 + j];
+  for (int i = threadIdx.x; i < B * 256; i += GDN_T) {
+    const int b = i >> 8, w = (i >> 7) & 1, e = i & 127;
+    const float *row = gin + (size_t)b * GS;
+    kq[b][w][(e >> 5) * KQ_PAD + (e & 31)] = w == 0 ? row[nkh * 128 + hk * 128 + e] : row[hk * 128 + e];
+  }
+  for (int i = threadIdx.x; i < B * 64; i += GDN_T) {
+    const int b = i >> 6, c = i & 63;
+    vsh[b][c] = gin[(size_t)b * GS + 2 * nkh * 128 + hv * 128 + half * 64 + c];
+  }
+  if (threadIdx.x < B) {
+    gb[threadIdx.x][0] = gin[(size_t)threadIdx.x * GS + QKV + hv];
+    gb[threadIdx.x][1] = gin[(size_t)threadIdx.x * GS + QKV + nvh + hv];
+  }
+  __syncthreads();
   const float scale = 1.f / sqrtf(128.f);
   for (int b = 0; b < B; b++) {
-    const float *row = gin + (size_t)b * GS;
-    __syncthreads();
-    if (threadIdx.x < 128) kq[0][threadIdx.x] = row[nkh * 128 + hk * 128 + threadIdx.x];
-    else kq[1][threadIdx.x - 128] = row[hk * 128 + threadIdx.x - 128];
-    const float g = row[QKV + hv], beta = row[QKV + nvh + hv];
-    const float v = row[2 * nkh * 128 + hv * 128 + j];
-    __syncthreads();
-    // S *= g; partial S^T k over this quarter
+    const float *kk = &kq[b][0][q4 * KQ_PAD], *qq = &kq[b][1][q4 * KQ_PAD];
+    const float g = gb[b][0], beta = gb[b][1];
+    // S *= g; S^T k over this quarter, then over the four quarters
     float sk = 0.f;
 #pragma unroll
     for (int i = 0; i < 32; i++) {
       s[i] = s[i] * g;
-      sk = fmaf(s[i], kq[0][q4 * 32 + i], sk);
+      sk = fmaf(s[i], kk[i], sk);
     }
-    part[q4][col] = sk;
-    __syncthreads();
-    if (q4 == 0) {
-      const float tot = (part[0][col] + part[1][col]) + (part[2][col] + part[3][col]);
-      const float d = beta * (v - tot);
-      dl[col] = d;
-      delta[(size_t)b * nvh * 128 + hv * 128 + j] = d;
-    }
-    __syncthreads();
-    const float d = dl[col];
+    sk += __shfl_xor_sync(0xffffffffu, sk, 8);
+    sk += __shfl_xor_sync(0xffffffffu, sk, 16);
+    const float d = beta * (vsh[b][col] - sk);
+    if (q4 == 0) delta[(size_t)b * nvh * 128 + hv * 128 + j] = d;
     float o = 0.f;
 #pragma unroll
     for (int i = 0; i < 32; i++) {
-      s[i] = fmaf(kq[0][q4 * 32 + i], d, s[i]);
-      o = fmaf(s[i], kq[1][q4 * 32 + i], o);
+      s[i] = fmaf(kk[i], d, s[i]);
+      o = fmaf(s[i], qq[i], o);
     }
-    __syncthreads();
-    part[q4][col] = o;
-    __syncthreads();
-    if (q4 == 0) ob[b][col] = ((part[0][col] + part[1][col]) + (part[2][col] + part[3][col])) * scale;
+    o += __shfl_xor_sync(0xffffffffu, o, 8);
+    o += __shfl_xor_sync(0xffffffffu, o, 16);
+    if (q4 == 0) ob[b][col] = o * scale;
   }
   float *S1 = Sout + (size_t)hv * 128 * 128;
 #pragma unroll
   for (int i = 0; i < 32; i++) S1[(size_t)(q4 * 32 + i) * 128 + j] = s[i];
+  __syncthreads();  // every row's outputs are in ob
   // gated RMSNorm: warp b (< 8) sums row b's 64 squares of this half (and row
   // b + 8), then the halves' sums are added in rank order
   namespace cg = cooperative_groups;
   cg::cluster_group cl = cg::this_cluster();
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int b = warp; b < B; b += GDN_T / 32) {
     const float a0 = ob[b][lane], a1 = ob[b][lane + 32];
     float ss = fmaf(a0, a0, a1 * a1);
@@ -178,14 +194,15 @@ __device__ __forceinline__ void replay_layer(const GdnLayerPtrs &P, int k, int n
   const int GS = QKV + 2 * nvh;
   const int nS = nvh * 2;
   if ((int)blockIdx.x >= nS) {
-    // conv state: channels handled by the remaining CTAs
+    // conv state after rows 0..k: the last three of [old state | raw rows]
     const int c = (blockIdx.x - nS) * GDN_T + threadIdx.x;
     if (c >= QKV) return;
-    float st[3] = {P.cstate[c * 3 + 0], P.cstate[c * 3 + 1], P.cstate[c * 3 + 2]};
-    for (int b = 0; b <= k; b++) {
-      st[0] = st[1];
-      st[1] = st[2];
-      st[2] = P.craw[(size_t)b * QKV + c];
+    const float o1 = P.cstate[c * 3 + 1], o2 = P.cstate[c * 3 + 2];
+    float st[3];
+#pragma unroll
+    for (int m = 0; m < 3; m++) {
+      const int src = k - 2 + m;  // >= -2; -2 and -1 are old slots 1 and 2
+      st[m] = src >= 0 ? P.craw[(size_t)src * QKV + c] : (src == -1 ? o2 : o1);
     }
     P.cstate[c * 3 + 0] = st[0];
     P.cstate[c * 3 + 1] = st[1];
@@ -196,17 +213,27 @@ __device__ __forceinline__ void replay_layer(const GdnLayerPtrs &P, int k, int n
   const int hk = hv % nkh;
   const int col = threadIdx.x & 63, q4 = threadIdx.x >> 6;
   const int j = half * 64 + col;
+  const int n = k + 1;  // rows replayed, <= GDN_MAXB (checked at launch)
+  __shared__ float kr[GDN_MAXB][128];  // the rows' normalised keys of key head hk
+  __shared__ float gr[GDN_MAXB];       // the rows' gates
   float *S = P.S + (size_t)hv * 128 * 128;
   float s[32];
 #pragma unroll
   for (int i = 0; i < 32; i++) s[i] = S[(size_t)(q4 * 32 + i) * 128 + j];
-  for (int b = 0; b <= k; b++) {
-    const float *row = P.gin + (size_t)b * GS;
-    const float g = row[QKV + hv];
-    const float d = P.delta[(size_t)b * nvh * 128 + hv * 128 + j];
-    const float *kk = row + nkh * 128 + hk * 128 + q4 * 32;
+  for (int i = threadIdx.x; i < n * 128; i += GDN_T)
+    kr[i >> 7][i & 127] = P.gin[(size_t)(i >> 7) * GS + nkh * 128 + hk * 128 + (i & 127)];
+  if ((int)threadIdx.x < n) gr[threadIdx.x] = P.gin[(size_t)threadIdx.x * GS + QKV + hv];
+  float dr[GDN_MAXB];
 #pragma unroll
-    for (int i = 0; i < 32; i++) s[i] = fmaf(kk[i], d, s[i] * g);
+  for (int b = 0; b < GDN_MAXB; b++) dr[b] = b < n ? P.delta[(size_t)b * nvh * 128 + hv * 128 + j] : 0.f;
+  __syncthreads();
+#pragma unroll
+  for (int b = 0; b < GDN_MAXB; b++) {
+    if (b >= n) break;
+    const float g = gr[b];
+    const float *kk = &kr[b][q4 * 32];
+#pragma unroll
+    for (int i = 0; i < 32; i++) s[i] = fmaf(kk[i], dr[b], s[i] * g);
   }
 #pragma unroll
   for (int i = 0; i < 32; i++) S[(size_t)(q4 * 32 + i) * 128 + j] = s[i];
@@ -239,6 +266,7 @@ cudaError_t launch_gdn_layer(const GdnLayerArgs &a, cudaStream_t st) {
 
 cudaError_t launch_gdn_replay(GdnLayerPtrs *dev_layers, int n_layers, int k, int nkh, int nvh, cudaStream_t st) {
   const int QKV = (2 * nkh + nvh) * 128;
+  if (k < 0 || k >= GDN_MAXB) return cudaErrorInvalidValue;
   dim3 grid(nvh * 2 + (QKV + GDN_T - 1) / GDN_T, n_layers);
   CW_TRY(launch_pdl(gdn_replay_kernel, grid, GDN_T, 0, st, dev_layers, k, nkh, nvh));
   return cudaGetLastError();
@@ -246,6 +274,7 @@ cudaError_t launch_gdn_replay(GdnLayerPtrs *dev_layers, int n_layers, int k, int
 
 cudaError_t launch_gdn_replay1(const GdnLayerPtrs &layer, int k, int nkh, int nvh, cudaStream_t st) {
   const int QKV = (2 * nkh + nvh) * 128;
+  if (k < 0 || k >= GDN_MAXB) return cudaErrorInvalidValue;
   CW_TRY(launch_pdl(gdn_replay1_kernel, nvh * 2 + (QKV + GDN_T - 1) / GDN_T, GDN_T, 0, st, layer, k, nkh, nvh));
   return cudaGetLastError();
 }
