@@ -69,6 +69,9 @@ _SIGS = {
     "cwen_cuda_ctx": (C.c_int, []),
     "cwen_cuda_stream": (C.c_void_p, []),
     "cwen_load_gguf": (C.c_int, [C.c_char_p]),
+    "cwen_gguf_dims": (C.c_int, [C.c_char_p, C.POINTER(Dims)]),
+    "cwen_write_synth_gguf": (C.c_int, [C.c_char_p, C.POINTER(Dims), C.c_uint64, C.c_int]),
+    "cw_model_tensor_count": (C.c_int, [C.POINTER(Dims)]),
     "cwen_load_synth": (C.c_int, [C.c_uint64, C.POINTER(Dims), C.c_int]),
     "cwen_dims_reference": (None, [C.POINTER(Dims)]),
     "cwen_dims_small": (None, [C.POINTER(Dims)]),
@@ -77,6 +80,10 @@ _SIGS = {
     "cwen_generate": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.POINTER(SpecCfg),
                                 C.POINTER(SpecStats)]),
     "cwen_ngram_draft": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_int]),
+    "cwen_ngram_map_new": (C.c_void_p, [C.c_int]),
+    "cwen_ngram_map_free": (None, [C.c_void_p]),
+    "cwen_ngram_map_update": (None, [C.c_void_p, C.c_void_p, C.c_int, C.c_int]),
+    "cwen_ngram_map_draft": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_int]),
     "cw_synth_q4_0": (None, [C.c_uint64, C.c_char_p, C.c_int, C.c_int, C.c_void_p, C.c_int]),
     "cw_synth_q8_0": (None, [C.c_uint64, C.c_char_p, C.c_int, C.c_int, C.c_void_p, C.c_int]),
     "cw_synth_normal": (None, [C.c_uint64, C.c_char_p, C.c_float, C.c_float, C.c_void_p, C.c_size_t]),

@@ -132,6 +132,9 @@ extern "C" {
 
 const char *cwen_cuda_last_error(void) { return g_err; }
 
+// Host-side (C) failures record their message here too (host/host_err.h).
+void cwen_host_set_error(const char *msg) { set_error("%s", msg ? msg : "unknown host error"); }
+
 int cwen_cuda_init(int device, int ctx, int bmax) {
   Engine &E = engine();
   if (E.live) {

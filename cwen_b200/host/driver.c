@@ -12,11 +12,13 @@
  */
 #define _GNU_SOURCE
 #include <limits.h>
+#include <stdarg.h>
 #include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
 
 #include "cwen_host.h"
+#include "host_err.h"
 
 /* ---- knobs ---- */
 void cwen_spec_defaults(cwen_spec_cfg *c) {
@@ -29,14 +31,26 @@ void cwen_spec_defaults(cwen_spec_cfg *c) {
   c->debug = 0;
 }
 
+/* A bad knob: reported on stderr, like the reference, and recorded for
+   cwen_cuda_last_error(). */
+static int env_fail(const char *fmt, ...) {
+  char buf[256];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  fprintf(stderr, "cwen: %s\n", buf);
+  cwen_host_set_error(buf);
+  return CWEN_EINVAL;
+}
+
 static int env_int_strict(const char *name, int *out, int *rc) {
   const char *e = getenv(name);
   if (!e || !e[0]) return 0;
   char *end;
   long v = strtol(e, &end, 10);
   if (end == e || *end || v < INT_MIN || v > INT_MAX) {
-    fprintf(stderr, "cwen: %s=%s is not an integer\n", name, e);
-    *rc = CWEN_EINVAL;
+    *rc = env_fail("%s=%s is not an integer", name, e);
     return 0;
   }
   *out = (int)v;
@@ -46,8 +60,7 @@ static int env_bool_strict(const char *name, int *out, int *rc) {
   const char *e = getenv(name);
   if (!e || !e[0]) return 0;
   if (strcmp(e, "0") && strcmp(e, "1")) {
-    fprintf(stderr, "cwen: %s must be 0 or 1\n", name);
-    *rc = CWEN_EINVAL;
+    *rc = env_fail("%s must be 0 or 1", name);
     return 0;
   }
   *out = e[0] == '1';
@@ -57,35 +70,29 @@ static int env_bool_strict(const char *name, int *out, int *rc) {
 int cwen_spec_from_env(cwen_spec_cfg *c) {
   int rc = 0, v;
   if (env_int_strict("CWEN_SPEC", &v, &rc)) {
-    if (v != 0 && v != 1) { fprintf(stderr, "cwen: CWEN_SPEC must be 0 or 1\n"); return CWEN_EINVAL; }
+    if (v != 0 && v != 1) return env_fail("CWEN_SPEC must be 0 or 1");
     c->spec = v;
   }
   if (env_int_strict("CWEN_SPEC_NGRAM_N", &v, &rc)) {
-    if (v < 2 || v > 256) { fprintf(stderr, "cwen: CWEN_SPEC_NGRAM_N must be in [2,256]\n"); return CWEN_EINVAL; }
+    if (v < 2 || v > 256) return env_fail("CWEN_SPEC_NGRAM_N must be in [2,256]");
     c->n_key = v;
   }
   if (env_int_strict("CWEN_SPEC_MAX_DRAFT", &v, &rc)) {
-    if (v < 1 || v > 15) { fprintf(stderr, "cwen: CWEN_SPEC_MAX_DRAFT must be in [1,15]\n"); return CWEN_EINVAL; }
+    if (v < 1 || v > 15) return env_fail("CWEN_SPEC_MAX_DRAFT must be in [1,15]");
     c->max_draft = v;
   }
   if (env_int_strict("CWEN_SPEC_MIN_DRAFT", &v, &rc)) {
-    if (v < 1 || v > c->max_draft) {
-      fprintf(stderr, "cwen: CWEN_SPEC_MIN_DRAFT must be in [1,%d]\n", c->max_draft);
-      return CWEN_EINVAL;
-    }
+    if (v < 1 || v > c->max_draft) return env_fail("CWEN_SPEC_MIN_DRAFT must be in [1,%d]", c->max_draft);
     c->min_draft = v;
   }
   if (env_int_strict("CWEN_SPEC_COOLDOWN", &v, &rc)) {
-    if (v < 0 || v > 100000) { fprintf(stderr, "cwen: CWEN_SPEC_COOLDOWN must be in [0,100000]\n"); return CWEN_EINVAL; }
+    if (v < 0 || v > 100000) return env_fail("CWEN_SPEC_COOLDOWN must be in [0,100000]");
     c->cooldown = v;
   }
   env_bool_strict("CWEN_SPEC_DEBUG", &c->debug, &rc);
   env_bool_strict("CWEN_MTP", &c->use_mtp, &rc);
-  if (c->min_draft > c->max_draft) {
-    fprintf(stderr, "cwen: CWEN_SPEC_MIN_DRAFT (%d) exceeds CWEN_SPEC_MAX_DRAFT (%d)\n", c->min_draft,
-            c->max_draft);
-    return CWEN_EINVAL;
-  }
+  if (c->min_draft > c->max_draft)
+    return env_fail("CWEN_SPEC_MIN_DRAFT (%d) exceeds CWEN_SPEC_MAX_DRAFT (%d)", c->min_draft, c->max_draft);
   return rc;
 }
 
@@ -204,6 +211,20 @@ static int ng_draft_map(const ngmap *m, const int32_t *h, int hn, int32_t *out, 
   }
   return n;
 }
+/* The n-gram proposal of a speculative cycle (run.c:4925-4933): chained
+   map lookups from the tail key, replaced by the history scan when the scan
+   proposes a longer run.  cap <= NG_MAX_PROPOSE. */
+#define NG_MAX_PROPOSE 256
+static int ng_propose(const ngmap *m, const int32_t *h, int hn, int32_t *out, int cap) {
+  int32_t scan[NG_MAX_PROPOSE];
+  int E = ng_draft_map(m, h, hn, out, cap);
+  int esc = cwen_ngram_draft(h, hn, scan, m->nk, cap);
+  if (esc > E) {
+    E = esc;
+    memcpy(out, scan, (size_t)E * sizeof(int32_t));
+  }
+  return E;
+}
 static int ng_init(ngmap *m, int nk) {
   memset(m, 0, sizeof *m);
   m->cap = NG_CAP;
@@ -219,6 +240,42 @@ static void ng_free(ngmap *m) {
   free(m->tok);
   free(m->cnt);
   free(m->used);
+}
+
+/* ---- the counted map as a drafter object (include/cwen_host.h) ---- */
+struct cwen_ngram_map {
+  ngmap m;
+};
+
+cwen_ngram_map *cwen_ngram_map_new(int n_key) {
+  if (n_key < 2 || n_key > 256) {
+    host_fail(CWEN_EINVAL, "cwen_ngram_map_new: n_key must be in [2,256]");
+    return NULL;
+  }
+  cwen_ngram_map *p = (cwen_ngram_map *)malloc(sizeof *p);
+  if (!p || ng_init(&p->m, n_key)) {
+    if (p) ng_free(&p->m);
+    free(p);
+    host_fail(CWEN_ENOMEM, "cwen_ngram_map_new: out of host memory");
+    return NULL;
+  }
+  return p;
+}
+
+void cwen_ngram_map_free(cwen_ngram_map *p) {
+  if (!p) return;
+  ng_free(&p->m);
+  free(p);
+}
+
+void cwen_ngram_map_update(cwen_ngram_map *p, const int32_t *hist, int a, int b) {
+  if (p && hist && a >= 0 && b > a) ng_update_range(&p->m, hist, a, b);
+}
+
+int cwen_ngram_map_draft(const cwen_ngram_map *p, const int32_t *hist, int hn, int32_t *out, int max_d) {
+  if (!p || !hist || !out || hn < 0) return host_fail(CWEN_EINVAL, "cwen_ngram_map_draft: bad arguments");
+  if (max_d > NG_MAX_PROPOSE) max_d = NG_MAX_PROPOSE;
+  return ng_propose(&p->m, hist, hn, out, max_d);
 }
 
 /* ---- drivers ---- */
@@ -304,7 +361,7 @@ int cwen_generate(const int32_t *tokens, int n_tok, int n_gen, int32_t *out, con
   if (use_map) { ng_update_range(&ngm, hist, upd, hn); upd = hn; }
   const int cap_hard = cfg->max_draft;
   int E_cap = cap_hard, streak = 0, cool = 0, fa_streak = 0;
-  int32_t blk[BMAX], scan[BMAX];
+  int32_t blk[BMAX];
   int am[BMAX];
   while (g < n_gen) {
     const int n_past = cwen_cuda_n_past();
@@ -320,9 +377,7 @@ int cwen_generate(const int32_t *tokens, int n_tok, int n_gen, int32_t *out, con
         if (E < 0) { rc = E; goto fail; }
       } else if (cap > 0) {
         if (use_map) {
-          E = ng_draft_map(&ngm, hist, hn, blk + 1, cap);
-          int esc = cwen_ngram_draft(hist, hn, scan, cfg->n_key, cap);
-          if (esc > E) { E = esc; memcpy(blk + 1, scan, (size_t)E * sizeof(int32_t)); }
+          E = ng_propose(&ngm, hist, hn, blk + 1, cap);
         } else {
           E = cwen_ngram_draft(hist, hn, blk + 1, cfg->n_key, cap);
         }

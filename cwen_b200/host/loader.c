@@ -16,7 +16,10 @@
 #include <sys/stat.h>
 #include <unistd.h>
 
+#include <errno.h>
+
 #include "cwen_host.h"
+#include "host_err.h"
 #include "synth.h"
 
 #define GG_MAX_TENSORS 4096
@@ -162,34 +165,47 @@ static int gg_dims(const gg_tensor *t, int n, cwen_dims *d, char *why, size_t wl
   return 0;
 }
 
-int cwen_load_gguf(const char *path) {
+/* A mapped and parsed GGUF file. */
+typedef struct {
+  uint8_t *map;
+  size_t len;
+  gg_tensor *t;
+  int nt;
+} gg_file;
+
+static void gg_close(gg_file *g) {
+  free(g->t);
+  if (g->map) munmap(g->map, g->len);
+  memset(g, 0, sizeof *g);
+}
+
+/* Map and parse a GGUF file: header, key/values (general.alignment), the
+ * tensor table, every tensor's extent inside the file.  On failure the
+ * message goes to cwen_cuda_last_error() and the code is returned. */
+static int gg_open(const char *path, gg_file *g) {
+  memset(g, 0, sizeof *g);
   int fd = open(path, O_RDONLY);
-  if (fd < 0) {
-    perror(path);
-    return CWEN_EINVAL;
-  }
+  if (fd < 0) return host_fail(CWEN_EINVAL, "gguf: %s: %s", path, strerror(errno));
   struct stat st;
-  if (fstat(fd, &st) || st.st_size < 20) {
+  if (fstat(fd, &st) || !S_ISREG(st.st_mode) || st.st_size < 24) {
     close(fd);
-    fprintf(stderr, "gguf: %s: not a gguf file\n", path);
-    return CWEN_EINVAL;
+    return host_fail(CWEN_EINVAL, "gguf: %s: not a gguf file", path);
   }
-  size_t len = (size_t)st.st_size;
-  uint8_t *map = (uint8_t *)mmap(NULL, len, PROT_READ, MAP_PRIVATE, fd, 0);
+  g->len = (size_t)st.st_size;
+  uint8_t *map = (uint8_t *)mmap(NULL, g->len, PROT_READ, MAP_PRIVATE, fd, 0);
   close(fd);
   if (map == MAP_FAILED) {
-    perror("mmap");
-    return CWEN_ENOMEM;
+    g->len = 0;
+    return host_fail(CWEN_ENOMEM, "gguf: %s: mmap: %s", path, strerror(errno));
   }
-  gg_cur c = {map, map + len, 0, {0}};
-  gg_tensor *t = NULL;
-  int rc = CWEN_EINVAL, nt = 0;
+  g->map = map;
+  gg_cur c = {map, map + g->len, 0, {0}};
   const uint8_t *magic = gg_take(&c, 4);
-  if (!magic || memcmp(magic, "GGUF", 4)) { gg_fail(&c, "bad magic"); goto out; }
+  if (!magic || memcmp(magic, "GGUF", 4)) gg_fail(&c, "bad magic");
   uint32_t ver = gg_u32(&c);
-  if (ver < 2 || ver > 3) { gg_fail(&c, "unsupported gguf version"); goto out; }
+  if (!c.bad && (ver < 2 || ver > 3)) gg_fail(&c, "unsupported gguf version");
   uint64_t n_t = gg_u64(&c), n_kv = gg_u64(&c);
-  if (n_t > GG_MAX_TENSORS) { gg_fail(&c, "too many tensors"); goto out; }
+  if (!c.bad && n_t > GG_MAX_TENSORS) gg_fail(&c, "too many tensors");
   uint64_t align = 32;
   for (uint64_t i = 0; i < n_kv && !c.bad; i++) {
     char key[256];
@@ -198,67 +214,105 @@ int cwen_load_gguf(const char *path) {
     uint64_t v = gg_skip(&c, ty, 0);
     if (!c.bad && !strcmp(key, "general.alignment") && (ty == 4 || ty == 5)) align = v;
   }
-  if (align == 0 || (align & (align - 1))) { gg_fail(&c, "bad general.alignment"); goto out; }
-  t = (gg_tensor *)calloc(n_t ? n_t : 1, sizeof *t);
-  if (!t) { rc = CWEN_ENOMEM; goto out; }
-  nt = (int)n_t;
-  for (int i = 0; i < nt && !c.bad; i++) {
-    gg_str(&c, t[i].name, sizeof t[i].name);
-    uint32_t nd = gg_u32(&c);
-    if (nd < 1 || nd > 4) { gg_fail(&c, "n_dims outside 1..4"); break; }
-    t[i].n_dims = (int)nd;
-    t[i].ne[0] = t[i].ne[1] = t[i].ne[2] = t[i].ne[3] = 1;
-    for (uint32_t k = 0; k < nd; k++) {
-      t[i].ne[k] = gg_u64(&c);
-      if (t[i].ne[k] == 0 || t[i].ne[k] > 0x7fffffffull) { gg_fail(&c, "dim zero or beyond INT_MAX"); break; }
+  if (!c.bad && (align == 0 || (align & (align - 1)))) gg_fail(&c, "bad general.alignment");
+  if (!c.bad) {
+    g->t = (gg_tensor *)calloc(n_t ? n_t : 1, sizeof *g->t);
+    if (!g->t) {
+      gg_close(g);
+      return host_fail(CWEN_ENOMEM, "gguf: %s: out of host memory", path);
     }
-    t[i].type = (int)gg_u32(&c);
-    t[i].off = gg_u64(&c);
+    g->nt = (int)n_t;
   }
-  if (c.bad) goto out;
-  {
+  for (int i = 0; i < g->nt && !c.bad; i++) {
+    gg_tensor *x = &g->t[i];
+    gg_str(&c, x->name, sizeof x->name);
+    uint32_t nd = gg_u32(&c);
+    if (c.bad) break;
+    if (nd < 1 || nd > 4) { gg_fail(&c, "n_dims outside 1..4"); break; }
+    x->n_dims = (int)nd;
+    x->ne[0] = x->ne[1] = x->ne[2] = x->ne[3] = 1;
+    for (uint32_t k = 0; k < nd && !c.bad; k++) {
+      x->ne[k] = gg_u64(&c);
+      if (!c.bad && (x->ne[k] == 0 || x->ne[k] > 0x7fffffffull)) gg_fail(&c, "dim zero or beyond INT_MAX");
+    }
+    x->type = (int)gg_u32(&c);
+    x->off = gg_u64(&c);
+    /* rows = ne1*ne2*ne3, checked after each product (each factor < 2^31) */
+    uint64_t rows = 1;
+    for (int k = 1; k < 4 && !c.bad; k++) {
+      rows *= x->ne[k];
+      if (rows > 0x7fffffffull) gg_fail(&c, "tensor rows beyond INT_MAX");
+    }
+    if (!c.bad && (x->type == CWEN_T_Q4_0 || x->type == CWEN_T_Q8_0) && x->ne[0] % 32)
+      gg_fail(&c, "quantized row length not a multiple of 32");
+  }
+  if (!c.bad) {
     uint64_t data_off = (uint64_t)(c.p - map);
     data_off = (data_off + align - 1) & ~(align - 1);
-    for (int i = 0; i < nt; i++) {
-      if (data_off >= len || t[i].off >= len - data_off) { gg_fail(&c, "tensor offset out of file"); goto out; }
-      t[i].data = map + data_off + t[i].off;
-      const uint64_t rows = t[i].ne[1] * t[i].ne[2] * t[i].ne[3];
-      const size_t nb = gg_nbytes(t[i].type, t[i].ne[0], rows);
-      if (nb && nb > len - data_off - t[i].off) {
-        snprintf(c.why, sizeof c.why, "%s: extent beyond file", t[i].name);
+    for (int i = 0; i < g->nt && !c.bad; i++) {
+      gg_tensor *x = &g->t[i];
+      if (data_off >= g->len || x->off >= g->len - data_off) {
+        snprintf(c.why, sizeof c.why, "%s: tensor offset out of file", x->name);
         c.bad = 1;
-        goto out;
+        break;
+      }
+      x->data = map + data_off + x->off;
+      const size_t nb = gg_nbytes(x->type, x->ne[0], x->ne[1] * x->ne[2] * x->ne[3]);
+      if (nb && nb > g->len - data_off - x->off) {
+        snprintf(c.why, sizeof c.why, "%s: extent beyond file", x->name);
+        c.bad = 1;
       }
     }
   }
-  {
-    cwen_dims d;
-    char why[160];
-    if (gg_dims(t, nt, &d, why, sizeof why)) {
-      snprintf(c.why, sizeof c.why, "%s", why);
-      c.bad = 1;
-      goto out;
-    }
-    rc = cwen_cuda_model_config(&d);
-    if (rc) goto out_engine;
-    for (int i = 0; i < nt; i++) {
-      const gg_tensor *x = &t[i];
-      if (x->type != CWEN_T_F32 && x->type != CWEN_T_Q4_0 && x->type != CWEN_T_Q8_0) continue;
-      const uint64_t rows = x->ne[1] * x->ne[2] * x->ne[3];
-      if (rows > 0x7fffffffull) continue;
-      rc = cwen_cuda_upload(x->name, x->type, x->data, (int)x->ne[0], (int)rows);
-      if (rc) goto out_engine;
-    }
-    rc = cwen_cuda_model_finalize();
-    if (!rc) fprintf(stderr, "loaded %d tensors from %s\n", nt, path);
+  if (c.bad) {
+    gg_close(g);
+    return host_fail(CWEN_EINVAL, "gguf: %s: %s", path, c.why);
   }
-out_engine:
-  if (rc) fprintf(stderr, "gguf: %s\n", cwen_cuda_last_error());
+  return CWEN_OK;
+}
+
+int cwen_gguf_dims(const char *path, cwen_dims *out) {
+  if (!path || !out) return host_fail(CWEN_EINVAL, "cwen_gguf_dims: null argument");
+  gg_file g;
+  int rc = gg_open(path, &g);
+  if (rc) return rc;
+  char why[160];
+  if (gg_dims(g.t, g.nt, out, why, sizeof why)) rc = host_fail(CWEN_EINVAL, "gguf: %s: %s", path, why);
+  gg_close(&g);
+  return rc;
+}
+
+int cwen_load_gguf(const char *path) {
+  if (!path) return host_fail(CWEN_EINVAL, "cwen_load_gguf: null path");
+  gg_file g;
+  int rc = gg_open(path, &g);
+  if (rc) return rc;
+  cwen_dims d;
+  char why[160];
+  if (gg_dims(g.t, g.nt, &d, why, sizeof why)) {
+    rc = host_fail(CWEN_EINVAL, "gguf: %s: %s", path, why);
+    goto out;
+  }
+  rc = cwen_cuda_model_config(&d);
+  for (int i = 0; i < g.nt && !rc; i++) {
+    const gg_tensor *x = &g.t[i];
+    if (x->type != CWEN_T_F32 && x->type != CWEN_T_Q4_0 && x->type != CWEN_T_Q8_0) continue;
+    rc = cwen_cuda_upload(x->name, x->type, x->data, (int)x->ne[0], (int)(x->ne[1] * x->ne[2] * x->ne[3]));
+  }
+  if (!rc) rc = cwen_cuda_model_finalize();
 out:
-  if (c.bad) fprintf(stderr, "gguf: %s: %s\n", path, c.why);
-  free(t);
-  munmap(map, len);
-  return c.bad ? CWEN_EINVAL : rc;
+  gg_close(&g);
+  return rc;
+}
+
+int cwen_write_synth_gguf(const char *path, const cwen_dims *dims, uint64_t seed, int threads) {
+  if (!path || !dims) return host_fail(CWEN_EINVAL, "cwen_write_synth_gguf: null argument");
+  cw_dims d;
+  memcpy(&d, dims, sizeof d);
+  if (d.n_layer < 1 || d.full_interval < 1 || d.n_embd < 32 || d.n_embd % 32 || d.n_ff % 32 || d.n_vocab < 1)
+    return host_fail(CWEN_EINVAL, "cwen_write_synth_gguf: geometry out of range");
+  if (cw_write_gguf(path, &d, seed, threads)) return host_fail(CWEN_EINVAL, "cwen_write_synth_gguf: cannot write %s", path);
+  return CWEN_OK;
 }
 
 void cwen_dims_reference(cwen_dims *d) {

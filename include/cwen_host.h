@@ -17,9 +17,19 @@ extern "C" {
  * derive the geometry from the tensor shapes, upload every tensor and
  * finalize.  The engine must be initialised (cwen_cuda_init). */
 int cwen_load_gguf(const char *path);
+/* The geometry cwen_load_gguf would derive from the file's tensor shapes,
+ * with the same parse and bounds checks, without touching the engine (no
+ * GPU needed).  CWEN_EINVAL with the reason in cwen_cuda_last_error() for a
+ * malformed file. */
+int cwen_gguf_dims(const char *path, cwen_dims *out);
 /* The seeded random-init model of the benchmark configurations: every tensor
  * generated on the host (`threads` threads, <= 0: all cores) and uploaded. */
 int cwen_load_synth(uint64_t seed, const cwen_dims *dims, int threads);
+/* Write that seeded model as a GGUF v3 file (the reference's tensor names,
+ * shapes and types; 32-byte aligned data) that cwen_load_gguf and the
+ * reference's own loader (load_gguf, run.c:3230) read back to the same bytes
+ * cwen_load_synth uploads.  No GPU needed. */
+int cwen_write_synth_gguf(const char *path, const cwen_dims *dims, uint64_t seed, int threads);
 /* Geometry of the reference (run.c:83-91) and the small test geometry. */
 void cwen_dims_reference(cwen_dims *d);
 void cwen_dims_small(cwen_dims *d);
@@ -56,6 +66,21 @@ int cwen_generate(const int32_t *tokens, int n_tok, int n_gen, int32_t *out, con
 /* Prompt-lookup scan (ngram_draft, run.c:4533): propose up to max_d ids that
  * followed the most useful earlier match of the last n_key ids. */
 int cwen_ngram_draft(const int32_t *hist, int hn, int32_t *out, int n_key, int max_d);
+/* The counted n-gram map (run.c:205-221, 4552-4654): key of n_key ids ->
+ * latest continuation and hit count, 2^18 entries, least-hit eviction when
+ * full.  The speculative driver keeps one per generation when n-gram
+ * drafting is on.  NULL (message in cwen_cuda_last_error) for n_key outside
+ * [2,256] or no memory. */
+typedef struct cwen_ngram_map cwen_ngram_map;
+cwen_ngram_map *cwen_ngram_map_new(int n_key);
+void cwen_ngram_map_free(cwen_ngram_map *m);
+/* Fold hist[a..b): every position p >= n_key adds hist[p-n_key..p) -> hist[p]
+ * (ng_update_range, run.c:4631). */
+void cwen_ngram_map_update(cwen_ngram_map *m, const int32_t *hist, int a, int b);
+/* The proposal of one speculative cycle (run.c:4925-4930): chained map
+ * lookups from the last n_key ids, replaced by cwen_ngram_draft's history
+ * scan when that proposes more; at most min(max_d, 256) ids. */
+int cwen_ngram_map_draft(const cwen_ngram_map *m, const int32_t *hist, int hn, int32_t *out, int max_d);
 
 #ifdef __cplusplus
 }

@@ -75,6 +75,37 @@ CWREF_API void cwref_gdn_step(float *S, float *conv_state, const float *conv_w, 
   gdn_step(0, qkv, z, decay, beta, out);
   Srec = saveS; Cstate = saveC; W[0].ssm_conv = sc; W[0].ssm_norm = sn;
 }
+/* ---- n-gram drafters ---- */
+/* Prompt-lookup scan (ngram_draft, run.c:4533). */
+CWREF_API int cwref_ngram_draft(const int *h, int hn, int *out, int n_key, int max_d) {
+  return ngram_draft(h, hn, out, n_key, max_d);
+}
+/* A fresh, empty counted map with key length n_key: the allocation of
+   alloc_state (run.c:3972-3978), eviction hand back at slot 0. */
+CWREF_API int cwref_ngmap_init(int n_key) {
+  free(NGM.keys); free(NGM.tok); free(NGM.cnt); free(NGM.used);
+  memset(&NGM, 0, sizeof NGM);
+  NG_evict_hand = 0;
+  Scfg_n_key = n_key;
+  NGM.cap = NG_CAP;
+  NGM.keys = malloc(sizeof(int) * NG_CAP * (size_t)n_key);
+  NGM.tok = malloc(sizeof(int) * NG_CAP);
+  NGM.cnt = calloc(NG_CAP, sizeof(int));
+  NGM.used = calloc(NG_CAP, 1);
+  return (NGM.keys && NGM.tok && NGM.cnt && NGM.used) ? 0 : -1;
+}
+CWREF_API void cwref_ng_update_range(const int *h, int a, int b) { ng_update_range(h, a, b); }
+/* The n-gram branch of a speculative cycle as generate_tokens_spec runs it
+   (run.c:4925-4930): map lookups, then the scan when it proposes more. */
+CWREF_API int cwref_ng_propose(const int *h, int hn, int *out, int cap) {
+  int scan[256];
+  if (cap > 256) cap = 256;
+  int E = ng_draft_map(h, hn, out, cap);
+  int esc = ngram_draft(h, hn, scan, Scfg_n_key, cap);
+  if (esc > E) { E = esc; memcpy(out, scan, (size_t)E * sizeof(int)); }
+  return E;
+}
+
 /* decay/beta transform of layer_linear (run.c:2339-2344). */
 CWREF_API void cwref_decay_beta(const float *A, const float *dt, float *ab, float *bb, int n) {
   for (int i = 0; i < n; i++) { ab[i] = A[i] * softplus(ab[i] + dt[i]); bb[i] = sigmoid(bb[i]); }
