@@ -99,6 +99,7 @@ int main(int argc, char **argv) {
     return 1;
   }
   int32_t *toks = (int32_t *)malloc(sizeof(int32_t) * (size_t)ctx);
+  if (!toks) { fprintf(stderr, "cwen: out of host memory\n"); return 1; }
   int n_tok = 0;
   if (ids) {
     FILE *f = fopen(ids, "rb");
@@ -111,6 +112,7 @@ int main(int argc, char **argv) {
   }
   if (n_tok < 1) { fprintf(stderr, "cwen: %s: no tokens in prompt\n", ids); return 1; }
   int32_t *out = (int32_t *)malloc(sizeof(int32_t) * (size_t)(n_predict ? n_predict : 1));
+  if (!out) { fprintf(stderr, "cwen: out of host memory\n"); return 1; }
   fprintf(stderr, "prefill %d tokens...\n", n_tok);
   cwen_spec_stats st;
   int n = cwen_generate(toks, n_tok, n_predict, out, &cfg, &st);
