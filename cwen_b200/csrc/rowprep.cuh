@@ -1,10 +1,11 @@
-// Row-wise producers of verify-GEMV inputs.
+// Row-wise producers of verify-GEMV inputs and the reductions they share.
 //
-// Every GEMV input row (one per verify position b) is produced by one CTA
-// that holds the whole row in shared memory, so the norm that precedes a
-// GEMV in the reference (rmsnorm run.c:346, the GDN gated norm run.c:2142,
-// the attention gate run.c:2396) fuses with the conversion of the row into
-// the GEMV's f16 hi/lo fragments.
+// A GEMV input row (one per verify position b) is produced by one CTA, or by
+// a thread-block cluster whose CTAs each hold a slice of the row in shared
+// memory and exchange the row-wide sums and maxima through distributed shared
+// memory, so the norm that precedes a GEMV in the reference (rmsnorm
+// run.c:346, the MTP input norms run.c:3100-3102) fuses with the conversion
+// of the row into the GEMV's f16 hi/lo fragments.
 #pragma once
 #include <cooperative_groups.h>
 
