@@ -561,6 +561,19 @@ int cwen_cuda_reset(void) {
 
 int cwen_cuda_n_past(void) { return g_model.n_past; }
 
+int cwen_cuda_model_dims(cwen_dims *out) {
+  if (!out) {
+    set_error("cwen_cuda_model_dims: out is NULL");
+    return CWEN_EINVAL;
+  }
+  if (!g_model.configured) {
+    set_error("cwen_cuda_model_dims: no model configured");
+    return CWEN_ESTATE;
+  }
+  *out = g_model.d;
+  return CWEN_OK;
+}
+
 int cwen_cuda_forward_block(const int *toks, int B, int nlogits) {
   if (!toks) {
     set_error("cwen_cuda_forward_block: toks is NULL");

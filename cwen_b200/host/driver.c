@@ -11,6 +11,7 @@
  * are batch-invariant, so the chunking cannot change a single bit).
  */
 #define _GNU_SOURCE
+#include <errno.h>
 #include <limits.h>
 #include <stdarg.h>
 #include <stdio.h>
@@ -172,11 +173,13 @@ static void ng_evict_one(ngmap *m) {
   }
   m->used_n--;
 }
-static void ng_update(ngmap *m, const int32_t *key, int32_t tok) {
+/* key -> tok with `hits` more hits (counts saturate at INT_MAX); a new key
+   in a full map first evicts one least-hit entry. */
+static void ng_update_n(ngmap *m, const int32_t *key, int32_t tok, int hits) {
   int found;
   size_t i = ng_find(m, key, &found);
   if (found) {
-    if (m->cnt[i] < INT_MAX) m->cnt[i]++;
+    m->cnt[i] = hits < INT_MAX - m->cnt[i] ? m->cnt[i] + hits : INT_MAX;
     m->tok[i] = tok;
     return;
   }
@@ -187,10 +190,11 @@ static void ng_update(ngmap *m, const int32_t *key, int32_t tok) {
   }
   memcpy(m->keys + i * (size_t)m->nk, key, (size_t)m->nk * sizeof(int32_t));
   m->tok[i] = tok;
-  m->cnt[i] = 1;
+  m->cnt[i] = hits;
   m->used[i] = 1;
   m->used_n++;
 }
+static void ng_update(ngmap *m, const int32_t *key, int32_t tok) { ng_update_n(m, key, tok, 1); }
 static void ng_update_range(ngmap *m, const int32_t *h, int a, int b) {
   for (int p = a; p < b; p++)
     if (p - m->nk >= 0) ng_update(m, h + p - m->nk, h[p]);
@@ -242,6 +246,59 @@ static void ng_free(ngmap *m) {
   free(m->used);
 }
 
+/* ---- NGC2 persistence of the map (run.c:4656-4716) ----
+   Header {magic "NGC2", n_key, n_vocab, entries} (uint32), then per occupied
+   slot in slot order {key[n_key], tok, cnt} (int32).  Loading merges counts
+   into the live map; a missing, foreign (other n_key or vocabulary), damaged
+   or truncated file contributes what it validly holds and never fails the
+   run: the map only proposes drafts, which are verified anyway. */
+#define NG_MAGIC 0x3243474eu
+
+static int ng_save_file(const ngmap *m, const char *path, int vocab) {
+  char tmp[4096];
+  if (snprintf(tmp, sizeof tmp, "%s.tmp", path) >= (int)sizeof tmp)
+    return host_fail(CWEN_EINVAL, "ngram cache: path too long");
+  FILE *f = fopen(tmp, "wb");
+  if (!f) return host_fail(CWEN_EINVAL, "ngram cache: %s: %s", tmp, strerror(errno));
+  const uint32_t hdr[4] = {NG_MAGIC, (uint32_t)m->nk, (uint32_t)vocab, (uint32_t)m->used_n};
+  int bad = fwrite(hdr, 4, 4, f) != 4;
+  for (size_t i = 0; !bad && i < m->cap; i++) {
+    if (!m->used[i]) continue;
+    bad |= fwrite(m->keys + i * (size_t)m->nk, 4, (size_t)m->nk, f) != (size_t)m->nk;
+    bad |= fwrite(&m->tok[i], 4, 1, f) != 1 || fwrite(&m->cnt[i], 4, 1, f) != 1;
+  }
+  bad |= fclose(f) != 0;
+  if (bad) {
+    remove(tmp);
+    return host_fail(CWEN_EINVAL, "ngram cache: %s: write failed", tmp);
+  }
+  if (rename(tmp, path)) {
+    remove(tmp);
+    return host_fail(CWEN_EINVAL, "ngram cache: %s: %s", path, strerror(errno));
+  }
+  return CWEN_OK;
+}
+
+static int ng_load_file(ngmap *m, const char *path, int vocab) {
+  FILE *f = fopen(path, "rb");
+  if (!f) return 0;  /* no file yet: a cold start */
+  uint32_t hdr[4];
+  int n = 0;
+  if (fread(hdr, 4, 4, f) == 4 && hdr[0] == NG_MAGIC && (int)hdr[1] == m->nk && (int)hdr[2] == vocab) {
+    int32_t key[256], tc[2];
+    for (uint32_t i = 0; i < hdr[3] && m->used_n < m->cap; i++) {
+      if (fread(key, 4, (size_t)m->nk, f) != (size_t)m->nk || fread(tc, 4, 2, f) != 2) break;
+      if (tc[0] < 0 || tc[0] >= vocab || tc[1] < 1) continue;
+      ng_update_n(m, key, tc[0], tc[1]);
+      n++;
+    }
+  } else {
+    fprintf(stderr, "cwen: ngram cache %s: not an NGC2 map of this n_key and vocabulary; ignoring\n", path);
+  }
+  fclose(f);
+  return n;
+}
+
 /* ---- the counted map as a drafter object (include/cwen_host.h) ---- */
 struct cwen_ngram_map {
   ngmap m;
@@ -270,6 +327,16 @@ void cwen_ngram_map_free(cwen_ngram_map *p) {
 
 void cwen_ngram_map_update(cwen_ngram_map *p, const int32_t *hist, int a, int b) {
   if (p && hist && a >= 0 && b > a) ng_update_range(&p->m, hist, a, b);
+}
+
+int cwen_ngram_map_save(const cwen_ngram_map *p, const char *path, int n_vocab) {
+  if (!p || !path || !path[0] || n_vocab < 1) return host_fail(CWEN_EINVAL, "cwen_ngram_map_save: bad arguments");
+  return ng_save_file(&p->m, path, n_vocab);
+}
+
+int cwen_ngram_map_load(cwen_ngram_map *p, const char *path, int n_vocab) {
+  if (!p || !path || !path[0] || n_vocab < 1) return host_fail(CWEN_EINVAL, "cwen_ngram_map_load: bad arguments");
+  return ng_load_file(&p->m, path, n_vocab);
 }
 
 int cwen_ngram_map_draft(const cwen_ngram_map *p, const int32_t *hist, int hn, int32_t *out, int max_d) {
@@ -353,6 +420,15 @@ int cwen_generate(const int32_t *tokens, int n_tok, int n_gen, int32_t *out, con
   int hn = n_tok, upd = 0, g = 0;
   ngmap ngm;
   const int use_map = !ng_init(&ngm, cfg->n_key);
+  /* CWEN_NGRAM_CACHE: the map persists across runs (run.c:5198-5205) */
+  const char *ngc = getenv("CWEN_NGRAM_CACHE");
+  cwen_dims md;
+  const int vocab = cwen_cuda_model_dims(&md) ? 0 : md.n_vocab;
+  const int use_cache = use_map && ngc && ngc[0] && vocab > 0;
+  if (use_cache) {
+    const int got = ng_load_file(&ngm, ngc, vocab);
+    if (got) fprintf(stderr, "ngram cache: loaded %d entries from %s\n", got, ngc);
+  }
   if (n_gen > 0 && cwen_cuda_n_past() < ctx) {
     hist[hn++] = pend;
     out[n++] = pend;
@@ -431,6 +507,8 @@ int cwen_generate(const int32_t *tokens, int n_tok, int n_gen, int32_t *out, con
   if (n < n_gen) fprintf(stderr, "cwen: context window full (ctx=%d); emitted %d of %d requested tokens\n", ctx, n, n_gen);
   fprintf(stderr, "spec: %lld cycles (%lld drafted, %lld full accept, %lld short; avg kept %.2f)\n", st.cycles,
           st.drafted, st.full, st.shortw, st.drafted ? (double)st.kept / (double)st.drafted : 0.0);
+  if (use_cache && ngm.used_n && ng_save_file(&ngm, ngc, vocab))
+    fprintf(stderr, "cwen: %s\n", cwen_cuda_last_error());  /* the run's tokens stand */
   if (use_map) ng_free(&ngm);
   free(hist);
   if (stats) *stats = st;

@@ -112,6 +112,8 @@ int cwen_cuda_gdn_verify(int nkh, int nvh, int B, const float *proj, int ps, con
 /* ---- the model ---- */
 /* Declare the geometry (run.c:83-91 constants) before any upload. */
 int cwen_cuda_model_config(const cwen_dims *dims);
+/* The configured geometry (CWEN_ESTATE before cwen_cuda_model_config). */
+int cwen_cuda_model_dims(cwen_dims *out);
 /* Upload one GGUF tensor by its GGUF name ("token_embd.weight",
  * "blk.<l>.ffn_gate.weight", "blk.<n_layer>.nextn.eh_proj.weight", ...),
  * validating type and shape like rebind_layers_from_tens (run.c:3366-3465).

@@ -44,6 +44,8 @@ typedef struct {
   int cooldown;   /* CWEN_SPEC_COOLDOWN: plain steps after 3 short walks */
   int debug;      /* CWEN_SPEC_DEBUG: per-cycle trace on stderr */
 } cwen_spec_cfg;
+/* (CWEN_NGRAM_CACHE=FILE, read by cwen_generate itself: the n-gram map of a
+ * speculative run is loaded from FILE before the prompt and saved after.) */
 void cwen_spec_defaults(cwen_spec_cfg *c);
 /* Apply the CWEN_SPEC* / CWEN_MTP environment with the reference's strict
  * parsing; returns CWEN_EINVAL (message in cwen_cuda_last_error) on a bad
@@ -81,6 +83,15 @@ void cwen_ngram_map_update(cwen_ngram_map *m, const int32_t *hist, int a, int b)
  * lookups from the last n_key ids, replaced by cwen_ngram_draft's history
  * scan when that proposes more; at most min(max_d, 256) ids. */
 int cwen_ngram_map_draft(const cwen_ngram_map *m, const int32_t *hist, int hn, int32_t *out, int max_d);
+/* NGC2 persistence (ng_save / ng_load, run.c:4656-4716; the CWEN_NGRAM_CACHE
+ * knob, which the speculative driver honours the same way): save writes
+ * {"NGC2", n_key, n_vocab, entries} and the occupied slots in slot order,
+ * through a temporary file and a rename.  load merges a file's entries into
+ * the map (hit counts add) and returns how many it merged: a missing file,
+ * another n_key or vocabulary, or a damaged tail merges nothing or only the
+ * valid records -- never an error, like the reference's cold start. */
+int cwen_ngram_map_save(const cwen_ngram_map *m, const char *path, int n_vocab);
+int cwen_ngram_map_load(cwen_ngram_map *m, const char *path, int n_vocab);
 
 #ifdef __cplusplus
 }

@@ -106,6 +106,11 @@ CWREF_API int cwref_ng_propose(const int *h, int hn, int *out, int cap) {
   return E;
 }
 
+/* NGC2 persistence of the counted map (ng_save / ng_load, run.c:4656-4716). */
+CWREF_API void cwref_ng_save(const char *path) { ng_save(path); }
+CWREF_API void cwref_ng_load(const char *path) { ng_load(path); }
+CWREF_API long long cwref_ng_used(void) { return (long long)NGM.used_n; }
+
 /* decay/beta transform of layer_linear (run.c:2339-2344). */
 CWREF_API void cwref_decay_beta(const float *A, const float *dt, float *ab, float *bb, int n) {
   for (int i = 0; i < n; i++) { ab[i] = A[i] * softplus(ab[i] + dt[i]); bb[i] = sigmoid(bb[i]); }

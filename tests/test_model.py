@@ -161,6 +161,24 @@ def test_spec_stream_equals_serial(small, max_draft):
     assert st.cycles > 0
 
 
+def test_ngram_cache_knob(small, tmp_path, monkeypatch):
+    """CWEN_NGRAM_CACHE (run.c:5198-5205): a speculative run saves its n-gram
+    map as an NGC2 file; the next run merges it before the prompt and still
+    emits the serial stream."""
+    import cwen_b200
+    L, d = small
+    path = tmp_path / "map.ngc"
+    prompt = _motif_prompt(200, d.n_vocab, 9)
+    ser, _ = cwen_b200.generate(prompt, 48, cwen_b200.spec_cfg(spec=0))
+    monkeypatch.setenv("CWEN_NGRAM_CACHE", str(path))
+    cfg = cwen_b200.spec_cfg(spec=1, use_mtp=0, max_draft=8, n_key=4, min_draft=1)
+    a, _ = cwen_b200.generate(prompt, 48, cfg)
+    hdr = np.frombuffer(path.read_bytes()[:16], np.uint32)
+    assert hdr[0] == 0x3243474E and hdr[1] == 4 and hdr[2] == d.n_vocab and hdr[3] > 0
+    b, _ = cwen_b200.generate(prompt, 48, cfg)
+    assert np.array_equal(a, ser) and np.array_equal(b, ser)
+
+
 def test_forced_rejections_keep_stream(small):
     """Short key + min_draft 1 forces short walks (run through rollback)."""
     import cwen_b200

@@ -136,3 +136,134 @@ def test_map_argument_errors(libs):
     assert not L.cwen_ngram_map_new(257)
     out = np.zeros(4, np.int32)
     assert L.cwen_ngram_map_draft(None, _p(out), 4, _p(out), 4) == -1
+
+
+# ---- NGC2 persistence (ng_save / ng_load, run.c:4656-4716) ----
+V_REF = 248320  # the reference's compiled-in vocabulary, which its files carry
+
+
+def _ngc2_libs(libs):
+    L, ref = libs
+    ref.cwref_ng_save.argtypes = [C.c_char_p]
+    ref.cwref_ng_load.argtypes = [C.c_char_p]
+    ref.cwref_ng_used.restype = C.c_longlong
+    L.cwen_ngram_map_save.argtypes = [C.c_void_p, C.c_char_p, C.c_int]
+    L.cwen_ngram_map_load.argtypes = [C.c_void_p, C.c_char_p, C.c_int]
+    return L, ref
+
+
+def _both_from(L, ref, h, n_key, upto):
+    m = L.cwen_ngram_map_new(n_key)
+    assert m and ref.cwref_ngmap_init(n_key) == 0
+    L.cwen_ngram_map_update(m, _p(h), 0, upto)
+    ref.cwref_ng_update_range(_p(h), 0, upto)
+    return m
+
+
+def _proposals(L, ref, m, h, n_key, points):
+    a, b = np.zeros(16, np.int32), np.zeros(16, np.int32)
+    for hn in points:
+        na = L.cwen_ngram_map_draft(m, _p(h), hn, _p(a), 15)
+        nb = ref.cwref_ng_propose(_p(h), hn, _p(b), 15)
+        assert na == nb and np.array_equal(a[:na], b[:nb]), hn
+
+
+def test_ngc2_file_equals_reference(libs, tmp_path):
+    L, ref = _ngc2_libs(libs)
+    n_key = 4
+    h = _history(np.random.default_rng(21), 4000, V_REF, 37, 0.05)
+    m = _both_from(L, ref, h, n_key, 3000)
+    try:
+        ours, theirs = tmp_path / "ours.ngc", tmp_path / "ref.ngc"
+        assert L.cwen_ngram_map_save(m, str(ours).encode(), V_REF) == 0
+        ref.cwref_ng_save(str(theirs).encode())
+        assert ours.read_bytes() == theirs.read_bytes()
+        assert not (tmp_path / "ours.ngc.tmp").exists()
+        hdr = np.frombuffer(ours.read_bytes()[:16], np.uint32)
+        assert hdr[0] == 0x3243474E and hdr[1] == n_key and hdr[2] == V_REF
+        assert hdr[3] == ref.cwref_ng_used() and len(ours.read_bytes()) == 16 + hdr[3] * (n_key + 2) * 4
+    finally:
+        L.cwen_ngram_map_free(m)
+
+
+def test_ngc2_load_merge_matches_reference(libs, tmp_path):
+    """Each side loads the other's file into a fresh map, twice (the counts
+    merge); both maps then save the same bytes and propose the same ids."""
+    L, ref = _ngc2_libs(libs)
+    n_key = 4
+    h = _history(np.random.default_rng(22), 4000, V_REF, 37, 0.05)
+    m = _both_from(L, ref, h, n_key, 2500)
+    src = tmp_path / "src.ngc"
+    try:
+        assert L.cwen_ngram_map_save(m, str(src).encode(), V_REF) == 0
+    finally:
+        L.cwen_ngram_map_free(m)
+    m = L.cwen_ngram_map_new(n_key)
+    try:
+        assert ref.cwref_ngmap_init(n_key) == 0
+        n1 = L.cwen_ngram_map_load(m, str(src).encode(), V_REF)
+        ref.cwref_ng_load(str(src).encode())
+        assert n1 > 0 and n1 == ref.cwref_ng_used()
+        assert L.cwen_ngram_map_load(m, str(src).encode(), V_REF) == n1  # same keys: counts add
+        ref.cwref_ng_load(str(src).encode())
+        a, b = tmp_path / "a.ngc", tmp_path / "b.ngc"
+        assert L.cwen_ngram_map_save(m, str(a).encode(), V_REF) == 0
+        ref.cwref_ng_save(str(b).encode())
+        assert a.read_bytes() == b.read_bytes()
+        # the reloaded maps draft alike on the rest of the history
+        L.cwen_ngram_map_update(m, _p(h), 2500, 3500)
+        ref.cwref_ng_update_range(_p(h), 2500, 3500)
+        _proposals(L, ref, m, h, n_key, range(2500, 3500, 11))
+    finally:
+        L.cwen_ngram_map_free(m)
+
+
+def test_ngc2_damaged_files_match_reference(libs, tmp_path):
+    """Foreign or damaged files: each side merges exactly the same records."""
+    L, ref = _ngc2_libs(libs)
+    n_key = 4
+    h = _history(np.random.default_rng(23), 3000, V_REF, 37, 0.05)
+    m = _both_from(L, ref, h, n_key, 2000)
+    good = tmp_path / "good.ngc"
+    try:
+        assert L.cwen_ngram_map_save(m, str(good).encode(), V_REF) == 0
+    finally:
+        L.cwen_ngram_map_free(m)
+    blob = bytearray(good.read_bytes())
+    rec = (n_key + 2) * 4
+    bad_tok = bytearray(blob)
+    bad_tok[16 + n_key * 4:16 + n_key * 4 + 4] = np.int32(V_REF).tobytes()       # first record: tok = V
+    bad_cnt = bytearray(blob)
+    bad_cnt[16 + rec + (n_key + 1) * 4:16 + 2 * rec] = np.int32(0).tobytes()      # second record: cnt = 0
+    cases = {
+        "short": bytes(blob[:10]),
+        "magic": b"NGC1" + bytes(blob[4:]),
+        "n_key": bytes(blob[:4]) + np.uint32(5).tobytes() + bytes(blob[8:]),
+        "vocab": bytes(blob[:8]) + np.uint32(1000).tobytes() + bytes(blob[12:]),
+        "truncated": bytes(blob[:16 + 7 * rec + 5]),
+        "bad_tok": bytes(bad_tok),
+        "bad_cnt": bytes(bad_cnt),
+        "count_beyond": bytes(blob[:12]) + np.uint32(1 << 30).tobytes() + bytes(blob[16:]),
+    }
+    for name, data in cases.items():
+        f = tmp_path / f"{name}.ngc"
+        f.write_bytes(data)
+        m = L.cwen_ngram_map_new(n_key)
+        try:
+            assert ref.cwref_ngmap_init(n_key) == 0
+            got = L.cwen_ngram_map_load(m, str(f).encode(), V_REF)
+            ref.cwref_ng_load(str(f).encode())
+            assert got == ref.cwref_ng_used(), name
+            a, b = tmp_path / "a.ngc", tmp_path / "b.ngc"
+            assert L.cwen_ngram_map_save(m, str(a).encode(), V_REF) == 0
+            ref.cwref_ng_save(str(b).encode())
+            assert a.read_bytes() == b.read_bytes(), name
+        finally:
+            L.cwen_ngram_map_free(m)
+    m = L.cwen_ngram_map_new(n_key)
+    try:
+        assert L.cwen_ngram_map_load(m, str(tmp_path / "missing.ngc").encode(), V_REF) == 0
+        assert L.cwen_ngram_map_load(m, None, V_REF) == -1
+        assert L.cwen_ngram_map_save(m, str(tmp_path / "no" / "dir.ngc").encode(), V_REF) == -1
+    finally:
+        L.cwen_ngram_map_free(m)
