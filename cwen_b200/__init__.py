@@ -87,6 +87,7 @@ _SIGS = {
     "cwen_ngram_map_save": (C.c_int, [C.c_void_p, C.c_char_p, C.c_int]),
     "cwen_ngram_map_load": (C.c_int, [C.c_void_p, C.c_char_p, C.c_int]),
     "cwen_cuda_model_dims": (C.c_int, [C.POINTER(Dims)]),
+    "cwen_serve": (C.c_int, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p]),
     "cw_synth_q4_0": (None, [C.c_uint64, C.c_char_p, C.c_int, C.c_int, C.c_void_p, C.c_int]),
     "cw_synth_q8_0": (None, [C.c_uint64, C.c_char_p, C.c_int, C.c_int, C.c_void_p, C.c_int]),
     "cw_synth_normal": (None, [C.c_uint64, C.c_char_p, C.c_float, C.c_float, C.c_void_p, C.c_size_t]),

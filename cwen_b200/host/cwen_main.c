@@ -6,7 +6,8 @@
  * random-init model (no file).  IDS_FILE holds little-endian int32 ids.
  * Generated ids go to stdout, logs to stderr.  Knobs: CWEN_SPEC, CWEN_MTP,
  * CWEN_CTX (64..32768), CWEN_SPEC_NGRAM_N/MAX_DRAFT/MIN_DRAFT/COOLDOWN/DEBUG,
- * CWEN_DEVICE (GPU index).
+ * CWEN_NGRAM_CACHE, CWEN_SERVER (binary-frame server on stdin/stdout,
+ * host/server.c), CWEN_DEVICE (GPU index).
  */
 #define _GNU_SOURCE
 #include <errno.h>
@@ -25,7 +26,26 @@ static void usage(FILE *o) {
           "  IDS_FILE   int32 token ids (omitted: the single token 248044)\n"
           "  N_PREDICT  tokens to generate, >= 0 (default 16)\n"
           "  -d, --draft-tokens N   speculate up to N drafts per verify block (1..15);\n"
-          "                         implies CWEN_SPEC=1\n");
+          "                         implies CWEN_SPEC=1\n"
+          "Environment:\n"
+          "  CWEN_CTX=N             context window, 64..32768 (default 4096)\n"
+          "  CWEN_DEVICE=N          GPU index (default 0)\n"
+          "  CWEN_SERVER=1          binary-frame server on stdin/stdout\n"
+          "  CWEN_SPEC=1            block speculation (greedy-lossless); drafter: the\n"
+          "                         model's MTP nextn head when present, else the n-gram map\n"
+          "  CWEN_MTP=0             do not draft with the MTP head\n"
+          "  CWEN_NGRAM_CACHE=FILE  persist the n-gram map across runs (NGC2)\n"
+          "    CWEN_SPEC_NGRAM_N=N      lookup key length (default 16)\n"
+          "    CWEN_SPEC_MAX_DRAFT=N    max drafts per block, 1..15 (default 8)\n"
+          "    CWEN_SPEC_MIN_DRAFT=N    skip blocks shorter than N drafts (default 2)\n"
+          "    CWEN_SPEC_COOLDOWN=N     plain steps after repeated full rejects (8)\n"
+          "    CWEN_SPEC_DEBUG=1        per-cycle speculation trace on stderr\n");
+}
+
+/* cwen_serve's generator: one request through the C driver. */
+static int serve_generate(void *user, const int32_t *tokens, int n_tok, int n_gen, int32_t *out) {
+  cwen_spec_stats st;
+  return cwen_generate(tokens, n_tok, n_gen, out, (const cwen_spec_cfg *)user, &st);
 }
 
 static int arg_int(const char *a, long lo, long hi, const char *what) {
@@ -65,6 +85,14 @@ int main(int argc, char **argv) {
   cwen_spec_cfg cfg;
   cwen_spec_defaults(&cfg);
   if (cwen_spec_from_env(&cfg)) return 1;
+  int server = 0;  /* CWEN_SERVER: checked before the model load, like the reference */
+  {
+    const char *sv = getenv("CWEN_SERVER");
+    if (sv && sv[0]) {
+      if (strcmp(sv, "0") && strcmp(sv, "1")) { fprintf(stderr, "cwen: CWEN_SERVER must be 0 or 1\n"); return 1; }
+      server = sv[0] == '1';
+    }
+  }
   if (draft > 0) {
     cfg.max_draft = draft;
     cfg.spec = 1;
@@ -97,6 +125,15 @@ int main(int argc, char **argv) {
   if (rc) {
     fprintf(stderr, "cwen: load failed: %s\n", cwen_cuda_last_error());
     return 1;
+  }
+  if (server) {
+    cwen_dims md;
+    if (cwen_cuda_model_dims(&md)) { fprintf(stderr, "cwen: %s\n", cwen_cuda_last_error()); return 1; }
+    fprintf(stderr, "cwen server: model loaded, waiting on stdin\n");
+    rc = cwen_serve(0, 1, ctx, md.n_vocab, serve_generate, &cfg);
+    if (rc) fprintf(stderr, "cwen: %s\n", cwen_cuda_last_error());
+    cwen_cuda_shutdown();
+    return rc ? 1 : 0;
   }
   int32_t *toks = (int32_t *)malloc(sizeof(int32_t) * (size_t)ctx);
   if (!toks) { fprintf(stderr, "cwen: out of host memory\n"); return 1; }

@@ -64,6 +64,18 @@ typedef struct {
 int cwen_generate(const int32_t *tokens, int n_tok, int n_gen, int32_t *out, const cwen_spec_cfg *cfg,
                   cwen_spec_stats *stats);
 
+/* ---- binary-frame server (CWEN_SERVER=1: server_loop, run.c:5063-5078) ---- */
+/* Generate for one request: prefill tokens[0..n_tok) and write up to n_gen
+ * ids to out; the number written, or a negative CWEN_E* code (which ends the
+ * server with that code). */
+typedef int (*cwen_generate_fn)(void *user, const int32_t *tokens, int n_tok, int n_gen, int32_t *out);
+/* Serve request frames from in_fd until end of input: {u32 n_prompt, u32
+ * n_gen, n_prompt x int32 ids} -> {u32 n_out, n_out x int32 ids}.  Frames with
+ * a count outside [1, ctx] or an id outside [0, n_vocab) get the reply 0
+ * (server_read_frame, run.c:4216-4235).  Returns 0 at end of input, or the
+ * error that ended it (a failed reply write, a generation error). */
+int cwen_serve(int in_fd, int out_fd, int ctx, int n_vocab, cwen_generate_fn gen, void *user);
+
 /* ---- drafters (the contract of run.c:4527-4532) ---- */
 /* Prompt-lookup scan (ngram_draft, run.c:4533): propose up to max_d ids that
  * followed the most useful earlier match of the last n_key ids. */
