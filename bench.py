@@ -12,6 +12,9 @@ K timed steps (CUDA events on the engine stream).  The same run also times
 config 3: n-gram speculative decode, draft depth 8, 2048-id motif prompt,
 512 new tokens, checked token-for-token against serial decode.
 
+On one GPU the decode line also carries `gemv_config0` and `gdn_config1`:
+the config-0 and config-1 measurements below (200 steps each, no CPU leg).
+
 Workload `gemv`: the B=8 Q4_0 verify GEMV, W 17408x5120,
 X fp32 8x5120 ~N(0,1), scales |N(0,0.01)|, nibbles uniform.  A step is one
 call over a weight copy from a ring of 8 distinct copies (400 MB > 126 MB L2),
@@ -295,6 +298,35 @@ def run_gemv_ours(args, ws, rank, local):
     return ms, kern, e2e_s, clk, W, X
 
 
+def gemv_config(ws):
+    return {"workload": "config0: Q4_0 verify GEMV W[17408x5120], X fp32[8x5120], Y[8x17408]",
+            "B": GEMV_B, "K": GEMV_K, "M": GEMV_M,
+            "l2": "weight ring of 8 copies (400 MB > 126 MB L2), new copy every step",
+            "parallelism": f"replicas{ws}" if ws > 1 else "single"}
+
+
+def gemv_ours_line(args, ws, rank, local, config):
+    """Config 0 through our engine: the JSON line without the CPU baseline."""
+    hbm, _, peak_kind = peaks()
+    ms, kern, e2e_s, clk, W, X = run_gemv_ours(args, ws, rank, local)
+    gbs = GEMV_BYTES / (ms * 1e-3) / 1e9
+    total = gbs * ws
+    line = {"metric": "verify-GEMV GB/s (B=8 Q4_0, config 0)", "value": round(total, 2), "unit": "GB/s",
+            "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "q4_0 x fp32 -> fp32",
+            "data": "synthetic (seeded)", "config": config, "gpu_launches": kern["launches"], "clocks": clk}
+    kern_ms = kern["ms"]
+    ach = kern["bytes"] / (kern_ms * 1e-3) / 1e9
+    line["roofline"] = {"bound": "hbm", "achieved": round(ach, 1), "peak": hbm, "unit": "GB/s",
+                        "frac": round(ach / hbm, 4), "peak_kind": peak_kind, "traffic": GEMV_NCU_TRAFFIC,
+                        "kernel": "qgemv_kernel<Q4_0, 2 n-tiles of 4 columns>", "kernel_ms": round(kern_ms, 5)}
+    e2e_gbs = GEMV_BYTES / e2e_s / 1e9
+    line["e2e"] = {"value": round(e2e_gbs * ws, 2), "unit": "GB/s", "h2d_bytes_per_step": GEMV_B * GEMV_K * 4,
+                   "d2h_bytes_per_step": GEMV_B * GEMV_M * 4,
+                   "note": "cwen_cuda_gemvb_host: pinned host X in, pinned host Y out, synchronous"}
+    return line, W, X
+
+
 # ---------------- decode (configs 2 / 3) ----------------
 def synth_ids(n, seed, stream, V):
     import cwen_b200
@@ -487,6 +519,22 @@ def main_decode(args, ws, rank, local):
             "e2e": {"value": round(e2e_tps * ws, 3), "unit": "tok/s", "h2d_bytes_per_step": 4,
                     "d2h_bytes_per_step": 12, "method": "cwen_generate (C host driver): (t(256)-t(1))/255"},
             "spec_d8": spec, "mtp_d8": spec.pop("mtp_d8", None), "model_load_s": round(load_s, 1)}
+    if ws == 1 and not args.no_side_workloads:
+        # configs 0 and 1 beside the headline (their own workloads give the
+        # full lines, CPU baselines included); a failure here is reported in
+        # the line and never costs the headline
+        sub = argparse.Namespace(**{**vars(args), "steps": 200, "warmup": 5})
+        for key, fn in (("gemv_config0", lambda: gemv_ours_line(sub, ws, rank, local, gemv_config(ws))[0]),
+                        ("gdn_config1", lambda: gdn_ours_line(sub, ws, rank, local, gdn_config(ws), GDN_METRIC))):
+            try:
+                r = fn()
+                line[key] = {k: r[k] for k in ("metric", "value", "unit", "steps", "ms_per_step", "gpu_launches",
+                                               "clocks", "roofline", "e2e", "timing", "stream_launched_us")
+                             if k in r}
+            except Exception as e:  # noqa: BLE001 -- recorded, not raised
+                line[key] = {"error": f"{type(e).__name__}: {e}"}
+                import cwen_b200
+                cwen_b200.lib().cwen_cuda_shutdown()  # no-op when the engine is not live
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
         res = cpu_decode_baseline(prompt)
         if res:
@@ -659,12 +707,8 @@ def main_gdn(args, ws, rank, local):
     rollback to a rejection index uniform in 0..8, through
     cwen_cuda_gdn_verify on device buffers, over a ring of 64 layers' states
     (253 MB > 126 MB L2) so every step reads its state from HBM."""
-    metric = "GDN verify step with rollback, us per step (config 1)"
-    config = {"workload": "config1: GatedDeltaNet verify step, 48 value / 16 key heads x 128, B=8, "
-                          "state ~N(0,0.1), rejection index uniform 0..8",
-              "B": GDN_B, "heads": [GDN_NVH, GDN_NKH], "head_dim": GDN_D, "conv_channels": GDN_QKV,
-              "l2": "ring of 64 layers' states and inputs (253 MB > 126 MB L2), next layer every step",
-              "parallelism": f"replicas{ws}" if ws > 1 else "single"}
+    metric = GDN_METRIC
+    config = gdn_config(ws)
     if args.impl == "reference":
         if rank != 0:
             return 0
@@ -681,6 +725,29 @@ def main_gdn(args, ws, rank, local):
                           "e2e": {"value": round(us, 3), "unit": "us", "h2d_bytes_per_step": 0,
                                   "d2h_bytes_per_step": 0}}))
         return 0
+    line = gdn_ours_line(args, ws, rank, local, config, metric)
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+        res = cpu_gdn_baseline()
+        if res:
+            line["cpu_baseline"] = {**res[1], "value": round(res[0], 3), "unit": "us"}
+    if rank == 0:
+        print(json.dumps(line))
+    return 0
+
+
+def gdn_config(ws):
+    return {"workload": "config1: GatedDeltaNet verify step, 48 value / 16 key heads x 128, B=8, "
+                        "state ~N(0,0.1), rejection index uniform 0..8",
+            "B": GDN_B, "heads": [GDN_NVH, GDN_NKH], "head_dim": GDN_D, "conv_channels": GDN_QKV,
+            "l2": "ring of 64 layers' states and inputs (253 MB > 126 MB L2), next layer every step",
+            "parallelism": f"replicas{ws}" if ws > 1 else "single"}
+
+
+GDN_METRIC = "GDN verify step with rollback, us per step (config 1)"
+
+
+def gdn_ours_line(args, ws, rank, local, config, metric):
+    """Config 1 through our engine: the JSON line without the CPU baseline."""
     import torch
 
     import cwen_b200
@@ -789,13 +856,7 @@ def main_gdn(args, ws, rank, local):
             "e2e": {"value": round(e2e_s * 1e6, 3), "unit": "us", "h2d_bytes_per_step": GDN_B * GDN_PS * 4,
                     "d2h_bytes_per_step": GDN_B * GDN_Z * 4,
                     "note": "pinned host rows in, head outputs out, stream synchronized every step"}}
-    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
-        res = cpu_gdn_baseline()
-        if res:
-            line["cpu_baseline"] = {**res[1], "value": round(res[0], 3), "unit": "us"}
-    if rank == 0:
-        print(json.dumps(line))
-    return 0
+    return line
 
 
 def main():
@@ -806,6 +867,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="decode", choices=["decode", "gemv", "mtp", "gdn"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-side-workloads", action="store_true",
+                    help="decode: skip the config-0 GEMV and config-1 GDN lines reported beside the headline")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -816,11 +879,7 @@ def main():
             import torch.distributed as dist
             dist.destroy_process_group()
         return rc
-    hbm, bf16, peak_kind = peaks()
-    config = {"workload": "config0: Q4_0 verify GEMV W[17408x5120], X fp32[8x5120], Y[8x17408]",
-              "B": GEMV_B, "K": GEMV_K, "M": GEMV_M,
-              "l2": "weight ring of 8 copies (400 MB > 126 MB L2), new copy every step",
-              "parallelism": f"replicas{ws}" if ws > 1 else "single"}
+    config = gemv_config(ws)
     if args.impl == "reference":
         if rank != 0:
             return 0
@@ -839,22 +898,7 @@ def main():
         print(json.dumps(line))
         return 0
 
-    ms, kern, e2e_s, clk, W, X = run_gemv_ours(args, ws, rank, local)
-    gbs = GEMV_BYTES / (ms * 1e-3) / 1e9
-    total = gbs * ws
-    line = {"metric": "verify-GEMV GB/s (B=8 Q4_0, config 0)", "value": round(total, 2), "unit": "GB/s",
-            "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "q4_0 x fp32 -> fp32",
-            "data": "synthetic (seeded)", "config": config, "gpu_launches": kern["launches"], "clocks": clk}
-    kern_ms = kern["ms"]
-    ach = kern["bytes"] / (kern_ms * 1e-3) / 1e9
-    line["roofline"] = {"bound": "hbm", "achieved": round(ach, 1), "peak": hbm, "unit": "GB/s",
-                        "frac": round(ach / hbm, 4), "peak_kind": peak_kind, "traffic": GEMV_NCU_TRAFFIC,
-                        "kernel": "qgemv_kernel<Q4_0, 2 n-tiles of 4 columns>", "kernel_ms": round(kern_ms, 5)}
-    e2e_gbs = GEMV_BYTES / e2e_s / 1e9
-    line["e2e"] = {"value": round(e2e_gbs * ws, 2), "unit": "GB/s", "h2d_bytes_per_step": GEMV_B * GEMV_K * 4,
-                   "d2h_bytes_per_step": GEMV_B * GEMV_M * 4,
-                   "note": "cwen_cuda_gemvb_host: pinned host X in, pinned host Y out, synchronous"}
+    line, W, X = gemv_ours_line(args, ws, rank, local, config)
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
         res = cpu_gemv_baseline(W, X)
         if res:
