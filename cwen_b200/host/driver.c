@@ -23,6 +23,7 @@
 
 /* ---- knobs ---- */
 void cwen_spec_defaults(cwen_spec_cfg *c) {
+  if (!c) return;
   c->spec = 0;
   c->use_mtp = 1;
   c->max_draft = 8;
@@ -69,6 +70,7 @@ static int env_bool_strict(const char *name, int *out, int *rc) {
 }
 
 int cwen_spec_from_env(cwen_spec_cfg *c) {
+  if (!c) return host_fail(CWEN_EINVAL, "cwen_spec_from_env: cfg is NULL");
   int rc = 0, v;
   if (env_int_strict("CWEN_SPEC", &v, &rc)) {
     if (v != 0 && v != 1) return env_fail("CWEN_SPEC must be 0 or 1");
@@ -99,7 +101,7 @@ int cwen_spec_from_env(cwen_spec_cfg *c) {
 
 /* ---- n-gram drafter ---- */
 int cwen_ngram_draft(const int32_t *h, int hn, int32_t *out, int n_key, int max_d) {
-  if (hn <= n_key || max_d <= 0) return 0;
+  if (!h || !out || n_key < 1 || hn <= n_key || max_d <= 0) return 0;
   const int32_t *tail = h + hn - n_key;
   int best = 0;
   /* newest match first; an older one wins only with a longer continuation */
@@ -390,7 +392,14 @@ int cwen_generate(const int32_t *tokens, int n_tok, int n_gen, int32_t *out, con
     cwen_spec_defaults(&def);
     cfg = &def;
   }
-  if (n_tok < 1 || n_gen < 0 || !tokens || (!out && n_gen)) return CWEN_EINVAL;
+  if (n_tok < 1 || n_gen < 0 || !tokens || (!out && n_gen))
+    return host_fail(CWEN_EINVAL, "cwen_generate: need tokens, n_tok >= 1, n_gen >= 0 and out for n_gen ids");
+  /* the knob ranges of spec_config_init (run.c:4021-4053): the driver's
+     block buffers hold 1 + max_draft rows */
+  if (cfg->max_draft < 1 || cfg->max_draft > BMAX - 1 || cfg->min_draft < 1 || cfg->n_key < 2 ||
+      cfg->n_key > 256 || cfg->cooldown < 0 || cfg->cooldown > 100000)
+    return host_fail(CWEN_EINVAL, "cwen_generate: spec knobs out of range (max_draft 1..%d, min_draft >= 1, "
+                     "n_key 2..256, cooldown 0..100000)", BMAX - 1);
   /* the MTP head drafts only in speculative mode (run.c:5195) */
   const int use_mtp = cfg->spec && cfg->use_mtp && cwen_cuda_mtp_ready();
   int pend = 0, rc = prefill(tokens, n_tok, &pend, use_mtp);

@@ -316,17 +316,20 @@ int cwen_write_synth_gguf(const char *path, const cwen_dims *dims, uint64_t seed
 }
 
 void cwen_dims_reference(cwen_dims *d) {
+  if (!d) return;
   cw_dims s;
   cw_dims_full(&s);
   memcpy(d, &s, sizeof *d);
 }
 void cwen_dims_small(cwen_dims *d) {
+  if (!d) return;
   cw_dims s;
   cw_dims_tiny(&s);
   memcpy(d, &s, sizeof *d);
 }
 
 int cwen_load_synth(uint64_t seed, const cwen_dims *dims, int threads) {
+  if (!dims) return host_fail(CWEN_EINVAL, "cwen_load_synth: dims is NULL");
   cw_dims d;
   memcpy(&d, dims, sizeof d);
   int rc = cwen_cuda_model_config(dims);

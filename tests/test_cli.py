@@ -101,3 +101,26 @@ def test_no_gpu_is_a_clean_error():
     r = _run("synth:1:small", "/nonexistent.ids", "2")
     assert r.returncode == 1, r.stderr
     assert r.stderr.strip().splitlines()[-1].startswith("cwen: "), r.stderr
+
+
+def test_generate_rejects_knobs_outside_the_reference_ranges():
+    """A caller-built cwen_spec_cfg is range-checked like the knobs (the
+    driver's block buffers hold 1 + max_draft rows); the check comes before
+    any engine call, so it runs without a GPU."""
+    import ctypes as C
+
+    import numpy as np
+
+    import cwen_b200
+    L = cwen_b200.lib()
+    toks = np.arange(4, dtype=np.int32)
+    out = np.zeros(4, np.int32)
+    for kw in ({"max_draft": 16}, {"max_draft": 0}, {"min_draft": 0}, {"n_key": 1}, {"n_key": 257},
+               {"cooldown": -1}):
+        c = cwen_b200.spec_cfg(spec=1, **kw)
+        rc = L.cwen_generate(cwen_b200.ptr(toks), 4, 4, cwen_b200.ptr(out), C.byref(c), None)
+        assert rc == -1, kw
+        assert b"spec knobs out of range" in L.cwen_cuda_last_error(), kw
+    assert L.cwen_generate(None, 4, 4, cwen_b200.ptr(out), None, None) == -1
+    c = cwen_b200.spec_cfg(spec=1)
+    assert L.cwen_generate(cwen_b200.ptr(toks), 4, 4, cwen_b200.ptr(out), C.byref(c), None) == -4  # no engine
