@@ -172,6 +172,13 @@ def ref_lib_path():
     return ROOT / "oracle" / "_ref" / f"libcwref_{v}.so", v
 
 
+def synth_threads(ws):
+    """Host threads for generating the seeded model: the cores shared by the
+    ranks of this node, so that N ranks do not each start one per core."""
+    per_node = int(os.environ.get("LOCAL_WORLD_SIZE", ws))
+    return max(1, host_cores() // max(1, per_node))
+
+
 def host_cores():
     try:
         return len(os.sched_getaffinity(0))
@@ -354,7 +361,7 @@ def run_decode_ours(args, ws, rank, local):
     d = cwen_b200.dims("reference")
     d.has_mtp = 1  # blk.64 nextn block (Q8_0), used only by the MTP-drafted run below
     t0 = time.perf_counter()
-    cwen_b200.check(L.cwen_load_synth(DEC_SEED, C.byref(d), 0), "load_synth")
+    cwen_b200.check(L.cwen_load_synth(DEC_SEED, C.byref(d), synth_threads(ws)), "load_synth")
     load_s = time.perf_counter() - t0
     V = d.n_vocab
     prompt = synth_ids(PROMPT_LEN, DEC_SEED, "bench.prompt", V)
@@ -575,7 +582,7 @@ def main_mtp(args, ws, rank, local):
     cwen_b200.check(L.cwen_cuda_init(local, MTP_CTX, 16), "init")
     d = cwen_b200.dims("reference")
     d.has_mtp = 1
-    cwen_b200.check(L.cwen_load_synth(DEC_SEED, C.byref(d), 0), "load_synth")
+    cwen_b200.check(L.cwen_load_synth(DEC_SEED, C.byref(d), synth_threads(ws)), "load_synth")
     prompt = synth_ids(MTP_PROMPT, DEC_SEED, "bench.mtp.prompt", d.n_vocab)
     mtp_cfg = cwen_b200.spec_cfg(spec=1, use_mtp=1, max_draft=8)
     barrier(ws)
