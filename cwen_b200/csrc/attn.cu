@@ -33,6 +33,8 @@ constexpr int KPAD = 260;   // padded K row (floats) in shared memory
 constexpr int PART = 4 + HD;
 constexpr int IPW = 3;      // (row, head) items per warp
 constexpr int MAXIT = 8 * IPW;
+// dynamic shared memory of attn_split_kernel: K chunk (padded rows), V chunk, the CTA's queries
+constexpr size_t SPLIT_SMEM = (size_t)(ACH * KPAD + ACH * HD + MAXIT * HD) * sizeof(float);
 
 // q/k RMSNorm (per head, shared 256-vector weight), RoPE on dims 0..63, KV write.
 __global__ void __launch_bounds__(HD) attn_prep_kernel(const float *__restrict__ proj, int ps, int nh, int nkv,
@@ -224,7 +226,6 @@ __global__ void __launch_bounds__(COMB_THREADS) attn_combine_kernel(const float 
 }
 
 cudaError_t launch_attention(const AttnArgs &a, GemvScratch &s, cudaStream_t st) {
-  (void)s;
   CW_TRY(launch_pdl(attn_prep_kernel, dim3(a.nh + 2 * a.nkv, a.B), HD, 0, st, a.proj, a.ps, a.nh, a.nkv, a.qn, a.kn, a.rope, a.pos0,
                                                                a.qbuf, a.Kc, a.Vc));
   const int last = a.pos0 + a.B - 1;
@@ -232,24 +233,12 @@ cudaError_t launch_attention(const AttnArgs &a, GemvScratch &s, cudaStream_t st)
   const int nsp = last / range + 1;
   const int G = a.nh / a.nkv;
   if (a.nch_max < NSPLIT || G > MAXIT || !a.out) return cudaErrorInvalidValue;
-  const size_t smem = (size_t)(ACH * KPAD + ACH * HD + MAXIT * HD) * sizeof(float);
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(attn_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
-    configured = true;
-  }
+  const size_t smem = SPLIT_SMEM;
   // Rows per CTA: split the block's rows over more CTAs only while the
   // (kv head, split) grid alone is short of two CTAs per SM -- each extra row
   // group stages the split's K/V again, which long contexts cannot afford --
   // and at most MAXIT (row, head) items per CTA.
-  static int n_sm = 0;
-  if (!n_sm) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev);
-    if (n_sm <= 0) n_sm = 148;
-  }
+  const int n_sm = s.G > 0 ? s.G : 148;  // the GEMV grid: one CTA per SM
   const int base = a.nkv * nsp;
   const int min_rb = G >= 8 ? 1 : 8 / G;  // about one (row, head) item per warp
   const int max_rb = MAXIT / G;
@@ -276,6 +265,9 @@ size_t attn_part_floats(int bmax, int nh, int nch_max) { return (size_t)bmax * n
 cudaError_t attn_configure() {
   cudaError_t e;
   if ((e = carveout_max(attn_prep_kernel)) != cudaSuccess) return e;
+  if ((e = cudaFuncSetAttribute(attn_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SPLIT_SMEM)) !=
+      cudaSuccess)
+    return e;
   if ((e = carveout_max(attn_split_kernel)) != cudaSuccess) return e;
   if ((e = carveout_max(attn_combine_kernel)) != cudaSuccess) return e;
   return cudaSuccess;
