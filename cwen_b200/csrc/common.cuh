@@ -77,36 +77,7 @@ inline cudaError_t carveout_max(F *fn) {
                               (int)cudaSharedmemCarveoutMaxShared);
 }
 
-// 16-byte / 8-byte global loads through the read-only path without L1
-// allocation: weights are streamed exactly once per sweep.
-CW_DEV uint4 ldg_stream_u4(const void *p) {
-  uint4 r;
-  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
-               : "l"(p));
-  return r;
-}
-CW_DEV uint2 ldg_stream_u2(const void *p) {
-  uint2 r;
-  asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];" : "=r"(r.x), "=r"(r.y) : "l"(p));
-  return r;
-}
-// Read-only, L1-cached (activations shared by every warp of a CTA).
-CW_DEV uint4 ldg_u4(const void *p) { return __ldg(reinterpret_cast<const uint4 *>(p)); }
-
 CW_DEV uint32_t smem_u32(const void *p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
-
-CW_DEV void cp_async16(void *smem, const void *gmem) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem)), "l"(gmem));
-}
-CW_DEV void cp_async8(void *smem, const void *gmem) {
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_u32(smem)), "l"(gmem));
-}
-CW_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;"); }
-template <int N>
-CW_DEV void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N));
-}
 
 // lop3 with an immediate truth table.
 template <int LUT>
