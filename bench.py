@@ -558,6 +558,42 @@ MTP_CTX, MTP_NEW = 32768, 256
 MTP_PROMPT = MTP_CTX - MTP_NEW - 17
 
 
+def cpu_mtp_baseline(n_gen=16, prompt_len=64):
+    """The reference's MTP-drafted speculation (generate_tokens_spec with the
+    nextn drafter, depth 8) on the same seeded model with blk.64, all host
+    cores, on a bounded sample: a 64-id prompt instead of the 32k prefill
+    (which takes the reference about an hour), (t(1 + n) - t(1)) / n."""
+    path, variant = ref_lib_path()
+    if not path.exists():
+        return None
+    os.environ.setdefault("OMP_NUM_THREADS", str(host_cores()))
+    os.environ.setdefault("OMP_PROC_BIND", "close")
+    os.environ.setdefault("OMP_PLACES", "cores")
+    ref = C.CDLL(str(path))
+    ref.cwref_threads.restype = C.c_int
+    vp = lambda a: a.ctypes.data_as(C.c_void_p)
+    t0 = time.perf_counter()
+    if ref.cwref_load_synth(C.c_uint64(DEC_SEED), 1, 0):
+        return None
+    load_s = time.perf_counter() - t0
+    ref.cwref_alloc_state(4096, 1, 1)
+    ref.cwref_spec_config(8, 2, 16, 8)
+    import cwen_b200
+    prompt = np.ascontiguousarray(cwen_b200.synth_ids(DEC_SEED, "bench.mtp.prompt", 248320, prompt_len), np.int32)
+    out = np.zeros(n_gen + 32, np.int32)
+    t0 = time.perf_counter()
+    ref.cwref_generate(vp(prompt), prompt_len, 1, vp(out))
+    t1 = time.perf_counter() - t0
+    t0 = time.perf_counter()
+    n = ref.cwref_generate(vp(prompt), prompt_len, 1 + n_gen, vp(out))
+    tn = time.perf_counter() - t0
+    return n_gen / max(tn - t1, 1e-9), {
+        "kind": "reference", "cores": int(ref.cwref_threads()), "variant": variant, "n_gen": n_gen,
+        "sample": f"reference MTP spec d=8 (generate_tokens_spec, nextn drafter) on the seeded model with blk.64: "
+                  f"{prompt_len}-id prompt instead of the 32k prefill, (t({1 + n_gen}) - t(1))/{n_gen} "
+                  f"({tn:.1f} s; {n} ids; model synth {load_s:.0f} s)"}
+
+
 def main_mtp(args, ws, rank, local):
     """the hybrid plus the blk.64 MTP block (Q8_0), a 32k
     context pre-filled with random ids, 256 new tokens drafted by the MTP head
@@ -569,9 +605,20 @@ def main_mtp(args, ws, rank, local):
                           f"in a {MTP_CTX} context, {MTP_NEW} new",
               "ctx": MTP_CTX, "parallelism": f"replicas{ws}" if ws > 1 else "single"}
     if args.impl == "reference":
-        if rank == 0:
-            print(json.dumps({"impl": "reference", "unavailable": "config 4 needs a 32767-token CPU prefill "
-                                                                  "(about an hour on the reference)"}))
+        if rank != 0:
+            return 0
+        res = cpu_mtp_baseline(n_gen=max(4, min(32, args.steps)))
+        if res is None:
+            print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref reference build missing"}))
+            return 0
+        tps, info = res
+        print(json.dumps({"impl": "reference", "metric": metric, "value": round(tps, 4), "unit": "tok/s",
+                          "n_gpus": 0, "steps": info["n_gen"], "warmup": 1, "ms_per_step": round(1000.0 / tps, 3),
+                          "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                          "dtype": "q4_0 / q8_0 weights, fp32 activations", "data": "synthetic (seeded)",
+                          "config": config, "cpu_baseline": {**info, "value": round(tps, 4), "unit": "tok/s"},
+                          "e2e": {"value": round(tps, 4), "unit": "tok/s", "h2d_bytes_per_step": 0,
+                                  "d2h_bytes_per_step": 0}}))
         return 0
     import torch
 
