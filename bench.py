@@ -647,7 +647,7 @@ def main_mtp(args, ws, rank, local):
     tps = (MTP_NEW - 1) / max(tn - t1, 1e-9)
     tps = 1.0 / barrier_max(ws, 1.0 / tps)
     if rank == 0:
-        print(json.dumps({
+        line = {
             "metric": metric, "value": round(tps * ws, 3), "unit": "tok/s", "n_gpus": ws, "steps": MTP_NEW,
             "warmup": 1, "ms_per_step": round(1000.0 / tps, 3), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "q4_0 / q8_0 weights, fp32 activations", "data": "synthetic (seeded)",
@@ -659,7 +659,12 @@ def main_mtp(args, ws, rank, local):
                     "avg_kept": round(st.kept / st.drafted, 3) if st.drafted else 0.0,
                     "note": "random-init weights: the nextn head is not trained on the target"},
             "e2e": {"value": round(tps * ws, 3), "unit": "tok/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 12,
-                    "method": "cwen_generate (C host driver): (t(256)-t(1))/255"}}))
+                    "method": "cwen_generate (C host driver): (t(256)-t(1))/255"}}
+        if ws == 1 and not args.no_cpu_baseline:
+            res = cpu_mtp_baseline(n_gen=8)
+            if res:
+                line["cpu_baseline"] = {**res[1], "value": round(res[0], 4), "unit": "tok/s"}
+        print(json.dumps(line))
     return 0
 
 
