@@ -46,3 +46,29 @@ def test_barrier_max_two_ranks():
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
     res = sorted(q.get(timeout=10) for _ in range(ws))
     assert res == [(0, 2, 2.5), (1, 2, 2.5)]
+
+
+def test_reference_arm_under_torchrun_prints_one_line():
+    """`bench.py --impl reference` launched like the driver's N>1 runs: rank 0
+    alone times the reference and prints one JSON line; the other rank exits
+    0 without work."""
+    import json
+    import subprocess
+    import sys
+    from pathlib import Path
+
+    import bench
+    if not bench.ref_lib_path()[0].exists():
+        pytest.skip("reference library (oracle/_ref) not built")
+    root = Path(__file__).resolve().parents[1]
+    env = {**os.environ, "CWEN_DIST_BACKEND": "gloo", "OMP_NUM_THREADS": "2"}
+    r = subprocess.run([sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2",
+                        "--master-addr", "127.0.0.1", "--master-port", str(_free_port()), "bench.py",
+                        "--gpus", "2", "--impl", "reference", "--workload", "gemv", "--steps", "2", "--warmup", "3"],
+                       cwd=root, env=env, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr[-2000:]
+    lines = [ln for ln in r.stdout.splitlines() if ln.startswith("{")]
+    assert len(lines) == 1, r.stdout
+    rec = json.loads(lines[0])
+    assert rec["impl"] == "reference" and rec["unit"] == "GB/s" and rec["value"] > 0
+    assert rec["e2e"]["h2d_bytes_per_step"] == 0 and rec["cpu_baseline"]["kind"] == "reference"
