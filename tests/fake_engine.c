@@ -1,0 +1,109 @@
+/* TEST INFRASTRUCTURE ONLY: a stand-in for the GPU engine, i.e. the
+ * cwen_cuda_* calls the C host driver (cwen_b200/host/driver.c) makes, over a
+ * deterministic toy model whose argmax after token t at slot p is
+ * fake_next(t, p).  Linked with driver.c into a test library (see
+ * tests/test_driver.py), it runs the serial and speculative drivers on the
+ * CPU so their control flow can be compared with a restatement of the
+ * reference's loops.  The conventions are the engine's (include/cwen_cuda.h):
+ * a block scores rows at slots n_past.., accept walks the drafts, commit(k)
+ * keeps rows 0..k. */
+#include <stdio.h>
+#include <string.h>
+
+#include "cwen_cuda.h"
+
+#define FAKE_BMAX 16
+
+static int g_V = 50, g_P = 7, g_Q = 3, g_ctx = 4096;
+static int g_np, g_pending, g_nlog;
+static int g_am[FAKE_BMAX], g_blk[FAKE_BMAX];
+static long long g_blocks, g_serial;
+static char g_err[256] = "no error";
+
+/* vocabulary V; at slots p with p % P == Q the toy model's answer shifts by one
+ * (P <= 0: never), so drafted repeats are sometimes rejected */
+int fake_config(int V, int P, int Q, int ctx) {
+  if (V < 2 || ctx < 1) return -1;
+  g_V = V;
+  g_P = P;
+  g_Q = Q;
+  g_ctx = ctx;
+  g_np = g_pending = 0;
+  g_blocks = g_serial = 0;
+  return 0;
+}
+int fake_next(int t, int p) { return (int)(((long long)t * 7 + 3 + (g_P > 0 && p % g_P == g_Q)) % g_V); }
+long long fake_blocks(void) { return g_blocks; }
+long long fake_serial(void) { return g_serial; }
+
+const char *cwen_cuda_last_error(void) { return g_err; }
+void cwen_host_set_error(const char *msg) { snprintf(g_err, sizeof g_err, "%s", msg ? msg : "?"); }
+int cwen_cuda_ctx(void) { return g_ctx; }
+int cwen_cuda_n_past(void) { return g_np; }
+int cwen_cuda_mtp_ready(void) { return 0; }
+int cwen_cuda_mtp_draft(int pend, int *out, int max_d) {
+  (void)pend;
+  (void)out;
+  (void)max_d;
+  return 0;
+}
+int cwen_cuda_mtp_commit_block(int pos0, const int *toks, int n) {
+  (void)pos0;
+  (void)toks;
+  (void)n;
+  return CWEN_ESTATE;
+}
+int cwen_cuda_model_dims(cwen_dims *d) {
+  memset(d, 0, sizeof *d);
+  d->n_vocab = g_V;
+  return CWEN_OK;
+}
+int cwen_cuda_reset(void) {
+  g_np = 0;
+  g_pending = 0;
+  return CWEN_OK;
+}
+int cwen_cuda_forward_block(const int *toks, int B, int nlogits) {
+  if (g_pending || !toks || B < 1 || B > FAKE_BMAX || nlogits < -1 || nlogits > B || g_np + B > g_ctx) {
+    cwen_host_set_error("fake forward_block: bad call");
+    return CWEN_EINVAL;
+  }
+  for (int j = 0; j < B; j++) {
+    if (toks[j] < 0 || toks[j] >= g_V) return CWEN_ERANGE;
+    g_blk[j] = toks[j];
+    g_am[j] = fake_next(toks[j], g_np + j);
+  }
+  g_pending = B;
+  g_nlog = nlogits;
+  g_blocks++;
+  return CWEN_OK;
+}
+int cwen_cuda_accept(int *k_out, int *ustar_out, int *argmax_out) {
+  if (!g_pending || g_nlog == 0) return CWEN_ESTATE;
+  int k = 0, ustar;
+  if (g_nlog == -1) {
+    ustar = g_am[g_pending - 1];
+  } else {
+    while (k < g_nlog - 1 && g_am[k] == g_blk[k + 1]) k++;
+    ustar = g_am[k];
+  }
+  if (k_out) *k_out = k;
+  if (ustar_out) *ustar_out = ustar;
+  if (argmax_out && g_nlog > 0) memcpy(argmax_out, g_am, (size_t)g_nlog * sizeof(int));
+  return CWEN_OK;
+}
+int cwen_cuda_commit(int k) {
+  if (!g_pending || k < 0 || k >= g_pending) return CWEN_EINVAL;
+  g_np += k + 1;
+  g_pending = 0;
+  return CWEN_OK;
+}
+int cwen_cuda_forward_serial(int token, int need_logits, int *argmax_out) {
+  (void)need_logits;
+  if (g_pending || g_np >= g_ctx) return CWEN_ESTATE;
+  if (token < 0 || token >= g_V) return CWEN_ERANGE;
+  if (argmax_out) *argmax_out = fake_next(token, g_np);
+  g_np++;
+  g_serial++;
+  return CWEN_OK;
+}
