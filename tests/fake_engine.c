@@ -40,18 +40,45 @@ const char *cwen_cuda_last_error(void) { return g_err; }
 void cwen_host_set_error(const char *msg) { snprintf(g_err, sizeof g_err, "%s", msg ? msg : "?"); }
 int cwen_cuda_ctx(void) { return g_ctx; }
 int cwen_cuda_n_past(void) { return g_np; }
-int cwen_cuda_mtp_ready(void) { return 0; }
-int cwen_cuda_mtp_draft(int pend, int *out, int max_d) {
-  (void)pend;
-  (void)out;
-  (void)max_d;
+/* A toy nextn head: it drafts the toy model's answer without the shift, so
+ * its drafts are rejected exactly at the shifted slots.  It drafts only when
+ * every committed slot has been folded into its stream, in order (the
+ * mtp_commit contract, run.c:3143-3159); a fold out of order is counted. */
+static int g_mtp, g_mtp_hpos = -1, g_mtp_bad;
+int fake_config_mtp(int on) {
+  g_mtp = on;
+  g_mtp_hpos = -1;
+  g_mtp_bad = 0;
   return 0;
 }
+int fake_mtp_bad(void) { return g_mtp_bad; }
+int fake_guess(int t, int p) {
+  (void)p;
+  return (int)(((long long)t * 7 + 3) % g_V);
+}
+int cwen_cuda_mtp_ready(void) { return g_mtp; }
 int cwen_cuda_mtp_commit_block(int pos0, const int *toks, int n) {
-  (void)pos0;
-  (void)toks;
-  (void)n;
-  return CWEN_ESTATE;
+  if (!g_mtp) return CWEN_ESTATE;
+  if (!toks || n < 1 || pos0 != g_mtp_hpos + 1 || pos0 + n > g_np) {
+    g_mtp_bad++;
+    cwen_host_set_error("fake mtp_commit_block: fold out of order");
+    return CWEN_EINVAL;
+  }
+  g_mtp_hpos = pos0 + n - 1;
+  return CWEN_OK;
+}
+int cwen_cuda_mtp_draft(int pend, int *out, int max_d) {
+  const int pos_n = g_np - 1;
+  if (!g_mtp || g_mtp_hpos != pos_n || max_d <= 0 || g_pending) return 0;
+  int n = max_d < FAKE_BMAX ? max_d : FAKE_BMAX;
+  if (pos_n + n >= g_ctx) n = g_ctx - 1 - pos_n;
+  if (n <= 0) return 0;
+  int t = pend;
+  for (int i = 0; i < n; i++) {
+    t = fake_guess(t, pos_n + 1 + i);
+    out[i] = t;
+  }
+  return n;
 }
 int cwen_cuda_model_dims(cwen_dims *d) {
   memset(d, 0, sizeof *d);
@@ -61,6 +88,7 @@ int cwen_cuda_model_dims(cwen_dims *d) {
 int cwen_cuda_reset(void) {
   g_np = 0;
   g_pending = 0;
+  g_mtp_hpos = -1;
   return CWEN_OK;
 }
 int cwen_cuda_forward_block(const int *toks, int B, int nlogits) {

@@ -48,6 +48,8 @@ def libs(tmp_path_factory):
     fake.cwen_generate.argtypes = [I32P, C.c_int, C.c_int, I32P, C.POINTER(SpecCfg), C.POINTER(SpecStats)]
     fake.fake_config.argtypes = [C.c_int] * 4
     fake.fake_next.argtypes = [C.c_int, C.c_int]
+    fake.fake_config_mtp.argtypes = [C.c_int]
+    fake.fake_guess.argtypes = [C.c_int, C.c_int]
     fake.fake_blocks.restype = C.c_longlong
     fake.fake_serial.restype = C.c_longlong
     ref = C.CDLL(str(path))
@@ -85,8 +87,10 @@ def ref_serial(prompt, n_gen, ctx, f):
     return out
 
 
-def ref_spec(ref, prompt, n_gen, ctx, cfg, f):
-    """generate_tokens_spec (run.c:4882-5018) with the n-gram drafter."""
+def ref_spec(ref, prompt, n_gen, ctx, cfg, f, guess=None):
+    """generate_tokens_spec (run.c:4882-5018) with the n-gram drafter, or
+    with the nextn head's drafts (mtp_draft, run.c:3166-3187) when `guess`
+    gives the toy head's answer after token t at slot p."""
     H = np.zeros(len(prompt) + n_gen + 64, np.int32)
     hist = [int(t) for t in prompt]
     pos_n = len(prompt) - 1
@@ -118,7 +122,14 @@ def ref_spec(ref, prompt, n_gen, ctx, cfg, f):
         else:
             room = ctx - 1 - (pos_n + 1)
             cap = min(E_cap, room)
-            if cap > 0:
+            if guess is not None:
+                n = min(cap, ctx - 1 - pos_n)
+                t = hist[-1]
+                for i in range(max(n, 0)):
+                    t = guess(t, pos_n + 1 + i)
+                    drafts.append(t)
+                E = len(drafts)
+            elif cap > 0:
                 H[:len(hist)] = hist
                 E = ref.cwref_ng_propose(_p(H), len(hist), _p(D), cap)
                 drafts = [int(x) for x in D[:E]]
@@ -206,6 +217,7 @@ def test_spec_driver_matches_reference_loop(libs, V, P, Q, ctx, n_tok, n_gen, ma
                                             cooldown):
     fake, ref = libs
     assert fake.fake_config(V, P, Q, ctx) == 0
+    fake.fake_config_mtp(0)
     f = Toy(V, P, Q)
     assert all(fake.fake_next(t, p) == f(t, p) for t in range(0, V, max(1, V // 17)) for p in range(40))
     prompt = _motif_prompt(n_tok, V, 37, V + P)
@@ -227,3 +239,37 @@ def test_spec_driver_matches_reference_loop(libs, V, P, Q, ctx, n_tok, n_gen, ma
         assert out[:len(serial)] == serial and len(out) == len(serial) + 1
     if n_gen > 50:
         assert stats[1] > 0  # the drafter did propose
+
+
+MTP_CASES = [
+    # V, P, Q, ctx, n_tok, n_gen, max_draft, min_draft, cooldown
+    (50, 7, 3, 4096, 100, 300, 8, 2, 8),
+    (50, 5, 2, 4096, 60, 200, 15, 1, 0),
+    (50, 0, 0, 4096, 40, 200, 15, 2, 8),      # the head is always right: full accepts, AIMD climbs
+    (50, 3, 1, 4096, 40, 200, 4, 3, 2),       # mostly short walks: min_draft gate and cooldowns
+    (50, 7, 3, 180, 100, 300, 8, 2, 8),       # the context window fills
+]
+
+
+@pytest.mark.parametrize("V,P,Q,ctx,n_tok,n_gen,max_draft,min_draft,cooldown", MTP_CASES)
+def test_mtp_drafted_driver_matches_reference_loop(libs, V, P, Q, ctx, n_tok, n_gen, max_draft, min_draft,
+                                                   cooldown):
+    """The same with the MTP head as the drafter (CWEN_MTP=1): the driver
+    folds every committed slot into the head's stream exactly once and in
+    order (the toy engine counts violations) and drafts as the reference."""
+    fake, ref = libs
+    assert fake.fake_config(V, P, Q, ctx) == 0
+    fake.fake_config_mtp(1)
+    f = Toy(V, P, Q)
+    guess = Toy(V, 0, 0)
+    assert all(fake.fake_guess(t, p) == guess(t, p) for t in range(V) for p in range(10))
+    prompt = np.random.default_rng(V + P + n_tok).integers(0, V, size=n_tok).astype(np.int32)
+    cfg = SpecCfg(1, 1, max_draft, min_draft, 16, cooldown, 0)
+    ref_out, ref_stats = ref_spec(ref, prompt, n_gen, ctx, cfg, f, guess)
+    out, stats = _ours(fake, prompt, n_gen, cfg)
+    assert fake.fake_mtp_bad() == 0
+    assert out == ref_out
+    assert stats == ref_stats, (stats, ref_stats)
+    serial = ref_serial(prompt, n_gen, ctx, f)
+    assert out[:len(serial)] == serial
+    assert stats[1] > 0
