@@ -204,3 +204,22 @@ def test_truncations_of_a_valid_file(L, tmp_path):
     for n in cuts:
         p.write_bytes(buf[:n])
         assert L.cwen_gguf_dims(str(p).encode(), C.byref(d)) == EINVAL, n
+
+
+def test_write_gguf_tool(L, tmp_path):
+    """python -m cwen_b200.write_gguf: the maintained writer of the seeded model."""
+    import subprocess
+    import sys
+
+    import cwen_b200
+    out = tmp_path / "tool.gguf"
+    r = subprocess.run([sys.executable, "-m", "cwen_b200.write_gguf", str(out), "--small", "--mtp", "--seed", "7"],
+                       capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr
+    assert out.read_bytes() == _write(L, tmp_path / "lib.gguf", _small(1))
+    got = cwen_b200.Dims()
+    cwen_b200.check(L.cwen_gguf_dims(str(out).encode(), C.byref(got)), "gguf_dims")
+    assert _dims_tuple(got) == _dims_tuple(_small(1))
+    r = subprocess.run([sys.executable, "-m", "cwen_b200.write_gguf", str(tmp_path / "no" / "x.gguf"), "--small"],
+                       capture_output=True, text=True, timeout=300)
+    assert r.returncode == 1 and "cannot write" in r.stderr
