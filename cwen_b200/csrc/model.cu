@@ -338,7 +338,9 @@ static int mtp_step_dev(int pos0, int B, const Toks16 &toks, const int *dtok, co
   CW_CHECK(timed_gemv(w.gate_up, B, M.h, I, EPI_SWIGLU, st));
   CW_CHECK(timed_gemv(w.down, B, M.mtp_x, H, EPI_ADD, st, M.h, I));
   CW_CHECK(launch_norm_prep(M.mtp_x, w.shared_head_norm, H, B, E.gs, hout, st));
-  E.prof.launches += 11;  // the ffn_down input preparation is counted by timed_gemv
+  // embed, cat_norm_prep, three norm_preps, attention prep/split/combine; the
+  // GEMVs (and any X preparation of theirs) are counted by timed_gemv
+  E.prof.launches += 8;
   return CWEN_OK;
 }
 
