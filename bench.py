@@ -350,6 +350,34 @@ def motif_prompt(n, V, seed=3):
     return p
 
 
+def verify_ceiling(L, prompt, reps=4):
+    """The reference's verify-ceiling gate (bench_spec, run.c:4455-4495): one
+    verify block of B rows against B serial steps from the same context, min
+    of `reps` alternating repetitions; batching must not lose (block <= 1.05 x
+    serial).  Wall clock around calls that end in a host read (accept, the
+    serial argmax), as the reference times them."""
+    import cwen_b200
+    toks = np.ascontiguousarray(prompt[:16], np.int32)
+    k, u = C.c_int(), C.c_int()
+    nxt = C.c_int()
+    res = {}
+    for B in (2, 4, 8, 16):
+        blk_ms = ser_ms = float("inf")
+        for _ in range(reps):
+            t0 = time.perf_counter()
+            cwen_b200.check(L.cwen_cuda_forward_block(cwen_b200.ptr(toks), B, B), "forward_block")
+            cwen_b200.check(L.cwen_cuda_accept(C.byref(k), C.byref(u), None), "accept")
+            cwen_b200.check(L.cwen_cuda_commit(B - 1), "commit")
+            blk_ms = min(blk_ms, (time.perf_counter() - t0) * 1e3)
+            t0 = time.perf_counter()
+            for i in range(B):
+                cwen_b200.check(L.cwen_cuda_forward_serial(int(toks[i]), 1, C.byref(nxt)), "forward_serial")
+            ser_ms = min(ser_ms, (time.perf_counter() - t0) * 1e3)
+        res[str(B)] = {"block_ms": round(blk_ms, 3), "serial_ms": round(ser_ms, 3),
+                       "x": round(ser_ms / blk_ms, 2), "pass": blk_ms <= 1.05 * ser_ms}
+    return res
+
+
 def run_decode_ours(args, ws, rank, local):
     import torch
 
@@ -401,6 +429,10 @@ def run_decode_ours(args, ws, rank, local):
     cwen_b200.check(L.cwen_cuda_profile(0), "profile")
     kern = {"gemv_ms_per_token": gm.value / kp, "gemv_bytes_per_token": gb.value / kp,
             "gemv_calls_per_token": gc.value / kp, "launches_per_token": nl.value / kp}
+    try:
+        kern["verify_ceiling"] = verify_ceiling(L, prompt)
+    except Exception as e:  # noqa: BLE001 -- reported beside the headline, never in place of it
+        kern["verify_ceiling"] = {"error": f"{type(e).__name__}: {e}"}
     # end to end through the public host API (bench_toks method): (t(n) - t(1)) / (n - 1)
     t0 = time.perf_counter()
     cwen_b200.generate(prompt, 1, serial)
@@ -525,7 +557,8 @@ def main_decode(args, ws, rank, local):
                          "gemv_share_of_step": round(kern["gemv_ms_per_token"] / ms, 3)},
             "e2e": {"value": round(e2e_tps * ws, 3), "unit": "tok/s", "h2d_bytes_per_step": 4,
                     "d2h_bytes_per_step": 12, "method": "cwen_generate (C host driver): (t(256)-t(1))/255"},
-            "spec_d8": spec, "mtp_d8": spec.pop("mtp_d8", None), "model_load_s": round(load_s, 1)}
+            "spec_d8": spec, "mtp_d8": spec.pop("mtp_d8", None), "model_load_s": round(load_s, 1),
+            "verify_ceiling": kern.get("verify_ceiling")}
     if ws == 1 and not args.no_side_workloads:
         # configs 0 and 1 beside the headline (their own workloads give the
         # full lines, CPU baselines included); a failure here is reported in
