@@ -223,3 +223,36 @@ def test_write_gguf_tool(L, tmp_path):
     r = subprocess.run([sys.executable, "-m", "cwen_b200.write_gguf", str(tmp_path / "no" / "x.gguf"), "--small"],
                        capture_output=True, text=True, timeout=300)
     assert r.returncode == 1 and "cannot write" in r.stderr
+
+
+def test_mutated_files_never_crash(L, tmp_path):
+    """Fuzz in the spirit of the reference's loader fuzzer (run.c:3811-3926):
+    random flips, overwrites and cuts of a valid file are accepted or
+    rejected -- never a crash, never a read outside the mapping (a fault here
+    would end the test process)."""
+    import cwen_b200
+    base = bytearray(_write(L, tmp_path / "m.gguf", _small(1)))
+    _, _, tensors, data = _read_gguf(bytes(base))
+    rng = np.random.default_rng(1234)
+    p = tmp_path / "fz.gguf"
+    d = cwen_b200.Dims()
+    outcomes = set()
+    for it in range(400):
+        b = bytearray(base)
+        kind = it % 4
+        if kind == 0:  # flip bytes in the header and tensor table
+            for _ in range(int(rng.integers(1, 6))):
+                b[int(rng.integers(0, data))] ^= int(rng.integers(1, 256))
+        elif kind == 1:  # a random u64 over a count, dim or offset field
+            pos = int(rng.integers(4, data - 8))
+            b[pos:pos + 8] = int(rng.integers(0, 1 << 63)).to_bytes(8, "little")
+        elif kind == 2:  # cut anywhere
+            b = b[:int(rng.integers(0, len(b)))]
+        else:  # a huge or tiny value in a tensor's dims
+            pos = int(rng.integers(24, data - 8))
+            b[pos:pos + 8] = int(rng.choice([0, 1, 31, 0x7FFFFFFF, 0x80000000, 1 << 40])).to_bytes(8, "little")
+        p.write_bytes(bytes(b))
+        rc = L.cwen_gguf_dims(str(p).encode(), C.byref(d))
+        assert rc in (0, EINVAL, -3), rc
+        outcomes.add(rc)
+    assert EINVAL in outcomes

@@ -267,3 +267,36 @@ def test_ngc2_damaged_files_match_reference(libs, tmp_path):
         assert L.cwen_ngram_map_save(m, str(tmp_path / "no" / "dir.ngc").encode(), V_REF) == -1
     finally:
         L.cwen_ngram_map_free(m)
+
+
+def test_ngc2_mutated_files_never_crash(libs, tmp_path):
+    """Random flips and cuts of an NGC2 file: a load merges what it can and
+    never crashes (the reference's cache fuzz hook, cw_fuzz_ngcache)."""
+    L, ref = _ngc2_libs(libs)
+    n_key = 4
+    h = _history(np.random.default_rng(31), 2000, V_REF, 37, 0.05)
+    m = _both_from(L, ref, h, n_key, 1500)
+    src = tmp_path / "src.ngc"
+    try:
+        assert L.cwen_ngram_map_save(m, str(src).encode(), V_REF) == 0
+    finally:
+        L.cwen_ngram_map_free(m)
+    base = bytearray(src.read_bytes())
+    rng = np.random.default_rng(5)
+    f = tmp_path / "fz.ngc"
+    for it in range(150):
+        b = bytearray(base)
+        if it % 2:
+            for _ in range(int(rng.integers(1, 8))):
+                b[int(rng.integers(0, len(b)))] ^= int(rng.integers(1, 256))
+        else:
+            b = b[:int(rng.integers(0, len(b)))]
+        f.write_bytes(bytes(b))
+        m = L.cwen_ngram_map_new(n_key)
+        try:
+            got = L.cwen_ngram_map_load(m, str(f).encode(), V_REF)
+            assert got >= 0
+            out = np.zeros(16, np.int32)
+            assert L.cwen_ngram_map_draft(m, _p(h), 1500, _p(out), 15) >= 0
+        finally:
+            L.cwen_ngram_map_free(m)

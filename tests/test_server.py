@@ -154,3 +154,22 @@ def test_cli_server_on_gpu():
     finally:
         L.cwen_cuda_shutdown()
     assert got == want + [[]]
+
+
+def test_random_byte_streams_never_crash(L):
+    """Random request streams (the reference fuzzes its frame decoder,
+    run.c:3873-3891): every complete frame gets exactly one reply, nothing
+    crashes, and the loop ends at end of input."""
+    rng = np.random.default_rng(99)
+    for it in range(60):
+        parts = []
+        for _ in range(int(rng.integers(1, 6))):
+            n = int(rng.integers(0, 8))
+            ids = rng.integers(-3, VOCAB + 3, size=n).tolist()
+            parts.append(_frame(ids, int(rng.integers(0, CTX + 3)), n_prompt=int(rng.choice([n, n, 0, CTX + 1]))))
+        data = b"".join(parts)
+        if it % 3 == 0:
+            data = data[:int(rng.integers(0, len(data) + 1))]
+        rc, out, _ = _serve(L, data, echo)
+        assert rc == 0
+        _replies(out)  # well-formed: a count and that many ids, frame after frame
