@@ -80,6 +80,21 @@ int cwen_cuda_mtp_draft(int pend, int *out, int max_d) {
   }
   return n;
 }
+/* the loader's engine calls: no engine here (the host code's own paths end
+ * at these with CWEN_ESTATE, as on a machine without a GPU) */
+int cwen_cuda_model_config(const cwen_dims *dims) {
+  (void)dims;
+  return CWEN_ESTATE;
+}
+int cwen_cuda_upload(const char *name, int type, const void *host, int ne0, int ne1) {
+  (void)name;
+  (void)type;
+  (void)host;
+  (void)ne0;
+  (void)ne1;
+  return CWEN_ESTATE;
+}
+int cwen_cuda_model_finalize(void) { return CWEN_ESTATE; }
 int cwen_cuda_model_dims(cwen_dims *d) {
   memset(d, 0, sizeof *d);
   d->n_vocab = g_V;
