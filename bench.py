@@ -513,9 +513,8 @@ def cpu_decode_baseline(prompt, budget_s: float = 20.0):
 
 def main_decode(args, ws, rank, local):
     hbm, bf16, peak_kind = peaks()
-    config = {"workload": "config2: serial greedy decode, random-init 27B hybrid (64 layers, Q4_0, "
-                          "scales |N(0,0.01)|), prompt 512 random ids",
-              "model": "cwen qwen35-style hybrid 27B (GDN:attention 3:1), synthetic weights",
+    config = {"workload": "config2: serial greedy decode, random-init 27B hybrid (64 layers, GDN:attention 3:1, "
+                          "Q4_0, scales |N(0,0.01)|, seeded synthetic weights), prompt 512 random ids",
               "prompt": PROMPT_LEN, "ctx": DEC_CTX, "batch": 1,
               "l2": "every step streams 14.4 GB of weights (>> 126 MB L2)",
               "parallelism": f"replicas{ws} (independent sequence per GPU)" if ws > 1 else "single"}
