@@ -320,7 +320,7 @@ def gemv_ours_line(args, ws, rank, local, config):
     total = gbs * ws
     line = {"metric": "verify-GEMV GB/s (B=8 Q4_0, config 0)", "value": round(total, 2), "unit": "GB/s",
             "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "q4_0 x fp32 -> fp32",
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "numerics": "q4_0 weights x f32 X -> f32 Y (f16 hi+lo tensor-core operands, f32 accumulate)",
             "data": "synthetic (seeded)", "config": config, "gpu_launches": kern["launches"], "clocks": clk}
     kern_ms = kern["ms"]
     ach = kern["bytes"] / (kern_ms * 1e-3) / 1e9
@@ -531,7 +531,7 @@ def main_decode(args, ws, rank, local):
         print(json.dumps({"impl": "reference", "metric": metric, "value": round(tps, 4), "unit": "tok/s",
                           "n_gpus": 0, "steps": args.steps, "warmup": args.warmup,
                           "ms_per_step": round(1000.0 / tps, 3), "higher_is_better": True, "scaling": "weak",
-                          "vs_baseline": None, "dtype": "q4_0 weights, fp32 activations", "data": "synthetic (seeded)",
+                          "vs_baseline": None, "dtype": "f32", "numerics": "q4_0 weights, f32 activations", "data": "synthetic (seeded)",
                           "config": config, "cpu_baseline": {**info, "value": round(tps, 4), "unit": "tok/s"},
                           "e2e": {"value": round(tps, 4), "unit": "tok/s", "h2d_bytes_per_step": 0,
                                   "d2h_bytes_per_step": 0}}))
@@ -543,7 +543,7 @@ def main_decode(args, ws, rank, local):
     ach = kern["gemv_bytes_per_token"] / (kern["gemv_ms_per_token"] * 1e-3) / 1e9
     line = {"metric": metric, "value": round(tps * ws, 3), "unit": "tok/s", "n_gpus": ws, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "q4_0 weights, fp32 activations (f16 hi+lo MMA, fp32 accumulate)",
+            "vs_baseline": None, "dtype": "f32", "numerics": "q4_0 weights, f32 activations (f16 hi+lo tensor-core operands, f32 accumulate)",
             "data": "synthetic (seeded random-init weights, random prompt ids)", "config": config,
             "gpu_launches": int(round(kern["launches_per_token"] * args.steps)), "clocks": clk,
             "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": hbm, "unit": "GB/s",
@@ -647,7 +647,7 @@ def main_mtp(args, ws, rank, local):
         print(json.dumps({"impl": "reference", "metric": metric, "value": round(tps, 4), "unit": "tok/s",
                           "n_gpus": 0, "steps": info["n_gen"], "warmup": 1, "ms_per_step": round(1000.0 / tps, 3),
                           "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-                          "dtype": "q4_0 / q8_0 weights, fp32 activations", "data": "synthetic (seeded)",
+                          "dtype": "f32", "numerics": "q4_0 / q8_0 weights, f32 activations", "data": "synthetic (seeded)",
                           "config": config, "cpu_baseline": {**info, "value": round(tps, 4), "unit": "tok/s"},
                           "e2e": {"value": round(tps, 4), "unit": "tok/s", "h2d_bytes_per_step": 0,
                                   "d2h_bytes_per_step": 0}}))
@@ -682,7 +682,7 @@ def main_mtp(args, ws, rank, local):
         line = {
             "metric": metric, "value": round(tps * ws, 3), "unit": "tok/s", "n_gpus": ws, "steps": MTP_NEW,
             "warmup": 1, "ms_per_step": round(1000.0 / tps, 3), "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "q4_0 / q8_0 weights, fp32 activations", "data": "synthetic (seeded)",
+            "vs_baseline": None, "dtype": "f32", "numerics": "q4_0 / q8_0 weights, f32 activations", "data": "synthetic (seeded)",
             "config": config, "clocks": clk,
             "prefill": {"tokens": MTP_PROMPT, "seconds": round(t1, 2), "tok_s": round(MTP_PROMPT / t1, 1),
                         "note": "blocks of 16 verify rows, each folded into the nextn stream in one 16-row MTP pass; includes the first token"},
@@ -983,7 +983,7 @@ def main():
         line = {"impl": "reference", "metric": "verify-GEMV GB/s (B=8 Q4_0, config 0)", "value": round(gbs, 2),
                 "unit": "GB/s", "n_gpus": 0, "steps": args.steps, "warmup": args.warmup,
                 "ms_per_step": round(GEMV_BYTES / gbs / 1e6, 4), "higher_is_better": True, "scaling": "weak",
-                "vs_baseline": None, "dtype": "q4_0 x fp32 -> fp32", "data": "synthetic (seeded)",
+                "vs_baseline": None, "dtype": "f32", "numerics": "q4_0 weights x f32 X -> f32 Y (f16 hi+lo tensor-core operands, f32 accumulate)", "data": "synthetic (seeded)",
                 "config": config, "cpu_baseline": {**info, "value": round(gbs, 2), "unit": "GB/s"},
                 "e2e": {"value": round(gbs, 2), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
         print(json.dumps(line))
