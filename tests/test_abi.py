@@ -74,3 +74,10 @@ def test_every_entry_point_before_init_fails_cleanly(built):
         assert L.cwen_cuda_last_error(), name
         called += 1
     assert called >= 20
+
+
+def test_python_binding_declares_every_entry_point(built):
+    """cwen_b200._SIGS gives every C-ABI function of include/*.h its ctypes
+    signature, so Python callers never pass arguments unchecked."""
+    import cwen_b200
+    assert not sorted(_declared() - set(cwen_b200._SIGS))
