@@ -74,7 +74,7 @@ cudaError_t timed_gemv(const QMat &m, int B, float *Y, int ys, int epi, cudaStre
   Prof &P = E.prof;
   if (!X) E.prof.launches += 1;
   else if (norm_w) E.prof.launches += gemv_norm_fused(m, X, xs, B, E.gs) ? 1 : 2;
-  else E.prof.launches += gemv_uses_local_x(m, E.gs) ? 1 : 2;
+  else E.prof.launches += gemv_uses_local_x(m, X, xs, E.gs) ? 1 : 2;
   auto run = [&]() {
     if (!X) return gemv_run(m, B, Y, ys, epi, E.gs, st);
     if (norm_w) return gemv_run_xn(m, X, xs, norm_w, B, Y, ys, epi, E.gs, st);

@@ -9,30 +9,31 @@
 // B = 8 columns at 28 FLOP/byte is beyond what the CUDA cores can do at HBM
 // speed, so the block dot runs on the tensor cores: (q - 8) is exact in f16,
 // and X is split into f16 hi + lo parts (x = hi + lo to ~2^-22 relative) after
-// a per-column power-of-two scale that keeps it inside f16 range.  One
-// m16n8k16 B operand carries the hi parts of 4 columns and their lo parts,
-// so per 16 rows x 32 weights x 4 columns two MMAs give
-//   c_hi = A*Xhi(k0..15) + A*Xhi(k16..31),  c_lo = the same with Xlo
-// (fp32 accumulate inside the MMA), then acc_hi = fma(d, c_hi, acc_hi) and
-// acc_lo likewise on the CUDA cores -- the reference's per-block scale,
-// applied to fp32 partials; y = (acc_hi + acc_lo) * 2^-e at the end.
+// a per-column power-of-two scale that keeps it inside f16 range.  The hi and
+// lo parts are two m16n8k16 B operands of 8 columns each; per 16 rows x 32
+// weights x 8 columns four MMAs chain into one fp32 result
+//   c = A*Xhi(k0..15) + A*Xlo(k0..15) + A*Xhi(k16..31) + A*Xlo(k16..31)
+// (products exact, fp32 accumulate inside the MMA), then acc = fma(d, c, acc)
+// on the CUDA cores -- the reference's per-block scale, applied to an fp32
+// block partial; y = acc * 2^-e at the end.
 //
 // Batch invariance.  Column b of any call depends only on column b of X: the
-// n-tile of 4 columns a column falls in runs the same MMA/FMA chain whether
+// n-tile of 8 columns a column falls in runs the same MMA/FMA chain whether
 // or not another n-tile runs, and the K partition (below) depends on the
 // matrix shape and grid only, never on B.  So a B-row verify block produces
 // the same bits as B single-row calls.
 //
 // Work split.  A fixed persistent grid of G <= #SM CTAs, one per SM, takes
 // equal contiguous shares of the (512-row tile, k-pair) space ("stream-K").
-// A tile cut between CTAs is reduced by the last CTA to arrive, summing the
-// partials in k order, so the result does not depend on arrival order.
+// A tile cut between CTAs is reduced by its contributors, each summing a
+// share of the rows over all contributors' partials in CTA (k) order, so the
+// result does not depend on arrival order.
 //
 // Memory.  The weights of one (tile, k-pair) -- 32 m-tiles of 16 rows, one
 // contiguous 18 KB (Q4_0) / 34 KB (Q8_0) block in the repacked layout -- and
 // the X fragments of that k-pair stream HBM -> shared memory as two bulk
-// (TMA) copies per stage into an 8-stage (Q8_0: 5) ring, issued by one
-// producer thread; 16 consumer warps (two m-tiles each) compute from shared
+// (TMA) copies per stage into an 8-stage (Q8_0: 5) ring, issued by two
+// producer threads; 16 consumer warps (two m-tiles each) compute from shared
 // memory and release each stage through an mbarrier.  Large copies matter:
 // the issue cost of a bulk copy is nearly independent of its size up to
 // ~9 KB.  Every wait is bounded in time; a timeout raises an error flag and
@@ -166,13 +167,12 @@ cudaError_t qmat_repack(const QMat &dst, const uint8_t *src, int M, int mt_off, 
 
 // ---- X preparation (launch_row_prep: one thread-block cluster per column) ----
 // Per column b: exponent e with max|x|*2^e in [2^14, 2^15), then per 32-block
-// the f16 hi and lo parts of the scaled column.  Columns
-// come in n-tiles of 4; in the m16n8k16 B operand of n-tile b/4, B column
-// b%4 holds the hi parts and B column b%4 + 4 the lo parts, so one MMA
-// multiplies a weight tile with both.  Lane (g, t) of a B operand holds, in
-// the K order the A fragments use,
+// the f16 hi and lo parts of the scaled column.  Columns come in n-tiles of
+// 8; column b is B-operand column b%8 of n-tile b/8, with one operand of hi
+// parts and one of lo parts.  Lane (g, t) of a B operand holds, in the K
+// order the A fragments use,
 //   (x[4t], x[4t+2]) (x[4t+1], x[4t+3]) (x[4t+16], x[4t+18]) (x[4t+17], x[4t+19])
-// of B column g; one uint4 per (32-block, n-tile, lane).
+// of column g; per (32-block, n-tile) 32 uint4 of hi parts then 32 of lo parts.
 cudaError_t gemv_prep_x(const float *X, int xs, int B, int K, GemvScratch &s, cudaStream_t st) {
   if (B < 1 || B > QG_MAXB || K % 64 || K > s.kmax) return cudaErrorInvalidValue;
   return launch_row_prep(X, xs, K, B, s, st);
@@ -211,30 +211,17 @@ CW_DEV void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
 }
 
-// Fold the lo-part accumulators into the hi-part ones: lane (g, t < 2) holds
-// B columns 2t, 2t+1 (hi parts), lane (g, t + 2) the same columns' lo parts.
-// Afterwards lanes t < 2 hold the sums (hi + lo, in that order).
-template <int NT>
-CW_DEV void fold_lo(float (&acc)[2][NT][4]) {
-#pragma unroll
-  for (int mt = 0; mt < 2; mt++)
-#pragma unroll
-    for (int n = 0; n < NT; n++)
-#pragma unroll
-      for (int i = 0; i < 4; i++) acc[mt][n][i] += __shfl_xor_sync(0xffffffffu, acc[mt][n][i], 2);
-}
-
-// Apply the epilogue for one warp's folded accumulators (rows of m-tiles
-// mt0, mt0+1; lanes t < 2 carry the columns n*4 + 2t + {0, 1}).
+// Apply the epilogue for one warp's accumulators (rows of m-tiles mt0,
+// mt0+1).  Lane (g, t) holds, per n-tile n, rows g and g+8 of columns
+// n*8 + 2t and n*8 + 2t + 1.
 template <int NT>
 CW_DEV void gemv_epilogue(const GemvArgs &a, int mt0, bool has1, const float (&acc)[2][NT][4], int g, int t,
                           const float *xun) {
-  if (t >= 2) return;
 #pragma unroll
   for (int n = 0; n < NT; n++) {
 #pragma unroll
     for (int i = 0; i < 4; i++) {
-      const int col = n * 4 + 2 * t + (i & 1);
+      const int col = n * 8 + 2 * t + (i & 1);
       if (col >= a.B) continue;
       const float sc = xun ? xun[col] : __int_as_float((127 - __ldg(a.xexp + col)) << 23);
       const int rr = g + ((i >> 1) << 3);
@@ -268,13 +255,13 @@ CW_DEV float split_unscale(const GemvArgs &a, int col) {
 }
 
 // Epilogue of a reduced split-tile share: lane (mt, row) holds row `row` of
-// m-tile mt0 + mt, four columns per n-tile.  The whole warp calls it (the
-// SwiGLU pairs gate and up rows across the warp's halves).
-template <int NT>
-CW_DEV void split_epilogue(const GemvArgs &a, int mt0, int mt, int row, bool live, const float4 (&sum)[NT],
+// m-tile mt0 + mt, four columns per float4 (NC4 of them).  The whole warp
+// calls it (the SwiGLU pairs gate and up rows across the warp's halves).
+template <int NC4>
+CW_DEV void split_epilogue(const GemvArgs &a, int mt0, int mt, int row, bool live, const float4 (&sum)[NC4],
                            float *wst) {
 #pragma unroll
-  for (int n = 0; n < NT; n++) {
+  for (int n = 0; n < NC4; n++) {
     const float e4[4] = {sum[n].x, sum[n].y, sum[n].z, sum[n].w};
 #pragma unroll
     for (int j = 0; j < 4; j++) {
@@ -309,76 +296,85 @@ CW_DEV void split_epilogue(const GemvArgs &a, int mt0, int mt, int row, bool liv
   }
 }
 
+// Shared-memory layout of the GEMV.  X fragments per (32-block, n-tile of 8
+// columns): 64 uint4 (32 lanes of hi parts, then 32 of lo parts) = 1 KB, so
+// one k-pair of NT n-tiles is NT * 2 KB.
 template <int TYPE, int NT, bool XL = false>
 struct QgLayout {
   static constexpr int CHUNK = TYPE == 8 ? 1088 : 576;       // one m-tile x one k-pair
   static constexpr int QB = TYPE == 8 ? 1024 : 512;          // its quant bytes (scales follow)
   static constexpr int WB = QG_TILE_MT * CHUNK;              // weights of one (tile, k-pair)
-  static constexpr int XB = XL ? 0 : NT * 1024;              // X fragments of one k-pair (streamed)
+  static constexpr int XKP = NT * 2048;                      // X fragments of one k-pair
+  static constexpr int XB = XL ? 0 : XKP;                    // ... streamed with each stage
   static constexpr int STAGE = WB + XB;
   static constexpr int STAGES = TYPE == 8 ? 5 : 8;
   static constexpr int BAR_OFF = STAGES * STAGE;
-  // local-X variant: the CTA's k-range of X fragments, resident (<= QG_XL_KP k-pairs x 4 n-tiles)
+  // local-X variant: the CTA's k-range of X fragments, resident (<= QG_XL_KP k-pairs)
   static constexpr int XL_OFF = BAR_OFF + 256;
-  static constexpr int XL_BYTES = XL ? QG_XL_KP * 4 * 1024 : 0;
-  static constexpr int XE_OFF = XL_OFF + XL_BYTES;  // per column: 2^-e [16] floats, scratch [16][16] floats
-  static constexpr int SMEM = XE_OFF + (XL ? 64 + 16 * 16 * 4 : 0);
+  static constexpr int XL_BYTES = XL ? QG_XL_KP * XKP : 0;
+  // per column: 2^-e [16] floats, the warps' output sums of squares [16][16],
+  // the prologue's per-warp column maxima [16]
+  static constexpr int XE_OFF = XL_OFF + XL_BYTES;
+  static constexpr int SMEM = XE_OFF + (XL ? 64 + 16 * 16 * 4 + 16 * 4 : 0);
   static_assert(WB % 16 == 0 && XB % 16 == 0 && STAGE % 16 == 0, "bulk copies need 16-byte multiples");
   static_assert(SMEM <= 227 * 1024, "shared memory");
 };
 
-// Persistent stream-K GEMV: warps 0..15 consume (warp w owns m-tiles 2w, 2w+1
-// of the current 512-row tile); lane 0 of warp 16 streams the weights and
-// lane 0 of warp 17 the X fragments.
 // Local X (run by the 16 consumer warps once, after pdl_wait): the CTA's
 // k-range [64*ka0, 64*(ka0+nkp)) of every column of the raw rows X becomes
 // f16 hi/lo fragments in shared memory, scaled by the CTA's own power of two
 // 2^e (max |x| over the range in [2^14, 2^15)); xun[col] = 2^-e unscales the
 // CTA's results.  The fragments hold the same values and layout gemv_prep_x
-// emits, except for the exponent's range.  Warp b owns column b; lane l holds
-// the 32-blocks l and l + 32 of the range in registers (one load round trip),
-// so 2 * nkp <= 64.
+// emits, except for the exponent's range.  Every warp works: a column gets
+// 16 / B warps (at least one), each lane loads 8 values per item (item =
+// 32-block x lane quad t), keeps them in registers while the column maxima
+// are combined through shared memory (one barrier), then converts them.
 template <int NT>
-CW_DEV void x_local_prologue(const GemvArgs &a, uint4 *xl, float *xun, int ka0, int nkp) {
+CW_DEV void x_local_prologue(const GemvArgs &a, uint4 *xl, float *xun, float *cmax, int ka0, int nkp) {
   constexpr int NTH = QG_CONS_WARPS * 32;
-  const int lane = threadIdx.x & 31, b = threadIdx.x >> 5;
-  const int nblk = 2 * nkp;
-  if (b < a.B) {
-    const float4 *x = reinterpret_cast<const float4 *>(a.xr + (size_t)b * a.xrs + (size_t)ka0 * 64);
-    const float4 *wn = reinterpret_cast<const float4 *>(a.xw + (size_t)ka0 * 64);
+  constexpr int MAXI = QG_XL_KP * 2 * 4 / 32;  // items per lane with one warp per column
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int nitems = 2 * nkp * 4;
+  const int wpc = a.B >= QG_CONS_WARPS ? 1 : QG_CONS_WARPS / a.B;  // warps per column
+  const int b = w / wpc, sub = w - b * wpc;
+  const bool live = b < a.B;
+  float4 v[MAXI][2];
+  float m = 0.f, ss = 0.f;
+  if (live) {
+    const float *x = a.xr + (size_t)b * a.xrs + (size_t)ka0 * 64;
+    const float *wn = a.xw ? a.xw + (size_t)ka0 * 64 : nullptr;
     // RMSNorm: the row's sum of squares from the per-CTA partials of the GEMV
     // that wrote it, in slot order then a fixed xor tree (every CTA, every B)
-    float ss = 0.f;
     if (a.xw)
 #pragma unroll
       for (int i = 0; i < 5; i++)
         if (lane + 32 * i < a.st_g) ss += __ldcg(a.st_in + (size_t)(lane + 32 * i) * QG_STAT_COLS + b);
-    // pass 1: max |w x| (or |x|) over the range, block j = 0 kept in registers;
-    // pass 2 converts block 0 from registers and reloads block 1 (cache hits)
-    float4 v[8];
-    float m = 0.f;
 #pragma unroll
-    for (int j = 0; j < 2; j++) {
-      const int kb = lane + 32 * j;
-      if (kb < nblk) {
-        float4 u[8];
-#pragma unroll
-        for (int q = 0; q < 8; q++) u[q] = __ldg(x + kb * 8 + q);
+    for (int j = 0; j < MAXI; j++) {
+      const int it = (sub + j * wpc) * 32 + lane;
+      if (it < nitems) {
+        const int kb = it >> 2, t = it & 3;
+        float4 p = __ldg(reinterpret_cast<const float4 *>(x + kb * 32 + 4 * t));
+        float4 q = __ldg(reinterpret_cast<const float4 *>(x + kb * 32 + 16 + 4 * t));
         if (a.xw) {
-#pragma unroll
-          for (int q = 0; q < 8; q++) {
-            const float4 w4 = __ldg(wn + kb * 8 + q);
-            u[q] = make_float4(w4.x * u[q].x, w4.y * u[q].y, w4.z * u[q].z, w4.w * u[q].w);
-          }
+          const float4 wp = __ldg(reinterpret_cast<const float4 *>(wn + kb * 32 + 4 * t));
+          const float4 wq = __ldg(reinterpret_cast<const float4 *>(wn + kb * 32 + 16 + 4 * t));
+          p = make_float4(wp.x * p.x, wp.y * p.y, wp.z * p.z, wp.w * p.w);
+          q = make_float4(wq.x * q.x, wq.y * q.y, wq.z * q.z, wq.w * q.w);
         }
-#pragma unroll
-        for (int q = 0; q < 8; q++) {
-          m = fmaxf(m, fmaxf(fmaxf(fabsf(u[q].x), fabsf(u[q].y)), fmaxf(fabsf(u[q].z), fabsf(u[q].w))));
-          if (j == 0) v[q] = u[q];
-        }
+        v[j][0] = p;
+        v[j][1] = q;
+        m = fmaxf(m, fmaxf(fmaxf(fabsf(p.x), fabsf(p.y)), fmaxf(fabsf(p.z), fabsf(p.w))));
+        m = fmaxf(m, fmaxf(fmaxf(fabsf(q.x), fabsf(q.y)), fmaxf(fabsf(q.z), fabsf(q.w))));
       }
     }
     m = warp_max(m);
+    if (lane == 0) cmax[w] = m;
+  }
+  named_bar(1, NTH);
+  if (live) {
+    m = 0.f;
+    for (int i = 0; i < wpc; i++) m = fmaxf(m, cmax[b * wpc + i]);
     float s = 1.f;
     if (a.xw) {
       s = 1.f / sqrtf(warp_sum(ss) / (float)(a.kp * 64) + 1e-6f);
@@ -387,52 +383,48 @@ CW_DEV void x_local_prologue(const GemvArgs &a, uint4 *xl, float *xun, int ka0, 
     const int e = xfrag_exponent(m);
     // ((w x) s) 2^e == (w x) (s 2^e) exactly: 2^e only shifts the exponent
     const float sc = s * __int_as_float((127 + e) << 23);
-    if (lane == 0) xun[b] = __int_as_float((127 - e) << 23);
-#pragma unroll 1
-    for (int j = 0; j < 2; j++) {
-      const int kb = lane + 32 * j;
-      if (kb < nblk) {
-        if (j == 1) {
+    if (sub == 0 && lane == 0) xun[b] = __int_as_float((127 - e) << 23);
+    uint4 *ob = xl + (b >> 3) * 64 + (b & 7) * 4;
 #pragma unroll
-          for (int q = 0; q < 8; q++) v[q] = __ldg(x + kb * 8 + q);
-          if (a.xw) {
+    for (int j = 0; j < MAXI; j++) {
+      const int it = (sub + j * wpc) * 32 + lane;
+      if (it < nitems) {
+        const int kb = it >> 2, t = it & 3;
+        // B operand lane (col & 7, t): (x[4t], x[4t+2]) (x[4t+1], x[4t+3]) (x[4t+16], x[4t+18]) (x[4t+17], x[4t+19])
+        const float r[8] = {v[j][0].x, v[j][0].z, v[j][0].y, v[j][0].w, v[j][1].x, v[j][1].z, v[j][1].y, v[j][1].w};
+        uint32_t hw[4], lw[4];
 #pragma unroll
-            for (int q = 0; q < 8; q++) {
-              const float4 w4 = __ldg(wn + kb * 8 + q);
-              v[q] = make_float4(w4.x * v[q].x, w4.y * v[q].y, w4.z * v[q].z, w4.w * v[q].w);
-            }
-          }
+        for (int i = 0; i < 4; i++) {
+          const float v0 = r[2 * i] * sc, v1 = r[2 * i + 1] * sc;
+          const half h0 = __float2half_rn(v0), h1 = __float2half_rn(v1);
+          const half l0 = __float2half_rn(v0 - __half2float(h0)), l1 = __float2half_rn(v1 - __half2float(h1));
+          hw[i] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
+          lw[i] = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
         }
-        const float *r = reinterpret_cast<const float *>(v);
-        // B operand lane (col & 3, t): (x[4t], x[4t+2]) (x[4t+1], x[4t+3]) (x[4t+16], x[4t+18]) (x[4t+17], x[4t+19])
-#pragma unroll
-        for (int t = 0; t < 4; t++) {
-          const int js[8] = {4 * t, 4 * t + 2, 4 * t + 1, 4 * t + 3, 4 * t + 16, 4 * t + 18, 4 * t + 17, 4 * t + 19};
-          uint32_t hw[4], lw[4];
-#pragma unroll
-          for (int i = 0; i < 4; i++) {
-            const float v0 = r[js[2 * i]] * sc, v1 = r[js[2 * i + 1]] * sc;
-            const half h0 = __float2half_rn(v0), h1 = __float2half_rn(v1);
-            const half l0 = __float2half_rn(v0 - __half2float(h0)), l1 = __float2half_rn(v1 - __half2float(h1));
-            hw[i] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
-            lw[i] = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
-          }
-          uint4 *o = xl + ((size_t)kb * NT + (b >> 2)) * 32 + (b & 3) * 4 + t;
-          o[0] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-          o[16] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
-        }
+        uint4 *o = ob + (size_t)kb * NT * 64 + t;
+        o[0] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+        o[32] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
       }
     }
-  } else if (lane == 0 && b < 16) {
-    xun[b] = 1.f;  // padding column
   }
+  if (threadIdx.x >= a.B && threadIdx.x < 16) xun[threadIdx.x] = 1.f;  // padding column
   named_bar(1, NTH);
 }
 
+// Persistent stream-K GEMV: warps 0..15 consume (warp w owns m-tiles 2w, 2w+1
+// of the current 512-row tile); lane 0 of warp 16 streams the weights and
+// lane 0 of warp 17 the X fragments.
+//
+// Per m-tile, 32-block and n-tile of 8 columns, four m16n8k16 MMAs chain into
+// one fp32 result c: (k 0..15, hi), (k 0..15, lo), (k 16..31, hi),
+// (k 16..31, lo) -- the f16 hi and lo parts of X are two B operands, so c
+// holds the block dot of 8 whole columns and one FFMA per element applies the
+// block's scale: acc = fma(d, c, acc).
 template <int TYPE, int NT, bool XL>
 __global__ void __launch_bounds__(QG_THREADS, 1) qgemv_kernel(GemvArgs a) {
   using Lay = QgLayout<TYPE, NT, XL>;
   constexpr int S = Lay::STAGES;
+  constexpr int NC4 = 2 * NT;  // float4 column groups of a split-tile row
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t *full = reinterpret_cast<uint64_t *>(smem + Lay::BAR_OFF);
   uint64_t *empty = full + S;
@@ -531,7 +523,8 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemv_kernel(GemvArgs a) {
   float *wst = XL ? xun + 16 + warp * 16 : nullptr;  // this warp's output sums of squares per column
   if (XL && a.st_out && lane < 16) wst[lane] = 0.f;
   if (XL) {
-    x_local_prologue<NT>(a, reinterpret_cast<uint4 *>(smem + Lay::XL_OFF), xun, ka0, (int)(u_end - u_begin));
+    x_local_prologue<NT>(a, reinterpret_cast<uint4 *>(smem + Lay::XL_OFF), xun, xun + 16 + 16 * 16, ka0,
+                         (int)(u_end - u_begin));
     if (threadIdx.x == 0) mbar_arrive(xready);
   }
   const float zero4[4] = {0.f, 0.f, 0.f, 0.f};
@@ -567,43 +560,64 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemv_kernel(GemvArgs a) {
       }
       if (ok && has0) {
         const uint8_t *stg = smem + st * Lay::STAGE;
-        const uint4 *xs = XL ? reinterpret_cast<const uint4 *>(smem + Lay::XL_OFF) + (size_t)(ka + i - ka0) * (2 * NT * 32)
+        const uint4 *xs = XL ? reinterpret_cast<const uint4 *>(smem + Lay::XL_OFF) + (size_t)(ka + i - ka0) * (NT * 128)
                              : reinterpret_cast<const uint4 *>(stg + Lay::WB);
-        // one n-tile: both m-tiles share the X loads; more: reload (registers)
-        uint4 xv1[2];
-        if (NT == 1) {
-          xv1[0] = xs[lane];
-          xv1[1] = xs[32 + lane];
-        }
+        const uint8_t *ch0 = stg + (warp * 2) * Lay::CHUNK;
+        // both m-tiles' quant words and scales first (independent shared loads)
+        uint4 qw[2][TYPE == 8 ? 2 : 1];
+        uint2 scw[2];
 #pragma unroll
         for (int mt = 0; mt < 2; mt++) {
-          if (mt == 1 && !has1) break;
-          const uint8_t *ch = stg + (warp * 2 + mt) * Lay::CHUNK;
-          const uint2 scw = *reinterpret_cast<const uint2 *>(ch + Lay::QB + g * 8);
+          const uint8_t *ch = ch0 + mt * Lay::CHUNK;
+          if (mt == 1 && !has1) {
+            scw[1] = make_uint2(0u, 0u);
 #pragma unroll
-          for (int kbi = 0; kbi < 2; kbi++) {
+            for (int h = 0; h < (TYPE == 8 ? 2 : 1); h++) qw[1][h] = make_uint4(0u, 0u, 0u, 0u);
+            continue;
+          }
+          if (TYPE == 8) {
+            qw[mt][0] = *reinterpret_cast<const uint4 *>(ch + lane * 32);
+            qw[mt][1] = *reinterpret_cast<const uint4 *>(ch + lane * 32 + 16);
+          } else {
+            qw[mt][0] = *reinterpret_cast<const uint4 *>(ch + lane * 16);
+          }
+          scw[mt] = *reinterpret_cast<const uint2 *>(ch + Lay::QB + g * 8);
+        }
+#pragma unroll
+        for (int kbi = 0; kbi < 2; kbi++) {
+          // this 32-block's X (hi and lo operands of each n-tile), shared by both m-tiles
+          uint4 xh[NT], xo[NT];
+#pragma unroll
+          for (int n = 0; n < NT; n++) {
+            xh[n] = xs[(kbi * NT + n) * 64 + lane];
+            xo[n] = xs[(kbi * NT + n) * 64 + 32 + lane];
+          }
+#pragma unroll
+          for (int mt = 0; mt < 2; mt++) {
+            if (mt == 1 && !has1) break;
             uint32_t a0s0, a1s0, a2s0, a3s0, a0s1, a1s1, a2s1, a3s1;
             if (TYPE == 8) {
-              const uint4 qw = *reinterpret_cast<const uint4 *>(ch + lane * 32 + kbi * 16);
-              q8_to_f16(qw.x, a0s0, a2s0);  // row g, bytes 4t..4t+3
-              q8_to_f16(qw.y, a0s1, a2s1);  // row g, bytes 16+4t..
-              q8_to_f16(qw.z, a1s0, a3s0);  // row g+8
-              q8_to_f16(qw.w, a1s1, a3s1);
+              const uint4 q = qw[mt][kbi];
+              q8_to_f16(q.x, a0s0, a2s0);  // row g, bytes 4t..4t+3
+              q8_to_f16(q.y, a0s1, a2s1);  // row g, bytes 16+4t..
+              q8_to_f16(q.z, a1s0, a3s0);  // row g+8
+              q8_to_f16(q.w, a1s1, a3s1);
             } else {
-              const uint4 qw = *reinterpret_cast<const uint4 *>(ch + lane * 16);
-              const uint32_t wg = kbi ? qw.z : qw.x, wg8 = kbi ? qw.w : qw.y;
+              const uint4 q = qw[mt][0];
+              const uint32_t wg = kbi ? q.z : q.x, wg8 = kbi ? q.w : q.y;
               q4_to_f16(wg, a0s0, a2s0, a0s1, a2s1);
               q4_to_f16(wg8, a1s0, a3s0, a1s1, a3s1);
             }
-            const uint32_t dw = kbi ? scw.y : scw.x;
+            const uint32_t dw = kbi ? scw[mt].y : scw[mt].x;
             const float dg = __half2float(__ushort_as_half((unsigned short)(dw & 0xFFFFu)));
             const float dg8 = __half2float(__ushort_as_half((unsigned short)(dw >> 16)));
 #pragma unroll
             for (int n = 0; n < NT; n++) {
-              const uint4 xv = NT == 1 ? xv1[kbi] : xs[(kbi * NT + n) * 32 + lane];
               float cc[4];
-              mma_16816(cc, a0s0, a1s0, a2s0, a3s0, xv.x, xv.y, zero4);
-              mma_16816(cc, a0s1, a1s1, a2s1, a3s1, xv.z, xv.w, cc);
+              mma_16816(cc, a0s0, a1s0, a2s0, a3s0, xh[n].x, xh[n].y, zero4);
+              mma_16816(cc, a0s0, a1s0, a2s0, a3s0, xo[n].x, xo[n].y, cc);
+              mma_16816(cc, a0s1, a1s1, a2s1, a3s1, xh[n].z, xh[n].w, cc);
+              mma_16816(cc, a0s1, a1s1, a2s1, a3s1, xo[n].z, xo[n].w, cc);
               acc[mt][n][0] = fmaf(dg, cc[0], acc[mt][n][0]);
               acc[mt][n][1] = fmaf(dg, cc[1], acc[mt][n][1]);
               acc[mt][n][2] = fmaf(dg8, cc[2], acc[mt][n][2]);
@@ -620,7 +634,6 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemv_kernel(GemvArgs a) {
       }
     }
 
-    fold_lo<NT>(acc);
     const bool full_tile = (ka == 0 && kb_end == a.kp);
     if (full_tile) {
       if (ok && has0) gemv_epilogue<NT>(a, mt0, has1, acc, g, t, xun);
@@ -632,18 +645,18 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemv_kernel(GemvArgs a) {
       const int slot = first_seg ? 0 : 1;
       float *mine = a.cl > 1 ? reinterpret_cast<float *>(smem) : a.ws + ((size_t)c * 2 + slot) * WS_TILE_FLOATS;
       if (a.cl > 1) named_bar(1, QG_CONS_WARPS * 32);  // every warp is done with the ring
-      if (has0 && t < 2) {
+      if (has0) {
 #pragma unroll
         for (int mt = 0; mt < 2; mt++)
 #pragma unroll
           for (int n = 0; n < NT; n++)
 #pragma unroll
             for (int h = 0; h < 2; h++) {
-              float *p = mine + ((warp * 2 + mt) * 16 + g + 8 * h) * 16 + n * 4 + 2 * t;
+              float *p = mine + ((warp * 2 + mt) * 16 + g + 8 * h) * 16 + n * 8 + 2 * t;
               float2 v = make_float2(acc[mt][n][2 * h], acc[mt][n][2 * h + 1]);
               if (XL) {  // local exponents differ between contributors: unscale before the sum (exact)
-                v.x *= xun[n * 4 + 2 * t];
-                v.y *= xun[n * 4 + 2 * t + 1];
+                v.x *= xun[n * 8 + 2 * t];
+                v.y *= xun[n * 8 + 2 * t + 1];
               }
               *reinterpret_cast<float2 *>(p) = v;
             }
@@ -657,8 +670,8 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemv_kernel(GemvArgs a) {
   if (np == 0) return;  // (sums of squares are only asked of fully split grids)
   // ---- split tiles: every contributor reduces a share of the rows ----
   // warp w's two m-tiles are reduced by contributor w % ncon: lane l sums row
-  // l & 15 of m-tile l >> 4, four columns per n-tile (one float4 per
-  // contributor and n-tile), over all contributors in CTA order.
+  // l & 15 of m-tile l >> 4, four columns per float4 (NC4 float4s per
+  // contributor), over all contributors in CTA order.
   const int mt = lane >> 4, row = lane & 15;
   if (a.cl > 1) {
     // Cluster mode: the tile's contributors are the cluster's CTAs (ranks 0..cl-1
@@ -672,24 +685,24 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemv_kernel(GemvArgs a) {
     const int mt0 = tile * QG_TILE_MT + warp * 2;
     if (__all_sync(0xffffffffu, ok) && warp % a.cl == r) {  // warp-uniform: split_epilogue shuffles
       const bool live = mt0 + mt < a.n_mt;
-      float4 sum[NT];
+      float4 sum[NC4];
 #pragma unroll
-      for (int n = 0; n < NT; n++) sum[n] = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int n = 0; n < NC4; n++) sum[n] = make_float4(0.f, 0.f, 0.f, 0.f);
       const int off = ((warp * 2 + mt) * 16 + row) * 16;
       if (live) {
-        float4 v[4][NT];
+        float4 v[4][NC4];
 #pragma unroll
         for (int q = 0; q < 4; q++) {
           if (q >= a.cl) break;
           const float *src = cluster.map_shared_rank(reinterpret_cast<float *>(smem), q) + off;
 #pragma unroll
-          for (int n = 0; n < NT; n++) v[q][n] = *reinterpret_cast<const float4 *>(src + 4 * n);
+          for (int n = 0; n < NC4; n++) v[q][n] = *reinterpret_cast<const float4 *>(src + 4 * n);
         }
 #pragma unroll
         for (int q = 0; q < 4; q++) {
           if (q >= a.cl) break;
 #pragma unroll
-          for (int n = 0; n < NT; n++) {
+          for (int n = 0; n < NC4; n++) {
             sum[n].x += v[q][n].x;
             sum[n].y += v[q][n].y;
             sum[n].z += v[q][n].z;
@@ -697,7 +710,7 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemv_kernel(GemvArgs a) {
           }
         }
       }
-      split_epilogue<NT>(a, mt0, mt, row, live, sum, wst);
+      split_epilogue<NC4>(a, mt0, mt, row, live, sum, wst);
     }
     cluster_sync_all();  // no CTA leaves while another reads its shared memory
     if (XL && a.st_out && threadIdx.x < QG_STAT_COLS) {  // this CTA's slot: the warps' sums in warp order
@@ -741,14 +754,14 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemv_kernel(GemvArgs a) {
     const int mt0 = tile * QG_TILE_MT + warp * 2;
     if (go && warp % ncon == r) {
       const bool live = mt0 + mt < a.n_mt;
-      float4 sum[NT];
+      float4 sum[NC4];
 #pragma unroll
-      for (int n = 0; n < NT; n++) sum[n] = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int n = 0; n < NC4; n++) sum[n] = make_float4(0.f, 0.f, 0.f, 0.f);
       const size_t off = (size_t)((warp * 2 + mt) * 16 + row) * 16;
-      constexpr int CH = NT == 1 ? 8 : (NT == 2 ? 4 : 2);  // independent loads in flight per lane
+      constexpr int CH = NC4 == 2 ? 4 : 2;  // independent loads in flight per lane
       if (live) {
         for (int c0 = c_first; c0 <= c_last; c0 += CH) {
-          float4 v[CH][NT];
+          float4 v[CH][NC4];
 #pragma unroll
           for (int q = 0; q < CH; q++) {
             const int cc = c0 + q;
@@ -756,13 +769,13 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemv_kernel(GemvArgs a) {
             const long long cu0 = (long long)cc * a.units / a.G;
             const float *src = a.ws + ((size_t)cc * 2 + (cu0 >= tu0 ? 0 : 1)) * WS_TILE_FLOATS + off;
 #pragma unroll
-            for (int n = 0; n < NT; n++) v[q][n] = __ldcg(reinterpret_cast<const float4 *>(src + 4 * n));
+            for (int n = 0; n < NC4; n++) v[q][n] = __ldcg(reinterpret_cast<const float4 *>(src + 4 * n));
           }
 #pragma unroll
           for (int q = 0; q < CH; q++) {
             if (c0 + q > c_last) break;
 #pragma unroll
-            for (int n = 0; n < NT; n++) {
+            for (int n = 0; n < NC4; n++) {
               sum[n].x += v[q][n].x;
               sum[n].y += v[q][n].y;
               sum[n].z += v[q][n].z;
@@ -771,7 +784,7 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemv_kernel(GemvArgs a) {
           }
         }
       }
-      split_epilogue<NT>(a, mt0, mt, row, live, sum, wst);
+      split_epilogue<NC4>(a, mt0, mt, row, live, sum, wst);
     }
     named_bar(1, QG_CONS_WARPS * 32);  // every read of the partials of this tile is done
     if (threadIdx.x == 0 && go) {
@@ -917,9 +930,7 @@ static cudaError_t gemv_launch(const QMat &m, int B, float *Y, int ys, int epi, 
     cudaError_t e;
     switch (nt) {
       case 1: e = launch_t<2, 1, true>(a, st); break;
-      case 2: e = launch_t<2, 2, true>(a, st); break;
-      case 3: e = launch_t<2, 3, true>(a, st); break;
-      default: e = launch_t<2, 4, true>(a, st); break;
+      default: e = launch_t<2, 2, true>(a, st); break;
     }
     if (e == cudaSuccess && a.st_out) {
       std::swap(s.stat, s.stat_next);
@@ -935,12 +946,8 @@ static cudaError_t gemv_launch(const QMat &m, int B, float *Y, int ys, int epi, 
   switch (nt * 16 + m.type) {
     case 16 + 8: return launch_t<8, 1, false>(a, st);
     case 32 + 8: return launch_t<8, 2, false>(a, st);
-    case 48 + 8: return launch_t<8, 3, false>(a, st);
-    case 64 + 8: return launch_t<8, 4, false>(a, st);
     case 16 + 2: return launch_t<2, 1, false>(a, st);
-    case 32 + 2: return launch_t<2, 2, false>(a, st);
-    case 48 + 2: return launch_t<2, 3, false>(a, st);
-    default: return launch_t<2, 4, false>(a, st);
+    default: return launch_t<2, 2, false>(a, st);
   }
 }
 
@@ -948,12 +955,15 @@ cudaError_t gemv_run(const QMat &m, int B, float *Y, int ys, int epi, GemvScratc
   return gemv_launch(m, B, Y, ys, epi, s, st, nullptr, 0);
 }
 
-bool gemv_uses_local_x(const QMat &m, const GemvScratch &s) { return gemv_local_x(m, s); }
+bool gemv_uses_local_x(const QMat &m, const float *X, int xs, const GemvScratch &s) {
+  return gemv_local_x(m, s) && (reinterpret_cast<uintptr_t>(X) & 15) == 0 && xs % 4 == 0;
+}
 
 cudaError_t gemv_run_x(const QMat &m, const float *X, int xs, int B, float *Y, int ys, int epi, GemvScratch &s,
                        cudaStream_t st, bool want_stats) {
   if (!X || xs < m.K) return cudaErrorInvalidValue;
-  if (gemv_local_x(m, s))
+  // the local-X prologue reads X as float4: rows must start on 16 bytes
+  if (gemv_local_x(m, s) && (reinterpret_cast<uintptr_t>(X) & 15) == 0 && xs % 4 == 0)
     return gemv_launch(m, B, Y, ys, epi, s, st, X, xs, nullptr,
                        want_stats && epi == EPI_ADD && s.stat && s.stat_next && gemv_all_split(m, s));
   CW_TRY(gemv_prep_x(X, xs, B, m.K, s, st));
@@ -961,7 +971,7 @@ cudaError_t gemv_run_x(const QMat &m, const float *X, int xs, int B, float *Y, i
 }
 
 bool gemv_norm_fused(const QMat &m, const float *X, int xs, int B, const GemvScratch &s) {
-  return gemv_local_x(m, s) && s.stat_ok && s.stat_y == X && s.stat_ys == xs && s.stat_len == m.K &&
+  return gemv_local_x(m, s) && (reinterpret_cast<uintptr_t>(X) & 15) == 0 && xs % 4 == 0 && s.stat_ok && s.stat_y == X && s.stat_ys == xs && s.stat_len == m.K &&
          s.stat_cols >= B && s.stat_g >= 1 && s.stat_g <= 160;
 }
 
@@ -980,12 +990,10 @@ cudaError_t qgemv_configure() {
   if ((e = carveout_max(repack_kernel<8>)) != cudaSuccess) return e;
   if ((e = carveout_max(qgemv_kernel<2, 1, false>)) != cudaSuccess) return e;
   if ((e = carveout_max(qgemv_kernel<2, 2, false>)) != cudaSuccess) return e;
-  if ((e = carveout_max(qgemv_kernel<2, 3, false>)) != cudaSuccess) return e;
-  if ((e = carveout_max(qgemv_kernel<2, 4, false>)) != cudaSuccess) return e;
   if ((e = carveout_max(qgemv_kernel<8, 1, false>)) != cudaSuccess) return e;
   if ((e = carveout_max(qgemv_kernel<8, 2, false>)) != cudaSuccess) return e;
-  if ((e = carveout_max(qgemv_kernel<8, 3, false>)) != cudaSuccess) return e;
-  if ((e = carveout_max(qgemv_kernel<8, 4, false>)) != cudaSuccess) return e;
+  if ((e = carveout_max(qgemv_kernel<2, 1, true>)) != cudaSuccess) return e;
+  if ((e = carveout_max(qgemv_kernel<2, 2, true>)) != cudaSuccess) return e;
   return cudaSuccess;
 }
 

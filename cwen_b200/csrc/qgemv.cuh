@@ -35,9 +35,10 @@ constexpr int WS_TILE_FLOATS = QG_TILE_MT * 16 * 16;   // split-K partials of on
 constexpr int QG_XL_KP = 20;  // local-X variant: at most this many k-pairs per CTA
 constexpr int QG_STAT_COLS = 16;  // per-CTA statistics slot: one float per column
 
-// GEMV input columns come in n-tiles of 4 (one m16n8k16 B operand holds the
-// f16 hi parts of 4 columns and their lo parts): 1 to 4 n-tiles.
-inline int gemv_ntiles(int B) { return (B + 3) / 4; }
+// GEMV input columns come in n-tiles of 8 (one m16n8k16 B operand holds 8
+// columns; the f16 hi and lo parts of X are two B operands accumulated into
+// the same MMA result): 1 or 2 n-tiles.
+inline int gemv_ntiles(int B) { return (B + 7) / 8; }
 
 inline size_t qmat_chunk_bytes(int type) { return type == 8 ? 1088 : 576; }
 inline size_t qmat_bytes(int type, int K, int n_mt) {
@@ -47,7 +48,7 @@ inline size_t qmat_bytes(int type, int K, int n_mt) {
 
 // Scratch the GEMV needs (owned by the caller, reused across calls on one stream).
 struct GemvScratch {
-  uint4 *xf = nullptr;   // X fragments, >= (Kmax/32) * 4 ntiles * 32 uint4
+  uint4 *xf = nullptr;   // X fragments, >= (Kmax/32) * 2 ntiles * 64 uint4
   int *xexp = nullptr;   // [16] per-column exponents
   float *ws = nullptr;   // split-K partials [G][2][WS_TILE_FLOATS]
   int *cnt = nullptr;    // per CTA-tile arrival counters (zero, self-resetting)
@@ -94,7 +95,7 @@ cudaError_t gemv_run_xn(const QMat &m, const float *X, int xs, const float *w, i
 bool gemv_norm_fused(const QMat &m, const float *X, int xs, int B, const GemvScratch &s);
 // Whether gemv_run_x takes the local-X variant for this matrix (one launch) or
 // prepares X first (two).
-bool gemv_uses_local_x(const QMat &m, const GemvScratch &s);
+bool gemv_uses_local_x(const QMat &m, const float *X, int xs, const GemvScratch &s);
 
 // Kernel attributes set once per process (shared-memory carveout).
 cudaError_t qgemv_configure();

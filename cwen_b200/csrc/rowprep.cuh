@@ -51,10 +51,12 @@ CW_DEV int xfrag_exponent(float mx) {
 
 // Emit GEMV fragments of column b for the 32-blocks [kb0, kb0 + nkb) from
 // v (v[0] is element 32*kb0 of the column), already scaled by nothing: the
-// power-of-two `scale` is applied here.  Layout: see prep comments in qgemv.cu.
+// power-of-two `scale` is applied here.  Layout: see prep comments in qgemv.cu
+// (per 32-block and n-tile of 8 columns: 32 uint4 of hi parts, then 32 of lo
+// parts, lane 4*(b & 7) + t).
 CW_DEV void emit_xfrag_blocks(const float *v, int kb0, int nkb, int b, int nt, uint4 *__restrict__ xf, float scale,
                               bool live) {
-  const int g = b & 3, n = b >> 2;
+  const int g = b & 7, n = b >> 3;
   for (int item = threadIdx.x; item < nkb * 4; item += blockDim.x) {
     const int kbl = item >> 2, t = item & 3;
     const float *r = v + kbl * 32;
@@ -68,9 +70,9 @@ CW_DEV void emit_xfrag_blocks(const float *v, int kb0, int nkb, int b, int nt, u
       hi[i] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
       lo[i] = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
     }
-    uint4 *o = xf + (size_t)((kb0 + kbl) * nt + n) * 32;
-    o[g * 4 + t] = make_uint4(hi[0], hi[1], hi[2], hi[3]);        // B column g: hi part
-    o[(g + 4) * 4 + t] = make_uint4(lo[0], lo[1], lo[2], lo[3]);  // B column g + 4: lo part
+    uint4 *o = xf + (size_t)((kb0 + kbl) * nt + n) * 64;
+    o[g * 4 + t] = make_uint4(hi[0], hi[1], hi[2], hi[3]);       // hi B operand, column g
+    o[32 + g * 4 + t] = make_uint4(lo[0], lo[1], lo[2], lo[3]);  // lo B operand, column g
   }
 }
 
