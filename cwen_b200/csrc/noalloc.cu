@@ -1,17 +1,18 @@
 // Verify GEMV whose scratch lives in statically allocated device memory.
 //
 // cwen_cuda_gemvb needs the split-K partials, the per-tile arrival counters
-// and the prepared X tiles of the engine's scratch, which cwen_cuda_init
-// allocates.  This variant runs the same two kernels (X preparation and the
-// GEMV) on file-scope __device__ arrays instead, so that a call allocates
-// nothing.  It is meant for callers that must not call cudaMalloc on their
-// per-call path: a host framework whose caching allocator already reserved
-// the device memory (a cudaMalloc there fails or fragments its pool), and
-// latency-critical loops where cudaMalloc / cudaFree would synchronize the
-// device and stall the other streams.
+// and (for shapes that prepare X first) the prepared X tiles of the engine's
+// scratch, which cwen_cuda_init allocates.  This variant runs the same
+// kernels, chosen by the same shape rule, on file-scope __device__ arrays
+// instead, so that a call allocates nothing and gives the same bits.  It is
+// meant for callers that must not call cudaMalloc on their per-call path: a
+// host framework whose caching allocator already reserved the device memory
+// (a cudaMalloc there fails or fragments its pool), and latency-critical
+// loops where cudaMalloc / cudaFree would synchronize the device and stall
+// the other streams.
 //
 // Limits (the arrays are sized for them; every GPU that loads the library
-// holds about 12 MiB of them until the process exits):
+// holds NA_STATIC_BYTES, about 22 MiB, of them until the process exits):
 //   K <= 32768, B <= 16, at most 2048 tiles of 512 rows (M <= 1,048,576),
 //   at most 320 CTAs of split-K partials.
 #include "engine.cuh"
@@ -32,6 +33,9 @@ static __device__ __align__(256) int g_na_xexp[QG_MAXB];
 static __device__ __align__(256) float g_na_ws[NA_WS_FLOATS];
 static __device__ __align__(256) int g_na_cnt[NA_MAX_TILES];
 static __device__ __align__(256) int g_na_err[1];
+constexpr size_t NA_STATIC_BYTES = sizeof(g_na_xf) + sizeof(g_na_xexp) + sizeof(g_na_ws) + sizeof(g_na_cnt) +
+                                   sizeof(g_na_err);
+static_assert(NA_STATIC_BYTES > (21u << 20) && NA_STATIC_BYTES < (23u << 20), "documented as about 22 MiB");
 
 struct NaDevice {
   bool ready = false;
@@ -49,12 +53,17 @@ int na_setup(int device, int n_sm) {
   CW_CHECK(cudaGetDevice(&cur));
   if (cur != device) CW_CHECK(cudaSetDevice(device));
   GemvScratch s;
-  CW_CHECK(cudaGetSymbolAddress((void **)&s.xf, g_na_xf));
-  CW_CHECK(cudaGetSymbolAddress((void **)&s.xexp, g_na_xexp));
-  CW_CHECK(cudaGetSymbolAddress((void **)&s.ws, g_na_ws));
-  CW_CHECK(cudaGetSymbolAddress((void **)&s.cnt, g_na_cnt));
-  CW_CHECK(cudaGetSymbolAddress((void **)&s.err, g_na_err));
-  if (cur != device) CW_CHECK(cudaSetDevice(cur));
+  // the first failing lookup is reported after the caller's device is current again
+  cudaError_t e = cudaGetSymbolAddress((void **)&s.xf, g_na_xf);
+  if (e == cudaSuccess) e = cudaGetSymbolAddress((void **)&s.xexp, g_na_xexp);
+  if (e == cudaSuccess) e = cudaGetSymbolAddress((void **)&s.ws, g_na_ws);
+  if (e == cudaSuccess) e = cudaGetSymbolAddress((void **)&s.cnt, g_na_cnt);
+  if (e == cudaSuccess) e = cudaGetSymbolAddress((void **)&s.err, g_na_err);
+  if (cur != device) {
+    const cudaError_t e2 = cudaSetDevice(cur);
+    if (e == cudaSuccess) e = e2;
+  }
+  if (e != cudaSuccess) return cuda_fail(e, "cwen_cuda_gemvb_static: static scratch lookup");
   s.kmax = NA_KMAX;
   s.G = n_sm < NA_MAX_CTAS ? n_sm : NA_MAX_CTAS;  // the engine's grid when it fits
   s.max_tiles = NA_MAX_TILES;
@@ -97,12 +106,32 @@ extern "C" int cwen_cuda_gemvb_static(int wid, const float *dX, int xs, float *d
   if (rc) return rc;
   GemvScratch &s = g_na[E.device].s;
   cudaStream_t st = stream ? (cudaStream_t)stream : E.stream;
-  // The arrival counters reset themselves at the end of a complete call; clear
-  // the ones this call uses, and the wait-timeout flag, in case an earlier
-  // call stopped part-way.
+  // The arrival counters reset themselves at the end of a complete call;
+  // clear the ones this call uses in case an earlier call stopped part-way.
+  // The wait-timeout flag is left alone: cwen_cuda_gemvb_static_status reads
+  // and clears it.
   CW_CHECK(cudaMemsetAsync(s.cnt, 0, (size_t)n_tiles * sizeof(int), st));
-  CW_CHECK(cudaMemsetAsync(s.err, 0, sizeof(int), st));
-  CW_CHECK(gemv_prep_x(dX, xs, B, m.K, s, st));
-  CW_CHECK(gemv_run(m, B, dY, ys, EPI_STORE, s, st));
+  // the same path as cwen_cuda_gemvb (local X for the shapes that allow it,
+  // else X preparation + GEMV), so both give the same bits
+  CW_CHECK(gemv_run_x(m, dX, xs, B, dY, ys, EPI_STORE, s, st, false));
   return CWEN_OK;
+}
+
+extern "C" int cwen_cuda_gemvb_static_status(void *stream) {
+  Engine &E = engine();
+  if (!E.live) {
+    set_error("cwen_cuda_gemvb_static_status: engine not initialised");
+    return CWEN_ESTATE;
+  }
+  if (E.device < 0 || E.device >= NA_MAX_DEVICES || !g_na[E.device].ready) return CWEN_OK;  // no call yet
+  GemvScratch &s = g_na[E.device].s;
+  CW_CHECK(cudaStreamSynchronize(stream ? (cudaStream_t)stream : E.stream));
+  int err = 0;
+  CW_CHECK(cudaMemcpy(&err, s.err, sizeof(int), cudaMemcpyDeviceToHost));
+  if (!err) return CWEN_OK;
+  CW_CHECK(cudaMemset(s.err, 0, sizeof(int)));
+  CW_CHECK(cudaMemset(s.cnt, 0, (size_t)s.max_tiles * sizeof(int)));
+  set_error("cwen_cuda_gemvb_static: a bounded device wait gave up (code %d); the output of the calls since the "
+            "last status check is not valid", err);
+  return CWEN_ETIMEOUT;
 }

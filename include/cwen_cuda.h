@@ -74,7 +74,7 @@ int cwen_cuda_gemvb_host(int wid, const float *hX, int xs, float *hY, int ys, in
 
 /* The same GEMV with no allocation at all: its scratch (prepared X, split-K
  * partials, tile counters) is a fixed array of device memory inside the
- * library (about 12 MiB on every GPU that loads it, held until exit) instead
+ * library (about 22 MiB on every GPU that loads it, held until exit) instead
  * of the engine's.  No counterpart in the reference, which has no device
  * memory.  For callers that must not call cudaMalloc while they run -- a
  * framework whose caching allocator already holds the device memory, or a
@@ -85,8 +85,17 @@ int cwen_cuda_gemvb_host(int wid, const float *hX, int xs, float *hY, int ys, in
  * array's device address (no allocation); make that first call before any
  * stream capture.  All calls share the one array: calls that overlap on the
  * GPU (different streams, no ordering between them) race and corrupt each
- * other's results.  Output matches cwen_cuda_gemvb. */
+ * other's results.  Runs the kernels cwen_cuda_gemvb runs for the shape, so
+ * the output is bit-identical to it.  The call itself does not synchronize:
+ * cwen_cuda_gemvb_static_status tells whether a call gave up on a wait. */
 int cwen_cuda_gemvb_static(int wid, const float *dX, int xs, float *dY, int ys, int B, void *stream);
+/* Synchronize `stream` (NULL: the engine's stream) and report whether any
+ * cwen_cuda_gemvb_static call since the last status check gave up on a
+ * bounded device wait: CWEN_OK, or CWEN_ETIMEOUT (those calls' outputs are not
+ * valid; the flag and the static tile counters are cleared).  No counterpart
+ * in the reference; the status half of cwen_cuda_gemvb_host's synchronous
+ * check. */
+int cwen_cuda_gemvb_static_status(void *stream);
 
 /* ---- stand-alone GatedDeltaNet verify step with rollback ---- */
 /* One linear-attention layer over the B <= 16 rows of a verify block, on

@@ -4,10 +4,11 @@ Some callers cannot call cudaMalloc while they run -- a framework whose
 caching allocator already holds the device memory, or a latency-critical
 loop where an allocation would synchronize the device.  This entry point
 runs the GEMV on scratch that is a fixed array of device memory inside the
-library.  Its output must match the regular entry point (cwen_cuda_gemvb) on
-the same weights and inputs, on consecutive calls that reuse the shared
-scratch.  Tolerance as in test_gemv.py: max abs <= 1e-4 (scaled by the
-output magnitude) and relative L2 <= 1e-5.
+library.  It takes the same kernel path as the regular entry point
+(cwen_cuda_gemvb), so on the same weights and inputs its output must be
+bit-identical to it, on consecutive calls that reuse the shared scratch; and
+both must match the CPU oracle within test_gemv.py's tolerance: max abs <=
+1e-4 (scaled by the output magnitude) and relative L2 <= 1e-5.
 
 This file is collected last on purpose, so a first-failure run has already
 run every other test before it.
@@ -17,7 +18,7 @@ import ctypes as C
 import numpy as np
 import pytest
 
-from oracle_lib import gen_normal, gen_q, rel_l2
+from oracle_lib import gen_normal, gen_q, rel_l2, vp
 
 pytestmark = pytest.mark.gpu
 
@@ -53,15 +54,22 @@ def test_static_scratch_matches_gemvb(eng, orc, typ, K, M):
     # two calls in a row with different inputs and batch sizes: the second
     # reuses the scratch the first one left behind
     for call, B in enumerate((8, 13)):
-        X = torch.from_numpy(gen_normal(orc, 22 + call, f"na_x{K}", B * K).reshape(B, K)).to(dev)
+        Xh = gen_normal(orc, 22 + call, f"na_x{K}", B * K).reshape(B, K)
+        X = torch.from_numpy(Xh).to(dev)
         Y_ref = torch.full((B, M), float("nan"), device=dev)
         Y = torch.full((B, M), float("nan"), device=dev)
+        torch.cuda.synchronize()  # the fills ran on torch's stream, the GEMVs run on the engine's
         cwen_b200.check(L.cwen_cuda_gemvb(wid.value, C.c_void_p(X.data_ptr()), K, C.c_void_p(Y_ref.data_ptr()), M, B,
                                           stream), "gemvb")
         cwen_b200.check(L.cwen_cuda_gemvb_static(wid.value, C.c_void_p(X.data_ptr()), K, C.c_void_p(Y.data_ptr()), M,
                                                  B, stream), "gemvb_static")
+        cwen_b200.check(L.cwen_cuda_gemvb_static_status(stream), "gemvb_static_status")
         torch.cuda.synchronize()
-        _close(Y.cpu().numpy(), Y_ref.cpu().numpy())
+        got, reg = Y.cpu().numpy(), Y_ref.cpu().numpy()
+        assert np.array_equal(got, reg), "static-scratch GEMV differs from cwen_cuda_gemvb"
+        ref = np.zeros((B, M), np.float32)
+        orc.or_gemvb(typ, vp(W), K, M, vp(np.ascontiguousarray(Xh)), K, vp(ref), M, B)
+        _close(got, ref)
 
 
 def test_static_scratch_rejects_oversize(eng, orc):
@@ -76,6 +84,7 @@ def test_static_scratch_rejects_oversize(eng, orc):
     cwen_b200.check(L.cwen_cuda_weight_upload(2, W.ctypes.data_as(C.c_void_p), K, M, C.byref(wid)), "upload")
     X = torch.zeros((17, K), device="cuda")
     Y = torch.zeros((17, M), device="cuda")
+    torch.cuda.synchronize()  # the zero fills ran on torch's stream
     rc = L.cwen_cuda_gemvb_static(wid.value, C.c_void_p(X.data_ptr()), K, C.c_void_p(Y.data_ptr()), M, 1, None)
     assert rc == -1 and b"static scratch" in L.cwen_cuda_last_error()
     rc = L.cwen_cuda_gemvb_static(wid.value, C.c_void_p(X.data_ptr()), K, C.c_void_p(Y.data_ptr()), M, 17, None)
@@ -83,3 +92,4 @@ def test_static_scratch_rejects_oversize(eng, orc):
     # the regular entry point still handles the shape
     cwen_b200.check(L.cwen_cuda_gemvb(wid.value, C.c_void_p(X.data_ptr()), K, C.c_void_p(Y.data_ptr()), M, 1, None))
     torch.cuda.synchronize()
+    assert L.cwen_cuda_gemvb_static_status(None) == 0
