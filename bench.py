@@ -69,6 +69,8 @@ RING = 8
 # one config-0 GEMV launch of the current kernel; scaled by algorithmic bytes for
 # the decode-step launches (traffic grows in proportion with the weight bytes).
 GEMV_NCU_TRAFFIC = 51_514_112
+GEMV_NCU_SOURCE = ("constant: dram__bytes_read.sum + dram__bytes_write.sum of one config-0 launch in the ncu "
+                   "capture summarised in profiles/qgemv_q4_0_b8_config0.md")
 
 
 def peaks():
@@ -190,14 +192,9 @@ def cpu_gemv_baseline(W, X, budget_s: float = 12.0):
     """Reference gemvb (run.c:1577) on the GGUF Q4_0 layout and on its split
     T_Q4_0RS layout (dot_q4_bcol, run.c:1544), best of the two; bounded by
     a time budget.  Returns (GB/s of the config-0 algorithmic bytes, info)."""
-    path, variant = ref_lib_path()
-    if not path.exists():
+    ref, variant = ref_lib()
+    if ref is None:
         return None
-    os.environ.setdefault("OMP_NUM_THREADS", str(host_cores()))
-    os.environ.setdefault("OMP_PROC_BIND", "close")
-    os.environ.setdefault("OMP_PLACES", "cores")
-    ref = C.CDLL(str(path))
-    ref.cwref_threads.restype = C.c_int
     vp = lambda a: a.ctypes.data_as(C.c_void_p)
     K, M, B = GEMV_K, GEMV_M, GEMV_B
     Y = np.zeros((B, M), np.float32)
@@ -227,10 +224,10 @@ def cpu_gemv_baseline(W, X, budget_s: float = 12.0):
 
 
 # ---------------- our engine ----------------
-def make_gemv_inputs(seed=1):
-    import cwen_b200
-    W = cwen_b200.synth_q(seed, "bench.gemv.w", 2, GEMV_K, GEMV_M)
-    X = cwen_b200.synth_normal(seed + 1, "bench.gemv.x", GEMV_B * GEMV_K).reshape(GEMV_B, GEMV_K)
+def make_gemv_inputs(seed=1, synth=None):
+    synth = synth or Synth()
+    W = synth.q(seed, "bench.gemv.w", 2, GEMV_K, GEMV_M)
+    X = synth.normal(seed + 1, "bench.gemv.x", GEMV_B * GEMV_K).reshape(GEMV_B, GEMV_K)
     return W, X
 
 
@@ -322,11 +319,15 @@ def gemv_ours_line(args, ws, rank, local, config):
             "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "numerics": "q4_0 weights x f32 X -> f32 Y (f16 hi+lo tensor-core operands, f32 accumulate)",
             "data": "synthetic (seeded)", "config": config, "gpu_launches": kern["launches"], "clocks": clk}
-    kern_ms = kern["ms"]
-    ach = kern["bytes"] / (kern_ms * 1e-3) / 1e9
+    # achieved bandwidth from the timed loop (one kernel launch per step,
+    # back to back on the launching stream); the per-launch event pass
+    # (launches serialised by the events) is reported beside it
+    ach = GEMV_BYTES / (ms * 1e-3) / 1e9
     line["roofline"] = {"bound": "hbm", "achieved": round(ach, 1), "peak": hbm, "unit": "GB/s",
                         "frac": round(ach / hbm, 4), "peak_kind": peak_kind, "traffic": GEMV_NCU_TRAFFIC,
-                        "kernel": "qgemv_kernel<Q4_0, 2 n-tiles of 4 columns>", "kernel_ms": round(kern_ms, 5)}
+                        "traffic_source": GEMV_NCU_SOURCE,
+                        "kernel": "qgemv_kernel<Q4_0, one n-tile of 8 columns, local X>",
+                        "kernel_ms": round(ms, 5), "serialised_kernel_ms": round(kern["ms"], 5)}
     e2e_gbs = GEMV_BYTES / e2e_s / 1e9
     line["e2e"] = {"value": round(e2e_gbs * ws, 2), "unit": "GB/s", "h2d_bytes_per_step": GEMV_B * GEMV_K * 4,
                    "d2h_bytes_per_step": GEMV_B * GEMV_M * 4,
@@ -335,9 +336,8 @@ def gemv_ours_line(args, ws, rank, local, config):
 
 
 # ---------------- decode (configs 2 / 3) ----------------
-def synth_ids(n, seed, stream, V):
-    import cwen_b200
-    return cwen_b200.synth_ids(seed, stream, V, n)
+def synth_ids(n, seed, stream, V, synth=None):
+    return (synth or Synth()).ids(seed, stream, V, n)
 
 
 def motif_prompt(n, V, seed=3):
@@ -478,37 +478,91 @@ def run_decode_ours(args, ws, rank, local):
     return ms, kern, e2e_tps, clk, spec, load_s, prompt
 
 
-def cpu_decode_baseline(prompt, budget_s: float = 20.0):
-    """The reference's own greedy decode (generate_tokens, run.c:5027) on the
-    seeded model in host memory, all host cores: (t(1+n) - t(1)) / n on a
-    4-id prefix of the bench prompt."""
+def ref_lib():
+    """The reference build (oracle/_ref, run.c compiled unmodified) with all
+    host cores; None when it is missing.  Nothing of the engine is loaded."""
     path, variant = ref_lib_path()
     if not path.exists():
-        return None
+        return None, variant
     os.environ.setdefault("OMP_NUM_THREADS", str(host_cores()))
     os.environ.setdefault("OMP_PROC_BIND", "close")
     os.environ.setdefault("OMP_PLACES", "cores")
     ref = C.CDLL(str(path))
     ref.cwref_threads.restype = C.c_int
+    ref.cwref_decode_step.restype = C.c_int
+    return ref, variant
+
+
+class Synth:
+    """Seeded synthetic inputs (cwen_b200/host/synth.c) through whichever
+    library is loaded: the engine's, or the reference build, which links the
+    same synth.c -- so the reference arm makes the same bytes without loading
+    the engine."""
+
+    def __init__(self, lib=None):
+        if lib is None:
+            import cwen_b200
+            lib = cwen_b200.lib()
+        self.L = lib
+        u64, vp, cp = C.c_uint64, C.c_void_p, C.c_char_p
+        lib.cw_synth_q4_0.argtypes = [u64, cp, C.c_int, C.c_int, vp, C.c_int]
+        lib.cw_synth_q8_0.argtypes = [u64, cp, C.c_int, C.c_int, vp, C.c_int]
+        lib.cw_synth_normal.argtypes = [u64, cp, C.c_float, C.c_float, vp, C.c_size_t]
+        lib.cw_synth_ids.argtypes = [u64, cp, C.c_int, vp, C.c_size_t]
+        for f in ("cw_synth_q4_0", "cw_synth_q8_0", "cw_synth_normal", "cw_synth_ids"):
+            getattr(lib, f).restype = None
+
+    def q(self, seed, stream, typ, K, M):
+        W = np.zeros((K // 32) * (18 if typ == 2 else 34) * M, np.uint8)
+        (self.L.cw_synth_q4_0 if typ == 2 else self.L.cw_synth_q8_0)(seed, stream.encode(), K, M,
+                                                                     W.ctypes.data_as(C.c_void_p), 0)
+        return W
+
+    def normal(self, seed, stream, n, mean=0.0, std=1.0):
+        v = np.zeros(n, np.float32)
+        self.L.cw_synth_normal(seed, stream.encode(), mean, std, v.ctypes.data_as(C.c_void_p), n)
+        return v
+
+    def ids(self, seed, stream, V, n):
+        v = np.zeros(n, np.int32)
+        self.L.cw_synth_ids(seed, stream.encode(), V, v.ctypes.data_as(C.c_void_p), n)
+        return v
+
+
+def cpu_decode_baseline(steps: int = 24, warmup: int = 2):
+    """The reference's own greedy decode on the seeded model in host memory,
+    all host cores, on the same workload as the engine: generate_tokens
+    (run.c:5027) prefills the same 512-id prompt and emits the first token,
+    then `warmup` untimed and `steps` timed iterations of its decode loop
+    (run.c:5033-5041: next slot, forward_ex, argmax of the logits).
+    Returns (tok/s, info, prompt)."""
+    ref, variant = ref_lib()
+    if ref is None:
+        return None
     vp = lambda a: a.ctypes.data_as(C.c_void_p)
     t0 = time.perf_counter()
     if ref.cwref_load_synth(C.c_uint64(DEC_SEED), 0, 0):
         return None
     load_s = time.perf_counter() - t0
-    ref.cwref_alloc_state(64, 0, 0)
-    p4 = np.ascontiguousarray(prompt[:4], np.int32)
-    out = np.zeros(64, np.int32)
+    ref.cwref_alloc_state(DEC_CTX, 0, 0)
+    prompt = Synth(ref).ids(DEC_SEED, "bench.prompt", 248320, PROMPT_LEN)
+    out = np.zeros(4, np.int32)
     t0 = time.perf_counter()
-    ref.cwref_generate(vp(p4), 4, 1, vp(out))
-    t1 = time.perf_counter() - t0
-    n = int(max(2, min(24, budget_s / max(t1 / 2.0, 1e-3))))
+    ref.cwref_generate(vp(prompt), PROMPT_LEN, 1, vp(out))
+    pf_s = time.perf_counter() - t0
+    tok = int(out[0])
+    for _ in range(warmup):
+        tok = ref.cwref_decode_step(tok)
     t0 = time.perf_counter()
-    ref.cwref_generate(vp(p4), 4, 1 + n, vp(out))
-    tn = time.perf_counter() - t0
-    tps = n / max(tn - t1, 1e-9)
+    for _ in range(steps):
+        tok = ref.cwref_decode_step(tok)
+    el = time.perf_counter() - t0
+    tps = steps / max(el, 1e-9)
     return tps, {"kind": "reference", "cores": int(ref.cwref_threads()), "variant": variant,
-                 "sample": f"reference generate_tokens on the same seeded 27B model: 4-id prompt, "
-                           f"(t({1 + n}) - t(1))/{n} decode steps ({tn:.1f} s; model synth {load_s:.0f} s)"}
+                 "sample": f"reference generate_tokens on the same seeded 27B model and 512-id prompt "
+                           f"(prefill {pf_s:.1f} s), then {steps} timed decode steps at slots "
+                           f"{PROMPT_LEN + warmup}..{PROMPT_LEN + warmup + steps - 1} ({el:.1f} s; "
+                           f"model synth {load_s:.0f} s)"}, prompt
 
 
 def main_decode(args, ws, rank, local):
@@ -522,12 +576,11 @@ def main_decode(args, ws, rank, local):
     if args.impl == "reference":
         if rank != 0:
             return 0
-        prompt = synth_ids(PROMPT_LEN, DEC_SEED, "bench.prompt", 248320)
-        res = cpu_decode_baseline(prompt, budget_s=max(5.0, min(60.0, 1.0 * args.steps)))
+        res = cpu_decode_baseline(steps=max(4, min(64, args.steps)), warmup=min(args.warmup, 8))
         if res is None:
             print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref reference build missing"}))
             return 0
-        tps, info = res
+        tps, info, _ = res
         print(json.dumps({"impl": "reference", "metric": metric, "value": round(tps, 4), "unit": "tok/s",
                           "n_gpus": 0, "steps": args.steps, "warmup": args.warmup,
                           "ms_per_step": round(1000.0 / tps, 3), "higher_is_better": True, "scaling": "weak",
@@ -550,6 +603,7 @@ def main_decode(args, ws, rank, local):
                          "frac": round(ach / hbm, 4), "peak_kind": peak_kind,
                          "traffic": round(GEMV_NCU_TRAFFIC / GEMV_BYTES * gemv_bytes),
                          "traffic_note": "ncu DRAM bytes of a config-0 launch, scaled to the average decode launch",
+                         "traffic_source": GEMV_NCU_SOURCE,
                          "kernel": "qgemv_kernel (all verify-GEMV launches of a decode step)",
                          "launches_per_token": round(kern["gemv_calls_per_token"], 1),
                          "avg_launch_ms": round(gemv_ms, 5), "avg_launch_bytes": round(gemv_bytes),
@@ -575,9 +629,10 @@ def main_decode(args, ws, rank, local):
                 import cwen_b200
                 cwen_b200.lib().cwen_cuda_shutdown()  # no-op when the engine is not live
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
-        res = cpu_decode_baseline(prompt)
+        res = cpu_decode_baseline()
         if res:
-            line["cpu_baseline"] = {**res[1], "value": round(res[0], 4), "unit": "tok/s"}
+            line["cpu_baseline"] = {**res[1], "value": round(res[0], 4), "unit": "tok/s",
+                                    "same_prompt": bool(np.array_equal(res[2], prompt))}
     if rank == 0:
         print(json.dumps(line))
     return 0
@@ -595,14 +650,9 @@ def cpu_mtp_baseline(n_gen=16, prompt_len=64):
     nextn drafter, depth 8) on the same seeded model with blk.64, all host
     cores, on a bounded sample: a 64-id prompt instead of the 32k prefill
     (which takes the reference about an hour), (t(1 + n) - t(1)) / n."""
-    path, variant = ref_lib_path()
-    if not path.exists():
+    ref, variant = ref_lib()
+    if ref is None:
         return None
-    os.environ.setdefault("OMP_NUM_THREADS", str(host_cores()))
-    os.environ.setdefault("OMP_PROC_BIND", "close")
-    os.environ.setdefault("OMP_PLACES", "cores")
-    ref = C.CDLL(str(path))
-    ref.cwref_threads.restype = C.c_int
     vp = lambda a: a.ctypes.data_as(C.c_void_p)
     t0 = time.perf_counter()
     if ref.cwref_load_synth(C.c_uint64(DEC_SEED), 1, 0):
@@ -610,8 +660,7 @@ def cpu_mtp_baseline(n_gen=16, prompt_len=64):
     load_s = time.perf_counter() - t0
     ref.cwref_alloc_state(4096, 1, 1)
     ref.cwref_spec_config(8, 2, 16, 8)
-    import cwen_b200
-    prompt = np.ascontiguousarray(cwen_b200.synth_ids(DEC_SEED, "bench.mtp.prompt", 248320, prompt_len), np.int32)
+    prompt = np.ascontiguousarray(Synth(ref).ids(DEC_SEED, "bench.mtp.prompt", 248320, prompt_len), np.int32)
     out = np.zeros(n_gen + 32, np.int32)
     t0 = time.perf_counter()
     ref.cwref_generate(vp(prompt), prompt_len, 1, vp(out))
@@ -725,17 +774,17 @@ def gdn_keeps(n: int) -> np.ndarray:
     return np.random.default_rng(GDN_SEED).integers(0, GDN_B + 1, size=n)
 
 
-def make_gdn_layer(i: int):
+def make_gdn_layer(i: int, synth=None):
     """One layer's seeded inputs (config 1): state ~N(0, 0.1), conv state and
     block rows ~N(0, 1) (q, k, v, z, alpha, beta; the kernel L2-normalises q
     and k after the conv and applies decay = exp(-softplus(alpha)), beta =
     sigmoid(beta): A = -1, dt = 0), conv weights ~N(0, 0.1), norm 1."""
-    import cwen_b200
+    synth = synth or Synth()
     sd = GDN_SEED * 1000 + i
-    return {"proj": cwen_b200.synth_normal(sd, "bench.gdn.proj", GDN_B * GDN_PS).reshape(GDN_B, GDN_PS),
-            "convw": cwen_b200.synth_normal(sd, "bench.gdn.convw", GDN_QKV * 4, 0.0, 0.1),
-            "S": cwen_b200.synth_normal(sd, "bench.gdn.S", GDN_S, 0.0, 0.1),
-            "conv": cwen_b200.synth_normal(sd, "bench.gdn.conv", GDN_QKV * 3)}
+    return {"proj": synth.normal(sd, "bench.gdn.proj", GDN_B * GDN_PS).reshape(GDN_B, GDN_PS),
+            "convw": synth.normal(sd, "bench.gdn.convw", GDN_QKV * 4, 0.0, 0.1),
+            "S": synth.normal(sd, "bench.gdn.S", GDN_S, 0.0, 0.1),
+            "conv": synth.normal(sd, "bench.gdn.conv", GDN_QKV * 3)}
 
 
 def cpu_gdn_baseline(budget_s: float = 12.0):
@@ -744,16 +793,11 @@ def cpu_gdn_baseline(budget_s: float = 12.0):
     2014-2180) and a snapshot of the state (the snap_save copy, run.c:2787),
     then the state restored from the snapshot at the rejection index
     (snap_load, run.c:2802).  Bounded by a time budget; all host cores."""
-    path, variant = ref_lib_path()
-    if not path.exists():
+    ref, variant = ref_lib()
+    if ref is None:
         return None
-    os.environ.setdefault("OMP_NUM_THREADS", str(host_cores()))
-    os.environ.setdefault("OMP_PROC_BIND", "close")
-    os.environ.setdefault("OMP_PLACES", "cores")
-    ref = C.CDLL(str(path))
-    ref.cwref_threads.restype = C.c_int
     vp = lambda a: a.ctypes.data_as(C.c_void_p)
-    lay = make_gdn_layer(0)
+    lay = make_gdn_layer(0, Synth(ref))
     S, cs = lay["S"].copy(), lay["conv"].copy()
     cw, nw = lay["convw"], np.ones(GDN_D, np.float32)
     A, dt = -np.ones(GDN_NVH, np.float32), np.zeros(GDN_NVH, np.float32)
@@ -974,7 +1018,11 @@ def main():
     if args.impl == "reference":
         if rank != 0:
             return 0
-        W, X = make_gemv_inputs()
+        ref, _ = ref_lib()
+        if ref is None:
+            print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref reference build missing"}))
+            return 0
+        W, X = make_gemv_inputs(synth=Synth(ref))
         res = cpu_gemv_baseline(W, X, budget_s=max(4.0, min(60.0, 2.0 * args.steps)))
         if res is None:
             print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref reference build missing"}))

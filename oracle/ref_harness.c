@@ -177,6 +177,13 @@ static void ref_sink_fn(int token, int idx, void *ud) {
   ref_sink *s = (ref_sink *)ud;
   if (s->n < s->cap) s->out[s->n++] = token;
 }
+/* One iteration of generate_tokens' loop (run.c:5033-5041) after a prefill:
+   the next slot, forward_ex of the token, the argmax of its logits. */
+CWREF_API int cwref_decode_step(int token) {
+  pos_n++;
+  forward_ex(token, 1);
+  return argmax_logits();
+}
 CWREF_API int cwref_generate(const int32_t *tokens, int n_tok, int n_gen, int32_t *out) {
   ref_sink s = {out, 0, n_gen};
   reset_state();

@@ -45,8 +45,8 @@ def test_decode_line(monkeypatch, capsys):
             "verify_ceiling": {"8": {"block_ms": 8.0, "serial_ms": 54.0, "x": 6.75, "pass": True}}}
     spec = {"workload": "config3", "tok_s": 600.0, "mtp_d8": {"workload": "mtp", "tok_s": 130.0}}
     monkeypatch.setattr(bench, "run_decode_ours", lambda a, ws, r, l: (6.8, kern, 145.0, CLK, spec, 30.0, [1, 2, 3]))
-    monkeypatch.setattr(bench, "cpu_decode_baseline", lambda prompt: (3.0, {"kind": "reference", "cores": 16,
-                                                                            "variant": "avx512", "sample": "s"}))
+    monkeypatch.setattr(bench, "cpu_decode_baseline", lambda: (3.0, {"kind": "reference", "cores": 16,
+                                                                     "variant": "avx512", "sample": "s"}, [1, 2, 3]))
     monkeypatch.setattr(bench, "gemv_ours_line", lambda *a, **k: ({"metric": "g", "value": 1.0, "unit": "GB/s",
                                                                     "roofline": {}, "e2e": {}}, None, None))
 
@@ -63,6 +63,7 @@ def test_decode_line(monkeypatch, capsys):
     assert rec["unit"] == "tok/s" and abs(rec["value"] - 1000.0 / 6.8) < 1e-2
     assert rec["gpu_launches"] == 470 * 8
     assert rec["cpu_baseline"]["kind"] == "reference" and rec["cpu_baseline"]["value"] == 3.0
+    assert rec["cpu_baseline"]["same_prompt"] is True
     assert rec["spec_d8"]["tok_s"] == 600.0 and rec["mtp_d8"]["tok_s"] == 130.0
     assert rec["verify_ceiling"]["8"]["pass"] is True
     assert rec["gemv_config0"]["value"] == 1.0
@@ -78,7 +79,9 @@ def test_gemv_line(monkeypatch):
     line, _, _ = bench.gemv_ours_line(_args(workload="gemv", steps=32), 1, 0, 0, bench.gemv_config(1))
     _check_common(line)
     assert abs(line["value"] - bench.GEMV_BYTES / 0.031e-3 / 1e9) < 0.1
-    assert abs(line["roofline"]["achieved"] - bench.GEMV_BYTES / 0.030e-3 / 1e9) < 0.1
+    # the roofline reads the timed loop (one launch per step), not the serialised event pass
+    assert abs(line["roofline"]["achieved"] - bench.GEMV_BYTES / 0.031e-3 / 1e9) < 0.1
+    assert line["roofline"]["serialised_kernel_ms"] == 0.030
     assert line["roofline"]["traffic"] == bench.GEMV_NCU_TRAFFIC
     assert line["e2e"]["h2d_bytes_per_step"] == bench.GEMV_B * bench.GEMV_K * 4
 
@@ -98,3 +101,28 @@ def test_synth_threads_share_the_node(monkeypatch, ws, local_ws, cores):
     monkeypatch.setenv("LOCAL_WORLD_SIZE", str(local_ws))
     monkeypatch.setattr(bench, "host_cores", lambda: cores)
     assert bench.synth_threads(ws) == max(1, cores // local_ws)
+
+
+def test_reference_arm_loads_no_engine(tmp_path):
+    """The reference arm runs the reference build alone: its inputs come from
+    the synth code linked into oracle/_ref, and the engine's library is never
+    loaded into the process."""
+    import subprocess
+    import sys
+    from pathlib import Path
+    root = Path(bench.__file__).resolve().parent
+    if not bench.ref_lib_path()[0].exists():
+        pytest.skip("reference build (oracle/_ref) missing")
+    code = ("import sys, argparse, bench\n"
+            "a = argparse.Namespace(gpus=1, steps=1, warmup=3, impl='reference', workload='gdn', "
+            "no_cpu_baseline=False, no_side_workloads=True)\n"
+            "rc = bench.main_gdn(a, 1, 0, 0)\n"
+            "maps = open('/proc/self/maps').read()\n"
+            "print('ENGINE_LOADED' if 'libcwen_cuda' in maps else 'ENGINE_NOT_LOADED')\n"
+            "print('REF_LOADED' if 'libcwref_' in maps else 'REF_NOT_LOADED')\n")
+    r = subprocess.run([sys.executable, "-c", code], cwd=root, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr[-2000:]
+    out = r.stdout
+    assert "ENGINE_NOT_LOADED" in out and "REF_LOADED" in out, out[-2000:]
+    rec = json.loads([ln for ln in out.splitlines() if ln.startswith("{")][-1])
+    assert rec["impl"] == "reference" and rec["cpu_baseline"]["kind"] == "reference"
