@@ -3,7 +3,7 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                     [--workload decode|gemv|mtp|gdn]
 
-Workload `decode` (default; BASELINE configs 2 and 3): the random-init 27B
+Workload `decode` (default; serial decode and n-gram speculation): the random-init 27B
 hybrid (64 layers, Q4_0 weights with scales |N(0,0.01)|, norms 1, seeded),
 greedy decode of one sequence after a 512-id random prompt.  A step is one
 decoded token: the forward pass of the previous token at the next slot plus
@@ -15,18 +15,18 @@ config 3: n-gram speculative decode, draft depth 8, 2048-id motif prompt,
 On one GPU the decode line also carries `gemv_config0` and `gdn_config1`:
 the config-0 and config-1 measurements below (200 steps each, no CPU leg).
 
-Workload `gemv`: the B=8 Q4_0 verify GEMV, W 17408x5120,
+Workload `gemv` (the verify-GEMV microkernel): the B=8 Q4_0 verify GEMV, W 17408x5120,
 X fp32 8x5120 ~N(0,1), scales |N(0,0.01)|, nibbles uniform.  A step is one
 call over a weight copy from a ring of 8 distinct copies (400 MB > 126 MB L2),
 so every step streams W from HBM.  value = algorithmic bytes / device time.
 
-Workload `gdn`: one GatedDeltaNet layer's verify block
+Workload `gdn` (GDN verify step with rollback): one GatedDeltaNet layer's verify block
 (B=8 rows) and the rollback to a rejection index uniform in 0..8, through
 cwen_cuda_gdn_verify, over a ring of 64 layers' states (253 MB > L2).
 value = us per step (CUDA events around the K steps captured in one CUDA
 graph; the stream-launched loop is reported beside it).
 
-Workload `mtp`: the hybrid plus the blk.64 MTP block,
+Workload `mtp` (MTP speculation at 32k context): the hybrid plus the blk.64 MTP block,
 a 32767-id prefill, 256 new tokens drafted by the MTP head and verified;
 MTP spec tok/s, prefill rate, stream checked against serial decode.
 
@@ -676,7 +676,7 @@ def cpu_mtp_baseline(n_gen=16, prompt_len=64):
 
 
 def main_mtp(args, ws, rank, local):
-    """the hybrid plus the blk.64 MTP block (Q8_0), a 32k
+    """MTP speculation at 32k context: the hybrid plus the blk.64 MTP block (Q8_0), a 32k
     context pre-filled with random ids, 256 new tokens drafted by the MTP head
     (depth 8) and verified; the stream must equal serial decode.  value =
     (t(256) - t(1)) / 255 through cwen_generate; the prefill rate (blocks of
@@ -837,7 +837,7 @@ def cpu_gdn_baseline(budget_s: float = 12.0):
 
 
 def main_gdn(args, ws, rank, local):
-    """BASELINE config 1.  A step is one layer's verify block (B = 8 rows:
+    """The GDN verify step with rollback.  A step is one layer's verify block (B = 8 rows:
     conv + decay/beta + recurrence with the gated norm) followed by the
     rollback to a rejection index uniform in 0..8, through
     cwen_cuda_gdn_verify on device buffers, over a ring of 64 layers' states

@@ -3,10 +3,11 @@
 # where it lies) into oracle/_ref/ for parity checks and the CPU baseline.
 # Two builds: AVX-512 (the reference's AVX512=1 flags minus -march=native, so
 # the library runs on any AVX-512 host) and AVX2 (its default flags).
-# Usage: oracle/build_ref.sh [REFERENCE_DIR]
+# Usage: oracle/build_ref.sh [REFERENCE_DIR]  (default: $CWEN_REFERENCE_DIR, else
+# a checkout named "reference" beside this repository)
 set -euo pipefail
 here="$(cd "$(dirname "$0")" && pwd)"
-ref="${1:-${CWEN_REFERENCE_DIR:-/root/reference}}"
+ref="${1:-${CWEN_REFERENCE_DIR:-$here/../../reference}}"
 out="$here/_ref"
 if [ ! -f "$ref/run.c" ]; then
   echo "build_ref: no reference at $ref (prebuilt libraries in $out are used as-is)" >&2

@@ -5,7 +5,7 @@ the kept rows only.
 
 Checked against the reference's own outputs (the golden fixture of three
 consecutive gdn_step positions, run.c:2014-2200), against the CPU oracle at
-the BASELINE config-1 geometry (48 value / 16 key heads, B = 8, every
+the benchmark geometry (48 value / 16 key heads, B = 8, every
 rejection index 0..8), and through the rollback property: keeping k rows of
 a B-row block leaves the state bit-identical to a k-row block.
 
