@@ -45,6 +45,10 @@ _SIGS = {
     "cwen_cuda_gemvb": (C.c_int, [C.c_int, C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_int, C.c_void_p]),
     "cwen_cuda_gemvb_static": (C.c_int, [C.c_int, C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_int, C.c_void_p]),
     "cwen_cuda_gemvb_static_status": (C.c_int, [C.c_void_p]),
+    "cwen_cuda_accept_logits": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_int, C.c_void_p,
+                                          C.c_void_p]),
+    "cwen_cuda_mtp_step": (C.c_int, [C.c_int, C.c_int, C.c_int, C.c_int]),
+    "cwen_cuda_mtp_read": (C.c_int, [C.c_int, C.c_void_p]),
     "cwen_cuda_gemvb_host": (C.c_int, [C.c_int, C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_int]),
     "cwen_cuda_gdn_verify": (C.c_int, [C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p,
                                        C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_void_p,

@@ -159,7 +159,8 @@ int cwen_cuda_init(int device, int ctx, int bmax) {
   s.kmax = 32768;
   s.G = E.n_sm;  // one persistent CTA per SM
   s.max_tiles = 1 << 16;
-  CW_CHECK(cudaMalloc(&s.xf, (size_t)(s.kmax / 32) * 2 * 2 * 32 * sizeof(uint4)));
+  CW_CHECK(cudaMalloc(&s.xf, (size_t)(s.kmax / 32) * 128 * sizeof(uint4)));
+  CW_CHECK(cudaMemset(s.xf, 0, (size_t)(s.kmax / 32) * 128 * sizeof(uint4)));  // padding columns stay finite
   CW_CHECK(cudaMalloc(&s.xexp, QG_MAXB * sizeof(int)));
   CW_CHECK(cudaMalloc(&s.ws, gemv_scratch_ws_floats(s.G) * sizeof(float)));
   CW_CHECK(cudaMalloc(&s.cnt, (size_t)s.max_tiles * sizeof(int)));
@@ -168,6 +169,9 @@ int cwen_cuda_init(int device, int ctx, int bmax) {
   CW_CHECK(cudaMemset(s.err, 0, sizeof(int)));
   CW_CHECK(cudaMalloc(&s.stat, (size_t)160 * QG_STAT_COLS * sizeof(float)));
   CW_CHECK(cudaMalloc(&s.stat_next, (size_t)160 * QG_STAT_COLS * sizeof(float)));
+  CW_CHECK(cudaMalloc(&E.aw, argmax_part_bytes(QG_MAXB)));
+  CW_CHECK(cudaMemset(E.aw, 0, argmax_part_bytes(QG_MAXB)));
+  CW_CHECK(cudaMalloc(&E.aw_res, (2 + QG_MAXB) * sizeof(int)));
   E.live = true;
   return CWEN_OK;
 }
@@ -191,6 +195,8 @@ void cwen_cuda_shutdown(void) {
   cudaFree(E.gs.err);
   cudaFree(E.gs.stat);
   cudaFree(E.gs.stat_next);
+  cudaFree(E.aw);
+  cudaFree(E.aw_res);
   if (E.staging) cudaFree(E.staging);
   if (E.io) cudaFree(E.io);
   cudaStreamDestroy(E.stream);
@@ -234,6 +240,29 @@ int cwen_cuda_gemvb(int wid, const float *dX, int xs, float *dY, int ys, int B, 
   }
   cudaStream_t st = stream ? (cudaStream_t)stream : E.stream;
   CW_CHECK(timed_gemv(m, B, dY, ys, EPI_STORE, st, dX, xs));
+  return CWEN_OK;
+}
+
+int cwen_cuda_accept_logits(const float *dlogits, int n, int ldl, int B, const int *blk, int E_drafts, int *res,
+                            void *stream) {
+  Engine &E = engine();
+  if (!E.live) {
+    set_error("cwen_cuda_accept_logits: engine not initialised");
+    return CWEN_ESTATE;
+  }
+  if (!dlogits || !res || n < 1 || ldl < n || B < 1 || B > QG_MAXB || E_drafts < 0 || E_drafts >= B ||
+      (E_drafts > 0 && !blk)) {
+    set_error("cwen_cuda_accept_logits: need logits, 1 <= B <= %d, 0 <= E < B, n <= ldl, blk when E > 0", QG_MAXB);
+    return CWEN_EINVAL;
+  }
+  Toks16 tk;
+  memset(&tk, 0, sizeof tk);
+  if (E_drafts > 0) memcpy(tk.t, blk, (size_t)(E_drafts + 1) * sizeof(int));
+  cudaStream_t st = stream ? (cudaStream_t)stream : E.stream;
+  CW_CHECK(launch_argmax_walk(dlogits, n, ldl, B, E_drafts, tk, E.aw, E.aw_res, st));
+  E.prof.launches++;
+  CW_CHECK(cudaMemcpyAsync(res, E.aw_res, (size_t)(2 + B) * sizeof(int), cudaMemcpyDeviceToHost, st));
+  CW_CHECK(cudaStreamSynchronize(st));
   return CWEN_OK;
 }
 

@@ -31,6 +31,8 @@ struct Engine {
   std::vector<QMat> mats;  // stand-alone GEMV weights (cwen_cuda_weight_upload)
   uint8_t *staging = nullptr;  // device staging for GGUF uploads
   size_t staging_bytes = 0;
+  void *aw = nullptr;    // argmax + walk scratch of cwen_cuda_accept_logits
+  int *aw_res = nullptr; // its result row [2 + 16]
   float *io = nullptr;  // device buffers for the host-buffer entry points
   size_t io_floats = 0;
   Prof prof;

@@ -212,7 +212,8 @@ static int alloc_state() {
   M.nch_max = attn_splits_max(ctx);
   if ((rc = A(M.attn_part, attn_part_floats(bm, d.n_head, M.nch_max)))) return rc;
   if ((rc = A(M.attn_o, (size_t)bm * d.n_head * 256))) return rc;
-  CW_CHECK(cudaMalloc(&M.best, (size_t)bm * sizeof(unsigned long long)));
+  CW_CHECK(cudaMalloc(&M.best, argmax_part_bytes(bm)));
+  CW_CHECK(cudaMemset(M.best, 0, argmax_part_bytes(bm)));
   CW_CHECK(cudaMalloc(&M.walk, (size_t)(bm + 2) * sizeof(int)));
   CW_CHECK(cudaMalloc(&M.toks, (size_t)bm * sizeof(int)));
   CW_CHECK(cudaMalloc(&M.err, sizeof(int)));
@@ -398,7 +399,7 @@ int forward_block_impl(const int *toks, int B, int nlogits) {
     memcpy(blk.t, toks + r0, (size_t)(B - r0) * sizeof(int));
     CW_CHECK(launch_argmax_walk(M.logits, d.n_vocab, d.n_vocab, nr, nlogits == -1 ? 0 : nr - 1, blk, M.best,
                                 M.walk, st));
-    E.prof.launches += 3;
+    E.prof.launches += 2;
     CW_CHECK(cudaMemcpyAsync(M.h_walk, M.walk, (size_t)(nr + 2) * sizeof(int), cudaMemcpyDeviceToHost, st));
     M.pending_nlog = nr;
   }
@@ -787,7 +788,7 @@ int cwen_cuda_mtp_draft(int pend, int *out, int max_d) {
     if (rc) return rc;
     CW_CHECK(timed_gemv(M.lm_head, 1, M.logits, V, EPI_STORE, st));
     CW_CHECK(launch_argmax_walk(M.logits, V, V, 1, 0, none, M.best, M.mtp_draft + 3 * t, st));
-    E.prof.launches += 2;
+    E.prof.launches += 1;
     hin = hout;
   }
   int res[3 * 16];
@@ -803,6 +804,61 @@ int cwen_cuda_mtp_draft(int pend, int *out, int max_d) {
   if (rc) return rc;
   for (int t = 0; t < n; t++) out[t] = res[3 * t + 1];
   return n;
+}
+
+// Hidden-state slots of the nextn stream seen by cwen_cuda_mtp_step.
+static float *mtp_slot(int slot) {
+  Model &M = g_model;
+  const int H = M.d.n_embd;
+  if (slot == CWEN_MTP_PARKED) return M.mtp_hprev;
+  if (slot == CWEN_MTP_OUT0) return M.mtp_out;
+  if (slot == CWEN_MTP_OUT1) return M.mtp_out + H;
+  return nullptr;
+}
+
+int cwen_cuda_mtp_step(int tok, int pos, int src, int dst) {
+  Model &M = g_model;
+  Engine &E = engine();
+  int rc = check_ready("cwen_cuda_mtp_step");
+  if (rc) return rc;
+  if (!M.mtp_on) {
+    set_error("cwen_cuda_mtp_step: the model has no MTP block (blk.%d.nextn.*)", M.d.n_layer);
+    return CWEN_ESTATE;
+  }
+  if (pos < 1 || pos >= E.ctx || !mtp_slot(src) || (dst != CWEN_MTP_OUT0 && dst != CWEN_MTP_OUT1) || E.bmax < 2) {
+    set_error("cwen_cuda_mtp_step: need 1 <= pos < ctx %d, a source slot 0..2 and an output slot 1..2", E.ctx);
+    return CWEN_EINVAL;
+  }
+  if (tok < 0 || tok >= M.d.n_vocab) {
+    set_error("token id %d out of range [0,%d)", tok, M.d.n_vocab);
+    return CWEN_ERANGE;
+  }
+  Toks16 tk;
+  memset(&tk, 0, sizeof tk);
+  tk.t[0] = tok;
+  rc = mtp_step_dev(pos, 1, tk, nullptr, mtp_slot(src), mtp_slot(dst), E.stream);
+  if (rc) return rc;
+  CW_CHECK(cudaStreamSynchronize(E.stream));
+  int err = 0;
+  CW_CHECK(cudaMemcpy(&err, M.err, sizeof(int), cudaMemcpyDeviceToHost));
+  if (err) {
+    set_error("device reported a token id out of range");
+    return CWEN_ERANGE;
+  }
+  return gemv_status();
+}
+
+int cwen_cuda_mtp_read(int slot, float *host) {
+  Model &M = g_model;
+  int rc = check_ready("cwen_cuda_mtp_read");
+  if (rc) return rc;
+  if (!M.mtp_on || !mtp_slot(slot) || !host) {
+    set_error("cwen_cuda_mtp_read: need an MTP model, a slot 0..2 and a host buffer");
+    return CWEN_EINVAL;
+  }
+  CW_CHECK(cudaStreamSynchronize(engine().stream));
+  CW_CHECK(cudaMemcpy(host, mtp_slot(slot), (size_t)M.d.n_embd * sizeof(float), cudaMemcpyDeviceToHost));
+  return CWEN_OK;
 }
 
 int cwen_cuda_gdn_state(int layer, float *S_host, float *conv_host) {

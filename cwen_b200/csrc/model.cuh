@@ -54,7 +54,7 @@ struct Model {
   float *attn_o = nullptr;  // gated attention output rows [bmax][n_head*256]
   int nch_max = 0;
   float *logits = nullptr;
-  unsigned long long *best = nullptr;
+  void *best = nullptr;  // argmax + walk scratch (launch_argmax_walk)
   int *walk = nullptr, *toks = nullptr, *err = nullptr;
   int *h_walk = nullptr, *h_toks = nullptr;  // pinned host mirrors
   float2 *rope = nullptr;

@@ -25,7 +25,7 @@ constexpr int NA_KMAX = 32768;
 constexpr int NA_MAX_CTAS = 320;
 constexpr int NA_MAX_TILES = 2048;
 constexpr int NA_MAX_DEVICES = 64;
-constexpr size_t NA_XF_UINT4 = (size_t)(NA_KMAX / 32) * 2 * 2 * 32;  // X tiles for K <= NA_KMAX, 2 column tiles
+constexpr size_t NA_XF_UINT4 = (size_t)(NA_KMAX / 32) * 128;  // X operands for K <= NA_KMAX (2 KB per 32-block)
 constexpr size_t NA_WS_FLOATS = (size_t)NA_MAX_CTAS * 2 * WS_TILE_FLOATS;
 
 static __device__ __align__(256) uint4 g_na_xf[NA_XF_UINT4];

@@ -11,11 +11,10 @@
 namespace cw {
 
 // Device layout of one (possibly fused) weight matrix: rows grouped in
-// 16-row m-tiles, m-tiles in 512-row tiles of 32; per (m-tile, pair of
-// 32-blocks) one 576-byte chunk [512 B nibbles in mma A-fragment order |
-// 64 B f16 scales] (Q8_0: 1088 B [1024 B int8 | 64 B scales]), stored
-// [tile][k-pair][m-tile in tile] so that one (tile, k-pair) is contiguous.
-// The m-tile count is padded to whole tiles (zero padding).
+// 16-row m-tiles, m-tiles in 512-row tiles of 32; per (tile, pair of
+// 32-blocks) one contiguous stage [block 0: 512 rows x quant bytes | block 1 |
+// f16 scales [2][512]] (QgStage), stages stored [tile][k-pair].  The m-tile
+// count is padded to whole tiles (zero padding).
 struct QMat {
   uint8_t *w = nullptr;  // device
   int type = 0;          // 2 = Q4_0, 8 = Q8_0
@@ -28,27 +27,30 @@ struct QMat {
 enum { EPI_STORE = 0, EPI_ADD = 1, EPI_SWIGLU = 2 };
 
 constexpr int QG_MAXB = 16;
-constexpr int QG_CONS_WARPS = 16;                    // consumer warps, two m-tiles each
-constexpr int QG_THREADS = (QG_CONS_WARPS + 2) * 32;  // + two producer warps
+constexpr int QG_CONS_WARPS = 16;                    // row warps, 32 rows (two m-tiles) each
+constexpr int QG_THREADS = (QG_CONS_WARPS + 6) * 32;  // + two producer warps + four MMA-issuing warps
 constexpr int QG_TILE_MT = 2 * QG_CONS_WARPS;         // m-tiles per CTA tile (512 rows)
+constexpr int QG_TILE_ROWS = 16 * QG_TILE_MT;
+// One stage of the repacked weights: one 512-row tile x one k-pair.
+template <int TYPE>
+struct QgStage {
+  static constexpr int QROW = TYPE == 8 ? 32 : 16;             // quant bytes per row and 32-block
+  static constexpr int QB = QG_TILE_ROWS * QROW;               // one 32-block of the tile
+  static constexpr int WB = 2 * QB + 2 * QG_TILE_ROWS * 2;     // both blocks + their f16 scales
+};
 constexpr int WS_TILE_FLOATS = QG_TILE_MT * 16 * 16;   // split-K partials of one tile (16 columns)
 constexpr int QG_XL_KP = 20;  // local-X variant: at most this many k-pairs per CTA
 constexpr int QG_STAT_COLS = 16;  // per-CTA statistics slot: one float per column
 
-// GEMV input columns come in n-tiles of 8 (one m16n8k16 B operand holds 8
-// columns; the f16 hi and lo parts of X are two B operands accumulated into
-// the same MMA result): 1 or 2 n-tiles.
-inline int gemv_ntiles(int B) { return (B + 7) / 8; }
-
-inline size_t qmat_chunk_bytes(int type) { return type == 8 ? 1088 : 576; }
+inline size_t qmat_stage_bytes(int type) { return type == 8 ? QgStage<8>::WB : QgStage<2>::WB; }
 inline size_t qmat_bytes(int type, int K, int n_mt) {
   const size_t tiles = (size_t)(n_mt + QG_TILE_MT - 1) / QG_TILE_MT;
-  return qmat_chunk_bytes(type) * (size_t)(K / 64) * tiles * QG_TILE_MT;
+  return qmat_stage_bytes(type) * (size_t)(K / 64) * tiles;
 }
 
 // Scratch the GEMV needs (owned by the caller, reused across calls on one stream).
 struct GemvScratch {
-  uint4 *xf = nullptr;   // X fragments, >= (Kmax/32) * 2 ntiles * 64 uint4
+  uint4 *xf = nullptr;   // X operands, >= (Kmax/32) * 128 uint4 (2 KB per 32-block)
   int *xexp = nullptr;   // [16] per-column exponents
   float *ws = nullptr;   // split-K partials [G][2][WS_TILE_FLOATS]
   int *cnt = nullptr;    // per CTA-tile arrival counters (zero, self-resetting)

@@ -52,7 +52,7 @@ cudaError_t launch_embed(const uint8_t *emb, int H, int V, const Toks16 &toks, i
 __global__ void __launch_bounds__(PREP_THREADS) cat_norm_prep_kernel(const float *__restrict__ e,
                                                                      const float *__restrict__ h,
                                                                      const float *__restrict__ we,
-                                                                     const float *__restrict__ wh, int H, int nt,
+                                                                     const float *__restrict__ wh, int H,
                                                                      uint4 *__restrict__ xf, int *__restrict__ xexp) {
   pdl_trigger();
   pdl_wait();
@@ -77,7 +77,7 @@ __global__ void __launch_bounds__(PREP_THREADS) cat_norm_prep_kernel(const float
     v[H + k] = wh[k] * v[H + k] * rh;
   }
   __syncthreads();
-  emit_xfrag(v, 2 * H, b, nt, xf, xexp, red, true);
+  emit_xfrag(v, 2 * H, b, xf, xexp, red, true);
 }
 
 cudaError_t launch_cat_norm_prep(const float *e, const float *h, const float *we, const float *wh, int H, int B,
@@ -86,7 +86,7 @@ cudaError_t launch_cat_norm_prep(const float *e, const float *h, const float *we
   static size_t done = 0;
   cudaError_t err = smem_optin(cat_norm_prep_kernel, smem, done);
   if (err != cudaSuccess) return err;
-  CW_TRY(launch_pdl(cat_norm_prep_kernel, B, PREP_THREADS, smem, st, e, h, we, wh, H, gemv_ntiles(B), s.xf, s.xexp));
+  CW_TRY(launch_pdl(cat_norm_prep_kernel, B, PREP_THREADS, smem, st, e, h, we, wh, H, s.xf, s.xexp));
   return cudaGetLastError();
 }
 
@@ -102,7 +102,7 @@ constexpr int ROW_THREADS = 256;
 // ---- RMSNorm (run.c:346) fused with GEMV input preparation ----
 // Optional copy of the normed row to `out`.
 __global__ void __launch_bounds__(ROW_THREADS) norm_prep_kernel(const float *__restrict__ x, const float *__restrict__ w,
-                                                                int H, int nt, uint4 *__restrict__ xf,
+                                                                int H, uint4 *__restrict__ xf,
                                                                 int *__restrict__ xexp, float *__restrict__ out) {
   pdl_trigger();
   pdl_wait();
@@ -130,19 +130,19 @@ __global__ void __launch_bounds__(ROW_THREADS) norm_prep_kernel(const float *__r
   __syncthreads();
   const int e = xfrag_exponent(sm.y * s);
   if (r == 0 && threadIdx.x == 0) xexp[b] = e;
-  emit_xfrag_blocks(v, k0 / 32, n / 32, b, nt, xf, __int_as_float((127 + e) << 23), true);
+  emit_xfrag_blocks(v, k0 / 32, n / 32, b, xf, __int_as_float((127 + e) << 23), true);
 }
 
 cudaError_t launch_norm_prep(const float *x, const float *w, int H, int B, GemvScratch &s, float *out,
                              cudaStream_t st) {
   const int cl = cluster_split(H / 32);
   CW_TRY(launch_pdl_cluster(norm_prep_kernel, dim3(cl, B), ROW_THREADS, (size_t)(H / cl) * sizeof(float), st, cl, x, w,
-                            H, gemv_ntiles(B), s.xf, s.xexp, out));
+                            H, s.xf, s.xexp, out));
   return cudaGetLastError();
 }
 
 // ---- plain row -> GEMV input (e.g. the SwiGLU output feeding ffn_down) ----
-__global__ void __launch_bounds__(ROW_THREADS) row_prep_kernel(const float *__restrict__ x, int xs, int K, int nt,
+__global__ void __launch_bounds__(ROW_THREADS) row_prep_kernel(const float *__restrict__ x, int xs, int K,
                                                                uint4 *__restrict__ xf, int *__restrict__ xexp) {
   pdl_trigger();
   pdl_wait();
@@ -158,66 +158,103 @@ __global__ void __launch_bounds__(ROW_THREADS) row_prep_kernel(const float *__re
   mx = cluster_reduce<true>(block_max(mx, red), &slot);
   const int e = xfrag_exponent(mx);
   if (r == 0 && threadIdx.x == 0) xexp[b] = e;
-  emit_xfrag_blocks(v, k0 / 32, n / 32, b, nt, xf, __int_as_float((127 + e) << 23), true);
+  emit_xfrag_blocks(v, k0 / 32, n / 32, b, xf, __int_as_float((127 + e) << 23), true);
 }
 
 cudaError_t launch_row_prep(const float *x, int xs, int K, int B, GemvScratch &s, cudaStream_t st) {
   const int cl = cluster_split(K / 32);
   CW_TRY(launch_pdl_cluster(row_prep_kernel, dim3(cl, B), ROW_THREADS, (size_t)(K / cl) * sizeof(float), st, cl, x, xs,
-                            K, gemv_ntiles(B), s.xf, s.xexp));
+                            K, s.xf, s.xexp));
   return cudaGetLastError();
 }
 
-// ---- argmax (argmax_of run.c:2647): first maximum over n logits per row ----
+// ---- argmax (argmax_of run.c:2647) + greedy walk (run.c:4954-4959), one launch ----
 // Packed key: order-preserving float bits in the high word, ~index in the low
 // word, so a 64-bit max picks the largest value and, among equal values, the
-// lowest index -- independent of the order CTAs finish.
+// lowest index -- independent of the order CTAs finish.  The reference scans
+// with a strict `>` from bv = lg[0]: -0.0 and +0.0 compare equal (canonicalised
+// to +0.0 here, so the lower index wins), a NaN never replaces the running
+// maximum (a NaN at index i > 0 is skipped: key of -inf), and a NaN at index 0
+// is never replaced, so the answer is 0 (top key).
 CW_DEV unsigned long long argmax_key(float v, int i) {
+  if (v != v) return i == 0 ? ~0ull : 0ull;
+  if (v == 0.f) v = 0.f;  // -0.0 -> +0.0
   uint32_t u = __float_as_uint(v);
   u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
   return ((unsigned long long)u << 32) | (uint32_t)(~(uint32_t)i);
 }
 
-__global__ void argmax_kernel(const float *__restrict__ lg, int n, int ldl, unsigned long long *__restrict__ best) {
+constexpr int AW_THREADS = 256;
+constexpr int AW_CTAS = 64;  // CTAs per logits row
+
+// Grid (AW_CTAS, B): each CTA reduces a strided slice of row b to one key and
+// parks it in part[b][cta]; the last CTA to arrive (arrival counter, reset by
+// that CTA) reduces every row's parked keys and walks the block:
+//   k = longest prefix with argmax(row j) == blk[j+1] (j < E), ustar = argmax(row k)
+//   res = [k, ustar, argmax(row 0..B-1)].
+__global__ void __launch_bounds__(AW_THREADS) argmax_walk_kernel(const float *__restrict__ lg, int n, int ldl, int E,
+                                                                 const Toks16 blk, unsigned long long *__restrict__ part,
+                                                                 unsigned int *__restrict__ count, int *__restrict__ res) {
   pdl_trigger();
   pdl_wait();
-  const int b = blockIdx.y;
+  __shared__ unsigned long long red[AW_THREADS / 32];
+  __shared__ int am[16];
+  __shared__ bool last;
+  const int b = blockIdx.y, B = gridDim.y, nb = gridDim.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   unsigned long long k = 0;
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
-    const float v = lg[(size_t)b * ldl + i];
-    const unsigned long long kk = argmax_key(v != v ? -INFINITY : v, i);
+    const unsigned long long kk = argmax_key(lg[(size_t)b * ldl + i], i);
     k = kk > k ? kk : k;
   }
+#pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     const unsigned long long t = __shfl_xor_sync(0xffffffffu, k, o);
     k = t > k ? t : k;
   }
-  if ((threadIdx.x & 31) == 0) atomicMax(best + b, k);
+  if (lane == 0) red[warp] = k;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < AW_THREADS / 32; w++) k = red[w] > k ? red[w] : k;
+    part[b * nb + blockIdx.x] = k;
+    __threadfence();  // the parked key before the arrival
+    last = atomicAdd(count, 1u) == (unsigned)(nb * B - 1);
+  }
+  __syncthreads();
+  if (!last) return;
+  __threadfence();  // every other CTA's parked key, after its arrival
+  for (int r = warp; r < B; r += AW_THREADS / 32) {
+    unsigned long long m = 0;
+    for (int c = lane; c < nb; c += 32) {
+      const unsigned long long t = __ldcg(part + r * nb + c);
+      m = t > m ? t : m;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const unsigned long long t = __shfl_xor_sync(0xffffffffu, m, o);
+      m = t > m ? t : m;
+    }
+    if (lane == 0) am[r] = (int)(~(uint32_t)(m & 0xffffffffu));
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int kk = 0;
+    while (kk < E && am[kk] == blk.t[kk + 1]) kk++;
+    res[0] = kk;
+    res[1] = am[kk];
+    for (int r = 0; r < B; r++) res[2 + r] = am[r];
+    *count = 0u;  // ready for the next launch (launches on a stream are ordered)
+  }
 }
 
-// Greedy walk of generate_tokens_spec (run.c:4954-4956) on device:
-// k = longest prefix with argmax(row j) == blk[j+1]; ustar = argmax(row k).
-// res = [k, ustar, argmax(row 0..B-1)].
-__global__ void walk_kernel(const unsigned long long *__restrict__ best, const Toks16 blk, int B, int E,
-                            int *__restrict__ res) {
-  pdl_trigger();
-  pdl_wait();
-  if (threadIdx.x != 0 || blockIdx.x != 0) return;
-  int am[16];
-  for (int b = 0; b < B; b++) am[b] = (int)(~(uint32_t)(best[b] & 0xffffffffu));
-  int k = 0;
-  while (k < E && am[k] == blk.t[k + 1]) k++;
-  res[0] = k;
-  res[1] = am[k];
-  for (int b = 0; b < B; b++) res[2 + b] = am[b];
-}
+size_t argmax_part_bytes(int bmax) { return (size_t)bmax * AW_CTAS * sizeof(unsigned long long) + 256; }
 
-cudaError_t launch_argmax_walk(const float *lg, int n, int ldl, int B, int E, const Toks16 &blk,
-                               unsigned long long *best, int *res, cudaStream_t st) {
-  cudaError_t e = cudaMemsetAsync(best, 0, (size_t)B * sizeof(unsigned long long), st);
-  if (e != cudaSuccess) return e;
-  CW_TRY(launch_pdl(argmax_kernel, dim3(64, B), 256, 0, st, lg, n, ldl, best));
-  CW_TRY(launch_pdl(walk_kernel, 1, 32, 0, st, best, blk, B, E, res));
+cudaError_t launch_argmax_walk(const float *lg, int n, int ldl, int B, int E, const Toks16 &blk, void *scratch,
+                               int *res, cudaStream_t st) {
+  if (B < 1 || B > 16 || E < 0 || E >= B) return cudaErrorInvalidValue;
+  auto *count = reinterpret_cast<unsigned int *>(scratch);  // first 256 bytes: the arrival counter
+  auto *part = reinterpret_cast<unsigned long long *>(static_cast<char *>(scratch) + 256);
+  CW_TRY(launch_pdl(argmax_walk_kernel, dim3(AW_CTAS, B), AW_THREADS, 0, st, lg, n, ldl, E, blk, part, count, res));
   return cudaGetLastError();
 }
 
@@ -227,8 +264,7 @@ cudaError_t rowops_configure() {
   if ((e = carveout_max(embed_kernel)) != cudaSuccess) return e;
   if ((e = carveout_max(norm_prep_kernel)) != cudaSuccess) return e;
   if ((e = carveout_max(row_prep_kernel)) != cudaSuccess) return e;
-  if ((e = carveout_max(argmax_kernel)) != cudaSuccess) return e;
-  if ((e = carveout_max(walk_kernel)) != cudaSuccess) return e;
+  if ((e = carveout_max(argmax_walk_kernel)) != cudaSuccess) return e;
   if ((e = carveout_max(cat_norm_prep_kernel)) != cudaSuccess) return e;
   return cudaSuccess;
 }

@@ -23,10 +23,13 @@ cudaError_t launch_norm_prep(const float *x, const float *w, int H, int B, GemvS
                              cudaStream_t st);
 // rows x [B][xs], first K values -> GEMV input.
 cudaError_t launch_row_prep(const float *x, int xs, int K, int B, GemvScratch &s, cudaStream_t st);
-// First-max argmax of B rows of logits (row stride ldl) and the greedy walk
-// against blk[0..E]: res = [k, ustar, argmax rows...].
-cudaError_t launch_argmax_walk(const float *lg, int n, int ldl, int B, int E, const Toks16 &blk,
-                               unsigned long long *best, int *res, cudaStream_t st);
+// First-max argmax of B <= 16 rows of logits (row stride ldl) and the greedy
+// walk against blk[0..E], E < B, in one launch: res = [k, ustar, argmax rows...].
+// scratch: argmax_part_bytes(B) bytes of device memory whose first word is
+// zero before the first launch (the kernel leaves it zero again).
+size_t argmax_part_bytes(int bmax);
+cudaError_t launch_argmax_walk(const float *lg, int n, int ldl, int B, int E, const Toks16 &blk, void *scratch,
+                               int *res, cudaStream_t st);
 
 // Kernel attributes set once per process (shared-memory carveout).
 cudaError_t rowops_configure();

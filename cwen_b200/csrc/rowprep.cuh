@@ -49,44 +49,43 @@ CW_DEV int xfrag_exponent(float mx) {
   return e;
 }
 
-// Emit GEMV fragments of column b for the 32-blocks [kb0, kb0 + nkb) from
-// v (v[0] is element 32*kb0 of the column), already scaled by nothing: the
-// power-of-two `scale` is applied here.  Layout: see prep comments in qgemv.cu
-// (per 32-block and n-tile of 8 columns: 32 uint4 of hi parts, then 32 of lo
-// parts, lane 4*(b & 7) + t).
-CW_DEV void emit_xfrag_blocks(const float *v, int kb0, int nkb, int b, int nt, uint4 *__restrict__ xf, float scale,
+// Emit the GEMV's X operands of column b for the 32-blocks [kb0, kb0 + nkb)
+// from v (v[0] is element 32*kb0 of the column); the power-of-two `scale` is
+// applied here.  Per 32-block 2 KB (128 uint4): two k16 steps x (hi tile,
+// lo tile), a tile 16 columns x 16 K, K-major without swizzle (column n,
+// 8-K chunk c at byte (n % 8) * 16 + (n / 8) * 256 + c * 128): the B operand
+// layout of the tensor cores.
+CW_DEV void emit_xfrag_blocks(const float *v, int kb0, int nkb, int b, uint4 *__restrict__ xf, float scale,
                               bool live) {
-  const int g = b & 7, n = b >> 3;
   for (int item = threadIdx.x; item < nkb * 4; item += blockDim.x) {
-    const int kbl = item >> 2, t = item & 3;
-    const float *r = v + kbl * 32;
-    const int js[8] = {4 * t, 4 * t + 2, 4 * t + 1, 4 * t + 3, 4 * t + 16, 4 * t + 18, 4 * t + 17, 4 * t + 19};
+    const int kbl = item >> 2, c = item & 3;
+    const float *r = v + kbl * 32 + c * 8;
     uint32_t hi[4], lo[4];
 #pragma unroll
     for (int i = 0; i < 4; i++) {
-      const float v0 = live ? r[js[2 * i]] * scale : 0.f, v1 = live ? r[js[2 * i + 1]] * scale : 0.f;
+      const float v0 = live ? r[2 * i] * scale : 0.f, v1 = live ? r[2 * i + 1] * scale : 0.f;
       const half h0 = __float2half_rn(v0), h1 = __float2half_rn(v1);
       const half l0 = __float2half_rn(v0 - __half2float(h0)), l1 = __float2half_rn(v1 - __half2float(h1));
       hi[i] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
       lo[i] = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
     }
-    uint4 *o = xf + (size_t)((kb0 + kbl) * nt + n) * 64;
-    o[g * 4 + t] = make_uint4(hi[0], hi[1], hi[2], hi[3]);       // hi B operand, column g
-    o[32 + g * 4 + t] = make_uint4(lo[0], lo[1], lo[2], lo[3]);  // lo B operand, column g
+    uint4 *o = xf + (size_t)(kb0 + kbl) * 128 + (c >> 1) * 64 + (b >> 3) * 16 + (c & 1) * 8 + (b & 7);
+    o[0] = make_uint4(hi[0], hi[1], hi[2], hi[3]);   // hi tile
+    o[32] = make_uint4(lo[0], lo[1], lo[2], lo[3]);  // lo tile, 512 bytes on
   }
 }
 
-// Emit GEMV fragments for column b from v[0..K) in shared memory (one CTA
-// holds the whole column; columns b >= B are zero padding of the n-tile).
-CW_DEV void emit_xfrag(const float *v, int K, int b, int nt, uint4 *__restrict__ xf, int *__restrict__ xexp,
-                       float *red, bool live) {
+// Emit the X operands for column b from v[0..K) in shared memory (one CTA
+// holds the whole column).
+CW_DEV void emit_xfrag(const float *v, int K, int b, uint4 *__restrict__ xf, int *__restrict__ xexp, float *red,
+                       bool live) {
   float mx = 0.f;
   if (live)
     for (int k = threadIdx.x; k < K; k += blockDim.x) mx = fmaxf(mx, fabsf(v[k]));
   mx = block_max(mx, red);
   const int e = xfrag_exponent(mx);
   if (threadIdx.x == 0) xexp[b] = e;
-  emit_xfrag_blocks(v, 0, K / 32, b, nt, xf, __int_as_float((127 + e) << 23), live);
+  emit_xfrag_blocks(v, 0, K / 32, b, xf, __int_as_float((127 + e) << 23), live);
 }
 
 // One float per CTA reduced over the thread-block cluster (<= 32 CTAs)

@@ -174,6 +174,20 @@ int cwen_cuda_mtp_commit_block(int pos0, const int *toks, int n);
  * negative CWEN_E* code (mtp_draft, run.c:3166-3187). */
 int cwen_cuda_mtp_draft(int pend, int *out, int max_d);
 
+/* Hidden-state slots of the nextn stream: the predecessor hidden parked by
+ * cwen_cuda_mtp_commit (rmsnorm(x_pre, output_norm) of the last committed
+ * slot, the reference's NHprev) and two output slots. */
+enum { CWEN_MTP_PARKED = 0, CWEN_MTP_OUT0 = 1, CWEN_MTP_OUT1 = 2 };
+/* One nextn step (mtp_step, run.c:3099-3131) at stream slot pos (1 <= pos <
+ * ctx): input token tok, predecessor hidden from slot src, the
+ * shared-head-normed output hidden into slot dst (CWEN_MTP_OUT0/OUT1); writes
+ * K/V at pos of the nextn cache, which later steps attend over (slots 1..pos).
+ * The parked slot and the stream position of cwen_cuda_mtp_commit are left as
+ * they are.  Synchronizes. */
+int cwen_cuda_mtp_step(int tok, int pos, int src, int dst);
+/* Copy slot `slot`'s hidden (n_embd floats) to host memory. */
+int cwen_cuda_mtp_read(int slot, float *host);
+
 /* Copies of device rows for parity checks: logits row (n_vocab floats), the
  * residual stream after the last layer (n_embd), per-layer residual streams
  * (the CWEN_DUMP layerNN files, run.c:2601-2629) while dumps are on, and a
@@ -183,6 +197,17 @@ int cwen_cuda_hidden(int row, float *host);
 int cwen_cuda_dump_layers(int on);
 int cwen_cuda_dump_read(int layer, int row, float *host);
 int cwen_cuda_gdn_state(int layer, float *S_host, float *conv_host);
+
+/* The fused argmax + greedy walk of cwen_cuda_accept on caller device logits:
+ * rows b < B (1 <= B <= 16) of n logits at stride ldl; row j's argmax is
+ * compared with blk[j+1] for j < E_drafts (0 <= E_drafts < B; blk may be
+ * NULL when E_drafts is 0).  res[0] = k (drafts accepted), res[1] = ustar
+ * (argmax of row k), res[2..2+B) = the rows' argmaxes.  First maximum, ties to
+ * the lowest index, -0.0 equal to +0.0, NaN never replacing the maximum, a NaN
+ * at index 0 kept (argmax_of, run.c:2647-2669; the walk, run.c:4954-4959).
+ * One kernel launch on `stream` (NULL: the engine's); synchronizes. */
+int cwen_cuda_accept_logits(const float *dlogits, int n, int ldl, int B, const int *blk, int E_drafts, int *res,
+                            void *stream);
 
 /* ---- instrumentation (the reference's CWEN_SPEC_DEBUG timers, run.c:3133) ---- */
 /* Reset counters and turn per-launch CUDA-event timing of the verify-GEMV

@@ -144,6 +144,34 @@ CWREF_API int cwref_load_synth(uint64_t seed, int has_mtp, int threads) {
   rebind_layers_from_tens();
   return 0;
 }
+/* The tensor blobs cwref_load_synth generated, in descriptor order (returns
+   their count), so that another build of this harness in the same process,
+   or the engine's upload, can use the same bytes instead of generating them
+   again. */
+CWREF_API int cwref_blobs(void **out, int cap) {
+  int n = g_model_nblobs < cap ? g_model_nblobs : cap;
+  for (int i = 0; i < n; i++) out[i] = g_model_blobs[i];
+  return g_model_nblobs;
+}
+/* Bind blobs made by cwref_load_synth of another build (same seed and
+   geometry, descriptor order) through the reference's validator. */
+CWREF_API int cwref_bind_blobs(void *const *blobs, int n, int has_mtp) {
+  cw_dims d;
+  cw_dims_full(&d);
+  d.has_mtp = has_mtp;
+  int nt = cw_model_tensor_count(&d);
+  if (nt != n || nt > (int)(sizeof Tens / sizeof Tens[0])) return -1;
+  Ntens = 0;
+  for (int i = 0; i < nt; i++) {
+    cw_tensor_desc t;
+    cw_model_tensor_desc(&d, i, &t);
+    snprintf(Tnames[Ntens], sizeof Tnames[0], "%s", t.name);
+    Tens[Ntens] = mk_tensor(t.type, blobs[i], t.ne0, t.ne1);
+    Ntens++;
+  }
+  rebind_layers_from_tens();
+  return 0;
+}
 /* alloc_state (run.c:3928) after choosing context / speculation / MTP use. */
 CWREF_API void cwref_alloc_state(int ctx, int spec, int use_mtp) {
   g_ctx = ctx;
@@ -176,6 +204,22 @@ static void ref_sink_fn(int token, int idx, void *ud) {
   (void)idx;
   ref_sink *s = (ref_sink *)ud;
   if (s->n < s->cap) s->out[s->n++] = token;
+}
+/* forward_ex (run.c:2594-2645) at the current slot with the residual stream
+   after every layer copied to layers_out[l*H] -- what CWEN_DUMP writes to
+   layerNN_posMM.bin (run.c:2624-2628) -- and the logits to logits_out, without
+   the file I/O, so that dumps can start at any slot of a block-prefilled
+   context (the reference fixes its dump choice at its first forward). */
+CWREF_API void cwref_forward_layers(int token, float *layers_out, float *logits_out) {
+  embed_token_to(token, x);
+  for (int l = 0; l < L; l++) {
+    if (W[l].is_linear) layer_linear(l);
+    else layer_full(l);
+    memcpy(layers_out + (size_t)l * H, x, (size_t)H * sizeof(float));
+  }
+  rmsnorm(xb, x, (const float *)output_norm.data, H);
+  gemv(&output, xb, logits);
+  memcpy(logits_out, logits, (size_t)V * sizeof(float));
 }
 /* One iteration of generate_tokens' loop (run.c:5033-5041) after a prefill:
    the next slot, forward_ex of the token, the argmax of its logits. */

@@ -141,3 +141,48 @@ def test_mtp_commit_block_equals_rows(mtp_model):
         (d0, p0, l0), (d1, p1, l1) = res
         assert p0 == p1 and list(d0) == list(d1), cuts
         assert np.array_equal(l0.view(np.uint32), l1.view(np.uint32)), cuts
+
+
+def test_mtp_step_export_matches_oracle(mtp_model, orc):
+    """cwen_cuda_mtp_step (mtp_step, run.c:3099-3131) from the parked hidden,
+    then chained from its own output slot, against the oracle's mtp_step on
+    the same stream: the output hiddens agree to rel L2 <= 1e-4."""
+    import cwen_b200
+    L, d = mtp_model
+    od, om = _oracle(orc)
+    orc.or_mtp_step.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p]
+    orc.or_mtp_hprev.argtypes = [C.c_void_p]
+    orc.or_mtp_hprev.restype = C.POINTER(C.c_float)
+    H = d.n_embd
+    try:
+        toks = np.random.default_rng(21).integers(0, d.n_vocab, size=7).astype(np.int32)
+        cwen_b200.check(L.cwen_cuda_reset())
+        cwen_b200.check(L.cwen_cuda_forward_block(vp(toks), len(toks), -1), "forward_block")
+        cwen_b200.check(L.cwen_cuda_accept(None, None, None), "accept")
+        cwen_b200.check(L.cwen_cuda_commit(len(toks) - 1), "commit")
+        cwen_b200.check(L.cwen_cuda_mtp_commit_block(0, vp(toks), len(toks)), "mtp_commit_block")
+        orc.or_reset(om)
+        for p, t in enumerate(toks):
+            orc.or_forward(om, int(t), p, 1)
+            orc.or_mtp_commit(om, p, int(t), orc.or_hidden(om))
+        park = np.zeros(H, np.float32)
+        cwen_b200.check(L.cwen_cuda_mtp_read(0, vp(park)), "mtp_read")
+        opark = np.ctypeslib.as_array(orc.or_mtp_hprev(om), shape=(H,)).copy()
+        assert rel_l2(park, opark) <= 1e-4
+        pos = len(toks)
+        h1, oh1, oh2 = np.zeros(H, np.float32), np.zeros(H, np.float32), np.zeros(H, np.float32)
+        cwen_b200.check(L.cwen_cuda_mtp_step(101, pos, 0, 1), "mtp_step")
+        cwen_b200.check(L.cwen_cuda_mtp_read(1, vp(h1)), "mtp_read")
+        orc.or_mtp_step(om, 101, pos, vp(opark), vp(oh1))
+        assert rel_l2(h1, oh1) <= 1e-4, rel_l2(h1, oh1)
+        h2 = np.zeros(H, np.float32)
+        cwen_b200.check(L.cwen_cuda_mtp_step(202, pos + 1, 1, 2), "mtp_step")
+        cwen_b200.check(L.cwen_cuda_mtp_read(2, vp(h2)), "mtp_read")
+        orc.or_mtp_step(om, 202, pos + 1, vp(oh1), vp(oh2))
+        assert rel_l2(h2, oh2) <= 1e-4, rel_l2(h2, oh2)
+        # range checks: slot 0 is not an output slot, pos 0 has no attendable slot
+        assert L.cwen_cuda_mtp_step(1, pos + 2, 1, 0) == -1
+        assert L.cwen_cuda_mtp_step(1, 0, 0, 1) == -1
+        assert L.cwen_cuda_mtp_step(d.n_vocab, pos + 2, 0, 1) == -5
+    finally:
+        orc.or_model_free(om)

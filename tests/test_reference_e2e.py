@@ -1,20 +1,20 @@
 """Full 27B geometry on seeded random weights: the engine against the
 reference itself (maci0/cwen run.c compiled into oracle/_ref, running its own
-forward_ex with its CWEN_DUMP per-layer dumps, run.c:2601-2629).
+forward_ex with its CWEN_DUMP per-layer dumps, run.c:2601-2629), at the
+first slots of a sequence (the 27B model past slot 512 is
+test_reference_chain.py).
 
 Bar (north star): per-layer hidden states and logits within 1e-3 relative L2
 of the reference's CPU path.  The random-init model is chaotic at some
 positions (position 0 of this seed): there, two fp32 CPU implementations of
 the reference's own algorithm (the oracle's scalar summation order and the
 reference's AVX-512 order) drift apart by far more than 1e-3 in the deep
-layers, and any other summation order lands an unrelated random distance of
-that order away (measured: 0.03 to 0.34 at layer 57 for engine builds that
-differ only in fp32 rounding order).  So: a layer is held to 1e-3 until the
-first layer where that oracle-vs-reference spread exceeds 1e-4 (the chaotic
-onset); from there on only to "not garbage" (rel L2 < 0.7; a wrong kernel
-gives ~1.0 or more).  Positions that never reach the onset are held to 1e-3
-at every layer and in the logits.  Token ids must agree wherever the oracle
-and the reference agree and the reference's top-2 margin exceeds 1e-4.
+layers, and any other summation order lands a random distance of that order
+away.  So every layer and the logits are held to max(1e-3, 3 x spread),
+spread = the oracle-vs-reference relative L2 at that layer and position; the
+test prints how many checks needed more than 1e-3.  Token ids must agree
+wherever the oracle and the reference agree and the reference's top-2 margin
+exceeds 1e-4.
 """
 import ctypes as C
 import os
@@ -70,6 +70,7 @@ def test_full_geometry_matches_reference(tmp_path):
         cwen_b200.check(L.cwen_cuda_dump_layers(1))
         H, V = d.n_embd, d.n_vocab
         hid = np.zeros(H, np.float32)
+        loose = checks = 0
         for p, t in enumerate(toks):
             ref.cwref_set_pos(p)
             ref.cwref_forward_ex(int(t), 1)
@@ -91,17 +92,21 @@ def test_full_geometry_matches_reference(tmp_path):
             e_lg, f_lg = rel_l2(gl, rl), rel_l2(ol, rl)
             print(f"pos {p}: engine-vs-ref per layer max {max(eng):.2e} (floor max {max(flo):.2e}); "
                   f"logits {e_lg:.2e} (floor {f_lg:.2e})")
-            chaotic = False
             for layer in range(d.n_layer):
-                chaotic = chaotic or flo[layer] > 1e-4
-                bar = 0.7 if chaotic else 1e-3
+                bar = max(1e-3, 3.0 * flo[layer])
+                loose += bar > 1e-3
+                checks += 1
                 assert eng[layer] <= bar, (p, layer, eng[layer], flo[layer])
-            assert e_lg <= (0.7 if chaotic or f_lg > 1e-4 else 1e-3), (p, e_lg, f_lg)
+            bar = max(1e-3, 3.0 * f_lg)
+            loose += bar > 1e-3
+            checks += 1
+            assert e_lg <= bar, (p, e_lg, f_lg)
             ref_am, orc_am = int(np.argmax(rl)), int(np.argmax(ol))
             top2 = np.sort(rl)[-2:]
             if ref_am == orc_am and top2[1] - top2[0] > 1e-4:
                 assert am.value == ref_am, p
         cwen_b200.check(L.cwen_cuda_dump_layers(0))
+        print(f"bar above 1e-3 (3 x the oracle-vs-reference spread) at {loose} of {checks} checks")
     finally:
         L.cwen_cuda_shutdown()
         orc.or_model_free(om)
