@@ -529,6 +529,91 @@ class Synth:
         return v
 
 
+SHARD_HANDLE = 256  # CWEN_SHARD_HANDLE_BYTES
+
+
+def shard_exchange(blob: bytes, ws: int) -> bytes:
+    """Every rank's exchange-buffer handles, in rank order (one all-gather of
+    small host objects over the process group: plumbing, not the data path)."""
+    import torch.distributed as dist
+    out = [None] * ws
+    dist.all_gather_object(out, blob)
+    assert all(isinstance(b, bytes) and len(b) == len(blob) for b in out)
+    return b"".join(out)
+
+
+def run_decode_sharded(args, ws, rank, local):
+    """The same serial greedy decode with the FFN and lm_head row-sharded
+    over the ws GPUs (cwen_cuda_shard_*): one sequence, every GPU works on
+    every token.  Returns the per-token device time (max over ranks), the
+    end-to-end rate through cwen_generate, and an n-gram speculative run
+    checked token for token against the group's own serial stream."""
+    import torch
+
+    import cwen_b200
+    L = cwen_b200.lib()
+    cwen_b200.check(L.cwen_cuda_init(local, DEC_CTX, 16), "init")
+    try:
+        cwen_b200.check(L.cwen_cuda_shard_config(rank, ws), "shard_config")
+        d = cwen_b200.dims("reference")
+        t0 = time.perf_counter()
+        cwen_b200.check(L.cwen_load_synth(DEC_SEED, C.byref(d), synth_threads(ws)), "load_synth")
+        load_s = time.perf_counter() - t0
+        blob = (C.c_uint8 * SHARD_HANDLE)()
+        cwen_b200.check(L.cwen_cuda_shard_handle(blob, SHARD_HANDLE), "shard_handle")
+        allb = shard_exchange(bytes(blob), ws)
+        cwen_b200.check(L.cwen_cuda_shard_open(allb, ws), "shard_open")
+        V = d.n_vocab
+        prompt = synth_ids(PROMPT_LEN, DEC_SEED, "bench.prompt", V)
+        serial = cwen_b200.spec_cfg(spec=0)
+        first, _ = cwen_b200.generate(prompt, 1, serial)
+        nxt = C.c_int(0)
+        stream = torch.cuda.ExternalStream(L.cwen_cuda_stream(), device=torch.device("cuda", local))
+
+        def steps(n, tok):
+            for _ in range(n):
+                cwen_b200.check(L.cwen_cuda_forward_serial(tok, 1, C.byref(nxt)), "forward_serial")
+                tok = nxt.value
+            return tok
+
+        tok = steps(args.warmup, int(first[0]))
+        torch.cuda.synchronize()
+        barrier(ws)
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev0.record(stream)
+        tok = steps(args.steps, tok)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        ms = barrier_max(ws, ev0.elapsed_time(ev1) / args.steps)
+        n_e2e = 64
+        t0 = time.perf_counter()
+        cwen_b200.generate(prompt, 1, serial)
+        t1 = time.perf_counter() - t0
+        t0 = time.perf_counter()
+        cwen_b200.generate(prompt, n_e2e, serial)
+        tn = time.perf_counter() - t0
+        e2e = 1.0 / barrier_max(ws, (tn - t1) / (n_e2e - 1))
+        mp = motif_prompt(SPEC_PROMPT, V)
+        n_spec = 128
+        ser_stream, _ = cwen_b200.generate(mp, n_spec, serial)
+        t0 = time.perf_counter()
+        cwen_b200.generate(mp, 1, serial)
+        s1 = time.perf_counter() - t0
+        t0 = time.perf_counter()
+        spec_stream, st = cwen_b200.generate(mp, n_spec, cwen_b200.spec_cfg(spec=1, use_mtp=0, max_draft=8))
+        sn = time.perf_counter() - t0
+        spec_tps = 1.0 / barrier_max(ws, (sn - s1) / (n_spec - 1))
+        return {"workload": f"serial greedy decode of one sequence, FFN + lm_head row-sharded over {ws} GPUs "
+                            f"(NVLink stores + cross-GPU barrier, replicated GDN/attention)",
+                "tok_s": round(1000.0 / ms, 3), "ms_per_token": round(ms, 4),
+                "e2e_tok_s": round(e2e, 3), "model_load_s": round(load_s, 1),
+                "spec_d8_tok_s": round(spec_tps, 2),
+                "spec_identical_to_serial": bool(np.array_equal(ser_stream, spec_stream)),
+                "spec_avg_kept": round(st.kept / st.drafted, 3) if st.drafted else 0.0}
+    finally:
+        L.cwen_cuda_shutdown()
+
+
 def cpu_decode_baseline(steps: int = 24, warmup: int = 2):
     """The reference's own greedy decode on the seeded model in host memory,
     all host cores, on the same workload as the engine: generate_tokens
@@ -612,6 +697,13 @@ def main_decode(args, ws, rank, local):
                     "d2h_bytes_per_step": 12, "method": "cwen_generate (C host driver): (t(256)-t(1))/255"},
             "spec_d8": spec, "mtp_d8": spec.pop("mtp_d8", None), "model_load_s": round(load_s, 1),
             "verify_ceiling": kern.get("verify_ceiling")}
+    if ws > 1:
+        # the latency-oriented alternative to the replicas: one sequence over
+        # all ws GPUs; a failure is reported in the line, never in place of it
+        try:
+            line["sharded"] = run_decode_sharded(args, ws, rank, local)
+        except Exception as e:  # noqa: BLE001 -- recorded, not raised
+            line["sharded"] = {"error": f"{type(e).__name__}: {e}"}
     if ws == 1 and not args.no_side_workloads:
         # configs 0 and 1 beside the headline (their own workloads give the
         # full lines, CPU baselines included); a failure here is reported in

@@ -49,6 +49,11 @@ _SIGS = {
                                           C.c_void_p]),
     "cwen_cuda_mtp_step": (C.c_int, [C.c_int, C.c_int, C.c_int, C.c_int]),
     "cwen_cuda_mtp_read": (C.c_int, [C.c_int, C.c_void_p]),
+    "cwen_cuda_shard_config": (C.c_int, [C.c_int, C.c_int]),
+    "cwen_cuda_shard_handle": (C.c_int, [C.c_void_p, C.c_int]),
+    "cwen_cuda_shard_open": (C.c_int, [C.c_void_p, C.c_int]),
+    "cwen_shard_rows": (C.c_int, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p]),
+    "cwen_cuda_shard_rows_for": (C.c_int, [C.c_char_p, C.c_int, C.c_void_p, C.c_void_p]),
     "cwen_cuda_gemvb_host": (C.c_int, [C.c_int, C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_int]),
     "cwen_cuda_gdn_verify": (C.c_int, [C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p,
                                        C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_void_p,

@@ -1,5 +1,6 @@
 // C ABI entry points (include/cwen_cuda.h): engine lifetime and the
 // stand-alone verify GEMV.
+#include <stdlib.h>
 #include <string.h>
 
 #include "engine.cuh"
@@ -7,6 +8,7 @@
 #include "gdn.cuh"
 #include "model.cuh"
 #include "rowops.cuh"
+#include "shard.cuh"
 
 namespace cw {
 
@@ -114,6 +116,7 @@ int gemv_status() {
 }
 
 int alloc_qmat(QMat &m, int type, int K, int n_mt, int M) {
+  m.tc = engine().gs.tc;  // the layout of the engine's GEMV kernel
   m.type = type;
   m.K = K;
   m.n_mt = n_mt;
@@ -156,6 +159,9 @@ int cwen_cuda_init(int device, int ctx, int bmax) {
   CW_CHECK(cudaDeviceGetAttribute(&E.n_sm, cudaDevAttrMultiProcessorCount, device));
   CW_CHECK(cudaStreamCreateWithFlags(&E.stream, cudaStreamNonBlocking));
   GemvScratch &s = E.gs;
+  // the verify-GEMV kernel of this engine: CWEN_GEMV=tcgen05, else mma.sync
+  const char *gk = getenv("CWEN_GEMV");
+  s.tc = gk && !strcmp(gk, "tcgen05");
   s.kmax = 32768;
   s.G = E.n_sm;  // one persistent CTA per SM
   s.max_tiles = 1 << 16;
@@ -183,6 +189,7 @@ void cwen_cuda_shutdown(void) {
   Engine &E = engine();
   if (!E.live) return;
   cudaStreamSynchronize(E.stream);
+  shard_free();
   model_free();
   gdn_verify_free();
   for (auto &m : E.mats) cudaFree(m.w);

@@ -10,6 +10,7 @@
 #include "engine.cuh"
 #include "model.cuh"
 #include "rowops.cuh"
+#include "shard.cuh"
 
 namespace cw {
 
@@ -106,6 +107,18 @@ static int bind_mat(const char *name, int type, const void *host, int ne0, int n
   return upload_qmat_rows(type, host, ne0, ne1, m, rows_off / 16 * stride_mt + mt_phase, stride_mt);
 }
 
+// A row-sharded matrix (the FFN and lm_head under a shard group): the full
+// GGUF shape is checked, this GPU's rows [r0, r1) of it are uploaded.
+static int bind_mat_shard(const char *name, int type, const void *host, int ne0, int ne1, int want0, int want1,
+                          QMat &m, int stride_mt, int mt_phase) {
+  if (ne0 != want0 || ne1 != want1) return shape_err(name, ne0, ne1, want0, want1);
+  int r0, r1;
+  shard_rows(want1, 16, r0, r1);
+  const size_t rb = (size_t)(ne0 / 32) * (type == CWEN_T_Q8_0 ? 34 : 18);
+  return bind_mat(name, type, (const uint8_t *)host + (size_t)r0 * rb, ne0, r1 - r0, want0, r1 - r0, m,
+                  (r1 - r0) * stride_mt, 0, stride_mt, mt_phase);
+}
+
 static int bind_vec(const char *name, int type, const void *host, int ne0, int ne1, int n, float *&dst) {
   if (type != CWEN_T_F32) {
     set_error("cwen_cuda_upload: %s: type %d, need F32", name, type);
@@ -124,9 +137,10 @@ static int upload_layer(int l, const char *suf, int type, const void *host, int 
   uint32_t bit = 0;
   if (!strcmp(suf, "attn_norm.weight")) { rc = bind_vec(name, type, host, ne0, ne1, H, w.attn_norm); bit = LB_ATTN_NORM; }
   else if (!strcmp(suf, "post_attention_norm.weight")) { rc = bind_vec(name, type, host, ne0, ne1, H, w.post_norm); bit = LB_POST_NORM; }
-  else if (!strcmp(suf, "ffn_gate.weight")) { rc = bind_mat(name, type, host, ne0, ne1, H, I, w.gate_up, 2 * I, 0, 2, 0); bit = LB_GATE; }
-  else if (!strcmp(suf, "ffn_up.weight")) { rc = bind_mat(name, type, host, ne0, ne1, H, I, w.gate_up, 2 * I, 0, 2, 1); bit = LB_UP; }
-  else if (!strcmp(suf, "ffn_down.weight")) { rc = bind_mat(name, type, host, ne0, ne1, I, H, w.down, H, 0, 1, 0); bit = LB_DOWN; }
+  // the FFN: this GPU's output rows under a shard group (all of them otherwise)
+  else if (!strcmp(suf, "ffn_gate.weight")) { rc = bind_mat_shard(name, type, host, ne0, ne1, H, I, w.gate_up, 2, 0); bit = LB_GATE; }
+  else if (!strcmp(suf, "ffn_up.weight")) { rc = bind_mat_shard(name, type, host, ne0, ne1, H, I, w.gate_up, 2, 1); bit = LB_UP; }
+  else if (!strcmp(suf, "ffn_down.weight")) { rc = bind_mat_shard(name, type, host, ne0, ne1, I, H, w.down, 1, 0); bit = LB_DOWN; }
   else if (w.linear) {
     const int NVH = d.ssm_n_vh;
     if (!strcmp(suf, "attn_qkv.weight")) { rc = bind_mat(name, type, host, ne0, ne1, H, M.QKV, w.in_proj, M.ps_lin, 0, 1, 0); bit = LB_QKV; }
@@ -263,6 +277,22 @@ static int alloc_state() {
   return CWEN_OK;
 }
 
+// The lm_head GEMV into the logits of rows 0..B-1 (row-sharded under a
+// shard group: every GPU then holds all logits after the barrier).
+static cudaError_t lm_head_gemv(int B, cudaStream_t st) {
+  Model &M = g_model;
+  Engine &E = engine();
+  const int V = M.d.n_vocab;
+  if (!shard().on()) return timed_gemv(M.lm_head, B, M.logits, V, EPI_STORE, st);
+  int r0, r1;
+  shard_rows(V, 16, r0, r1);
+  shard_target(E.gs, M.logits, r0);
+  const cudaError_t e = timed_gemv(M.lm_head, B, M.logits, V, EPI_STORE, st);
+  shard_untarget(E.gs);
+  if (e != cudaSuccess) return e;
+  return shard_barrier(st);
+}
+
 // ---- the forward pass ----
 static int run_layer_block(int l, int B, int pos0, cudaStream_t st) {
   Model &M = g_model;
@@ -300,9 +330,31 @@ static int run_layer_block(int l, int B, int pos0, cudaStream_t st) {
   else CW_CHECK(timed_gemv(w.out_proj, B, M.x, H, EPI_ADD, st, M.attn_o, d.n_head * 256));
   CW_CHECK(launch_norm_prep(M.x, w.post_norm, H, B, E.gs, nullptr, st));
   nl++;
-  CW_CHECK(timed_gemv(w.gate_up, B, M.h, I, EPI_SWIGLU, st));
-  // the SwiGLU rows, raw; the new residual's sums of squares for the next layer's attn_norm
-  CW_CHECK(timed_gemv(w.down, B, M.x, H, EPI_ADD, st, M.h, I, nullptr, l + 1 < d.n_layer));
+  const bool sh = shard().on();
+  int r0, r1;
+  if (sh) {
+    shard_rows(I, 16, r0, r1);
+    shard_target(E.gs, M.h, r0);
+  }
+  cudaError_t ge = timed_gemv(w.gate_up, B, M.h, I, EPI_SWIGLU, st);
+  if (sh) {
+    shard_untarget(E.gs);
+    if (ge == cudaSuccess) ge = shard_barrier(st);
+  }
+  CW_CHECK(ge);
+  // the SwiGLU rows, raw; the new residual's sums of squares for the next
+  // layer's attn_norm (sharded: each GPU sees only its rows, so the next
+  // layer normalises in a row kernel instead)
+  if (sh) {
+    shard_rows(H, 16, r0, r1);
+    shard_target(E.gs, M.x, r0);
+  }
+  ge = timed_gemv(w.down, B, M.x, H, EPI_ADD, st, M.h, I, nullptr, !sh && l + 1 < d.n_layer);
+  if (sh) {
+    shard_untarget(E.gs);
+    if (ge == cudaSuccess) ge = shard_barrier(st);
+  }
+  CW_CHECK(ge);
   if (M.dump_on)
     CW_CHECK(cudaMemcpyAsync(M.dump + (size_t)l * E.bmax * H, M.x, (size_t)B * H * sizeof(float),
                              cudaMemcpyDeviceToDevice, st));
@@ -364,6 +416,10 @@ int forward_block_impl(const int *toks, int B, int nlogits) {
     set_error("cwen_cuda_forward_block: previous block not committed (cwen_cuda_commit)");
     return CWEN_ESTATE;
   }
+  if (shard().configured && !shard().opened) {
+    set_error("cwen_cuda_forward_block: shard group configured but not opened (cwen_cuda_shard_open)");
+    return CWEN_ESTATE;
+  }
   if (B < 1 || B > E.bmax || nlogits < -1 || nlogits > B) {
     set_error("cwen_cuda_forward_block: need 1 <= B <= %d and -1 <= nlogits <= B", E.bmax);
     return CWEN_EINVAL;
@@ -392,7 +448,7 @@ int forward_block_impl(const int *toks, int B, int nlogits) {
   if (nlogits != 0) {
     const int r0 = nlogits == -1 ? B - 1 : 0, nr = nlogits == -1 ? 1 : nlogits;
     CW_CHECK(launch_norm_prep(M.x + (size_t)r0 * d.n_embd, M.output_norm, d.n_embd, nr, E.gs, nullptr, st));
-    CW_CHECK(timed_gemv(M.lm_head, nr, M.logits, d.n_vocab, EPI_STORE, st));
+    CW_CHECK(lm_head_gemv(nr, st));
     // blk = toks of the block: row j's argmax is checked against toks[j+1]
     Toks16 blk;
     memset(&blk, 0, sizeof blk);
@@ -451,6 +507,10 @@ int cwen_cuda_model_config(const cwen_dims *dims) {
               "n_embd and n_ff multiples of 512, value heads a multiple of key heads)");
     return CWEN_EINVAL;
   }
+  if (shard().configured && d.n_ff % (16 * shard().world)) {
+    set_error("cwen_cuda_model_config: n_ff %d is not a multiple of 16 x %d GPUs", d.n_ff, shard().world);
+    return CWEN_EINVAL;
+  }
   M.d = d;
   M.QKV = (2 * d.ssm_n_kh + d.ssm_n_vh) * 128;
   M.Z = d.ssm_n_vh * 128;
@@ -494,7 +554,7 @@ int cwen_cuda_upload(const char *name, int type, const void *host, int ne0, int 
     return CWEN_OK;
   }
   if (!strcmp(name, "output.weight")) {
-    rc = bind_mat(name, type, host, ne0, ne1, d.n_embd, d.n_vocab, M.lm_head, d.n_vocab, 0, 1, 0);
+    rc = bind_mat_shard(name, type, host, ne0, ne1, d.n_embd, d.n_vocab, M.lm_head, 1, 0);
     if (!rc) M.gbound |= GB_OUT;
     return rc;
   }
@@ -542,6 +602,7 @@ int cwen_cuda_model_finalize(void) {
   }
   int rc = alloc_state();
   if (rc) return rc;
+  if ((rc = shard_alloc_local())) return rc;
   CW_CHECK(cudaDeviceSynchronize());
   M.finalized = true;
   return CWEN_OK;
@@ -602,6 +663,7 @@ int cwen_cuda_accept(int *k_out, int *ustar_out, int *argmax_out) {
   }
   rc = gemv_status();
   if (rc) return rc;
+  if ((rc = shard_status())) return rc;
   if (k_out) *k_out = M.h_walk[0];
   if (ustar_out) *ustar_out = M.h_walk[1];
   if (argmax_out) memcpy(argmax_out, M.h_walk + 2, (size_t)M.pending_nlog * sizeof(int));
@@ -786,7 +848,7 @@ int cwen_cuda_mtp_draft(int pend, int *out, int max_d) {
     tk.t[0] = pend;
     rc = mtp_step_dev(pos_n + 1 + t, 1, tk, t ? M.mtp_draft + 3 * (t - 1) + 1 : nullptr, hin, hout, st);
     if (rc) return rc;
-    CW_CHECK(timed_gemv(M.lm_head, 1, M.logits, V, EPI_STORE, st));
+    CW_CHECK(lm_head_gemv(1, st));
     CW_CHECK(launch_argmax_walk(M.logits, V, V, 1, 0, none, M.best, M.mtp_draft + 3 * t, st));
     E.prof.launches += 1;
     hin = hout;

@@ -105,6 +105,7 @@ extern "C" int cwen_cuda_gemvb_static(int wid, const float *dX, int xs, float *d
   const int rc = na_setup(E.device, E.n_sm);
   if (rc) return rc;
   GemvScratch &s = g_na[E.device].s;
+  s.tc = E.gs.tc;  // the engine's kernel (its weights are in that kernel's layout)
   cudaStream_t st = stream ? (cudaStream_t)stream : E.stream;
   // The arrival counters reset themselves at the end of a complete call;
   // clear the ones this call uses in case an earlier call stopped part-way.

@@ -43,44 +43,12 @@
 
 #include "common.cuh"
 #include "qgemv.cuh"
+#include "qgemv_dev.cuh"
 #include "rowops.cuh"
 #include "rowprep.cuh"
 #include "sm100.cuh"
 
 namespace cw {
-
-// ---- nibble / int8 -> f16 (exact) ----
-// Q4: word w = qs bytes [4t..4t+3] of one row's block.  Returns half2s:
-//   s0 = (lo(b0), lo(b2))  t0 = (lo(b1), lo(b3))  s1 = (hi(b0), hi(b2))  t1 = (hi(b1), hi(b3))
-// each value (nibble - 8), via the 0x6400 (=1024.0) exponent trick.
-CW_DEV void q4_to_f16(uint32_t w, uint32_t &s0, uint32_t &t0, uint32_t &s1, uint32_t &t1) {
-  constexpr uint32_t MAGIC = 0x64006400u;
-  constexpr int AND_OR = (0xF0 & 0xCC) | 0xAA;
-  const uint32_t lo0 = lop3<AND_OR>(w, 0x000F000Fu, MAGIC);
-  const uint32_t hi0 = lop3<AND_OR>(w, 0x00F000F0u, MAGIC);
-  const uint32_t w2 = w >> 8;
-  const uint32_t lo1 = lop3<AND_OR>(w2, 0x000F000Fu, MAGIC);
-  const uint32_t hi1 = lop3<AND_OR>(w2, 0x00F000F0u, MAGIC);
-  const half2 k1032 = __halves2half2(__ushort_as_half(0xE408u), __ushort_as_half(0xE408u));  // -1032
-  const half2 k16th = __halves2half2(__ushort_as_half(0x2C00u), __ushort_as_half(0x2C00u));  // 1/16
-  const half2 k72 = __halves2half2(__ushort_as_half(0xD480u), __ushort_as_half(0xD480u));    // -72
-  half2 r;
-  r = __hadd2(*reinterpret_cast<const half2 *>(&lo0), k1032); s0 = *reinterpret_cast<uint32_t *>(&r);
-  r = __hadd2(*reinterpret_cast<const half2 *>(&lo1), k1032); t0 = *reinterpret_cast<uint32_t *>(&r);
-  r = __hfma2(*reinterpret_cast<const half2 *>(&hi0), k16th, k72); s1 = *reinterpret_cast<uint32_t *>(&r);
-  r = __hfma2(*reinterpret_cast<const half2 *>(&hi1), k16th, k72); t1 = *reinterpret_cast<uint32_t *>(&r);
-}
-// Q8: word of 4 int8 (b0..b3) -> (b0, b2), (b1, b3) as half2, exact.
-CW_DEV void q8_to_f16(uint32_t w, uint32_t &s, uint32_t &t) {
-  const uint32_t u = w ^ 0x80808080u;  // int8 -> uint8 + 128
-  uint32_t a, b;
-  asm("prmt.b32 %0, %1, %2, 0x4240;" : "=r"(a) : "r"(u), "r"(0x64646464u));
-  asm("prmt.b32 %0, %1, %2, 0x4341;" : "=r"(b) : "r"(u), "r"(0x64646464u));
-  const half2 k1152 = __halves2half2(__ushort_as_half(0xE480u), __ushort_as_half(0xE480u));  // -1152
-  half2 r;
-  r = __hadd2(*reinterpret_cast<const half2 *>(&a), k1152); s = *reinterpret_cast<uint32_t *>(&r);
-  r = __hadd2(*reinterpret_cast<const half2 *>(&b), k1152); t = *reinterpret_cast<uint32_t *>(&r);
-}
 
 // ---- weight repack: GGUF rows -> row-contiguous blocks per (tile, k-pair) ----
 // One stage = one 512-row tile x one k-pair (two 32-blocks):
@@ -124,6 +92,7 @@ cudaError_t qmat_repack(const QMat &dst, const uint8_t *src, int M, int mt_off, 
   const int src_mt = (M + 15) / 16;
   if (dst.K % 64 || mt_off < 0 || mt_stride < 1 || mt_off + (src_mt - 1) * mt_stride >= dst.n_mt)
     return cudaErrorInvalidValue;
+  if (!dst.tc) return mma::repack(dst, src, M, mt_off, mt_stride, st);
   const long long total = (long long)M * (dst.K / 64);
   const int threads = 256;
   const long long blocks = (total + threads - 1) / threads;
@@ -144,88 +113,6 @@ cudaError_t qmat_repack(const QMat &dst, const uint8_t *src, int M, int mt_off, 
 cudaError_t gemv_prep_x(const float *X, int xs, int B, int K, GemvScratch &s, cudaStream_t st) {
   if (B < 1 || B > QG_MAXB || K % 64 || K > s.kmax) return cudaErrorInvalidValue;
   return launch_row_prep(X, xs, K, B, s, st);
-}
-
-// ---- the GEMV ----
-struct GemvArgs {
-  const uint8_t *w;
-  int n_mt, kp, M;
-  const uint4 *xf;
-  const int *xexp;
-  int B;
-  float *y;
-  int ys, epi;
-  float *ws;
-  int *cnt;
-  int *err;
-  int G;
-  long long units;
-  int cl;  // > 1: the contributors of each split tile form one thread-block cluster of cl CTAs
-  // local-X variant: raw fp32 rows X (column b at xr + b*xrs), turned into
-  // fragments by each CTA for its own k-range with its own column exponents
-  const float *xr;
-  int xrs;
-  const float *xw;     // != nullptr: X = RMSNorm(xr) * xw (run.c:346), scale from st_in
-  const float *st_in;  // sums of squares of the rows, [st_g][16] per-CTA partials of the GEMV that wrote them
-  int st_g;
-  float *st_out;       // != nullptr: this GEMV's per-CTA sums of squares of its output rows [G][16]
-};
-
-CW_DEV float silu_f(float x) { return x * (1.f / (1.f + expf(-x))); }
-
-// Thread-block cluster barrier (every thread of every CTA of the cluster),
-// release / acquire at cluster scope.
-CW_DEV void cluster_sync_all() {
-  asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
-}
-
-// Power-of-two unscale of column col: the global exponent of prepared
-// fragments, or (local-X variant) 1 for partials already unscaled by the CTA
-// that computed them.
-CW_DEV float split_unscale(const GemvArgs &a, int col) {
-  return a.xr ? 1.f : __int_as_float((127 - __ldg(a.xexp + col)) << 23);
-}
-
-// Epilogue of a reduced split-tile share: lane (mt, row) holds row `row` of
-// m-tile mt0 + mt, four columns per float4 (NC4 of them).  The whole warp
-// calls it (the SwiGLU pairs gate and up rows across the warp's halves).
-template <int NC4>
-CW_DEV void split_epilogue(const GemvArgs &a, int mt0, int mt, int row, bool live, const float4 (&sum)[NC4],
-                           float *wst) {
-#pragma unroll
-  for (int n = 0; n < NC4; n++) {
-    const float e4[4] = {sum[n].x, sum[n].y, sum[n].z, sum[n].w};
-#pragma unroll
-    for (int j = 0; j < 4; j++) {
-      const int col = n * 4 + j;
-      if (col >= a.B) continue;
-      if (a.st_out && a.epi == EPI_ADD) {  // sums of squares of the new rows (warp order, then CTA order)
-        float v2 = 0.f;
-        const int grow = (mt0 + mt) * 16 + row;
-        if (live && grow < a.M) {
-          const float v = a.y[(size_t)col * a.ys + grow] + e4[j] * split_unscale(a, col);
-          v2 = v * v;
-        }
-        v2 = warp_sum(v2);
-        if ((threadIdx.x & 31) == 0) wst[col] += v2;
-      }
-      const float sc = split_unscale(a, col);
-      if (a.epi == EPI_SWIGLU) {
-        const float up = __shfl_down_sync(0xffffffffu, e4[j], 16);
-        if (live && mt == 0) {
-          const int orow = (mt0 >> 1) * 16 + row;
-          if (orow * 2 < a.M) a.y[(size_t)col * a.ys + orow] = silu_f(e4[j] * sc) * (up * sc);
-        }
-      } else if (live) {
-        const int grow = (mt0 + mt) * 16 + row;
-        if (grow < a.M) {
-          float *p = a.y + (size_t)col * a.ys + grow;
-          if (a.epi == EPI_ADD) *p += e4[j] * sc;
-          else *p = e4[j] * sc;
-        }
-      }
-    }
-  }
 }
 
 // Tensor-memory plan of a CTA (512 columns): per row group rg (128 rows,
@@ -677,7 +564,7 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemv_kernel(GemvArgs a) {
             if (col < a.B && lane < 16) {
               const float sc = xun ? xun[col] : __int_as_float((127 - __ldg(a.xexp + col)) << 23);
               const int row = (mt0 >> 1) * 16 + lane;
-              if (row * 2 < a.M) a.y[(size_t)col * a.ys + row] = silu_f(acc[col] * sc) * (up * sc);
+              if (row * 2 < a.M) y_put(a, y_off(a, col, row), silu_f(acc[col] * sc) * (up * sc));
             }
           }
         } else {
@@ -686,9 +573,7 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemv_kernel(GemvArgs a) {
           for (int col = 0; col < NC; col++) {
             if (col >= a.B || row >= a.M) continue;
             const float sc = xun ? xun[col] : __int_as_float((127 - __ldg(a.xexp + col)) << 23);
-            float *p = a.y + (size_t)col * a.ys + row;
-            if (a.epi == EPI_ADD) *p += acc[col] * sc;
-            else *p = acc[col] * sc;
+            y_out(a, col, row, acc[col] * sc);
           }
         }
       }
@@ -727,6 +612,7 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemv_kernel(GemvArgs a) {
   // the tensor memory is no longer read by this warp
   tc_fence_before();
   named_bar(2, (QG_CONS_WARPS + 4) * 32);
+  y_fence(a);  // full tiles' peer stores
 
   if (np == 0) {
     if (a.cl > 1) {
@@ -779,6 +665,7 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemv_kernel(GemvArgs a) {
       }
       split_epilogue<NC4>(a, mt0, mt, row, live, sum, wst);
     }
+    y_fence(a);
     cluster_sync_all();  // no CTA leaves while another reads its shared memory
     if (XL && a.st_out && threadIdx.x < QG_STAT_COLS) {  // this CTA's slot: the warps' sums in warp order
       const float *w0 = xun + 16;
@@ -858,6 +745,7 @@ __global__ void __launch_bounds__(QG_THREADS, 1) qgemv_kernel(GemvArgs a) {
       if (atomicAdd(a.cnt + tile, 1) == 2 * ncon - 1) a.cnt[tile] = 0;
     }
   }
+  y_fence(a);
   if (XL && a.st_out && threadIdx.x < QG_STAT_COLS) {  // this CTA's slot: the warps' sums in warp order
     const float *w0 = xun + 16;
     float ss = 0.f;
@@ -955,7 +843,7 @@ static bool gemv_all_split(const QMat &m, const GemvScratch &s) {
 
 static cudaError_t gemv_launch(const QMat &m, int B, float *Y, int ys, int epi, GemvScratch &s, cudaStream_t st,
                                const float *xr, int xrs, const float *norm_w = nullptr, bool want_stats = false) {
-  if (B < 1 || B > QG_MAXB || m.K % 64 || m.K > s.kmax || !m.w || !s.err) return cudaErrorInvalidValue;
+  if (B < 1 || B > QG_MAXB || m.K % 64 || m.K > s.kmax || !m.w || !s.err || m.tc != s.tc) return cudaErrorInvalidValue;
   if (epi == EPI_SWIGLU && (m.n_mt % 2)) return cudaErrorInvalidValue;
   GemvArgs a;
   a.w = m.w;
@@ -983,6 +871,9 @@ static cudaError_t gemv_launch(const QMat &m, int B, float *Y, int ys, int epi, 
     a.st_g = s.stat_g;
   }
   if (xr && want_stats) a.st_out = s.stat_next;
+  a.row0 = s.row0;
+  a.np = s.np;
+  for (int i = 0; i < QG_MAX_PEERS; i++) a.yp[i] = i < s.np ? s.yp[i] : nullptr;
   int n_tiles;
   const long long g = gemv_grid(m, s, n_tiles, a.units);
   if (n_tiles > s.max_tiles) return cudaErrorInvalidValue;
@@ -996,7 +887,8 @@ static cudaError_t gemv_launch(const QMat &m, int B, float *Y, int ys, int epi, 
   s.stat_ok = false;  // statistics describe the output of the GEMV right before
   if (xr) {
     cudaError_t e;
-    switch (nc) {
+    if (!s.tc) e = mma::launch(a, m.type, true, st);
+    else switch (nc) {
       case 1: e = launch_t<2, 1, true>(a, st); break;
       case 8: e = launch_t<2, 8, true>(a, st); break;
       default: e = launch_t<2, 16, true>(a, st); break;
@@ -1012,6 +904,7 @@ static cudaError_t gemv_launch(const QMat &m, int B, float *Y, int ys, int epi, 
     }
     return e;
   }
+  if (!s.tc) return mma::launch(a, m.type, false, st);
   switch (nc * 16 + m.type) {
     case 16 + 8: return launch_t<8, 1, false>(a, st);
     case 128 + 8: return launch_t<8, 8, false>(a, st);
@@ -1057,6 +950,7 @@ cudaError_t gemv_run_xn(const QMat &m, const float *X, int xs, const float *w, i
 // One-time kernel attributes (called at engine set-up).
 cudaError_t qgemv_configure() {
   cudaError_t e;
+  if ((e = mma::configure()) != cudaSuccess) return e;
   if ((e = carveout_max(repack_kernel<2>)) != cudaSuccess) return e;
   if ((e = carveout_max(repack_kernel<8>)) != cudaSuccess) return e;
   if ((e = carveout_max(qgemv_kernel<2, 1, false>)) != cudaSuccess) return e;

@@ -11,12 +11,15 @@
 namespace cw {
 
 // Device layout of one (possibly fused) weight matrix: rows grouped in
-// 16-row m-tiles, m-tiles in 512-row tiles of 32; per (tile, pair of
-// 32-blocks) one contiguous stage [block 0: 512 rows x quant bytes | block 1 |
-// f16 scales [2][512]] (QgStage), stages stored [tile][k-pair].  The m-tile
-// count is padded to whole tiles (zero padding).
+// 16-row m-tiles, m-tiles in 512-row tiles of 32, one contiguous stage per
+// (tile, pair of 32-blocks), stages stored [tile][k-pair].  Inside a stage:
+// tcgen05 kernel [block 0: 512 rows x quant bytes | block 1 | f16 scales
+// [2][512]] (QgStage); mma.sync kernel [m-tile][576-byte chunk in A-fragment
+// order] (qgemv_mma.cu).  Same stage size either way.  The m-tile count is
+// padded to whole tiles (zero padding).
 struct QMat {
   uint8_t *w = nullptr;  // device
+  bool tc = false;       // layout of the tcgen05 kernel (else of the mma.sync kernel)
   int type = 0;          // 2 = Q4_0, 8 = Q8_0
   int K = 0;             // row length
   int n_mt = 0;          // m-tiles (16 rows) holding rows; storage is padded to QG_TILE_MT
@@ -41,6 +44,7 @@ struct QgStage {
 constexpr int WS_TILE_FLOATS = QG_TILE_MT * 16 * 16;   // split-K partials of one tile (16 columns)
 constexpr int QG_XL_KP = 20;  // local-X variant: at most this many k-pairs per CTA
 constexpr int QG_STAT_COLS = 16;  // per-CTA statistics slot: one float per column
+constexpr int QG_MAX_PEERS = 8;   // GPUs of a row-shard group
 
 inline size_t qmat_stage_bytes(int type) { return type == 8 ? QgStage<8>::WB : QgStage<2>::WB; }
 inline size_t qmat_bytes(int type, int K, int n_mt) {
@@ -50,6 +54,10 @@ inline size_t qmat_bytes(int type, int K, int n_mt) {
 
 // Scratch the GEMV needs (owned by the caller, reused across calls on one stream).
 struct GemvScratch {
+  // Which kernel the engine runs (chosen once, before any weight upload, so
+  // every batch size of an engine takes the same arithmetic): the tcgen05
+  // kernel of qgemv.cu, or the mma.sync kernel of qgemv_mma.cu (default).
+  bool tc = false;
   uint4 *xf = nullptr;   // X operands, >= (Kmax/32) * 128 uint4 (2 KB per 32-block)
   int *xexp = nullptr;   // [16] per-column exponents
   float *ws = nullptr;   // split-K partials [G][2][WS_TILE_FLOATS]
@@ -65,6 +73,11 @@ struct GemvScratch {
   bool stat_ok = false;  // stat describes the output (stat_y, stat_ys) of the GEMV right before
   int stat_g = 0, stat_len = 0, stat_cols = 0, stat_ys = 0;
   const float *stat_y = nullptr;
+  // Row sharding of the next GEMV launch (set by the caller around it): the
+  // output is rows row0.. of the full matrix, stored into np copies of Y
+  // (yp[i] is GPU i's copy of the buffer passed as Y); np = 0: not sharded.
+  int np = 0, row0 = 0;
+  float *yp[QG_MAX_PEERS] = {};
 };
 size_t gemv_scratch_ws_floats(int G);
 

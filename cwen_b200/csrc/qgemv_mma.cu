@@ -1,0 +1,738 @@
+// Batched Q4_0 / Q8_0 verify GEMV on warp-level tensor-core MMAs
+// (mma.sync m16n8k16), the engine's default kernel; the same arithmetic and
+// work split as the tcgen05 kernel of qgemv.cu, with its own weight layout.
+//
+// Replaces the reference's gemvb()/gemv() (run.c:1577-1680, 1419-1527) and
+// the row dots under them (dot_q4_0 run.c:1009-1025, dot_nib16 run.c:432,
+// dot_q8_0 run.c:1248-1274).
+//
+// Arithmetic.  Per 16 rows x 32 weights x 8 columns four m16n8k16 MMAs (the
+// f16 hi and lo parts of X, both k halves) accumulate one fp32 block partial
+// (products exact, fp32 accumulate in the MMA); one FFMA per element applies
+// the block's f16 scale: acc = fma(d, c, acc).  (q - 8) is exact in f16.
+//
+// Weight layout.  Rows in 16-row m-tiles, m-tiles in 512-row tiles of 32; per
+// (m-tile, pair of 32-blocks) one 576-byte chunk [512 B nibbles in mma
+// A-fragment order | 64 B f16 scales] (Q8_0: 1088 B [1024 B int8 | 64 B
+// scales]), stored [tile][k-pair][m-tile] so that one (tile, k-pair) is one
+// contiguous 18 KB / 34 KB stage -- the same stage size as the tcgen05 layout.
+//
+// X operands.  Per (32-block, n-tile of 8 columns) 64 uint4: 32 lanes of hi
+// parts then 32 of lo parts; lane (g, t) holds column g's
+//   (x[4t], x[4t+2]) (x[4t+1], x[4t+3]) (x[4t+16], x[4t+18]) (x[4t+17], x[4t+19]).
+//
+// Work split, pipeline and the split-tile reduction: as in qgemv.cu (bulk-copy
+// ring with two producer threads, 16 consumer warps with two m-tiles each,
+// stream-K over (tile, k-pair) units, cluster or global split-K reduction).
+#include <utility>
+
+#include "common.cuh"
+#include "qgemv.cuh"
+#include "qgemv_dev.cuh"
+#include "rowprep.cuh"
+#include "sm100.cuh"
+
+namespace cw {
+namespace mma {
+
+constexpr int QGM_THREADS = (QG_CONS_WARPS + 2) * 32;  // 16 consumer warps + two producer warps
+
+// ---- weight repack: GGUF rows -> fragment-ordered chunks ----
+// One thread per (m-tile, k-pair, lane); each writes its lane's qs bytes and
+// lanes 0..7 also the scale words of row pair (g, g+8).
+template <int TYPE>
+__global__ void repack_kernel(uint8_t *dst, int dst_kp, const uint8_t *src, int M, int K, int mt_off,
+                              int mt_stride) {
+  const int nb = K / 32, kp = K / 64;
+  const int src_mt = (M + 15) / 16;
+  const long long total = (long long)src_mt * kp * 32;
+  for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < total;
+       idx += (long long)gridDim.x * blockDim.x) {
+    const int lane = (int)(idx % 32);
+    const int p = (int)((idx / 32) % kp);
+    const int smt = (int)(idx / 32 / kp);
+    const int g = lane >> 2, t = lane & 3;
+    const int dmt = mt_off + smt * mt_stride;
+    const size_t chunk = (size_t)(TYPE == 8 ? 1088 : 576);
+    // [tile][k-pair][m-tile within tile]: one (tile, k-pair) is contiguous
+    uint8_t *c = dst + (((size_t)(dmt / QG_TILE_MT) * dst_kp + p) * QG_TILE_MT + dmt % QG_TILE_MT) * chunk;
+    const int r0 = smt * 16 + g, r1 = r0 + 8;
+    uint32_t words[8];
+    uint16_t sc[4];
+    for (int kbi = 0; kbi < 2; kbi++) {
+      const int kb = 2 * p + kbi;
+      for (int ri = 0; ri < 2; ri++) {
+        const int r = ri ? r1 : r0;
+        uint16_t d = 0;
+        uint32_t wa = 0, wb = 0;
+        if (r < M) {
+          if (TYPE == 8) {
+            const uint8_t *blk = src + ((size_t)r * nb + kb) * 34;
+            d = (uint16_t)(blk[0] | (blk[1] << 8));
+            const uint8_t *q = blk + 2;
+            wa = q[4 * t] | (q[4 * t + 1] << 8) | (q[4 * t + 2] << 16) | ((uint32_t)q[4 * t + 3] << 24);
+            wb = q[16 + 4 * t] | (q[16 + 4 * t + 1] << 8) | (q[16 + 4 * t + 2] << 16) |
+                 ((uint32_t)q[16 + 4 * t + 3] << 24);
+          } else {
+            const uint8_t *blk = src + ((size_t)r * nb + kb) * 18;
+            d = (uint16_t)(blk[0] | (blk[1] << 8));
+            const uint8_t *q = blk + 2;
+            wa = q[4 * t] | (q[4 * t + 1] << 8) | (q[4 * t + 2] << 16) | ((uint32_t)q[4 * t + 3] << 24);
+          }
+        }
+        if (TYPE == 8) {
+          words[kbi * 4 + ri * 2 + 0] = wa;
+          words[kbi * 4 + ri * 2 + 1] = wb;
+        } else {
+          words[kbi * 2 + ri] = wa;
+        }
+        sc[kbi * 2 + ri] = d;
+      }
+    }
+    if (TYPE == 8) {
+      uint4 *o = reinterpret_cast<uint4 *>(c + lane * 32);
+      o[0] = make_uint4(words[0], words[1], words[2], words[3]);
+      o[1] = make_uint4(words[4], words[5], words[6], words[7]);
+    } else {
+      *reinterpret_cast<uint4 *>(c + lane * 16) = make_uint4(words[0], words[1], words[2], words[3]);
+    }
+    if (t == 0) {
+      const size_t qbytes = TYPE == 8 ? 1024 : 512;
+      uint2 s;
+      s.x = (uint32_t)sc[0] | ((uint32_t)sc[1] << 16);  // kb0: (d_g, d_g8)
+      s.y = (uint32_t)sc[2] | ((uint32_t)sc[3] << 16);  // kb1
+      *reinterpret_cast<uint2 *>(c + qbytes + g * 8) = s;
+    }
+  }
+}
+
+cudaError_t repack(const QMat &dst, const uint8_t *src, int M, int mt_off, int mt_stride, cudaStream_t st) {
+  const int src_mt = (M + 15) / 16;
+  if (dst.K % 64 || mt_off < 0 || mt_stride < 1 || mt_off + (src_mt - 1) * mt_stride >= dst.n_mt)
+    return cudaErrorInvalidValue;
+  const long long total = (long long)src_mt * (dst.K / 64) * 32;
+  const int threads = 256;
+  const long long blocks = (total + threads - 1) / threads;
+  const int grid = (int)(blocks < 65535 ? blocks : 65535);
+  if (dst.type == 8)
+    repack_kernel<8><<<grid, threads, 0, st>>>(dst.w, dst.K / 64, src, M, dst.K, mt_off, mt_stride);
+  else
+    repack_kernel<2><<<grid, threads, 0, st>>>(dst.w, dst.K / 64, src, M, dst.K, mt_off, mt_stride);
+  return cudaGetLastError();
+}
+
+// Apply the epilogue for one warp's accumulators (rows of m-tiles mt0,
+// mt0+1).  Lane (g, t) holds, per n-tile n, rows g and g+8 of columns
+// n*8 + 2t and n*8 + 2t + 1.
+template <int NT>
+CW_DEV void gemv_epilogue(const GemvArgs &a, int mt0, bool has1, const float (&acc)[2][NT][4], int g, int t,
+                          const float *xun) {
+#pragma unroll
+  for (int n = 0; n < NT; n++) {
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      const int col = n * 8 + 2 * t + (i & 1);
+      if (col >= a.B) continue;
+      const float sc = xun ? xun[col] : __int_as_float((127 - __ldg(a.xexp + col)) << 23);
+      const int rr = g + ((i >> 1) << 3);
+      if (a.epi == EPI_SWIGLU) {
+        const int row = (mt0 >> 1) * 16 + rr;
+        if (row * 2 < a.M) {
+          const float gt = acc[0][n][i] * sc, up = acc[1][n][i] * sc;
+          y_put(a, y_off(a, col, row), silu_f(gt) * up);
+        }
+      } else {
+#pragma unroll
+        for (int mt = 0; mt < 2; mt++) {
+          if (mt == 1 && !has1) continue;
+          const int row = (mt0 + mt) * 16 + rr;
+          if (row >= a.M) continue;
+          y_out(a, col, row, acc[mt][n][i] * sc);
+        }
+      }
+    }
+  }
+}
+
+// Shared-memory layout of the GEMV.  X fragments per (32-block, n-tile of 8
+// columns): 64 uint4 (32 lanes of hi parts, then 32 of lo parts) = 1 KB, so
+// one k-pair of NT n-tiles is NT * 2 KB.
+template <int TYPE, int NT, bool XL = false>
+struct QgLayout {
+  static constexpr int CHUNK = TYPE == 8 ? 1088 : 576;       // one m-tile x one k-pair
+  static constexpr int QB = TYPE == 8 ? 1024 : 512;          // its quant bytes (scales follow)
+  static constexpr int WB = QG_TILE_MT * CHUNK;              // weights of one (tile, k-pair)
+  static constexpr int XKP = NT * 2048;                      // X fragments of one k-pair
+  static constexpr int XB = XL ? 0 : XKP;                    // ... streamed with each stage
+  static constexpr int STAGE = WB + XB;
+  static constexpr int STAGES = TYPE == 8 ? 5 : 8;
+  static constexpr int BAR_OFF = STAGES * STAGE;
+  // local-X variant: the CTA's k-range of X fragments, resident (<= QG_XL_KP k-pairs)
+  static constexpr int XL_OFF = BAR_OFF + 256;
+  static constexpr int XL_BYTES = XL ? QG_XL_KP * XKP : 0;
+  // per column: 2^-e [16] floats, the warps' output sums of squares [16][16],
+  // the prologue's per-warp column maxima [16]
+  static constexpr int XE_OFF = XL_OFF + XL_BYTES;
+  static constexpr int SMEM = XE_OFF + (XL ? 64 + 16 * 16 * 4 + 16 * 4 : 0);
+  static_assert(WB % 16 == 0 && XB % 16 == 0 && STAGE % 16 == 0, "bulk copies need 16-byte multiples");
+  static_assert(SMEM <= 227 * 1024, "shared memory");
+};
+
+// Local X (run by the 16 consumer warps once, after pdl_wait): the CTA's
+// k-range [64*ka0, 64*(ka0+nkp)) of every column of the raw rows X becomes
+// f16 hi/lo fragments in shared memory, scaled by the CTA's own power of two
+// 2^e (max |x| over the range in [2^14, 2^15)); xun[col] = 2^-e unscales the
+// CTA's results.  The fragments hold the same values and layout gemv_prep_x
+// emits, except for the exponent's range.  Every warp works: a column gets
+// 16 / B warps (at least one), each lane loads 8 values per item (item =
+// 32-block x lane quad t), keeps them in registers while the column maxima
+// are combined through shared memory (one barrier), then converts them.
+template <int NT>
+CW_DEV void x_local_prologue(const GemvArgs &a, uint4 *xl, float *xun, float *cmax, int ka0, int nkp) {
+  constexpr int NTH = QG_CONS_WARPS * 32;
+  constexpr int MAXI = QG_XL_KP * 2 * 4 / 32;  // items per lane with one warp per column
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int nitems = 2 * nkp * 4;
+  const int wpc = a.B >= QG_CONS_WARPS ? 1 : QG_CONS_WARPS / a.B;  // warps per column
+  const int b = w / wpc, sub = w - b * wpc;
+  const bool live = b < a.B;
+  float4 v[MAXI][2];
+  float m = 0.f, ss = 0.f;
+  if (live) {
+    const float *x = a.xr + (size_t)b * a.xrs + (size_t)ka0 * 64;
+    const float *wn = a.xw ? a.xw + (size_t)ka0 * 64 : nullptr;
+    // RMSNorm: the row's sum of squares from the per-CTA partials of the GEMV
+    // that wrote it, in slot order then a fixed xor tree (every CTA, every B)
+    if (a.xw)
+#pragma unroll
+      for (int i = 0; i < 5; i++)
+        if (lane + 32 * i < a.st_g) ss += __ldcg(a.st_in + (size_t)(lane + 32 * i) * QG_STAT_COLS + b);
+#pragma unroll
+    for (int j = 0; j < MAXI; j++) {
+      const int it = (sub + j * wpc) * 32 + lane;
+      if (it < nitems) {
+        const int kb = it >> 2, t = it & 3;
+        float4 p = __ldg(reinterpret_cast<const float4 *>(x + kb * 32 + 4 * t));
+        float4 q = __ldg(reinterpret_cast<const float4 *>(x + kb * 32 + 16 + 4 * t));
+        if (a.xw) {
+          const float4 wp = __ldg(reinterpret_cast<const float4 *>(wn + kb * 32 + 4 * t));
+          const float4 wq = __ldg(reinterpret_cast<const float4 *>(wn + kb * 32 + 16 + 4 * t));
+          p = make_float4(wp.x * p.x, wp.y * p.y, wp.z * p.z, wp.w * p.w);
+          q = make_float4(wq.x * q.x, wq.y * q.y, wq.z * q.z, wq.w * q.w);
+        }
+        v[j][0] = p;
+        v[j][1] = q;
+        m = fmaxf(m, fmaxf(fmaxf(fabsf(p.x), fabsf(p.y)), fmaxf(fabsf(p.z), fabsf(p.w))));
+        m = fmaxf(m, fmaxf(fmaxf(fabsf(q.x), fabsf(q.y)), fmaxf(fabsf(q.z), fabsf(q.w))));
+      }
+    }
+    m = warp_max(m);
+    if (lane == 0) cmax[w] = m;
+  }
+  named_bar(1, NTH);
+  if (live) {
+    m = 0.f;
+    for (int i = 0; i < wpc; i++) m = fmaxf(m, cmax[b * wpc + i]);
+    float s = 1.f;
+    if (a.xw) {
+      s = 1.f / sqrtf(warp_sum(ss) / (float)(a.kp * 64) + 1e-6f);
+      m *= s;  // max |(w x) s| = max |w x| * s: s > 0 and rounding is monotonic
+    }
+    const int e = xfrag_exponent(m);
+    // ((w x) s) 2^e == (w x) (s 2^e) exactly: 2^e only shifts the exponent
+    const float sc = s * __int_as_float((127 + e) << 23);
+    if (sub == 0 && lane == 0) xun[b] = __int_as_float((127 - e) << 23);
+    uint4 *ob = xl + (b >> 3) * 64 + (b & 7) * 4;
+#pragma unroll
+    for (int j = 0; j < MAXI; j++) {
+      const int it = (sub + j * wpc) * 32 + lane;
+      if (it < nitems) {
+        const int kb = it >> 2, t = it & 3;
+        // B operand lane (col & 7, t): (x[4t], x[4t+2]) (x[4t+1], x[4t+3]) (x[4t+16], x[4t+18]) (x[4t+17], x[4t+19])
+        const float r[8] = {v[j][0].x, v[j][0].z, v[j][0].y, v[j][0].w, v[j][1].x, v[j][1].z, v[j][1].y, v[j][1].w};
+        uint32_t hw[4], lw[4];
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+          const float v0 = r[2 * i] * sc, v1 = r[2 * i + 1] * sc;
+          const half h0 = __float2half_rn(v0), h1 = __float2half_rn(v1);
+          const half l0 = __float2half_rn(v0 - __half2float(h0)), l1 = __float2half_rn(v1 - __half2float(h1));
+          hw[i] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
+          lw[i] = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
+        }
+        uint4 *o = ob + (size_t)kb * NT * 64 + t;
+        o[0] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+        o[32] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+      }
+    }
+  }
+  if (threadIdx.x >= a.B && threadIdx.x < 16) xun[threadIdx.x] = 1.f;  // padding column
+  named_bar(1, NTH);
+}
+
+// Persistent stream-K GEMV: warps 0..15 consume (warp w owns m-tiles 2w, 2w+1
+// of the current 512-row tile); lane 0 of warp 16 streams the weights and
+// lane 0 of warp 17 the X fragments.
+//
+// Per m-tile, 32-block and n-tile of 8 columns, four m16n8k16 MMAs chain into
+// one fp32 result c: (k 0..15, hi), (k 0..15, lo), (k 16..31, hi),
+// (k 16..31, lo) -- the f16 hi and lo parts of X are two B operands, so c
+// holds the block dot of 8 whole columns and one FFMA per element applies the
+// block's scale: acc = fma(d, c, acc).
+template <int TYPE, int NT, bool XL>
+__global__ void __launch_bounds__(QGM_THREADS, 1) qgemv_kernel(GemvArgs a) {
+  using Lay = QgLayout<TYPE, NT, XL>;
+  constexpr int S = Lay::STAGES;
+  constexpr int NC4 = 2 * NT;  // float4 column groups of a split-tile row
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + Lay::BAR_OFF);
+  uint64_t *empty = full + S;
+  uint64_t *xready = empty + S;  // local X: the prologue's fragments are in shared memory
+  volatile int *abort_p = reinterpret_cast<volatile int *>(xready + 1);
+  int *last_p = const_cast<int *>(abort_p) + 1;  // [2]
+
+  const int c = blockIdx.x;
+  const long long u_begin = (long long)c * a.units / a.G, u_end = (long long)(c + 1) * a.units / a.G;
+  if (u_begin >= u_end) return;  // whole CTA, before any barrier
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  pdl_trigger();
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S; i++) {
+      mbar_init(&full[i], XL ? 1 : 2);  // the weight and the X producer
+      mbar_init(&empty[i], QG_CONS_WARPS);
+    }
+    mbar_init(xready, 1);
+    *abort_p = 0;
+    mbar_fence_init();
+  }
+  __syncthreads();
+
+  if (warp >= QG_CONS_WARPS) {
+    // ---------------- producers ----------------
+    // Two producer threads in two warps, one for the weights and one for X:
+    // a bulk copy occupies its issuing thread for ~0.3 us whatever its size,
+    // so one thread issuing both copies of a stage would cap the stream.
+    // Consecutive units are consecutive (tile, k-pair) blocks of the repacked
+    // weights, so the weight source just advances; no divisions in the loops.
+    if (lane == 0 && (!XL || warp == QG_CONS_WARPS)) {  // local X: no X copies
+      const bool wprod = warp == QG_CONS_WARPS;
+      const int n = (int)(u_end - u_begin);
+      const uint8_t *wsrc = a.w + (size_t)u_begin * Lay::WB;
+      const uint8_t *xbase = reinterpret_cast<const uint8_t *>(a.xf);
+      // Weights are not written by any kernel of the decode step: the weight
+      // producer never waits for the previous kernel (PDL), so the ring fills
+      // while that kernel finishes.  X is that kernel's output.
+      if (!wprod) pdl_wait();
+      int k = (int)(u_begin % a.kp);
+      int st = 0;
+      uint32_t ph = 0;
+      int issued = 0;
+      bool ok = true;
+      for (; issued < n; issued++) {
+        if (!mbar_wait(&empty[st], ph ^ 1, abort_p)) {
+          ok = false;
+          break;
+        }
+        if (*abort_p) break;  // consumers gave up: issue nothing more
+        // Local X: two weight stages go ahead, the rest after the prologue has
+        // read X -- its loads would otherwise queue behind a full ring of weights.
+        if (XL && wprod && issued == 2 && !mbar_wait(xready, 0, abort_p)) {
+          ok = false;
+          break;
+        }
+        uint8_t *dst = smem + st * Lay::STAGE;
+        if (wprod) {
+          mbar_expect_tx(&full[st], Lay::WB);
+          bulk_g2s(dst, wsrc, Lay::WB, &full[st]);
+          wsrc += Lay::WB;
+        } else {
+          mbar_expect_tx(&full[st], Lay::XB);
+          bulk_g2s(dst + Lay::WB, xbase + (size_t)k * Lay::XB, Lay::XB, &full[st]);
+          if (++k == a.kp) k = 0;
+        }
+        if (++st == S) {
+          st = 0;
+          ph ^= 1;
+        }
+      }
+      if (!ok) {
+        atomicExch(a.err, 1);
+        *abort_p = 1;
+      }
+      // never leave bulk copies in flight: wait (bounded, one deadline) for
+      // the last stages issued
+      const long long t0 = cycles_now();
+      for (int i = issued > S ? issued - S : 0; i < issued; i++) {
+        while (!mbar_try_wait(&full[i % S], (uint32_t)((i / S) & 1)) && !spin_expired(t0)) {
+        }
+      }
+    }
+    if (a.cl > 1) {  // the two cluster barriers of the split-tile reduction
+      cluster_sync_all();
+      cluster_sync_all();
+    }
+    return;  // the producers take part in no later CTA barrier
+  }
+
+  // ---------------- consumers ----------------
+  pdl_wait();  // before touching Y, the split-K partials or the tile counters
+  const int g = lane >> 2, t = lane & 3;
+  const int ka0 = (int)(u_begin % a.kp);  // local X: the CTA's one segment starts here
+  float *xun = XL ? reinterpret_cast<float *>(smem + Lay::XE_OFF) : nullptr;
+  float *wst = XL ? xun + 16 + warp * 16 : nullptr;  // this warp's output sums of squares per column
+  if (XL && a.st_out && lane < 16) wst[lane] = 0.f;
+  if (XL) {
+    x_local_prologue<NT>(a, reinterpret_cast<uint4 *>(smem + Lay::XL_OFF), xun, xun + 16 + 16 * 16, ka0,
+                         (int)(u_end - u_begin));
+    if (threadIdx.x == 0) mbar_arrive(xready);
+  }
+  const float zero4[4] = {0.f, 0.f, 0.f, 0.f};
+  bool ok = true;
+  int st = 0;        // ring position, advanced identically by every consumer warp and the producer
+  uint32_t ph = 0;   // its phase parity
+  long long u = u_begin;
+  bool first_seg = true;
+  int ptile[2];  // split tiles of this CTA (its first and last segments), uniform across the CTA
+  int np = 0;
+  while (u < u_end) {
+    const int tile = (int)(u / a.kp);
+    const int ka = (int)(u % a.kp);
+    const long long remain = u_end - u;
+    const int kb_end = (int)((long long)(a.kp - ka) < remain ? a.kp : ka + remain);
+    const int nk = kb_end - ka;
+    const int mt0 = tile * QG_TILE_MT + warp * 2;
+    const bool has0 = mt0 < a.n_mt, has1 = mt0 + 1 < a.n_mt;
+
+    float acc[2][NT][4];
+#pragma unroll
+    for (int mt = 0; mt < 2; mt++)
+#pragma unroll
+      for (int n = 0; n < NT; n++)
+#pragma unroll
+        for (int i = 0; i < 4; i++) acc[mt][n][i] = 0.f;
+
+    for (int i = 0; i < nk; i++) {
+      if (ok && !mbar_wait(&full[st], ph, abort_p)) {
+        ok = false;
+        atomicExch(a.err, 2);
+        *abort_p = 1;
+      }
+      if (ok && has0) {
+        const uint8_t *stg = smem + st * Lay::STAGE;
+        const uint4 *xs = XL ? reinterpret_cast<const uint4 *>(smem + Lay::XL_OFF) + (size_t)(ka + i - ka0) * (NT * 128)
+                             : reinterpret_cast<const uint4 *>(stg + Lay::WB);
+        const uint8_t *ch0 = stg + (warp * 2) * Lay::CHUNK;
+        // both m-tiles' quant words and scales first (independent shared loads)
+        uint4 qw[2][TYPE == 8 ? 2 : 1];
+        uint2 scw[2];
+#pragma unroll
+        for (int mt = 0; mt < 2; mt++) {
+          const uint8_t *ch = ch0 + mt * Lay::CHUNK;
+          if (mt == 1 && !has1) {
+            scw[1] = make_uint2(0u, 0u);
+#pragma unroll
+            for (int h = 0; h < (TYPE == 8 ? 2 : 1); h++) qw[1][h] = make_uint4(0u, 0u, 0u, 0u);
+            continue;
+          }
+          if (TYPE == 8) {
+            qw[mt][0] = *reinterpret_cast<const uint4 *>(ch + lane * 32);
+            qw[mt][1] = *reinterpret_cast<const uint4 *>(ch + lane * 32 + 16);
+          } else {
+            qw[mt][0] = *reinterpret_cast<const uint4 *>(ch + lane * 16);
+          }
+          scw[mt] = *reinterpret_cast<const uint2 *>(ch + Lay::QB + g * 8);
+        }
+#pragma unroll
+        for (int kbi = 0; kbi < 2; kbi++) {
+          // this 32-block's X (hi and lo operands of each n-tile), shared by both m-tiles
+          uint4 xh[NT], xo[NT];
+#pragma unroll
+          for (int n = 0; n < NT; n++) {
+            xh[n] = xs[(kbi * NT + n) * 64 + lane];
+            xo[n] = xs[(kbi * NT + n) * 64 + 32 + lane];
+          }
+#pragma unroll
+          for (int mt = 0; mt < 2; mt++) {
+            if (mt == 1 && !has1) break;
+            uint32_t a0s0, a1s0, a2s0, a3s0, a0s1, a1s1, a2s1, a3s1;
+            if (TYPE == 8) {
+              const uint4 q = qw[mt][kbi];
+              q8_to_f16(q.x, a0s0, a2s0);  // row g, bytes 4t..4t+3
+              q8_to_f16(q.y, a0s1, a2s1);  // row g, bytes 16+4t..
+              q8_to_f16(q.z, a1s0, a3s0);  // row g+8
+              q8_to_f16(q.w, a1s1, a3s1);
+            } else {
+              const uint4 q = qw[mt][0];
+              const uint32_t wg = kbi ? q.z : q.x, wg8 = kbi ? q.w : q.y;
+              q4_to_f16(wg, a0s0, a2s0, a0s1, a2s1);
+              q4_to_f16(wg8, a1s0, a3s0, a1s1, a3s1);
+            }
+            const uint32_t dw = kbi ? scw[mt].y : scw[mt].x;
+            const float dg = __half2float(__ushort_as_half((unsigned short)(dw & 0xFFFFu)));
+            const float dg8 = __half2float(__ushort_as_half((unsigned short)(dw >> 16)));
+#pragma unroll
+            for (int n = 0; n < NT; n++) {
+              float cc[4];
+              mma_16816(cc, a0s0, a1s0, a2s0, a3s0, xh[n].x, xh[n].y, zero4);
+              mma_16816(cc, a0s0, a1s0, a2s0, a3s0, xo[n].x, xo[n].y, cc);
+              mma_16816(cc, a0s1, a1s1, a2s1, a3s1, xh[n].z, xh[n].w, cc);
+              mma_16816(cc, a0s1, a1s1, a2s1, a3s1, xo[n].z, xo[n].w, cc);
+              acc[mt][n][0] = fmaf(dg, cc[0], acc[mt][n][0]);
+              acc[mt][n][1] = fmaf(dg, cc[1], acc[mt][n][1]);
+              acc[mt][n][2] = fmaf(dg8, cc[2], acc[mt][n][2]);
+              acc[mt][n][3] = fmaf(dg8, cc[3], acc[mt][n][3]);
+            }
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[st]);
+      if (++st == S) {
+        st = 0;
+        ph ^= 1;
+      }
+    }
+
+    const bool full_tile = (ka == 0 && kb_end == a.kp);
+    if (full_tile) {
+      if (ok && has0) gemv_epilogue<NT>(a, mt0, has1, acc, g, t, xun);
+    } else {
+      // Partial tile: park this segment's sums; the arrival count and the
+      // reduction wait until this CTA's last segment, so the stream never stalls.
+      // In cluster mode the CTA holds its one segment in its own shared
+      // memory (the drained ring), read by the other CTAs of the cluster.
+      const int slot = first_seg ? 0 : 1;
+      float *mine = a.cl > 1 ? reinterpret_cast<float *>(smem) : a.ws + ((size_t)c * 2 + slot) * WS_TILE_FLOATS;
+      if (a.cl > 1) named_bar(1, QG_CONS_WARPS * 32);  // every warp is done with the ring
+      if (has0) {
+#pragma unroll
+        for (int mt = 0; mt < 2; mt++)
+#pragma unroll
+          for (int n = 0; n < NT; n++)
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+              float *p = mine + ((warp * 2 + mt) * 16 + g + 8 * h) * 16 + n * 8 + 2 * t;
+              float2 v = make_float2(acc[mt][n][2 * h], acc[mt][n][2 * h + 1]);
+              if (XL) {  // local exponents differ between contributors: unscale before the sum (exact)
+                v.x *= xun[n * 8 + 2 * t];
+                v.y *= xun[n * 8 + 2 * t + 1];
+              }
+              *reinterpret_cast<float2 *>(p) = v;
+            }
+      }
+      ptile[np++] = tile;
+    }
+    u += nk;
+    first_seg = false;
+  }
+
+  y_fence(a);  // full tiles' peer stores
+  if (np == 0) return;  // (sums of squares are only asked of fully split grids)
+  // ---- split tiles: every contributor reduces a share of the rows ----
+  // warp w's two m-tiles are reduced by contributor w % ncon: lane l sums row
+  // l & 15 of m-tile l >> 4, four columns per float4 (NC4 float4s per
+  // contributor), over all contributors in CTA order.
+  const int mt = lane >> 4, row = lane & 15;
+  if (a.cl > 1) {
+    // Cluster mode: the tile's contributors are the cluster's CTAs (ranks 0..cl-1
+    // in CTA order); partials are read from their shared memory.  Both cluster
+    // barriers are hardware barriers that every thread of the cluster reaches
+    // (all earlier waits are bounded).
+    namespace cg = cooperative_groups;
+    cg::cluster_group cluster = cg::this_cluster();
+    cluster_sync_all();  // every CTA's partials are in its shared memory
+    const int tile = ptile[0], r = (int)cluster.block_rank();
+    const int mt0 = tile * QG_TILE_MT + warp * 2;
+    if (__all_sync(0xffffffffu, ok) && warp % a.cl == r) {  // warp-uniform: split_epilogue shuffles
+      const bool live = mt0 + mt < a.n_mt;
+      float4 sum[NC4];
+#pragma unroll
+      for (int n = 0; n < NC4; n++) sum[n] = make_float4(0.f, 0.f, 0.f, 0.f);
+      const int off = ((warp * 2 + mt) * 16 + row) * 16;
+      if (live) {
+        float4 v[4][NC4];
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+          if (q >= a.cl) break;
+          const float *src = cluster.map_shared_rank(reinterpret_cast<float *>(smem), q) + off;
+#pragma unroll
+          for (int n = 0; n < NC4; n++) v[q][n] = *reinterpret_cast<const float4 *>(src + 4 * n);
+        }
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+          if (q >= a.cl) break;
+#pragma unroll
+          for (int n = 0; n < NC4; n++) {
+            sum[n].x += v[q][n].x;
+            sum[n].y += v[q][n].y;
+            sum[n].z += v[q][n].z;
+            sum[n].w += v[q][n].w;
+          }
+        }
+      }
+      split_epilogue<NC4>(a, mt0, mt, row, live, sum, wst);
+    }
+    y_fence(a);
+    cluster_sync_all();  // no CTA leaves while another reads its shared memory
+    if (XL && a.st_out && threadIdx.x < QG_STAT_COLS) {  // this CTA's slot: the warps' sums in warp order
+      const float *w0 = xun + 16;
+      float ss = 0.f;
+      for (int w = 0; w < QG_CONS_WARPS; w++) ss += w0[w * 16 + threadIdx.x];
+      a.st_out[(size_t)c * QG_STAT_COLS + threadIdx.x] = ss;
+    }
+    return;
+  }
+  // Global mode.  All contributors of a split tile are resident (one CTA per
+  // SM, G <= SMs, and PDL successors start only after every CTA of this grid
+  // started), and each first counts itself in for all its split tiles and
+  // only then waits, so the waits below end; they are bounded all the same.
+  // The counter of a tile goes 0 -> n (partials parked) -> 2n (shares
+  // reduced) -> 0.
+  named_bar(1, QG_CONS_WARPS * 32);
+  if (threadIdx.x == 0) {
+    __threadfence();  // the CTA's partials (ordered before by the barrier), before the arrival
+    for (int j = 0; j < np; j++) atomicAdd(a.cnt + ptile[j], 1);
+  }
+  for (int j = 0; j < np; j++) {
+    const int tile = ptile[j];
+    const long long tu0 = (long long)tile * a.kp, tu1 = tu0 + a.kp - 1;
+    const int c_first = (int)(((tu0 + 1) * a.G - 1) / a.units);
+    const int c_last = (int)(((tu1 + 1) * a.G - 1) / a.units);
+    const int ncon = c_last - c_first + 1, r = c - c_first;
+    if (threadIdx.x == 0) {
+      const long long t0 = cycles_now();
+      while (ok && *(volatile int *)(a.cnt + tile) < ncon) {
+        if (spin_expired(t0)) {
+          atomicExch(a.err, 3);
+          ok = false;
+        }
+      }
+      __threadfence();  // the other contributors' partials, after their arrivals
+      last_p[0] = ok;
+    }
+    named_bar(1, QG_CONS_WARPS * 32);
+    const bool go = last_p[0] != 0;
+    const int mt0 = tile * QG_TILE_MT + warp * 2;
+    if (go && warp % ncon == r) {
+      const bool live = mt0 + mt < a.n_mt;
+      float4 sum[NC4];
+#pragma unroll
+      for (int n = 0; n < NC4; n++) sum[n] = make_float4(0.f, 0.f, 0.f, 0.f);
+      const size_t off = (size_t)((warp * 2 + mt) * 16 + row) * 16;
+      constexpr int CH = NC4 == 2 ? 4 : 2;  // independent loads in flight per lane
+      if (live) {
+        for (int c0 = c_first; c0 <= c_last; c0 += CH) {
+          float4 v[CH][NC4];
+#pragma unroll
+          for (int q = 0; q < CH; q++) {
+            const int cc = c0 + q;
+            if (cc > c_last) break;
+            const long long cu0 = (long long)cc * a.units / a.G;
+            const float *src = a.ws + ((size_t)cc * 2 + (cu0 >= tu0 ? 0 : 1)) * WS_TILE_FLOATS + off;
+#pragma unroll
+            for (int n = 0; n < NC4; n++) v[q][n] = __ldcg(reinterpret_cast<const float4 *>(src + 4 * n));
+          }
+#pragma unroll
+          for (int q = 0; q < CH; q++) {
+            if (c0 + q > c_last) break;
+#pragma unroll
+            for (int n = 0; n < NC4; n++) {
+              sum[n].x += v[q][n].x;
+              sum[n].y += v[q][n].y;
+              sum[n].z += v[q][n].z;
+              sum[n].w += v[q][n].w;
+            }
+          }
+        }
+      }
+      split_epilogue<NC4>(a, mt0, mt, row, live, sum, wst);
+    }
+    named_bar(1, QG_CONS_WARPS * 32);  // every read of the partials of this tile is done
+    if (threadIdx.x == 0 && go) {
+      if (atomicAdd(a.cnt + tile, 1) == 2 * ncon - 1) a.cnt[tile] = 0;
+    }
+  }
+  y_fence(a);
+  if (XL && a.st_out && threadIdx.x < QG_STAT_COLS) {  // this CTA's slot: the warps' sums in warp order
+    const float *w0 = xun + 16;
+    float ss = 0.f;
+    for (int w = 0; w < QG_CONS_WARPS; w++) ss += w0[w * 16 + threadIdx.x];
+    a.st_out[(size_t)c * QG_STAT_COLS + threadIdx.x] = ss;
+  }
+}
+
+// Thread-block clusters of cl CTAs of this kernel that can be resident at once
+// (0: none / not queryable).
+template <int TYPE, int NT, bool XL>
+static int max_clusters(int cl) {
+  using Lay = QgLayout<TYPE, NT, XL>;
+  static int cache[5] = {-1, -1, -1, -1, -1};
+  if (cl < 2 || cl > 4) return 0;
+  if (cache[cl] < 0) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(cl * 64);
+    cfg.blockDim = dim3(QGM_THREADS);
+    cfg.dynamicSmemBytes = Lay::SMEM;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = cl;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, qgemv_kernel<TYPE, NT, XL>, &cfg) != cudaSuccess) {
+      (void)cudaGetLastError();
+      n = 0;
+    }
+    cache[cl] = n;
+  }
+  return cache[cl];
+}
+
+template <int TYPE, int NT, bool XL>
+static cudaError_t launch_t(GemvArgs a, cudaStream_t st) {
+  using Lay = QgLayout<TYPE, NT, XL>;
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(qgemv_kernel<TYPE, NT, XL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         Lay::SMEM);
+    if (e != cudaSuccess) return e;
+    e = carveout_max(qgemv_kernel<TYPE, NT, XL>);
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  // Split tiles reduced inside thread-block clusters only when every tile's
+  // cluster can be resident at once (the grid is one wave); the sums are the
+  // same as the global path's (contributors in CTA order).
+  if (a.cl > 1 && max_clusters<TYPE, NT, XL>(a.cl) < a.G / a.cl) a.cl = 1;
+  if (a.cl > 1) return launch_pdl_cluster(qgemv_kernel<TYPE, NT, XL>, a.G, QGM_THREADS, Lay::SMEM, st, a.cl, a);
+  return launch_pdl(qgemv_kernel<TYPE, NT, XL>, a.G, QGM_THREADS, Lay::SMEM, st, a);
+}
+
+
+cudaError_t launch(const GemvArgs &a, int type, bool xl, cudaStream_t st) {
+  const int nt = (a.B + 7) / 8;  // n-tiles of 8 columns
+  if (xl) return nt == 1 ? launch_t<2, 1, true>(a, st) : launch_t<2, 2, true>(a, st);
+  switch (nt * 16 + type) {
+    case 16 + 8: return launch_t<8, 1, false>(a, st);
+    case 32 + 8: return launch_t<8, 2, false>(a, st);
+    case 16 + 2: return launch_t<2, 1, false>(a, st);
+    default: return launch_t<2, 2, false>(a, st);
+  }
+}
+
+cudaError_t configure() {
+  cudaError_t e;
+  if ((e = carveout_max(repack_kernel<2>)) != cudaSuccess) return e;
+  if ((e = carveout_max(repack_kernel<8>)) != cudaSuccess) return e;
+  if ((e = carveout_max(qgemv_kernel<2, 1, false>)) != cudaSuccess) return e;
+  if ((e = carveout_max(qgemv_kernel<2, 2, false>)) != cudaSuccess) return e;
+  if ((e = carveout_max(qgemv_kernel<8, 1, false>)) != cudaSuccess) return e;
+  if ((e = carveout_max(qgemv_kernel<8, 2, false>)) != cudaSuccess) return e;
+  if ((e = carveout_max(qgemv_kernel<2, 1, true>)) != cudaSuccess) return e;
+  if ((e = carveout_max(qgemv_kernel<2, 2, true>)) != cudaSuccess) return e;
+  return cudaSuccess;
+}
+
+}  // namespace mma
+}  // namespace cw

@@ -5,6 +5,10 @@
 
 namespace cw {
 
+// Layout selector of the X operands for the engine's GEMV kernel: 0 for the
+// tcgen05 kernel, else the n-tile count of the mma.sync kernel.
+static int xops_nt(const GemvScratch &s, int B) { return s.tc ? 0 : (B + 7) / 8; }
+
 // Dynamic shared memory above the 48 KB default needs an explicit opt-in.
 template <typename F>
 static cudaError_t smem_optin(F *fn, size_t bytes, size_t &done) {
@@ -52,7 +56,7 @@ cudaError_t launch_embed(const uint8_t *emb, int H, int V, const Toks16 &toks, i
 __global__ void __launch_bounds__(PREP_THREADS) cat_norm_prep_kernel(const float *__restrict__ e,
                                                                      const float *__restrict__ h,
                                                                      const float *__restrict__ we,
-                                                                     const float *__restrict__ wh, int H,
+                                                                     const float *__restrict__ wh, int H, int mma_nt,
                                                                      uint4 *__restrict__ xf, int *__restrict__ xexp) {
   pdl_trigger();
   pdl_wait();
@@ -77,7 +81,7 @@ __global__ void __launch_bounds__(PREP_THREADS) cat_norm_prep_kernel(const float
     v[H + k] = wh[k] * v[H + k] * rh;
   }
   __syncthreads();
-  emit_xfrag(v, 2 * H, b, xf, xexp, red, true);
+  emit_xfrag(v, 2 * H, b, mma_nt, xf, xexp, red, true);
 }
 
 cudaError_t launch_cat_norm_prep(const float *e, const float *h, const float *we, const float *wh, int H, int B,
@@ -86,7 +90,7 @@ cudaError_t launch_cat_norm_prep(const float *e, const float *h, const float *we
   static size_t done = 0;
   cudaError_t err = smem_optin(cat_norm_prep_kernel, smem, done);
   if (err != cudaSuccess) return err;
-  CW_TRY(launch_pdl(cat_norm_prep_kernel, B, PREP_THREADS, smem, st, e, h, we, wh, H, s.xf, s.xexp));
+  CW_TRY(launch_pdl(cat_norm_prep_kernel, B, PREP_THREADS, smem, st, e, h, we, wh, H, xops_nt(s, B), s.xf, s.xexp));
   return cudaGetLastError();
 }
 
@@ -102,7 +106,7 @@ constexpr int ROW_THREADS = 256;
 // ---- RMSNorm (run.c:346) fused with GEMV input preparation ----
 // Optional copy of the normed row to `out`.
 __global__ void __launch_bounds__(ROW_THREADS) norm_prep_kernel(const float *__restrict__ x, const float *__restrict__ w,
-                                                                int H, uint4 *__restrict__ xf,
+                                                                int H, int mma_nt, uint4 *__restrict__ xf,
                                                                 int *__restrict__ xexp, float *__restrict__ out) {
   pdl_trigger();
   pdl_wait();
@@ -130,19 +134,19 @@ __global__ void __launch_bounds__(ROW_THREADS) norm_prep_kernel(const float *__r
   __syncthreads();
   const int e = xfrag_exponent(sm.y * s);
   if (r == 0 && threadIdx.x == 0) xexp[b] = e;
-  emit_xfrag_blocks(v, k0 / 32, n / 32, b, xf, __int_as_float((127 + e) << 23), true);
+  emit_xops(v, k0 / 32, n / 32, b, mma_nt, xf, __int_as_float((127 + e) << 23), true);
 }
 
 cudaError_t launch_norm_prep(const float *x, const float *w, int H, int B, GemvScratch &s, float *out,
                              cudaStream_t st) {
   const int cl = cluster_split(H / 32);
   CW_TRY(launch_pdl_cluster(norm_prep_kernel, dim3(cl, B), ROW_THREADS, (size_t)(H / cl) * sizeof(float), st, cl, x, w,
-                            H, s.xf, s.xexp, out));
+                            H, xops_nt(s, B), s.xf, s.xexp, out));
   return cudaGetLastError();
 }
 
 // ---- plain row -> GEMV input (e.g. the SwiGLU output feeding ffn_down) ----
-__global__ void __launch_bounds__(ROW_THREADS) row_prep_kernel(const float *__restrict__ x, int xs, int K,
+__global__ void __launch_bounds__(ROW_THREADS) row_prep_kernel(const float *__restrict__ x, int xs, int K, int mma_nt,
                                                                uint4 *__restrict__ xf, int *__restrict__ xexp) {
   pdl_trigger();
   pdl_wait();
@@ -158,13 +162,13 @@ __global__ void __launch_bounds__(ROW_THREADS) row_prep_kernel(const float *__re
   mx = cluster_reduce<true>(block_max(mx, red), &slot);
   const int e = xfrag_exponent(mx);
   if (r == 0 && threadIdx.x == 0) xexp[b] = e;
-  emit_xfrag_blocks(v, k0 / 32, n / 32, b, xf, __int_as_float((127 + e) << 23), true);
+  emit_xops(v, k0 / 32, n / 32, b, mma_nt, xf, __int_as_float((127 + e) << 23), true);
 }
 
 cudaError_t launch_row_prep(const float *x, int xs, int K, int B, GemvScratch &s, cudaStream_t st) {
   const int cl = cluster_split(K / 32);
   CW_TRY(launch_pdl_cluster(row_prep_kernel, dim3(cl, B), ROW_THREADS, (size_t)(K / cl) * sizeof(float), st, cl, x, xs,
-                            K, s.xf, s.xexp));
+                            K, xops_nt(s, B), s.xf, s.xexp));
   return cudaGetLastError();
 }
 

@@ -75,17 +75,50 @@ CW_DEV void emit_xfrag_blocks(const float *v, int kb0, int nkb, int b, uint4 *__
   }
 }
 
+// The same for the mma.sync kernel (qgemv_mma.cu): per (32-block, n-tile of
+// 8 columns) 64 uint4, 32 lanes of hi parts then 32 of lo parts; lane
+// (b % 8, t) holds (x[4t], x[4t+2]) (x[4t+1], x[4t+3]) (x[4t+16], x[4t+18])
+// (x[4t+17], x[4t+19]), the K order of that kernel's A fragments; nt n-tiles.
+CW_DEV void emit_xfrag_blocks_mma(const float *v, int kb0, int nkb, int b, int nt, uint4 *__restrict__ xf,
+                                  float scale, bool live) {
+  const int g = b & 7, n = b >> 3;
+  for (int item = threadIdx.x; item < nkb * 4; item += blockDim.x) {
+    const int kbl = item >> 2, t = item & 3;
+    const float *r = v + kbl * 32;
+    const int js[8] = {4 * t, 4 * t + 2, 4 * t + 1, 4 * t + 3, 4 * t + 16, 4 * t + 18, 4 * t + 17, 4 * t + 19};
+    uint32_t hi[4], lo[4];
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      const float v0 = live ? r[js[2 * i]] * scale : 0.f, v1 = live ? r[js[2 * i + 1]] * scale : 0.f;
+      const half h0 = __float2half_rn(v0), h1 = __float2half_rn(v1);
+      const half l0 = __float2half_rn(v0 - __half2float(h0)), l1 = __float2half_rn(v1 - __half2float(h1));
+      hi[i] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
+      lo[i] = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
+    }
+    uint4 *o = xf + (size_t)((kb0 + kbl) * nt + n) * 64;
+    o[g * 4 + t] = make_uint4(hi[0], hi[1], hi[2], hi[3]);       // hi B operand, column g
+    o[32 + g * 4 + t] = make_uint4(lo[0], lo[1], lo[2], lo[3]);  // lo B operand, column g
+  }
+}
+// One of the two: mma_nt == 0 the tcgen05 layout, else the mma.sync layout
+// with mma_nt n-tiles.
+CW_DEV void emit_xops(const float *v, int kb0, int nkb, int b, int mma_nt, uint4 *__restrict__ xf, float scale,
+                      bool live) {
+  if (mma_nt) emit_xfrag_blocks_mma(v, kb0, nkb, b, mma_nt, xf, scale, live);
+  else emit_xfrag_blocks(v, kb0, nkb, b, xf, scale, live);
+}
+
 // Emit the X operands for column b from v[0..K) in shared memory (one CTA
 // holds the whole column).
-CW_DEV void emit_xfrag(const float *v, int K, int b, uint4 *__restrict__ xf, int *__restrict__ xexp, float *red,
-                       bool live) {
+CW_DEV void emit_xfrag(const float *v, int K, int b, int mma_nt, uint4 *__restrict__ xf, int *__restrict__ xexp,
+                       float *red, bool live) {
   float mx = 0.f;
   if (live)
     for (int k = threadIdx.x; k < K; k += blockDim.x) mx = fmaxf(mx, fabsf(v[k]));
   mx = block_max(mx, red);
   const int e = xfrag_exponent(mx);
   if (threadIdx.x == 0) xexp[b] = e;
-  emit_xfrag_blocks(v, 0, K / 32, b, xf, __int_as_float((127 + e) << 23), live);
+  emit_xops(v, 0, K / 32, b, mma_nt, xf, __int_as_float((127 + e) << 23), live);
 }
 
 // One float per CTA reduced over the thread-block cluster (<= 32 CTAs)

@@ -347,7 +347,10 @@ int cwen_load_synth(uint64_t seed, const cwen_dims *dims, int threads) {
   for (int i = 0; i < n && !rc; i++) {
     cw_tensor_desc td;
     cw_model_tensor_desc(&d, i, &td);
-    cw_synth_tensor(seed, &td, buf, threads);
+    /* a row-sharded matrix: only the rows this GPU keeps are generated */
+    int r0 = 0, r1 = td.ne1;
+    cwen_cuda_shard_rows_for(td.name, td.ne1, &r0, &r1);
+    cw_synth_tensor_rows(seed, &td, buf, threads, r0, r1);
     rc = cwen_cuda_upload(td.name, td.type, buf, td.ne0, td.ne1);
   }
   free(buf);

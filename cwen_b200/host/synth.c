@@ -215,10 +215,12 @@ static int n_threads(int want) {
   long n = sysconf(_SC_NPROCESSORS_ONLN);
   return n < 1 ? 1 : (n > 64 ? 64 : (int)n);
 }
-static void fill_quant(uint64_t key, int type, size_t nblk, uint8_t *dst, int threads) {
+/* Blocks [lo, hi) of a quantized tensor (each written at its own offset of dst). */
+static void fill_quant_range(uint64_t key, int type, size_t lo, size_t hi, uint8_t *dst, int threads) {
   int nt = n_threads(threads);
+  const size_t nblk = hi - lo;
   if (nblk < 65536 || nt == 1) {
-    fill_job j = {key, type, nblk, 0, nblk, dst};
+    fill_job j = {key, type, nblk, lo, hi, dst};
     fill_worker(&j);
     return;
   }
@@ -227,7 +229,7 @@ static void fill_quant(uint64_t key, int type, size_t nblk, uint8_t *dst, int th
   size_t per = (nblk + (size_t)nt - 1) / (size_t)nt;
   int launched = 0;
   for (int t = 0; t < nt; t++) {
-    size_t b0 = (size_t)t * per, b1 = b0 + per < nblk ? b0 + per : nblk;
+    size_t b0 = lo + (size_t)t * per, b1 = b0 + per < hi ? b0 + per : hi;
     if (b0 >= b1) break;
     jobs[t] = (fill_job){key, type, nblk, b0, b1, dst};
     if (pthread_create(&tid[t], NULL, fill_worker, &jobs[t])) { fill_worker(&jobs[t]); tid[t] = 0; }
@@ -238,10 +240,10 @@ static void fill_quant(uint64_t key, int type, size_t nblk, uint8_t *dst, int th
 }
 
 void cw_synth_q4_0(uint64_t seed, const char *stream, int ne0, int ne1, void *dst, int threads) {
-  fill_quant(stream_key(seed, stream), CW_T_Q4_0, (size_t)(ne0 / 32) * (size_t)ne1, (uint8_t *)dst, threads);
+  fill_quant_range(stream_key(seed, stream), CW_T_Q4_0, 0, (size_t)(ne0 / 32) * (size_t)ne1, (uint8_t *)dst, threads);
 }
 void cw_synth_q8_0(uint64_t seed, const char *stream, int ne0, int ne1, void *dst, int threads) {
-  fill_quant(stream_key(seed, stream), CW_T_Q8_0, (size_t)(ne0 / 32) * (size_t)ne1, (uint8_t *)dst, threads);
+  fill_quant_range(stream_key(seed, stream), CW_T_Q8_0, 0, (size_t)(ne0 / 32) * (size_t)ne1, (uint8_t *)dst, threads);
 }
 void cw_synth_normal(uint64_t seed, const char *stream, float mean, float std, float *dst, size_t n) {
   uint64_t key = stream_key(seed, stream);
@@ -250,6 +252,15 @@ void cw_synth_normal(uint64_t seed, const char *stream, float mean, float std, f
 void cw_synth_ids(uint64_t seed, const char *stream, int hi, int32_t *dst, size_t n) {
   uint64_t key = stream_key(seed, stream);
   for (size_t i = 0; i < n; i++) dst[i] = (int32_t)(rnd_at(key, i) % (uint64_t)hi);
+}
+
+void cw_synth_tensor_rows(uint64_t seed, const cw_tensor_desc *t, void *dst, int threads, int r0, int r1) {
+  if (t->kind != CW_GEN_QMAT) {
+    cw_synth_tensor(seed, t, dst, threads);
+    return;
+  }
+  const size_t nb = (size_t)(t->ne0 / 32);
+  fill_quant_range(stream_key(seed, t->name), t->type, (size_t)r0 * nb, (size_t)r1 * nb, (uint8_t *)dst, threads);
 }
 
 void cw_synth_tensor(uint64_t seed, const cw_tensor_desc *t, void *dst, int threads) {

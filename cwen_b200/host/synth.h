@@ -61,6 +61,9 @@ size_t cw_tensor_nbytes(int type, int ne0, int ne1);
 /* Fill `dst` (cw_tensor_nbytes bytes) with the tensor's seeded contents,
  * using up to `threads` host threads (<=0: all cores). */
 void cw_synth_tensor(uint64_t seed, const cw_tensor_desc *t, void *dst, int threads);
+/* Only rows [r0, r1) of a quantized matrix, at their own offsets of the
+ * full-size dst (other kinds: the whole tensor). */
+void cw_synth_tensor_rows(uint64_t seed, const cw_tensor_desc *t, void *dst, int threads, int r0, int r1);
 
 /* Generic seeded fills used by benches and tests. */
 void cw_synth_q4_0(uint64_t seed, const char *stream, int ne0, int ne1, void *dst, int threads);

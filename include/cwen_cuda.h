@@ -51,7 +51,11 @@ const char *cwen_cuda_last_error(void);
 /* Select `device`, create the engine's stream and GEMV scratch.  `ctx` is the
  * context window (CWEN_CTX, run.c:4098-4104) and `bmax` the largest verify
  * block (SPEC_BMAX = 16, run.c:192).  Replaces alloc_state (run.c:3928) for
- * the kernel-level scratch. */
+ * the kernel-level scratch.  The verify GEMV of the engine is chosen here,
+ * for its lifetime: the warp-level mma.sync kernel (default), or with
+ * CWEN_GEMV=tcgen05 in the environment the 5th-generation tensor-core kernel
+ * (faster for verify blocks of 9-16 rows, slower for serial decode); weights
+ * are repacked for the chosen kernel. */
 int cwen_cuda_init(int device, int ctx, int bmax);
 /* Free everything (process exit in the reference). */
 void cwen_cuda_shutdown(void);
@@ -208,6 +212,34 @@ int cwen_cuda_gdn_state(int layer, float *S_host, float *conv_host);
  * One kernel launch on `stream` (NULL: the engine's); synchronizes. */
 int cwen_cuda_accept_logits(const float *dlogits, int n, int ldl, int B, const int *blk, int E_drafts, int *res,
                             void *stream);
+
+/* ---- row sharding across the GPUs of one node (one engine per GPU) ----
+ * The FFN matrices (ffn_gate, ffn_up, ffn_down) and the lm_head (output.weight)
+ * are split by output rows, K never split (gemvb rows are independent,
+ * run.c:1577-1680; OpenMP over rows at run.c:1588, 1656); the GDN and
+ * attention layers, the recurrent state, the KV cache and the MTP block are
+ * replicated.  A sharded GEMV writes its rows into every GPU's copy of its
+ * output (NVLink stores into buffers opened through CUDA IPC) and a bounded
+ * cross-GPU barrier follows it.  Sequence: cwen_cuda_init, cwen_cuda_shard_config,
+ * cwen_cuda_model_config, uploads (each GPU keeps its rows), finalize,
+ * cwen_cuda_shard_handle on every GPU, exchange the blobs (rank order),
+ * cwen_cuda_shard_open; then every GPU runs the same calls.  Output bits do
+ * not depend on the batch size for a given group size; they may differ from
+ * a single GPU's in fp32 summation order only.  No counterpart in the
+ * reference (a CPU program). */
+enum { CWEN_SHARD_HANDLE_BYTES = 256 };
+int cwen_cuda_shard_config(int rank, int world);
+/* This GPU's exchange buffers as a CWEN_SHARD_HANDLE_BYTES blob. */
+int cwen_cuda_shard_handle(void *out, int cap);
+/* Map the other GPUs' buffers: `handles` holds world blobs in rank order. */
+int cwen_cuda_shard_open(const void *handles, int world);
+/* The rows [r0, r1) of a matrix of M rows that GPU `rank` of `world` holds
+ * (equal shares in units of `align` rows); needs no GPU. */
+int cwen_shard_rows(int M, int align, int rank, int world, int *r0, int *r1);
+/* The rows [r0, r1) of GGUF tensor `name` (ne1 rows) this GPU keeps: a
+ * shard for the FFN matrices and output.weight under a shard group, all rows
+ * otherwise (so a loader need only read or generate those). */
+int cwen_cuda_shard_rows_for(const char *name, int ne1, int *r0, int *r1);
 
 /* ---- instrumentation (the reference's CWEN_SPEC_DEBUG timers, run.c:3133) ---- */
 /* Reset counters and turn per-launch CUDA-event timing of the verify-GEMV

@@ -95,6 +95,12 @@ int cwen_cuda_upload(const char *name, int type, const void *host, int ne0, int 
   return CWEN_ESTATE;
 }
 int cwen_cuda_model_finalize(void) { return CWEN_ESTATE; }
+int cwen_cuda_shard_rows_for(const char *name, int ne1, int *r0, int *r1) {
+  (void)name;
+  *r0 = 0;
+  *r1 = ne1;  /* no shard group: every row */
+  return CWEN_OK;
+}
 int cwen_cuda_model_dims(cwen_dims *d) {
   memset(d, 0, sizeof *d);
   d->n_vocab = g_V;

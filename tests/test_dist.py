@@ -72,3 +72,59 @@ def test_reference_arm_under_torchrun_prints_one_line():
     rec = json.loads(lines[0])
     assert rec["impl"] == "reference" and rec["unit"] == "GB/s" and rec["value"] > 0
     assert rec["e2e"]["h2d_bytes_per_step"] == 0 and rec["cpu_baseline"]["kind"] == "reference"
+
+
+def test_shard_rows_partition():
+    """cwen_shard_rows: for every group size the ranks' row ranges are
+    contiguous, disjoint, cover [0, M) in rank order, and start on multiples
+    of the alignment (the FFN and lm_head row split of the sharded decode)."""
+    import ctypes as C
+
+    import cwen_b200
+    L = cwen_b200.lib()
+    r0, r1 = C.c_int(), C.c_int()
+    for M in (0, 16, 512, 1024, 5120, 17408, 248320, 1000):
+        for world in range(1, 9):
+            for align in (1, 16):
+                edge = 0
+                for rank in range(world):
+                    assert L.cwen_shard_rows(M, align, rank, world, C.byref(r0), C.byref(r1)) == 0
+                    assert r0.value == edge and r1.value >= r0.value, (M, world, align, rank)
+                    assert r0.value % align == 0 or r0.value == M
+                    edge = r1.value
+                assert edge == M, (M, world, align)
+    assert L.cwen_shard_rows(10, 1, 2, 2, C.byref(r0), C.byref(r1)) < 0  # rank outside the group
+
+
+def _shard_exchange_main(rank, ws, port, q):
+    import sys
+    from pathlib import Path
+    sys.path.insert(0, str(Path(__file__).resolve().parents[1]))
+    os.environ.update({"RANK": str(rank), "LOCAL_RANK": str(rank), "WORLD_SIZE": str(ws),
+                       "MASTER_ADDR": "127.0.0.1", "MASTER_PORT": str(port), "CWEN_DIST_BACKEND": "gloo"})
+    import torch.distributed as dist
+
+    import bench
+    w, r, _ = bench.dist_init(None)
+    blob = bytes([r]) * bench.SHARD_HANDLE
+    q.put((r, bench.shard_exchange(blob, w)))
+    dist.destroy_process_group()
+
+
+def test_shard_handle_exchange_two_ranks():
+    """The sharded decode's set-up step over a process group: every rank ends
+    with all ranks' handle blobs concatenated in rank order."""
+    import bench
+    ws = 2
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_shard_exchange_main, args=(r, ws, port, q)) for r in range(ws)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    want = b"".join(bytes([r]) * bench.SHARD_HANDLE for r in range(ws))
+    res = dict(q.get(timeout=10) for _ in range(ws))
+    assert res == {0: want, 1: want}

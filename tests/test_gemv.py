@@ -1,5 +1,7 @@
 """Verify GEMV (a): CUDA path vs the CPU oracle and the reference goldens,
-through the C ABI (include/cwen_cuda.h), plus batch invariance.
+through the C ABI (include/cwen_cuda.h), plus batch invariance -- for both
+kernels an engine can run (the warp-level mma.sync kernel, the default, and
+the tcgen05 kernel selected with CWEN_GEMV=tcgen05 at cwen_cuda_init).
 
 Tolerance: the reference's gemv acceptance, max_abs <= 1e-4 (run.c:4352),
 and relative L2 <= 1e-5 (the kernel computes X as f16 hi+lo, ~2^-22
@@ -15,13 +17,23 @@ from oracle_lib import gen_normal, gen_q, oracle_gemvb, rel_l2
 pytestmark = pytest.mark.gpu
 
 
-@pytest.fixture(scope="module")
-def eng():
+@pytest.fixture(scope="module", params=["mma", "tcgen05"])
+def eng(request):
+    import os
+
     import cwen_b200
     from cwen_b200 import build
     build.build()
     L = cwen_b200.lib()
-    cwen_b200.check(L.cwen_cuda_init(0, 64, 16), "init")
+    old = os.environ.get("CWEN_GEMV")
+    os.environ["CWEN_GEMV"] = request.param
+    try:
+        cwen_b200.check(L.cwen_cuda_init(0, 64, 16), "init")
+    finally:
+        if old is None:
+            os.environ.pop("CWEN_GEMV")
+        else:
+            os.environ["CWEN_GEMV"] = old
     yield L
     L.cwen_cuda_shutdown()
 

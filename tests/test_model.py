@@ -6,6 +6,8 @@
 - the verify block is bit-identical to serial decode (batch invariance), and
   a short-walk commit restores exactly the serial state;
 - speculative generation emits exactly the serial token stream.
+Every test runs under both verify-GEMV kernels an engine can use (mma.sync,
+the default, and tcgen05 with CWEN_GEMV=tcgen05).
 """
 import ctypes as C
 
@@ -20,13 +22,23 @@ SEED = 7
 CTX = 512
 
 
-@pytest.fixture(scope="module")
-def small():
+@pytest.fixture(scope="module", params=["mma", "tcgen05"])
+def small(request):
+    import os
+
     import cwen_b200
     from cwen_b200 import build
     build.build()
     L = cwen_b200.lib()
-    cwen_b200.check(L.cwen_cuda_init(0, CTX, 16), "init")
+    old = os.environ.get("CWEN_GEMV")
+    os.environ["CWEN_GEMV"] = request.param
+    try:
+        cwen_b200.check(L.cwen_cuda_init(0, CTX, 16), "init")
+    finally:
+        if old is None:
+            os.environ.pop("CWEN_GEMV")
+        else:
+            os.environ["CWEN_GEMV"] = old
     d = cwen_b200.dims("small")
     cwen_b200.check(L.cwen_load_synth(SEED, C.byref(d), 0), "load_synth")
     yield L, d
