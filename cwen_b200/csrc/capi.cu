@@ -7,6 +7,7 @@
 #include "attn.cuh"
 #include "gdn.cuh"
 #include "model.cuh"
+#include "qmv.cuh"
 #include "rowops.cuh"
 #include "shard.cuh"
 
@@ -51,7 +52,10 @@ int ensure_io(size_t floats) {
   return CWEN_OK;
 }
 
-int upload_qmat_rows(int type, const void *host, int ne0, int ne1, QMat &m, int mt_off, int mt_stride) {
+// Source row r of the tensor becomes row rows_off + r of the fused matrix;
+// with stride 2 (interleaved gate/up) its 8-row group (qmv) or 16-row group
+// (the other kernels) lands in every second slot, phase 0 or 1.
+int upload_qmat_rows(int type, const void *host, int ne0, int ne1, QMat &m, int rows_off, int stride, int phase) {
   Engine &E = engine();
   const size_t rb = (size_t)(ne0 / 32) * (type == CWEN_T_Q8_0 ? 34 : 18);
   const size_t bytes = rb * (size_t)ne1;
@@ -64,7 +68,11 @@ int upload_qmat_rows(int type, const void *host, int ne0, int ne1, QMat &m, int 
   for (size_t r0 = 0; r0 < (size_t)ne1; r0 += rows_per) {
     const size_t nr = (size_t)ne1 - r0 < rows_per ? (size_t)ne1 - r0 : rows_per;
     CW_CHECK(cudaMemcpyAsync(E.staging, (const uint8_t *)host + r0 * rb, nr * rb, cudaMemcpyHostToDevice, E.stream));
-    CW_CHECK(qmat_repack(m, E.staging, (int)nr, mt_off + (int)(r0 / 16) * mt_stride, mt_stride, E.stream));
+    if (m.kern == GK_QMV)
+      CW_CHECK(qmv_repack(m, E.staging, (int)nr, (long long)r0, rows_off / 8 * stride + phase, stride, E.stream));
+    else
+      CW_CHECK(qmat_repack(m, E.staging, (int)nr, rows_off / 16 * stride + phase + (int)(r0 / 16) * stride, stride,
+                           E.stream));
     CW_CHECK(cudaStreamSynchronize(E.stream));
   }
   return CWEN_OK;
@@ -115,13 +123,18 @@ int gemv_status() {
   return CWEN_ETIMEOUT;
 }
 
-int alloc_qmat(QMat &m, int type, int K, int n_mt, int M) {
-  m.tc = engine().gs.tc;  // the layout of the engine's GEMV kernel
+int alloc_qmat(QMat &m, int type, int K, int rows, bool pair) {
+  Engine &E = engine();
+  m.kern = E.gs.kern;  // the layout of the engine's GEMV kernel
+  m.tc = m.kern == GK_TC;
   m.type = type;
   m.K = K;
-  m.n_mt = n_mt;
-  m.M = M;
-  m.bytes = qmat_bytes(type, K, n_mt);
+  m.n_mt = (rows + 15) / 16;
+  m.M = rows;
+  m.pair = pair;
+  m.n_ht = (rows + 7) / 8;
+  m.G = E.n_sm;
+  m.bytes = m.kern == GK_QMV ? qmv_bytes(type, K, m.n_ht) : qmat_bytes(type, K, m.n_mt);
   CW_CHECK(cudaMalloc(&m.w, m.bytes));
   CW_CHECK(cudaMemsetAsync(m.w, 0, m.bytes, engine().stream));
   return CWEN_OK;
@@ -159,15 +172,19 @@ int cwen_cuda_init(int device, int ctx, int bmax) {
   CW_CHECK(cudaDeviceGetAttribute(&E.n_sm, cudaDevAttrMultiProcessorCount, device));
   CW_CHECK(cudaStreamCreateWithFlags(&E.stream, cudaStreamNonBlocking));
   GemvScratch &s = E.gs;
-  // the verify-GEMV kernel of this engine: CWEN_GEMV=tcgen05, else mma.sync
+  // the verify-GEMV kernel of this engine: mma.sync (default), CWEN_GEMV=qmv or tcgen05
   const char *gk = getenv("CWEN_GEMV");
-  s.tc = gk && !strcmp(gk, "tcgen05");
+  s.kern = gk && !strcmp(gk, "tcgen05") ? GK_TC : (gk && !strcmp(gk, "qmv") ? GK_QMV : GK_MMA);
+  s.tc = s.kern == GK_TC;
   s.kmax = 32768;
   s.G = E.n_sm;  // one persistent CTA per SM
   s.max_tiles = 1 << 16;
   CW_CHECK(cudaMalloc(&s.xf, (size_t)(s.kmax / 32) * 128 * sizeof(uint4)));
   CW_CHECK(cudaMemset(s.xf, 0, (size_t)(s.kmax / 32) * 128 * sizeof(uint4)));  // padding columns stay finite
   CW_CHECK(cudaMalloc(&s.xexp, QG_MAXB * sizeof(int)));
+  CW_CHECK(cudaMalloc(&s.qx, qmv_xbuf_bytes(s.kmax)));
+  CW_CHECK(cudaMalloc(&s.qflag, (size_t)qmv_nflags(s.kmax) * sizeof(int)));
+  CW_CHECK(cudaMemset(s.qflag, 0, (size_t)qmv_nflags(s.kmax) * sizeof(int)));
   CW_CHECK(cudaMalloc(&s.ws, gemv_scratch_ws_floats(s.G) * sizeof(float)));
   CW_CHECK(cudaMalloc(&s.cnt, (size_t)s.max_tiles * sizeof(int)));
   CW_CHECK(cudaMemset(s.cnt, 0, (size_t)s.max_tiles * sizeof(int)));
@@ -197,6 +214,8 @@ void cwen_cuda_shutdown(void) {
   for (auto e : E.prof.ev) cudaEventDestroy(e);
   cudaFree(E.gs.xf);
   cudaFree(E.gs.xexp);
+  cudaFree(E.gs.qx);
+  cudaFree(E.gs.qflag);
   cudaFree(E.gs.ws);
   cudaFree(E.gs.cnt);
   cudaFree(E.gs.err);
@@ -222,9 +241,9 @@ int cwen_cuda_weight_upload(int type, const void *host, int ne0, int ne1, int *w
     return CWEN_EINVAL;
   }
   QMat m;
-  int rc = alloc_qmat(m, type, ne0, (ne1 + 15) / 16, ne1);
+  int rc = alloc_qmat(m, type, ne0, ne1, false);
   if (rc) return rc;
-  rc = upload_qmat_rows(type, host, ne0, ne1, m, 0, 1);
+  rc = upload_qmat_rows(type, host, ne0, ne1, m, 0, 1, 0);
   if (rc) {
     cudaFree(m.w);
     return rc;

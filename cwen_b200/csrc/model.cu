@@ -14,8 +14,8 @@
 
 namespace cw {
 
-int alloc_qmat(QMat &m, int type, int K, int n_mt, int M);
-int upload_qmat_rows(int type, const void *host, int ne0, int ne1, QMat &m, int mt_off, int mt_stride);
+int alloc_qmat(QMat &m, int type, int K, int rows, bool pair);
+int upload_qmat_rows(int type, const void *host, int ne0, int ne1, QMat &m, int rows_off, int stride, int phase);
 
 static Model g_model;
 Model &model() { return g_model; }
@@ -98,13 +98,13 @@ static int bind_mat(const char *name, int type, const void *host, int ne0, int n
     return CWEN_EINVAL;
   }
   if (!m.w) {
-    int rc = alloc_qmat(m, type, ne0, (total_rows + 15) / 16, total_rows);
+    int rc = alloc_qmat(m, type, ne0, total_rows, stride_mt == 2);
     if (rc) return rc;
   } else if (m.type != type) {
     set_error("cwen_cuda_upload: %s: all parts of a fused matrix must share one type", name);
     return CWEN_EINVAL;
   }
-  return upload_qmat_rows(type, host, ne0, ne1, m, rows_off / 16 * stride_mt + mt_phase, stride_mt);
+  return upload_qmat_rows(type, host, ne0, ne1, m, rows_off, stride_mt, mt_phase);
 }
 
 // A row-sharded matrix (the FFN and lm_head under a shard group): the full
@@ -268,7 +268,7 @@ static int alloc_state() {
   if (M.mtp_on) {
     CW_CHECK(cudaMalloc(&M.mtp_K, (size_t)ctx * KO * sizeof(float)));
     CW_CHECK(cudaMalloc(&M.mtp_V, (size_t)ctx * KO * sizeof(float)));
-    if ((rc = A(M.mtp_hprev, (size_t)H)) || (rc = A(M.mtp_x, (size_t)bm * H)) || (rc = A(M.mtp_cat, (size_t)2 * H)) ||
+    if ((rc = A(M.mtp_hprev, (size_t)H)) || (rc = A(M.mtp_x, (size_t)bm * H)) || (rc = A(M.mtp_cat, (size_t)bm * 2 * H)) ||
         (rc = A(M.mtp_out, (size_t)bm * H)) || (rc = A(M.mtp_emb, (size_t)bm * H)) || (rc = A(M.mtp_hin, (size_t)bm * H)))
       return rc;
     CW_CHECK(cudaMalloc(&M.mtp_draft, (size_t)3 * (bm + 1) * sizeof(int)));  // walk results per draft step
@@ -279,15 +279,22 @@ static int alloc_state() {
 
 // The lm_head GEMV into the logits of rows 0..B-1 (row-sharded under a
 // shard group: every GPU then holds all logits after the barrier).
-static cudaError_t lm_head_gemv(int B, cudaStream_t st) {
+// X: the rows (raw fp32, RMSNorm(X) * norm_w when norm_w is set) for an
+// engine whose kernel takes raw X; otherwise the prepared fragments are used.
+static cudaError_t lm_head_gemv(int B, const float *X, const float *norm_w, cudaStream_t st) {
   Model &M = g_model;
   Engine &E = engine();
-  const int V = M.d.n_vocab;
-  if (!shard().on()) return timed_gemv(M.lm_head, B, M.logits, V, EPI_STORE, st);
+  const int V = M.d.n_vocab, H = M.d.n_embd;
+  const bool raw = gemv_raw_x(E.gs);
+  auto run = [&]() {
+    return raw ? timed_gemv(M.lm_head, B, M.logits, V, EPI_STORE, st, X, H, norm_w)
+               : timed_gemv(M.lm_head, B, M.logits, V, EPI_STORE, st);
+  };
+  if (!shard().on()) return run();
   int r0, r1;
   shard_rows(V, 16, r0, r1);
   shard_target(E.gs, M.logits, r0);
-  const cudaError_t e = timed_gemv(M.lm_head, B, M.logits, V, EPI_STORE, st);
+  const cudaError_t e = run();
   shard_untarget(E.gs);
   if (e != cudaSuccess) return e;
   return shard_barrier(st);
@@ -328,15 +335,19 @@ static int run_layer_block(int l, int B, int pos0, cudaStream_t st) {
   // ssm_out reads the gated-norm rows raw, wo the attention combine's rows
   if (w.linear) CW_CHECK(timed_gemv(w.out_proj, B, M.x, H, EPI_ADD, st, M.gdn_out, M.Z));
   else CW_CHECK(timed_gemv(w.out_proj, B, M.x, H, EPI_ADD, st, M.attn_o, d.n_head * 256));
-  CW_CHECK(launch_norm_prep(M.x, w.post_norm, H, B, E.gs, nullptr, st));
-  nl++;
+  const bool raw = gemv_raw_x(E.gs);  // post_attention_norm inside the gate/up GEMV
+  if (!raw) {
+    CW_CHECK(launch_norm_prep(M.x, w.post_norm, H, B, E.gs, nullptr, st));
+    nl++;
+  }
   const bool sh = shard().on();
   int r0, r1;
   if (sh) {
     shard_rows(I, 16, r0, r1);
     shard_target(E.gs, M.h, r0);
   }
-  cudaError_t ge = timed_gemv(w.gate_up, B, M.h, I, EPI_SWIGLU, st);
+  cudaError_t ge = raw ? timed_gemv(w.gate_up, B, M.h, I, EPI_SWIGLU, st, M.x, H, w.post_norm)
+                       : timed_gemv(w.gate_up, B, M.h, I, EPI_SWIGLU, st);
   if (sh) {
     shard_untarget(E.gs);
     if (ge == cudaSuccess) ge = shard_barrier(st);
@@ -376,24 +387,34 @@ static int mtp_step_dev(int pos0, int B, const Toks16 &toks, const int *dtok, co
   const cwen_dims &d = M.d;
   MtpW &w = M.mtp;
   const int H = d.n_embd, I = d.n_ff;
+  const bool raw = gemv_raw_x(E.gs);
   CW_CHECK(launch_embed(M.tok_embd, H, d.n_vocab, toks, B, M.mtp_emb, M.err, st, dtok));
-  CW_CHECK(launch_cat_norm_prep(M.mtp_emb, hin, w.enorm, w.hnorm, H, B, E.gs, st));
-  CW_CHECK(timed_gemv(w.eh_proj, B, M.mtp_x, H, EPI_STORE, st));
-  CW_CHECK(launch_norm_prep(M.mtp_x, w.attn_norm, H, B, E.gs, nullptr, st));
-  CW_CHECK(timed_gemv(w.in_proj, B, M.proj, M.PS, EPI_STORE, st));
+  CW_CHECK(launch_cat_norm_prep(M.mtp_emb, hin, w.enorm, w.hnorm, H, B, E.gs, st, raw ? M.mtp_cat : nullptr));
+  if (raw) {
+    CW_CHECK(timed_gemv(w.eh_proj, B, M.mtp_x, H, EPI_STORE, st, M.mtp_cat, 2 * H));
+    CW_CHECK(timed_gemv(w.in_proj, B, M.proj, M.PS, EPI_STORE, st, M.mtp_x, H, w.attn_norm));
+  } else {
+    CW_CHECK(timed_gemv(w.eh_proj, B, M.mtp_x, H, EPI_STORE, st));
+    CW_CHECK(launch_norm_prep(M.mtp_x, w.attn_norm, H, B, E.gs, nullptr, st));
+    CW_CHECK(timed_gemv(w.in_proj, B, M.proj, M.PS, EPI_STORE, st));
+  }
   AttnArgs a;
   a.proj = M.proj; a.ps = M.PS; a.nh = d.n_head; a.nkv = d.n_head_kv; a.B = B;
   a.qn = w.q_norm; a.kn = w.k_norm; a.rope = M.rope; a.pos0 = pos0; a.t0 = 1;  // the nextn stream starts at slot 1
   a.qbuf = M.qbuf; a.Kc = M.mtp_K; a.Vc = M.mtp_V; a.part = M.attn_part; a.nch_max = M.nch_max; a.out = M.attn_o;
   CW_CHECK(launch_attention(a, E.gs, st));
   CW_CHECK(timed_gemv(w.out_proj, B, M.mtp_x, H, EPI_ADD, st, M.attn_o, d.n_head * 256));
-  CW_CHECK(launch_norm_prep(M.mtp_x, w.post_norm, H, B, E.gs, nullptr, st));
-  CW_CHECK(timed_gemv(w.gate_up, B, M.h, I, EPI_SWIGLU, st));
+  if (raw) {
+    CW_CHECK(timed_gemv(w.gate_up, B, M.h, I, EPI_SWIGLU, st, M.mtp_x, H, w.post_norm));
+  } else {
+    CW_CHECK(launch_norm_prep(M.mtp_x, w.post_norm, H, B, E.gs, nullptr, st));
+    CW_CHECK(timed_gemv(w.gate_up, B, M.h, I, EPI_SWIGLU, st));
+  }
   CW_CHECK(timed_gemv(w.down, B, M.mtp_x, H, EPI_ADD, st, M.h, I));
   CW_CHECK(launch_norm_prep(M.mtp_x, w.shared_head_norm, H, B, E.gs, hout, st));
-  // embed, cat_norm_prep, three norm_preps, attention prep/split/combine; the
+  // embed, cat_norm_prep, the norm_preps, attention prep/split/combine; the
   // GEMVs (and any X preparation of theirs) are counted by timed_gemv
-  E.prof.launches += 8;
+  E.prof.launches += raw ? 6 : 8;
   return CWEN_OK;
 }
 
@@ -447,15 +468,19 @@ int forward_block_impl(const int *toks, int B, int nlogits) {
   M.pending_nlog = 0;
   if (nlogits != 0) {
     const int r0 = nlogits == -1 ? B - 1 : 0, nr = nlogits == -1 ? 1 : nlogits;
-    CW_CHECK(launch_norm_prep(M.x + (size_t)r0 * d.n_embd, M.output_norm, d.n_embd, nr, E.gs, nullptr, st));
-    CW_CHECK(lm_head_gemv(nr, st));
+    const float *xr = M.x + (size_t)r0 * d.n_embd;
+    if (!gemv_raw_x(E.gs)) {
+      CW_CHECK(launch_norm_prep(xr, M.output_norm, d.n_embd, nr, E.gs, nullptr, st));
+      E.prof.launches++;
+    }
+    CW_CHECK(lm_head_gemv(nr, xr, M.output_norm, st));
     // blk = toks of the block: row j's argmax is checked against toks[j+1]
     Toks16 blk;
     memset(&blk, 0, sizeof blk);
     memcpy(blk.t, toks + r0, (size_t)(B - r0) * sizeof(int));
     CW_CHECK(launch_argmax_walk(M.logits, d.n_vocab, d.n_vocab, nr, nlogits == -1 ? 0 : nr - 1, blk, M.best,
                                 M.walk, st));
-    E.prof.launches += 2;
+    E.prof.launches += 1;
     CW_CHECK(cudaMemcpyAsync(M.h_walk, M.walk, (size_t)(nr + 2) * sizeof(int), cudaMemcpyDeviceToHost, st));
     M.pending_nlog = nr;
   }
@@ -848,7 +873,7 @@ int cwen_cuda_mtp_draft(int pend, int *out, int max_d) {
     tk.t[0] = pend;
     rc = mtp_step_dev(pos_n + 1 + t, 1, tk, t ? M.mtp_draft + 3 * (t - 1) + 1 : nullptr, hin, hout, st);
     if (rc) return rc;
-    CW_CHECK(lm_head_gemv(1, st));
+    CW_CHECK(lm_head_gemv(1, hout, nullptr, st));
     CW_CHECK(launch_argmax_walk(M.logits, V, V, 1, 0, none, M.best, M.mtp_draft + 3 * t, st));
     E.prof.launches += 1;
     hin = hout;

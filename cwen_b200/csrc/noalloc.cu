@@ -1,10 +1,12 @@
 // Verify GEMV whose scratch lives in statically allocated device memory.
 //
-// cwen_cuda_gemvb needs the split-K partials, the per-tile arrival counters
-// and (for shapes that prepare X first) the prepared X tiles of the engine's
-// scratch, which cwen_cuda_init allocates.  This variant runs the same
-// kernels, chosen by the same shape rule, on file-scope __device__ arrays
-// instead, so that a call allocates nothing and gives the same bits.  It is
+// cwen_cuda_gemvb needs scratch of the engine, which cwen_cuda_init
+// allocates: for the default kernel the buffer its X operands are converted
+// into and the per-phase flags that publish them; for the earlier kernels the
+// split-K partials, the per-tile arrival counters and the prepared X tiles.
+// This variant runs the same kernels, chosen by the same shape rule, on
+// file-scope __device__ arrays instead, so that a call allocates nothing and
+// gives the same bits.  It is
 // meant for callers that must not call cudaMalloc on their per-call path: a
 // host framework whose caching allocator already reserved the device memory
 // (a cudaMalloc there fails or fragments its pool), and latency-critical
@@ -12,11 +14,12 @@
 // the other streams.
 //
 // Limits (the arrays are sized for them; every GPU that loads the library
-// holds NA_STATIC_BYTES, about 22 MiB, of them until the process exits):
+// holds NA_STATIC_BYTES, about 24 MiB, of them until the process exits):
 //   K <= 32768, B <= 16, at most 2048 tiles of 512 rows (M <= 1,048,576),
 //   at most 320 CTAs of split-K partials.
 #include "engine.cuh"
 #include "qgemv.cuh"
+#include "qmv.cuh"
 
 namespace cw {
 namespace {
@@ -33,9 +36,14 @@ static __device__ __align__(256) int g_na_xexp[QG_MAXB];
 static __device__ __align__(256) float g_na_ws[NA_WS_FLOATS];
 static __device__ __align__(256) int g_na_cnt[NA_MAX_TILES];
 static __device__ __align__(256) int g_na_err[1];
+// the default kernel's X operands (per K phase of 512: a 128-byte header and
+// 16 blocks x 4 n-tiles x 512 bytes) and its phase flags (zero at load)
+constexpr int NA_PHASES = NA_KMAX / 512;
+static __device__ __align__(256) uint8_t g_na_qx[(size_t)NA_PHASES * (128 + 16 * 4 * 512)];
+static __device__ __align__(256) int g_na_qflag[NA_PHASES];
 constexpr size_t NA_STATIC_BYTES = sizeof(g_na_xf) + sizeof(g_na_xexp) + sizeof(g_na_ws) + sizeof(g_na_cnt) +
-                                   sizeof(g_na_err);
-static_assert(NA_STATIC_BYTES > (21u << 20) && NA_STATIC_BYTES < (23u << 20), "documented as about 22 MiB");
+                                   sizeof(g_na_err) + sizeof(g_na_qx) + sizeof(g_na_qflag);
+static_assert(NA_STATIC_BYTES > (23u << 20) && NA_STATIC_BYTES < (25u << 20), "documented as about 24 MiB");
 
 struct NaDevice {
   bool ready = false;
@@ -59,12 +67,18 @@ int na_setup(int device, int n_sm) {
   if (e == cudaSuccess) e = cudaGetSymbolAddress((void **)&s.ws, g_na_ws);
   if (e == cudaSuccess) e = cudaGetSymbolAddress((void **)&s.cnt, g_na_cnt);
   if (e == cudaSuccess) e = cudaGetSymbolAddress((void **)&s.err, g_na_err);
+  if (e == cudaSuccess) e = cudaGetSymbolAddress((void **)&s.qx, g_na_qx);
+  if (e == cudaSuccess) e = cudaGetSymbolAddress((void **)&s.qflag, g_na_qflag);
   if (cur != device) {
     const cudaError_t e2 = cudaSetDevice(cur);
     if (e == cudaSuccess) e = e2;
   }
   if (e != cudaSuccess) return cuda_fail(e, "cwen_cuda_gemvb_static: static scratch lookup");
   s.kmax = NA_KMAX;
+  if (qmv_xbuf_bytes(NA_KMAX) > sizeof(g_na_qx) || qmv_nflags(NA_KMAX) > NA_PHASES) {
+    set_error("cwen_cuda_gemvb_static: static X operand buffer too small");
+    return CWEN_EINVAL;
+  }
   s.G = n_sm < NA_MAX_CTAS ? n_sm : NA_MAX_CTAS;  // the engine's grid when it fits
   s.max_tiles = NA_MAX_TILES;
   D.s = s;
@@ -105,6 +119,7 @@ extern "C" int cwen_cuda_gemvb_static(int wid, const float *dX, int xs, float *d
   const int rc = na_setup(E.device, E.n_sm);
   if (rc) return rc;
   GemvScratch &s = g_na[E.device].s;
+  s.kern = E.gs.kern;
   s.tc = E.gs.tc;  // the engine's kernel (its weights are in that kernel's layout)
   cudaStream_t st = stream ? (cudaStream_t)stream : E.stream;
   // The arrival counters reset themselves at the end of a complete call;

@@ -44,6 +44,7 @@
 #include "common.cuh"
 #include "qgemv.cuh"
 #include "qgemv_dev.cuh"
+#include "qmv.cuh"
 #include "rowops.cuh"
 #include "rowprep.cuh"
 #include "sm100.cuh"
@@ -90,7 +91,7 @@ __global__ void repack_kernel(uint8_t *dst, int dst_kp, const uint8_t *src, int 
 
 cudaError_t qmat_repack(const QMat &dst, const uint8_t *src, int M, int mt_off, int mt_stride, cudaStream_t st) {
   const int src_mt = (M + 15) / 16;
-  if (dst.K % 64 || mt_off < 0 || mt_stride < 1 || mt_off + (src_mt - 1) * mt_stride >= dst.n_mt)
+  if (dst.kern == GK_QMV || dst.K % 64 || mt_off < 0 || mt_stride < 1 || mt_off + (src_mt - 1) * mt_stride >= dst.n_mt)
     return cudaErrorInvalidValue;
   if (!dst.tc) return mma::repack(dst, src, M, mt_off, mt_stride, st);
   const long long total = (long long)M * (dst.K / 64);
@@ -843,7 +844,9 @@ static bool gemv_all_split(const QMat &m, const GemvScratch &s) {
 
 static cudaError_t gemv_launch(const QMat &m, int B, float *Y, int ys, int epi, GemvScratch &s, cudaStream_t st,
                                const float *xr, int xrs, const float *norm_w = nullptr, bool want_stats = false) {
-  if (B < 1 || B > QG_MAXB || m.K % 64 || m.K > s.kmax || !m.w || !s.err || m.tc != s.tc) return cudaErrorInvalidValue;
+  if (B < 1 || B > QG_MAXB || m.K % 64 || m.K > s.kmax || !m.w || !s.err || m.tc != s.tc || m.kern != s.kern ||
+      m.kern == GK_QMV)
+    return cudaErrorInvalidValue;
   if (epi == EPI_SWIGLU && (m.n_mt % 2)) return cudaErrorInvalidValue;
   GemvArgs a;
   a.w = m.w;
@@ -920,12 +923,14 @@ cudaError_t gemv_run(const QMat &m, int B, float *Y, int ys, int epi, GemvScratc
 }
 
 bool gemv_uses_local_x(const QMat &m, const float *X, int xs, const GemvScratch &s) {
+  if (m.kern == GK_QMV) return true;  // raw X, one launch
   return gemv_local_x(m, s) && (reinterpret_cast<uintptr_t>(X) & 15) == 0 && xs % 4 == 0;
 }
 
 cudaError_t gemv_run_x(const QMat &m, const float *X, int xs, int B, float *Y, int ys, int epi, GemvScratch &s,
                        cudaStream_t st, bool want_stats) {
   if (!X || xs < m.K) return cudaErrorInvalidValue;
+  if (m.kern == GK_QMV) return qmv_run(m, X, xs, nullptr, B, Y, ys, epi, s, st);
   // the local-X prologue reads X as float4: rows must start on 16 bytes
   if (gemv_local_x(m, s) && (reinterpret_cast<uintptr_t>(X) & 15) == 0 && xs % 4 == 0)
     return gemv_launch(m, B, Y, ys, epi, s, st, X, xs, nullptr,
@@ -935,6 +940,7 @@ cudaError_t gemv_run_x(const QMat &m, const float *X, int xs, int B, float *Y, i
 }
 
 bool gemv_norm_fused(const QMat &m, const float *X, int xs, int B, const GemvScratch &s) {
+  if (m.kern == GK_QMV) return true;  // the norm is folded into the kernel
   return gemv_local_x(m, s) && (reinterpret_cast<uintptr_t>(X) & 15) == 0 && xs % 4 == 0 && s.stat_ok && s.stat_y == X && s.stat_ys == xs && s.stat_len == m.K &&
          s.stat_cols >= B && s.stat_g >= 1 && s.stat_g <= 160;
 }
@@ -942,6 +948,7 @@ bool gemv_norm_fused(const QMat &m, const float *X, int xs, int B, const GemvScr
 cudaError_t gemv_run_xn(const QMat &m, const float *X, int xs, const float *w, int B, float *Y, int ys, int epi,
                         GemvScratch &s, cudaStream_t st) {
   if (!X || !w || xs < m.K) return cudaErrorInvalidValue;
+  if (m.kern == GK_QMV) return qmv_run(m, X, xs, w, B, Y, ys, epi, s, st);
   if (gemv_norm_fused(m, X, xs, B, s)) return gemv_launch(m, B, Y, ys, epi, s, st, X, xs, w, false);
   CW_TRY(launch_norm_prep(X, w, m.K, B, s, nullptr, st));
   return gemv_launch(m, B, Y, ys, epi, s, st, nullptr, 0);
@@ -950,6 +957,7 @@ cudaError_t gemv_run_xn(const QMat &m, const float *X, int xs, const float *w, i
 // One-time kernel attributes (called at engine set-up).
 cudaError_t qgemv_configure() {
   cudaError_t e;
+  if ((e = qmv_configure()) != cudaSuccess) return e;
   if ((e = mma::configure()) != cudaSuccess) return e;
   if ((e = carveout_max(repack_kernel<2>)) != cudaSuccess) return e;
   if ((e = carveout_max(repack_kernel<8>)) != cudaSuccess) return e;

@@ -17,9 +17,19 @@ namespace cw {
 // [2][512]] (QgStage); mma.sync kernel [m-tile][576-byte chunk in A-fragment
 // order] (qgemv_mma.cu).  Same stage size either way.  The m-tile count is
 // padded to whole tiles (zero padding).
+// The verify-GEMV kernels an engine can run (chosen once at cwen_cuda_init;
+// a matrix is stored in the layout of that kernel): the warp-level mma.sync
+// kernel of qgemv_mma.cu (default), the tcgen05 kernel of qgemv.cu, and
+// qmv.cu (whole rows per CTA, no split-K reduction).
+enum { GK_MMA = 0, GK_QMV = 1, GK_TC = 2 };
+
 struct QMat {
   uint8_t *w = nullptr;  // device
-  bool tc = false;       // layout of the tcgen05 kernel (else of the mma.sync kernel)
+  int kern = GK_MMA;     // layout of this kernel
+  bool tc = false;       // kern == GK_TC
+  int n_ht = 0;          // qmv layout: 8-row half-tiles
+  bool pair = false;     // qmv layout: gate/up rows interleaved by half-tile (SwiGLU)
+  int G = 0;             // qmv layout: CTAs the rows are partitioned over
   int type = 0;          // 2 = Q4_0, 8 = Q8_0
   int K = 0;             // row length
   int n_mt = 0;          // m-tiles (16 rows) holding rows; storage is padded to QG_TILE_MT
@@ -57,7 +67,12 @@ struct GemvScratch {
   // Which kernel the engine runs (chosen once, before any weight upload, so
   // every batch size of an engine takes the same arithmetic): the tcgen05
   // kernel of qgemv.cu, or the mma.sync kernel of qgemv_mma.cu (default).
-  bool tc = false;
+  int kern = GK_MMA;
+  bool tc = false;  // kern == GK_TC
+  // qmv: X operands converted once per call, published per K phase
+  uint8_t *qx = nullptr;
+  int *qflag = nullptr;  // zero-initialised
+  int qepoch = 0;
   uint4 *xf = nullptr;   // X operands, >= (Kmax/32) * 128 uint4 (2 KB per 32-block)
   int *xexp = nullptr;   // [16] per-column exponents
   float *ws = nullptr;   // split-K partials [G][2][WS_TILE_FLOATS]
@@ -80,6 +95,9 @@ struct GemvScratch {
   float *yp[QG_MAX_PEERS] = {};
 };
 size_t gemv_scratch_ws_floats(int G);
+// The engine's kernel takes raw fp32 X (and an RMSNorm weight) in one launch:
+// callers pass rows instead of preparing GEMV fragments first.
+inline bool gemv_raw_x(const GemvScratch &s) { return s.kern == GK_QMV; }
 
 // Repack `M` GGUF rows (Q4_0 18 B/block or Q8_0 34 B/block) already on the
 // device at `src` into `dst`: source row r lands in m-tile

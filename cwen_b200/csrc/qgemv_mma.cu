@@ -1,15 +1,19 @@
 // Batched Q4_0 / Q8_0 verify GEMV on warp-level tensor-core MMAs
-// (mma.sync m16n8k16), the engine's default kernel; the same arithmetic and
-// work split as the tcgen05 kernel of qgemv.cu, with its own weight layout.
+// (mma.sync m16n8k16), the engine's default kernel; the work split of the
+// tcgen05 kernel of qgemv.cu, with its own weight and X layouts.
 //
 // Replaces the reference's gemvb()/gemv() (run.c:1577-1680, 1419-1527) and
 // the row dots under them (dot_q4_0 run.c:1009-1025, dot_nib16 run.c:432,
 // dot_q8_0 run.c:1248-1274).
 //
-// Arithmetic.  Per 16 rows x 32 weights x 8 columns four m16n8k16 MMAs (the
-// f16 hi and lo parts of X, both k halves) accumulate one fp32 block partial
-// (products exact, fp32 accumulate in the MMA); one FFMA per element applies
-// the block's f16 scale: acc = fma(d, c, acc).  (q - 8) is exact in f16.
+// Arithmetic.  Columns come in n-tiles of 4: B-operand columns 0..3 hold the
+// f16 hi parts of the 4 columns and 4..7 their lo parts.  Per 16 rows x 32
+// weights and n-tile two chained m16n8k16 MMAs (k 0..15, k 16..31; products
+// exact, fp32 accumulate) give the block partials of the hi and the lo
+// halves; one FFMA per element applies the block's f16 scale, acc = fma(d,
+// c, acc), and the hi and lo sums are added at the end of the tile.  (q - 8)
+// is exact in f16.  Two MMAs per 16 x 32 weights at B <= 4 (one column per
+// decode step), 4 at B <= 8, 6 at a 9-row verify block.
 //
 // Weight layout.  Rows in 16-row m-tiles, m-tiles in 512-row tiles of 32; per
 // (m-tile, pair of 32-blocks) one 576-byte chunk [512 B nibbles in mma
@@ -17,8 +21,9 @@
 // scales]), stored [tile][k-pair][m-tile] so that one (tile, k-pair) is one
 // contiguous 18 KB / 34 KB stage -- the same stage size as the tcgen05 layout.
 //
-// X operands.  Per (32-block, n-tile of 8 columns) 64 uint4: 32 lanes of hi
-// parts then 32 of lo parts; lane (g, t) holds column g's
+// X operands.  Per (32-block, n-tile of 4 columns) 32 uint4; lane (g, t) of
+// the B operand holds, of column 4n + g % 4 (hi parts for g < 4, lo parts for
+// g >= 4),
 //   (x[4t], x[4t+2]) (x[4t+1], x[4t+3]) (x[4t+16], x[4t+18]) (x[4t+17], x[4t+19]).
 //
 // Work split, pipeline and the split-tile reduction: as in qgemv.cu (bulk-copy
@@ -121,17 +126,30 @@ cudaError_t repack(const QMat &dst, const uint8_t *src, int M, int mt_off, int m
   return cudaGetLastError();
 }
 
-// Apply the epilogue for one warp's accumulators (rows of m-tiles mt0,
-// mt0+1).  Lane (g, t) holds, per n-tile n, rows g and g+8 of columns
-// n*8 + 2t and n*8 + 2t + 1.
+// Fold the lo-part accumulators into the hi-part ones: lane (g, t < 2) holds
+// B columns 2t, 2t+1 (hi parts), lane (g, t + 2) the same columns' lo parts.
+// Afterwards lanes t < 2 hold the sums (hi + lo, in that order).
+template <int NT>
+CW_DEV void fold_lo(float (&acc)[2][NT][4]) {
+#pragma unroll
+  for (int mt = 0; mt < 2; mt++)
+#pragma unroll
+    for (int n = 0; n < NT; n++)
+#pragma unroll
+      for (int i = 0; i < 4; i++) acc[mt][n][i] += __shfl_xor_sync(0xffffffffu, acc[mt][n][i], 2);
+}
+
+// Apply the epilogue for one warp's folded accumulators (rows of m-tiles
+// mt0, mt0+1; lanes t < 2 carry the columns n*4 + 2t + {0, 1}).
 template <int NT>
 CW_DEV void gemv_epilogue(const GemvArgs &a, int mt0, bool has1, const float (&acc)[2][NT][4], int g, int t,
                           const float *xun) {
+  if (t >= 2) return;
 #pragma unroll
   for (int n = 0; n < NT; n++) {
 #pragma unroll
     for (int i = 0; i < 4; i++) {
-      const int col = n * 8 + 2 * t + (i & 1);
+      const int col = n * 4 + 2 * t + (i & 1);
       if (col >= a.B) continue;
       const float sc = xun ? xun[col] : __int_as_float((127 - __ldg(a.xexp + col)) << 23);
       const int rr = g + ((i >> 1) << 3);
@@ -154,85 +172,77 @@ CW_DEV void gemv_epilogue(const GemvArgs &a, int mt0, bool has1, const float (&a
   }
 }
 
-// Shared-memory layout of the GEMV.  X fragments per (32-block, n-tile of 8
-// columns): 64 uint4 (32 lanes of hi parts, then 32 of lo parts) = 1 KB, so
-// one k-pair of NT n-tiles is NT * 2 KB.
+
 template <int TYPE, int NT, bool XL = false>
 struct QgLayout {
   static constexpr int CHUNK = TYPE == 8 ? 1088 : 576;       // one m-tile x one k-pair
   static constexpr int QB = TYPE == 8 ? 1024 : 512;          // its quant bytes (scales follow)
   static constexpr int WB = QG_TILE_MT * CHUNK;              // weights of one (tile, k-pair)
-  static constexpr int XKP = NT * 2048;                      // X fragments of one k-pair
-  static constexpr int XB = XL ? 0 : XKP;                    // ... streamed with each stage
+  static constexpr int XB = XL ? 0 : NT * 1024;              // X fragments of one k-pair (streamed)
   static constexpr int STAGE = WB + XB;
   static constexpr int STAGES = TYPE == 8 ? 5 : 8;
   static constexpr int BAR_OFF = STAGES * STAGE;
-  // local-X variant: the CTA's k-range of X fragments, resident (<= QG_XL_KP k-pairs)
+  // local-X variant: the CTA's k-range of X fragments, resident (<= QG_XL_KP k-pairs x 4 n-tiles)
   static constexpr int XL_OFF = BAR_OFF + 256;
-  static constexpr int XL_BYTES = XL ? QG_XL_KP * XKP : 0;
-  // per column: 2^-e [16] floats, the warps' output sums of squares [16][16],
-  // the prologue's per-warp column maxima [16]
-  static constexpr int XE_OFF = XL_OFF + XL_BYTES;
-  static constexpr int SMEM = XE_OFF + (XL ? 64 + 16 * 16 * 4 + 16 * 4 : 0);
+  static constexpr int XL_BYTES = XL ? QG_XL_KP * 4 * 1024 : 0;
+  static constexpr int XE_OFF = XL_OFF + XL_BYTES;  // per column: 2^-e [16] floats, scratch [16][16] floats
+  static constexpr int SMEM = XE_OFF + (XL ? 64 + 16 * 16 * 4 : 0);
   static_assert(WB % 16 == 0 && XB % 16 == 0 && STAGE % 16 == 0, "bulk copies need 16-byte multiples");
   static_assert(SMEM <= 227 * 1024, "shared memory");
 };
 
+// Persistent stream-K GEMV: warps 0..15 consume (warp w owns m-tiles 2w, 2w+1
+// of the current 512-row tile); lane 0 of warp 16 streams the weights and
+// lane 0 of warp 17 the X fragments.
 // Local X (run by the 16 consumer warps once, after pdl_wait): the CTA's
 // k-range [64*ka0, 64*(ka0+nkp)) of every column of the raw rows X becomes
 // f16 hi/lo fragments in shared memory, scaled by the CTA's own power of two
 // 2^e (max |x| over the range in [2^14, 2^15)); xun[col] = 2^-e unscales the
 // CTA's results.  The fragments hold the same values and layout gemv_prep_x
-// emits, except for the exponent's range.  Every warp works: a column gets
-// 16 / B warps (at least one), each lane loads 8 values per item (item =
-// 32-block x lane quad t), keeps them in registers while the column maxima
-// are combined through shared memory (one barrier), then converts them.
+// emits, except for the exponent's range.  Warp b owns column b; lane l holds
+// the 32-blocks l and l + 32 of the range in registers (one load round trip),
+// so 2 * nkp <= 64.
 template <int NT>
-CW_DEV void x_local_prologue(const GemvArgs &a, uint4 *xl, float *xun, float *cmax, int ka0, int nkp) {
+CW_DEV void x_local_prologue(const GemvArgs &a, uint4 *xl, float *xun, int ka0, int nkp) {
   constexpr int NTH = QG_CONS_WARPS * 32;
-  constexpr int MAXI = QG_XL_KP * 2 * 4 / 32;  // items per lane with one warp per column
-  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-  const int nitems = 2 * nkp * 4;
-  const int wpc = a.B >= QG_CONS_WARPS ? 1 : QG_CONS_WARPS / a.B;  // warps per column
-  const int b = w / wpc, sub = w - b * wpc;
-  const bool live = b < a.B;
-  float4 v[MAXI][2];
-  float m = 0.f, ss = 0.f;
-  if (live) {
-    const float *x = a.xr + (size_t)b * a.xrs + (size_t)ka0 * 64;
-    const float *wn = a.xw ? a.xw + (size_t)ka0 * 64 : nullptr;
+  const int lane = threadIdx.x & 31, b = threadIdx.x >> 5;
+  const int nblk = 2 * nkp;
+  if (b < a.B) {
+    const float4 *x = reinterpret_cast<const float4 *>(a.xr + (size_t)b * a.xrs + (size_t)ka0 * 64);
+    const float4 *wn = reinterpret_cast<const float4 *>(a.xw + (size_t)ka0 * 64);
     // RMSNorm: the row's sum of squares from the per-CTA partials of the GEMV
     // that wrote it, in slot order then a fixed xor tree (every CTA, every B)
+    float ss = 0.f;
     if (a.xw)
 #pragma unroll
       for (int i = 0; i < 5; i++)
         if (lane + 32 * i < a.st_g) ss += __ldcg(a.st_in + (size_t)(lane + 32 * i) * QG_STAT_COLS + b);
+    // pass 1: max |w x| (or |x|) over the range, block j = 0 kept in registers;
+    // pass 2 converts block 0 from registers and reloads block 1 (cache hits)
+    float4 v[8];
+    float m = 0.f;
 #pragma unroll
-    for (int j = 0; j < MAXI; j++) {
-      const int it = (sub + j * wpc) * 32 + lane;
-      if (it < nitems) {
-        const int kb = it >> 2, t = it & 3;
-        float4 p = __ldg(reinterpret_cast<const float4 *>(x + kb * 32 + 4 * t));
-        float4 q = __ldg(reinterpret_cast<const float4 *>(x + kb * 32 + 16 + 4 * t));
+    for (int j = 0; j < 2; j++) {
+      const int kb = lane + 32 * j;
+      if (kb < nblk) {
+        float4 u[8];
+#pragma unroll
+        for (int q = 0; q < 8; q++) u[q] = __ldg(x + kb * 8 + q);
         if (a.xw) {
-          const float4 wp = __ldg(reinterpret_cast<const float4 *>(wn + kb * 32 + 4 * t));
-          const float4 wq = __ldg(reinterpret_cast<const float4 *>(wn + kb * 32 + 16 + 4 * t));
-          p = make_float4(wp.x * p.x, wp.y * p.y, wp.z * p.z, wp.w * p.w);
-          q = make_float4(wq.x * q.x, wq.y * q.y, wq.z * q.z, wq.w * q.w);
+#pragma unroll
+          for (int q = 0; q < 8; q++) {
+            const float4 w4 = __ldg(wn + kb * 8 + q);
+            u[q] = make_float4(w4.x * u[q].x, w4.y * u[q].y, w4.z * u[q].z, w4.w * u[q].w);
+          }
         }
-        v[j][0] = p;
-        v[j][1] = q;
-        m = fmaxf(m, fmaxf(fmaxf(fabsf(p.x), fabsf(p.y)), fmaxf(fabsf(p.z), fabsf(p.w))));
-        m = fmaxf(m, fmaxf(fmaxf(fabsf(q.x), fabsf(q.y)), fmaxf(fabsf(q.z), fabsf(q.w))));
+#pragma unroll
+        for (int q = 0; q < 8; q++) {
+          m = fmaxf(m, fmaxf(fmaxf(fabsf(u[q].x), fabsf(u[q].y)), fmaxf(fabsf(u[q].z), fabsf(u[q].w))));
+          if (j == 0) v[q] = u[q];
+        }
       }
     }
     m = warp_max(m);
-    if (lane == 0) cmax[w] = m;
-  }
-  named_bar(1, NTH);
-  if (live) {
-    m = 0.f;
-    for (int i = 0; i < wpc; i++) m = fmaxf(m, cmax[b * wpc + i]);
     float s = 1.f;
     if (a.xw) {
       s = 1.f / sqrtf(warp_sum(ss) / (float)(a.kp * 64) + 1e-6f);
@@ -241,48 +251,52 @@ CW_DEV void x_local_prologue(const GemvArgs &a, uint4 *xl, float *xun, float *cm
     const int e = xfrag_exponent(m);
     // ((w x) s) 2^e == (w x) (s 2^e) exactly: 2^e only shifts the exponent
     const float sc = s * __int_as_float((127 + e) << 23);
-    if (sub == 0 && lane == 0) xun[b] = __int_as_float((127 - e) << 23);
-    uint4 *ob = xl + (b >> 3) * 64 + (b & 7) * 4;
+    if (lane == 0) xun[b] = __int_as_float((127 - e) << 23);
+#pragma unroll 1
+    for (int j = 0; j < 2; j++) {
+      const int kb = lane + 32 * j;
+      if (kb < nblk) {
+        if (j == 1) {
 #pragma unroll
-    for (int j = 0; j < MAXI; j++) {
-      const int it = (sub + j * wpc) * 32 + lane;
-      if (it < nitems) {
-        const int kb = it >> 2, t = it & 3;
-        // B operand lane (col & 7, t): (x[4t], x[4t+2]) (x[4t+1], x[4t+3]) (x[4t+16], x[4t+18]) (x[4t+17], x[4t+19])
-        const float r[8] = {v[j][0].x, v[j][0].z, v[j][0].y, v[j][0].w, v[j][1].x, v[j][1].z, v[j][1].y, v[j][1].w};
-        uint32_t hw[4], lw[4];
+          for (int q = 0; q < 8; q++) v[q] = __ldg(x + kb * 8 + q);
+          if (a.xw) {
 #pragma unroll
-        for (int i = 0; i < 4; i++) {
-          const float v0 = r[2 * i] * sc, v1 = r[2 * i + 1] * sc;
-          const half h0 = __float2half_rn(v0), h1 = __float2half_rn(v1);
-          const half l0 = __float2half_rn(v0 - __half2float(h0)), l1 = __float2half_rn(v1 - __half2float(h1));
-          hw[i] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
-          lw[i] = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
+            for (int q = 0; q < 8; q++) {
+              const float4 w4 = __ldg(wn + kb * 8 + q);
+              v[q] = make_float4(w4.x * v[q].x, w4.y * v[q].y, w4.z * v[q].z, w4.w * v[q].w);
+            }
+          }
         }
-        uint4 *o = ob + (size_t)kb * NT * 64 + t;
-        o[0] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-        o[32] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+        const float *r = reinterpret_cast<const float *>(v);
+        // B operand lane (col & 3, t): (x[4t], x[4t+2]) (x[4t+1], x[4t+3]) (x[4t+16], x[4t+18]) (x[4t+17], x[4t+19])
+#pragma unroll
+        for (int t = 0; t < 4; t++) {
+          const int js[8] = {4 * t, 4 * t + 2, 4 * t + 1, 4 * t + 3, 4 * t + 16, 4 * t + 18, 4 * t + 17, 4 * t + 19};
+          uint32_t hw[4], lw[4];
+#pragma unroll
+          for (int i = 0; i < 4; i++) {
+            const float v0 = r[js[2 * i]] * sc, v1 = r[js[2 * i + 1]] * sc;
+            const half h0 = __float2half_rn(v0), h1 = __float2half_rn(v1);
+            const half l0 = __float2half_rn(v0 - __half2float(h0)), l1 = __float2half_rn(v1 - __half2float(h1));
+            hw[i] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
+            lw[i] = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
+          }
+          uint4 *o = xl + ((size_t)kb * NT + (b >> 2)) * 32 + (b & 3) * 4 + t;
+          o[0] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+          o[16] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+        }
       }
     }
+  } else if (lane == 0 && b < 16) {
+    xun[b] = 1.f;  // padding column
   }
-  if (threadIdx.x >= a.B && threadIdx.x < 16) xun[threadIdx.x] = 1.f;  // padding column
   named_bar(1, NTH);
 }
 
-// Persistent stream-K GEMV: warps 0..15 consume (warp w owns m-tiles 2w, 2w+1
-// of the current 512-row tile); lane 0 of warp 16 streams the weights and
-// lane 0 of warp 17 the X fragments.
-//
-// Per m-tile, 32-block and n-tile of 8 columns, four m16n8k16 MMAs chain into
-// one fp32 result c: (k 0..15, hi), (k 0..15, lo), (k 16..31, hi),
-// (k 16..31, lo) -- the f16 hi and lo parts of X are two B operands, so c
-// holds the block dot of 8 whole columns and one FFMA per element applies the
-// block's scale: acc = fma(d, c, acc).
 template <int TYPE, int NT, bool XL>
 __global__ void __launch_bounds__(QGM_THREADS, 1) qgemv_kernel(GemvArgs a) {
   using Lay = QgLayout<TYPE, NT, XL>;
   constexpr int S = Lay::STAGES;
-  constexpr int NC4 = 2 * NT;  // float4 column groups of a split-tile row
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t *full = reinterpret_cast<uint64_t *>(smem + Lay::BAR_OFF);
   uint64_t *empty = full + S;
@@ -381,8 +395,7 @@ __global__ void __launch_bounds__(QGM_THREADS, 1) qgemv_kernel(GemvArgs a) {
   float *wst = XL ? xun + 16 + warp * 16 : nullptr;  // this warp's output sums of squares per column
   if (XL && a.st_out && lane < 16) wst[lane] = 0.f;
   if (XL) {
-    x_local_prologue<NT>(a, reinterpret_cast<uint4 *>(smem + Lay::XL_OFF), xun, xun + 16 + 16 * 16, ka0,
-                         (int)(u_end - u_begin));
+    x_local_prologue<NT>(a, reinterpret_cast<uint4 *>(smem + Lay::XL_OFF), xun, ka0, (int)(u_end - u_begin));
     if (threadIdx.x == 0) mbar_arrive(xready);
   }
   const float zero4[4] = {0.f, 0.f, 0.f, 0.f};
@@ -418,64 +431,43 @@ __global__ void __launch_bounds__(QGM_THREADS, 1) qgemv_kernel(GemvArgs a) {
       }
       if (ok && has0) {
         const uint8_t *stg = smem + st * Lay::STAGE;
-        const uint4 *xs = XL ? reinterpret_cast<const uint4 *>(smem + Lay::XL_OFF) + (size_t)(ka + i - ka0) * (NT * 128)
+        const uint4 *xs = XL ? reinterpret_cast<const uint4 *>(smem + Lay::XL_OFF) + (size_t)(ka + i - ka0) * (2 * NT * 32)
                              : reinterpret_cast<const uint4 *>(stg + Lay::WB);
-        const uint8_t *ch0 = stg + (warp * 2) * Lay::CHUNK;
-        // both m-tiles' quant words and scales first (independent shared loads)
-        uint4 qw[2][TYPE == 8 ? 2 : 1];
-        uint2 scw[2];
-#pragma unroll
-        for (int mt = 0; mt < 2; mt++) {
-          const uint8_t *ch = ch0 + mt * Lay::CHUNK;
-          if (mt == 1 && !has1) {
-            scw[1] = make_uint2(0u, 0u);
-#pragma unroll
-            for (int h = 0; h < (TYPE == 8 ? 2 : 1); h++) qw[1][h] = make_uint4(0u, 0u, 0u, 0u);
-            continue;
-          }
-          if (TYPE == 8) {
-            qw[mt][0] = *reinterpret_cast<const uint4 *>(ch + lane * 32);
-            qw[mt][1] = *reinterpret_cast<const uint4 *>(ch + lane * 32 + 16);
-          } else {
-            qw[mt][0] = *reinterpret_cast<const uint4 *>(ch + lane * 16);
-          }
-          scw[mt] = *reinterpret_cast<const uint2 *>(ch + Lay::QB + g * 8);
+        // one n-tile: both m-tiles share the X loads; more: reload (registers)
+        uint4 xv1[2];
+        if (NT == 1) {
+          xv1[0] = xs[lane];
+          xv1[1] = xs[32 + lane];
         }
 #pragma unroll
-        for (int kbi = 0; kbi < 2; kbi++) {
-          // this 32-block's X (hi and lo operands of each n-tile), shared by both m-tiles
-          uint4 xh[NT], xo[NT];
+        for (int mt = 0; mt < 2; mt++) {
+          if (mt == 1 && !has1) break;
+          const uint8_t *ch = stg + (warp * 2 + mt) * Lay::CHUNK;
+          const uint2 scw = *reinterpret_cast<const uint2 *>(ch + Lay::QB + g * 8);
 #pragma unroll
-          for (int n = 0; n < NT; n++) {
-            xh[n] = xs[(kbi * NT + n) * 64 + lane];
-            xo[n] = xs[(kbi * NT + n) * 64 + 32 + lane];
-          }
-#pragma unroll
-          for (int mt = 0; mt < 2; mt++) {
-            if (mt == 1 && !has1) break;
+          for (int kbi = 0; kbi < 2; kbi++) {
             uint32_t a0s0, a1s0, a2s0, a3s0, a0s1, a1s1, a2s1, a3s1;
             if (TYPE == 8) {
-              const uint4 q = qw[mt][kbi];
-              q8_to_f16(q.x, a0s0, a2s0);  // row g, bytes 4t..4t+3
-              q8_to_f16(q.y, a0s1, a2s1);  // row g, bytes 16+4t..
-              q8_to_f16(q.z, a1s0, a3s0);  // row g+8
-              q8_to_f16(q.w, a1s1, a3s1);
+              const uint4 qw = *reinterpret_cast<const uint4 *>(ch + lane * 32 + kbi * 16);
+              q8_to_f16(qw.x, a0s0, a2s0);  // row g, bytes 4t..4t+3
+              q8_to_f16(qw.y, a0s1, a2s1);  // row g, bytes 16+4t..
+              q8_to_f16(qw.z, a1s0, a3s0);  // row g+8
+              q8_to_f16(qw.w, a1s1, a3s1);
             } else {
-              const uint4 q = qw[mt][0];
-              const uint32_t wg = kbi ? q.z : q.x, wg8 = kbi ? q.w : q.y;
+              const uint4 qw = *reinterpret_cast<const uint4 *>(ch + lane * 16);
+              const uint32_t wg = kbi ? qw.z : qw.x, wg8 = kbi ? qw.w : qw.y;
               q4_to_f16(wg, a0s0, a2s0, a0s1, a2s1);
               q4_to_f16(wg8, a1s0, a3s0, a1s1, a3s1);
             }
-            const uint32_t dw = kbi ? scw[mt].y : scw[mt].x;
+            const uint32_t dw = kbi ? scw.y : scw.x;
             const float dg = __half2float(__ushort_as_half((unsigned short)(dw & 0xFFFFu)));
             const float dg8 = __half2float(__ushort_as_half((unsigned short)(dw >> 16)));
 #pragma unroll
             for (int n = 0; n < NT; n++) {
+              const uint4 xv = NT == 1 ? xv1[kbi] : xs[(kbi * NT + n) * 32 + lane];
               float cc[4];
-              mma_16816(cc, a0s0, a1s0, a2s0, a3s0, xh[n].x, xh[n].y, zero4);
-              mma_16816(cc, a0s0, a1s0, a2s0, a3s0, xo[n].x, xo[n].y, cc);
-              mma_16816(cc, a0s1, a1s1, a2s1, a3s1, xh[n].z, xh[n].w, cc);
-              mma_16816(cc, a0s1, a1s1, a2s1, a3s1, xo[n].z, xo[n].w, cc);
+              mma_16816(cc, a0s0, a1s0, a2s0, a3s0, xv.x, xv.y, zero4);
+              mma_16816(cc, a0s1, a1s1, a2s1, a3s1, xv.z, xv.w, cc);
               acc[mt][n][0] = fmaf(dg, cc[0], acc[mt][n][0]);
               acc[mt][n][1] = fmaf(dg, cc[1], acc[mt][n][1]);
               acc[mt][n][2] = fmaf(dg8, cc[2], acc[mt][n][2]);
@@ -492,6 +484,7 @@ __global__ void __launch_bounds__(QGM_THREADS, 1) qgemv_kernel(GemvArgs a) {
       }
     }
 
+    fold_lo<NT>(acc);
     const bool full_tile = (ka == 0 && kb_end == a.kp);
     if (full_tile) {
       if (ok && has0) gemv_epilogue<NT>(a, mt0, has1, acc, g, t, xun);
@@ -503,18 +496,18 @@ __global__ void __launch_bounds__(QGM_THREADS, 1) qgemv_kernel(GemvArgs a) {
       const int slot = first_seg ? 0 : 1;
       float *mine = a.cl > 1 ? reinterpret_cast<float *>(smem) : a.ws + ((size_t)c * 2 + slot) * WS_TILE_FLOATS;
       if (a.cl > 1) named_bar(1, QG_CONS_WARPS * 32);  // every warp is done with the ring
-      if (has0) {
+      if (has0 && t < 2) {
 #pragma unroll
         for (int mt = 0; mt < 2; mt++)
 #pragma unroll
           for (int n = 0; n < NT; n++)
 #pragma unroll
             for (int h = 0; h < 2; h++) {
-              float *p = mine + ((warp * 2 + mt) * 16 + g + 8 * h) * 16 + n * 8 + 2 * t;
+              float *p = mine + ((warp * 2 + mt) * 16 + g + 8 * h) * 16 + n * 4 + 2 * t;
               float2 v = make_float2(acc[mt][n][2 * h], acc[mt][n][2 * h + 1]);
               if (XL) {  // local exponents differ between contributors: unscale before the sum (exact)
-                v.x *= xun[n * 8 + 2 * t];
-                v.y *= xun[n * 8 + 2 * t + 1];
+                v.x *= xun[n * 4 + 2 * t];
+                v.y *= xun[n * 4 + 2 * t + 1];
               }
               *reinterpret_cast<float2 *>(p) = v;
             }
@@ -525,12 +518,11 @@ __global__ void __launch_bounds__(QGM_THREADS, 1) qgemv_kernel(GemvArgs a) {
     first_seg = false;
   }
 
-  y_fence(a);  // full tiles' peer stores
   if (np == 0) return;  // (sums of squares are only asked of fully split grids)
   // ---- split tiles: every contributor reduces a share of the rows ----
   // warp w's two m-tiles are reduced by contributor w % ncon: lane l sums row
-  // l & 15 of m-tile l >> 4, four columns per float4 (NC4 float4s per
-  // contributor), over all contributors in CTA order.
+  // l & 15 of m-tile l >> 4, four columns per n-tile (one float4 per
+  // contributor and n-tile), over all contributors in CTA order.
   const int mt = lane >> 4, row = lane & 15;
   if (a.cl > 1) {
     // Cluster mode: the tile's contributors are the cluster's CTAs (ranks 0..cl-1
@@ -544,24 +536,24 @@ __global__ void __launch_bounds__(QGM_THREADS, 1) qgemv_kernel(GemvArgs a) {
     const int mt0 = tile * QG_TILE_MT + warp * 2;
     if (__all_sync(0xffffffffu, ok) && warp % a.cl == r) {  // warp-uniform: split_epilogue shuffles
       const bool live = mt0 + mt < a.n_mt;
-      float4 sum[NC4];
+      float4 sum[NT];
 #pragma unroll
-      for (int n = 0; n < NC4; n++) sum[n] = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int n = 0; n < NT; n++) sum[n] = make_float4(0.f, 0.f, 0.f, 0.f);
       const int off = ((warp * 2 + mt) * 16 + row) * 16;
       if (live) {
-        float4 v[4][NC4];
+        float4 v[4][NT];
 #pragma unroll
         for (int q = 0; q < 4; q++) {
           if (q >= a.cl) break;
           const float *src = cluster.map_shared_rank(reinterpret_cast<float *>(smem), q) + off;
 #pragma unroll
-          for (int n = 0; n < NC4; n++) v[q][n] = *reinterpret_cast<const float4 *>(src + 4 * n);
+          for (int n = 0; n < NT; n++) v[q][n] = *reinterpret_cast<const float4 *>(src + 4 * n);
         }
 #pragma unroll
         for (int q = 0; q < 4; q++) {
           if (q >= a.cl) break;
 #pragma unroll
-          for (int n = 0; n < NC4; n++) {
+          for (int n = 0; n < NT; n++) {
             sum[n].x += v[q][n].x;
             sum[n].y += v[q][n].y;
             sum[n].z += v[q][n].z;
@@ -569,9 +561,8 @@ __global__ void __launch_bounds__(QGM_THREADS, 1) qgemv_kernel(GemvArgs a) {
           }
         }
       }
-      split_epilogue<NC4>(a, mt0, mt, row, live, sum, wst);
+      split_epilogue<NT>(a, mt0, mt, row, live, sum, wst);
     }
-    y_fence(a);
     cluster_sync_all();  // no CTA leaves while another reads its shared memory
     if (XL && a.st_out && threadIdx.x < QG_STAT_COLS) {  // this CTA's slot: the warps' sums in warp order
       const float *w0 = xun + 16;
@@ -579,6 +570,7 @@ __global__ void __launch_bounds__(QGM_THREADS, 1) qgemv_kernel(GemvArgs a) {
       for (int w = 0; w < QG_CONS_WARPS; w++) ss += w0[w * 16 + threadIdx.x];
       a.st_out[(size_t)c * QG_STAT_COLS + threadIdx.x] = ss;
     }
+    y_fence(a);  // row-sharded output: peer stores before the cross-GPU barrier
     return;
   }
   // Global mode.  All contributors of a split tile are resident (one CTA per
@@ -614,14 +606,14 @@ __global__ void __launch_bounds__(QGM_THREADS, 1) qgemv_kernel(GemvArgs a) {
     const int mt0 = tile * QG_TILE_MT + warp * 2;
     if (go && warp % ncon == r) {
       const bool live = mt0 + mt < a.n_mt;
-      float4 sum[NC4];
+      float4 sum[NT];
 #pragma unroll
-      for (int n = 0; n < NC4; n++) sum[n] = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int n = 0; n < NT; n++) sum[n] = make_float4(0.f, 0.f, 0.f, 0.f);
       const size_t off = (size_t)((warp * 2 + mt) * 16 + row) * 16;
-      constexpr int CH = NC4 == 2 ? 4 : 2;  // independent loads in flight per lane
+      constexpr int CH = NT == 1 ? 8 : (NT == 2 ? 4 : 2);  // independent loads in flight per lane
       if (live) {
         for (int c0 = c_first; c0 <= c_last; c0 += CH) {
-          float4 v[CH][NC4];
+          float4 v[CH][NT];
 #pragma unroll
           for (int q = 0; q < CH; q++) {
             const int cc = c0 + q;
@@ -629,13 +621,13 @@ __global__ void __launch_bounds__(QGM_THREADS, 1) qgemv_kernel(GemvArgs a) {
             const long long cu0 = (long long)cc * a.units / a.G;
             const float *src = a.ws + ((size_t)cc * 2 + (cu0 >= tu0 ? 0 : 1)) * WS_TILE_FLOATS + off;
 #pragma unroll
-            for (int n = 0; n < NC4; n++) v[q][n] = __ldcg(reinterpret_cast<const float4 *>(src + 4 * n));
+            for (int n = 0; n < NT; n++) v[q][n] = __ldcg(reinterpret_cast<const float4 *>(src + 4 * n));
           }
 #pragma unroll
           for (int q = 0; q < CH; q++) {
             if (c0 + q > c_last) break;
 #pragma unroll
-            for (int n = 0; n < NC4; n++) {
+            for (int n = 0; n < NT; n++) {
               sum[n].x += v[q][n].x;
               sum[n].y += v[q][n].y;
               sum[n].z += v[q][n].z;
@@ -644,20 +636,20 @@ __global__ void __launch_bounds__(QGM_THREADS, 1) qgemv_kernel(GemvArgs a) {
           }
         }
       }
-      split_epilogue<NC4>(a, mt0, mt, row, live, sum, wst);
+      split_epilogue<NT>(a, mt0, mt, row, live, sum, wst);
     }
     named_bar(1, QG_CONS_WARPS * 32);  // every read of the partials of this tile is done
     if (threadIdx.x == 0 && go) {
       if (atomicAdd(a.cnt + tile, 1) == 2 * ncon - 1) a.cnt[tile] = 0;
     }
   }
-  y_fence(a);
   if (XL && a.st_out && threadIdx.x < QG_STAT_COLS) {  // this CTA's slot: the warps' sums in warp order
     const float *w0 = xun + 16;
     float ss = 0.f;
     for (int w = 0; w < QG_CONS_WARPS; w++) ss += w0[w * 16 + threadIdx.x];
     a.st_out[(size_t)c * QG_STAT_COLS + threadIdx.x] = ss;
   }
+  y_fence(a);  // row-sharded output: peer stores before the cross-GPU barrier
 }
 
 // Thread-block clusters of cl CTAs of this kernel that can be resident at once
@@ -711,13 +703,22 @@ static cudaError_t launch_t(GemvArgs a, cudaStream_t st) {
 
 
 cudaError_t launch(const GemvArgs &a, int type, bool xl, cudaStream_t st) {
-  const int nt = (a.B + 7) / 8;  // n-tiles of 8 columns
-  if (xl) return nt == 1 ? launch_t<2, 1, true>(a, st) : launch_t<2, 2, true>(a, st);
+  const int nt = (a.B + 3) / 4;  // n-tiles of 4 columns (hi | lo)
+  if (xl) switch (nt) {
+      case 1: return launch_t<2, 1, true>(a, st);
+      case 2: return launch_t<2, 2, true>(a, st);
+      case 3: return launch_t<2, 3, true>(a, st);
+      default: return launch_t<2, 4, true>(a, st);
+    }
   switch (nt * 16 + type) {
     case 16 + 8: return launch_t<8, 1, false>(a, st);
     case 32 + 8: return launch_t<8, 2, false>(a, st);
+    case 48 + 8: return launch_t<8, 3, false>(a, st);
+    case 64 + 8: return launch_t<8, 4, false>(a, st);
     case 16 + 2: return launch_t<2, 1, false>(a, st);
-    default: return launch_t<2, 2, false>(a, st);
+    case 32 + 2: return launch_t<2, 2, false>(a, st);
+    case 48 + 2: return launch_t<2, 3, false>(a, st);
+    default: return launch_t<2, 4, false>(a, st);
   }
 }
 
@@ -727,10 +728,16 @@ cudaError_t configure() {
   if ((e = carveout_max(repack_kernel<8>)) != cudaSuccess) return e;
   if ((e = carveout_max(qgemv_kernel<2, 1, false>)) != cudaSuccess) return e;
   if ((e = carveout_max(qgemv_kernel<2, 2, false>)) != cudaSuccess) return e;
+  if ((e = carveout_max(qgemv_kernel<2, 3, false>)) != cudaSuccess) return e;
+  if ((e = carveout_max(qgemv_kernel<2, 4, false>)) != cudaSuccess) return e;
   if ((e = carveout_max(qgemv_kernel<8, 1, false>)) != cudaSuccess) return e;
   if ((e = carveout_max(qgemv_kernel<8, 2, false>)) != cudaSuccess) return e;
+  if ((e = carveout_max(qgemv_kernel<8, 3, false>)) != cudaSuccess) return e;
+  if ((e = carveout_max(qgemv_kernel<8, 4, false>)) != cudaSuccess) return e;
   if ((e = carveout_max(qgemv_kernel<2, 1, true>)) != cudaSuccess) return e;
   if ((e = carveout_max(qgemv_kernel<2, 2, true>)) != cudaSuccess) return e;
+  if ((e = carveout_max(qgemv_kernel<2, 3, true>)) != cudaSuccess) return e;
+  if ((e = carveout_max(qgemv_kernel<2, 4, true>)) != cudaSuccess) return e;
   return cudaSuccess;
 }
 

@@ -7,7 +7,7 @@ namespace cw {
 
 // Layout selector of the X operands for the engine's GEMV kernel: 0 for the
 // tcgen05 kernel, else the n-tile count of the mma.sync kernel.
-static int xops_nt(const GemvScratch &s, int B) { return s.tc ? 0 : (B + 7) / 8; }
+static int xops_nt(const GemvScratch &s, int B) { return s.kern == GK_TC ? 0 : (B + 3) / 4; }
 
 // Dynamic shared memory above the 48 KB default needs an explicit opt-in.
 template <typename F>
@@ -57,7 +57,8 @@ __global__ void __launch_bounds__(PREP_THREADS) cat_norm_prep_kernel(const float
                                                                      const float *__restrict__ h,
                                                                      const float *__restrict__ we,
                                                                      const float *__restrict__ wh, int H, int mma_nt,
-                                                                     uint4 *__restrict__ xf, int *__restrict__ xexp) {
+                                                                     uint4 *__restrict__ xf, int *__restrict__ xexp,
+                                                                     float *__restrict__ out) {
   pdl_trigger();
   pdl_wait();
   extern __shared__ __align__(16) float v[];
@@ -81,16 +82,20 @@ __global__ void __launch_bounds__(PREP_THREADS) cat_norm_prep_kernel(const float
     v[H + k] = wh[k] * v[H + k] * rh;
   }
   __syncthreads();
+  if (out) {  // the concatenated rows for a GEMV kernel that takes raw X
+    for (int k = threadIdx.x; k < 2 * H; k += blockDim.x) out[(size_t)b * 2 * H + k] = v[k];
+    return;
+  }
   emit_xfrag(v, 2 * H, b, mma_nt, xf, xexp, red, true);
 }
 
 cudaError_t launch_cat_norm_prep(const float *e, const float *h, const float *we, const float *wh, int H, int B,
-                                 GemvScratch &s, cudaStream_t st) {
+                                 GemvScratch &s, cudaStream_t st, float *out) {
   const size_t smem = (size_t)2 * H * sizeof(float);
   static size_t done = 0;
   cudaError_t err = smem_optin(cat_norm_prep_kernel, smem, done);
   if (err != cudaSuccess) return err;
-  CW_TRY(launch_pdl(cat_norm_prep_kernel, B, PREP_THREADS, smem, st, e, h, we, wh, H, xops_nt(s, B), s.xf, s.xexp));
+  CW_TRY(launch_pdl(cat_norm_prep_kernel, B, PREP_THREADS, smem, st, e, h, we, wh, H, xops_nt(s, B), s.xf, s.xexp, out));
   return cudaGetLastError();
 }
 

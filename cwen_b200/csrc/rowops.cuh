@@ -15,9 +15,10 @@ struct Toks16 {
 
 cudaError_t launch_embed(const uint8_t *emb, int H, int V, const Toks16 &toks, int B, float *x, int *err,
                          cudaStream_t st, const int *dtok = nullptr);
-// MTP input rows b < B: [rmsnorm(e_b, we) | rmsnorm(h_b, wh)] (2H) -> GEMV input column b.
+// MTP input rows b < B: [rmsnorm(e_b, we) | rmsnorm(h_b, wh)] (2H) -> GEMV input column b,
+// or, with out, the fp32 rows out [B][2H] (for a kernel that takes raw X).
 cudaError_t launch_cat_norm_prep(const float *e, const float *h, const float *we, const float *wh, int H, int B,
-                                 GemvScratch &s, cudaStream_t st);
+                                 GemvScratch &s, cudaStream_t st, float *out = nullptr);
 // x [B][H] -> rmsnorm(x) * w as GEMV input (and optionally into out [B][H]).
 cudaError_t launch_norm_prep(const float *x, const float *w, int H, int B, GemvScratch &s, float *out,
                              cudaStream_t st);

@@ -76,12 +76,13 @@ CW_DEV void emit_xfrag_blocks(const float *v, int kb0, int nkb, int b, uint4 *__
 }
 
 // The same for the mma.sync kernel (qgemv_mma.cu): per (32-block, n-tile of
-// 8 columns) 64 uint4, 32 lanes of hi parts then 32 of lo parts; lane
-// (b % 8, t) holds (x[4t], x[4t+2]) (x[4t+1], x[4t+3]) (x[4t+16], x[4t+18])
-// (x[4t+17], x[4t+19]), the K order of that kernel's A fragments; nt n-tiles.
+// 4 columns) 32 uint4; column b is B-operand column b % 4 (hi parts) and
+// b % 4 + 4 (lo parts) of n-tile b / 4, lane (column, t) holding (x[4t],
+// x[4t+2]) (x[4t+1], x[4t+3]) (x[4t+16], x[4t+18]) (x[4t+17], x[4t+19]), the
+// K order of that kernel's A fragments; nt n-tiles.
 CW_DEV void emit_xfrag_blocks_mma(const float *v, int kb0, int nkb, int b, int nt, uint4 *__restrict__ xf,
                                   float scale, bool live) {
-  const int g = b & 7, n = b >> 3;
+  const int g = b & 3, n = b >> 2;
   for (int item = threadIdx.x; item < nkb * 4; item += blockDim.x) {
     const int kbl = item >> 2, t = item & 3;
     const float *r = v + kbl * 32;
@@ -95,9 +96,9 @@ CW_DEV void emit_xfrag_blocks_mma(const float *v, int kb0, int nkb, int b, int n
       hi[i] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
       lo[i] = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
     }
-    uint4 *o = xf + (size_t)((kb0 + kbl) * nt + n) * 64;
-    o[g * 4 + t] = make_uint4(hi[0], hi[1], hi[2], hi[3]);       // hi B operand, column g
-    o[32 + g * 4 + t] = make_uint4(lo[0], lo[1], lo[2], lo[3]);  // lo B operand, column g
+    uint4 *o = xf + (size_t)((kb0 + kbl) * nt + n) * 32;
+    o[g * 4 + t] = make_uint4(hi[0], hi[1], hi[2], hi[3]);        // B column g: hi part
+    o[(g + 4) * 4 + t] = make_uint4(lo[0], lo[1], lo[2], lo[3]);  // B column g + 4: lo part
   }
 }
 // One of the two: mma_nt == 0 the tcgen05 layout, else the mma.sync layout

@@ -78,7 +78,7 @@ int cwen_cuda_gemvb_host(int wid, const float *hX, int xs, float *hY, int ys, in
 
 /* The same GEMV with no allocation at all: its scratch (prepared X, split-K
  * partials, tile counters) is a fixed array of device memory inside the
- * library (about 22 MiB on every GPU that loads it, held until exit) instead
+ * library (about 24 MiB on every GPU that loads it, held until exit) instead
  * of the engine's.  No counterpart in the reference, which has no device
  * memory.  For callers that must not call cudaMalloc while they run -- a
  * framework whose caching allocator already holds the device memory, or a

@@ -1,7 +1,8 @@
 """Verify GEMV (a): CUDA path vs the CPU oracle and the reference goldens,
-through the C ABI (include/cwen_cuda.h), plus batch invariance -- for both
-kernels an engine can run (the warp-level mma.sync kernel, the default, and
-the tcgen05 kernel selected with CWEN_GEMV=tcgen05 at cwen_cuda_init).
+through the C ABI (include/cwen_cuda.h), plus batch invariance -- for every
+kernel an engine can run (the warp-level mma.sync kernel, the default; qmv
+with CWEN_GEMV=qmv and the tcgen05 kernel with CWEN_GEMV=tcgen05, selected at
+cwen_cuda_init).
 
 Tolerance: the reference's gemv acceptance, max_abs <= 1e-4 (run.c:4352),
 and relative L2 <= 1e-5 (the kernel computes X as f16 hi+lo, ~2^-22
@@ -17,7 +18,7 @@ from oracle_lib import gen_normal, gen_q, oracle_gemvb, rel_l2
 pytestmark = pytest.mark.gpu
 
 
-@pytest.fixture(scope="module", params=["mma", "tcgen05"])
+@pytest.fixture(scope="module", params=["mma", "qmv", "tcgen05"])
 def eng(request):
     import os
 

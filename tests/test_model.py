@@ -6,8 +6,8 @@
 - the verify block is bit-identical to serial decode (batch invariance), and
   a short-walk commit restores exactly the serial state;
 - speculative generation emits exactly the serial token stream.
-Every test runs under both verify-GEMV kernels an engine can use (mma.sync,
-the default, and tcgen05 with CWEN_GEMV=tcgen05).
+Every test runs under each verify-GEMV kernel an engine can use (mma.sync,
+the default; qmv with CWEN_GEMV=qmv; tcgen05 with CWEN_GEMV=tcgen05).
 """
 import ctypes as C
 
@@ -22,7 +22,7 @@ SEED = 7
 CTX = 512
 
 
-@pytest.fixture(scope="module", params=["mma", "tcgen05"])
+@pytest.fixture(scope="module", params=["mma", "qmv", "tcgen05"])
 def small(request):
     import os
 
