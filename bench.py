@@ -1046,7 +1046,7 @@ def gdn_ours_line(args, ws, rank, local, config, metric):
     ms = barrier_max(ws, ms)
     stream_ms = barrier_max(ws, stream_ms)
     kk = [int(keeps[i]) for i in idx]
-    launches = sum(2 + (1 if 0 < k < GDN_B else 0) for k in kk)
+    launches = len(kk)  # one fused launch per step (conv, recurrence, gated norm, rollback)
     min_bytes = sum(gdn_min_bytes(k) for k in kk) / args.steps
     ach = min_bytes / (ms * 1e-3) / 1e9
 

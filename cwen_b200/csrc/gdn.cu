@@ -186,6 +186,239 @@ __global__ void __launch_bounds__(GDN_T) gdn_recur_kernel(const float *__restric
   cl.sync();  // the other half has read oss before this CTA leaves
 }
 
+// ---- the whole layer step in one launch: conv + SiLU + q/k l2norm +
+// decay/beta + the recurrence + the gated norm.  A thread-block cluster holds
+// every value head of one key head (R = nvh / nkh heads x 2 halves, R <= 4):
+// rank r = 2 * (value head index within the key head) + half, value head
+// hv = hk + nkh * (r / 2).  Each CTA convolves the channels it reads (the key
+// head's 128 q and 128 k channels, its half's 64 v channels) itself, so no
+// intermediate rows go through global memory; the q/k channels' conv state
+// and rollback records are written by rank 0 after a cluster barrier (every
+// CTA of the cluster has read the old state by then), the v channels' by
+// their own CTA.  The arithmetic is the two-kernel path's, operation for
+// operation, so both give the same bits.
+// keep < 0: the engine's verify block -- the state after the last row goes to
+// S_out / cstate_out and the rank-1 records (normalised k, gate, delta, raw
+// rows) stay for a later commit.  keep >= 0: rollback on the caller's
+// buffers in place (S_out == S_in, cstate_out == cstate_in): the state after
+// row keep - 1 is written (nothing when keep == 0), no records. ----
+__global__ void __launch_bounds__(GDN_T) gdn_fused_kernel(const GdnLayerArgs a, int keep) {
+  pdl_trigger();
+  pdl_wait();
+  namespace cg = cooperative_groups;
+  cg::cluster_group cl = cg::this_cluster();
+  const int nkh = a.nkh, nvh = a.nvh, B = a.B;
+  const int R2 = 2 * (nvh / nkh);
+  const int hk = blockIdx.x / R2, rank = blockIdx.x % R2;
+  const int half = rank & 1, hv = hk + nkh * (rank >> 1);
+  const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+  const int q4 = lane >> 3, col = warp * 8 + (lane & 7);
+  const int j = half * 64 + col;
+  const int QKV = (2 * nkh + nvh) * 128;
+  const int GS = QKV + 2 * nvh;
+  __shared__ float kq[GDN_MAXB][2][4 * KQ_PAD];
+  __shared__ float vsh[GDN_MAXB][64];
+  __shared__ float gb[GDN_MAXB][2];
+  __shared__ float ob[GDN_MAXB][64];
+  __shared__ float oss[GDN_MAXB];
+  __shared__ float red[GDN_MAXB][8];
+  const int nsnap = keep < 0 ? B : keep;  // rows in the state written
+  constexpr int NZ = GDN_MAXB * 64 / GDN_T;  // output items per thread at most
+
+  // ---- every global read first: one memory round trip for the whole step ----
+  const bool isk = t >= 128;
+  const int ch = isk ? nkh * 128 + hk * 128 + (t - 128) : hk * 128 + t;  // this thread's q or k channel
+  float raw[GDN_MAXB];
+#pragma unroll
+  for (int b = 0; b < GDN_MAXB; b++) raw[b] = b < B ? a.proj[(size_t)b * a.ps + ch] : 0.f;
+  const float w0 = a.convw[ch * 4 + 0], w1 = a.convw[ch * 4 + 1], w2 = a.convw[ch * 4 + 2], w3 = a.convw[ch * 4 + 3];
+  const float o0 = a.cstate_in[ch * 3 + 0], o1 = a.cstate_in[ch * 3 + 1], o2 = a.cstate_in[ch * 3 + 2];
+  const int vc = 2 * nkh * 128 + hv * 128 + half * 64 + (t & 63);  // v channel (threads < 64)
+  float vr[GDN_MAXB];
+  float u0 = 0.f, u1 = 0.f, u2 = 0.f, u3 = 0.f, p0 = 0.f, p1 = 0.f, p2 = 0.f;
+  if (t < 64) {
+#pragma unroll
+    for (int b = 0; b < GDN_MAXB; b++) vr[b] = b < B ? a.proj[(size_t)b * a.ps + vc] : 0.f;
+    u0 = a.convw[vc * 4 + 0]; u1 = a.convw[vc * 4 + 1]; u2 = a.convw[vc * 4 + 2]; u3 = a.convw[vc * 4 + 3];
+    p0 = a.cstate_in[vc * 3 + 0]; p1 = a.cstate_in[vc * 3 + 1]; p2 = a.cstate_in[vc * 3 + 2];
+  }
+  float al = 0.f, be = 0.f, dtv = 0.f, Av = 0.f;
+  if (t < B) {
+    al = a.proj[(size_t)t * a.ps + a.a_off + hv];
+    be = a.proj[(size_t)t * a.ps + a.b_off + hv];
+    dtv = a.dt[hv];
+    Av = a.A[hv];
+  }
+  const float *S0 = a.S_in + (size_t)hv * 128 * 128;
+  float s[32];
+#pragma unroll
+  for (int i = 0; i < 32; i++) s[i] = S0[(size_t)(q4 * 32 + i) * 128 + j];
+  float zv[NZ], wnv[NZ];
+#pragma unroll
+  for (int m = 0; m < NZ; m++) {
+    const int i = t + GDN_T * m, b = i >> 6, c = i & 63, jj = half * 64 + c;
+    zv[m] = b < B ? a.z[(size_t)b * a.ps + hv * 128 + jj] : 0.f;
+    wnv[m] = a.wn[jj];
+  }
+
+  // ---- conv + SiLU + l2norm of the q/k channels, all rows ----
+  float y[GDN_MAXB];
+  {
+    float c0 = o0, c1 = o1, c2 = o2;
+#pragma unroll
+    for (int b = 0; b < GDN_MAXB; b++) {
+      if (b >= B) break;
+      const float cur = raw[b];
+      const float v = c0 * w0 + c1 * w1 + c2 * w2 + cur * w3;
+      c0 = c1;
+      c1 = c2;
+      c2 = cur;
+      y[b] = silu_dev(v);
+      const float ss = warp_sum(y[b] * y[b]);
+      if (lane == 0) red[b][warp] = ss;
+    }
+  }
+  // ---- v channels of this half (threads 0..63), their conv state owned here ----
+  if (t < 64) {
+    float c0 = p0, c1 = p1, c2 = p2;
+#pragma unroll
+    for (int b = 0; b < GDN_MAXB; b++) {
+      if (b >= B) break;
+      const float cur = vr[b];
+      const float v = c0 * u0 + c1 * u1 + c2 * u2 + cur * u3;
+      c0 = c1;
+      c1 = c2;
+      c2 = cur;
+      const float yv = silu_dev(v);
+      vsh[b][t] = yv;
+      if (keep < 0) {
+        a.gin[(size_t)b * GS + vc] = yv;
+        a.craw[(size_t)b * QKV + vc] = cur;
+      }
+    }
+    if (nsnap > 0 || keep < 0) {
+#pragma unroll
+      for (int m = 0; m < 3; m++) {
+        const int pidx = nsnap + m;  // position in [old0 old1 old2 raw0 raw1 ...]
+        float st = pidx == 0 ? p0 : (pidx == 1 ? p1 : p2);
+#pragma unroll
+        for (int b = 0; b < GDN_MAXB; b++)
+          if (pidx == b + 3) st = vr[b];
+        a.cstate_out[vc * 3 + m] = st;
+      }
+    }
+  }
+  // ---- decay / beta of this value head for every row ----
+  if (t < B) {
+    const float x = al + dtv;
+    const float sp = x > 20.f ? x : logf(1.f + expf(x));
+    gb[t][0] = expf(Av * sp);
+    gb[t][1] = 1.f / (1.f + expf(-be));
+    if (keep < 0 && half == 0) {
+      a.gin[(size_t)t * GS + QKV + hv] = gb[t][0];
+      a.gin[(size_t)t * GS + QKV + nvh + hv] = gb[t][1];
+    }
+  }
+  __syncthreads();
+  {
+    const int w4 = isk ? 4 : 0;  // the 4 warps of this head's q or k channels
+    const int e = t & 127;
+#pragma unroll
+    for (int b = 0; b < GDN_MAXB; b++) {
+      if (b >= B) break;
+      const float *r = red[b] + w4;
+      const float ss = (r[0] + r[1]) + (r[2] + r[3]);
+      const float yn = y[b] * (1.f / sqrtf(ss + 1e-6f));
+      kq[b][isk ? 0 : 1][(e >> 5) * KQ_PAD + (e & 31)] = yn;
+      if (keep < 0 && rank == 0) {
+        a.gin[(size_t)b * GS + ch] = yn;
+        a.craw[(size_t)b * QKV + ch] = raw[b];
+      }
+    }
+  }
+  __syncthreads();
+
+  // ---- the recurrence (as gdn_recur_kernel) ----
+  float sn[32];
+#pragma unroll
+  for (int i = 0; i < 32; i++) sn[i] = s[i];
+  const float scale = 1.f / sqrtf(128.f);
+  for (int b = 0; b < B; b++) {
+    const float *kk = &kq[b][0][q4 * KQ_PAD], *qq = &kq[b][1][q4 * KQ_PAD];
+    const float g = gb[b][0], beta = gb[b][1];
+    float sk = 0.f;
+#pragma unroll
+    for (int i = 0; i < 32; i++) {
+      s[i] = s[i] * g;
+      sk = fmaf(s[i], kk[i], sk);
+    }
+    sk += __shfl_xor_sync(0xffffffffu, sk, 8);
+    sk += __shfl_xor_sync(0xffffffffu, sk, 16);
+    const float d = beta * (vsh[b][col] - sk);
+    if (keep < 0 && q4 == 0) a.delta[(size_t)b * nvh * 128 + hv * 128 + j] = d;
+    float o = 0.f;
+#pragma unroll
+    for (int i = 0; i < 32; i++) {
+      s[i] = fmaf(kk[i], d, s[i]);
+      o = fmaf(s[i], qq[i], o);
+    }
+    o += __shfl_xor_sync(0xffffffffu, o, 8);
+    o += __shfl_xor_sync(0xffffffffu, o, 16);
+    if (q4 == 0) ob[b][col] = o * scale;
+    if (b == nsnap - 1) {
+#pragma unroll
+      for (int i = 0; i < 32; i++) sn[i] = s[i];
+    }
+  }
+  if (nsnap > 0) {
+    float *S1 = a.S_out + (size_t)hv * 128 * 128;
+#pragma unroll
+    for (int i = 0; i < 32; i++) S1[(size_t)(q4 * 32 + i) * 128 + j] = sn[i];
+  }
+  __syncthreads();
+  // ---- gated RMSNorm of the head's outputs (the halves exchange sums) ----
+  for (int b = warp; b < B; b += GDN_T / 32) {
+    const float a0 = ob[b][lane], a1 = ob[b][lane + 32];
+    float ss = fmaf(a0, a0, a1 * a1);
+    ss = warp_sum(ss);
+    if (lane == 0) oss[b] = ss;
+  }
+  cl.sync();  // also: every CTA of the key head has read the old conv state
+  const float *oth = cl.map_shared_rank(oss, rank ^ 1);
+#pragma unroll
+  for (int m = 0; m < NZ; m++) {
+    const int i = t + GDN_T * m, b = i >> 6, c = i & 63, jj = half * 64 + c;
+    if (b < B) {
+      const float tot = half == 0 ? oss[b] + oth[b] : oth[b] + oss[b];
+      const float sq = 1.f / sqrtf(tot / 128.f + 1e-6f);
+      a.out[(size_t)b * nvh * 128 + hv * 128 + jj] = wnv[m] * ob[b][c] * sq * silu_dev(zv[m]);
+    }
+  }
+  // the key head's q/k conv state (in place for the caller's rollback: every
+  // CTA of the cluster has read it before the barrier above)
+  if (rank == 0 && (nsnap > 0 || keep < 0)) {
+#pragma unroll
+    for (int m = 0; m < 3; m++) {
+      const int pidx = nsnap + m;
+      float st = pidx == 0 ? o0 : (pidx == 1 ? o1 : o2);
+#pragma unroll
+      for (int b = 0; b < GDN_MAXB; b++)
+        if (pidx == b + 3) st = raw[b];
+      a.cstate_out[ch * 3 + m] = st;
+    }
+  }
+  cl.sync();  // the pair has read oss before this CTA leaves
+}
+
+bool gdn_fusable(int nkh, int nvh) { return nkh >= 1 && nvh % nkh == 0 && 2 * (nvh / nkh) <= 8; }
+
+cudaError_t launch_gdn_fused(const GdnLayerArgs &a, int keep, cudaStream_t st) {
+  if (a.B < 1 || a.B > GDN_MAXB || !gdn_fusable(a.nkh, a.nvh) || keep > a.B) return cudaErrorInvalidValue;
+  const int r2 = 2 * (a.nvh / a.nkh);
+  CW_TRY(launch_pdl_cluster(gdn_fused_kernel, a.nkh * r2, GDN_T, 0, st, r2, a, keep));
+  return cudaGetLastError();
+}
+
 // ---- rollback: replay rows 0..k (inclusive) onto the committed state in
 // place; conv state <- last three raw inputs. One CTA per (layer, head, half)
 // for S, plus conv CTAs. ----
@@ -257,6 +490,7 @@ __global__ void __launch_bounds__(GDN_T) gdn_replay1_kernel(const GdnLayerPtrs P
 cudaError_t launch_gdn_layer(const GdnLayerArgs &a, cudaStream_t st) {
   const int QKV = (2 * a.nkh + a.nvh) * 128;
   if (a.B < 1 || a.B > GDN_MAXB) return cudaErrorInvalidValue;
+  if (gdn_fusable(a.nkh, a.nvh)) return launch_gdn_fused(a, -1, st);
   CW_TRY(launch_pdl(gdn_conv_kernel, QKV / 128 + 1, 128, 0, st, a.proj, a.ps, a.B, a.nkh, a.nvh, a.a_off, a.b_off, a.convw,
                                                   a.cstate_in, a.cstate_out, a.craw, a.A, a.dt, a.gin));
   CW_TRY(launch_pdl_cluster(gdn_recur_kernel, a.nvh * 2, GDN_T, 0, st, 2, a.S_in, a.S_out, a.gin, a.B, a.nkh, a.nvh,
@@ -284,6 +518,7 @@ cudaError_t gdn_configure() {
   cudaError_t e;
   if ((e = carveout_max(gdn_conv_kernel)) != cudaSuccess) return e;
   if ((e = carveout_max(gdn_recur_kernel)) != cudaSuccess) return e;
+  if ((e = carveout_max(gdn_fused_kernel)) != cudaSuccess) return e;
   if ((e = carveout_max(gdn_replay_kernel)) != cudaSuccess) return e;
   if ((e = carveout_max(gdn_replay1_kernel)) != cudaSuccess) return e;
   return cudaSuccess;

@@ -36,6 +36,12 @@ struct GdnLayerPtrs {
 };
 
 cudaError_t launch_gdn_layer(const GdnLayerArgs &a, cudaStream_t st);
+// The same step in one launch (a cluster per key head; gdn_fusable: at most 4
+// value heads per key head).  keep < 0: as launch_gdn_layer.  keep >= 0: roll
+// the caller's state forward by rows 0..keep-1 in place (S_out == S_in,
+// cstate_out == cstate_in), no rollback records.
+bool gdn_fusable(int nkh, int nvh);
+cudaError_t launch_gdn_fused(const GdnLayerArgs &a, int keep, cudaStream_t st);
 // Advance every layer's committed state by block rows 0..k.
 cudaError_t launch_gdn_replay(GdnLayerPtrs *dev_layers, int n_layers, int k, int nkh, int nvh, cudaStream_t st);
 // The same for one layer given by value.

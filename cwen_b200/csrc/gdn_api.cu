@@ -45,6 +45,17 @@ extern "C" int cwen_cuda_gdn_verify(int nkh, int nvh, int B, const float *proj, 
     return CWEN_EINVAL;
   }
   cudaStream_t st = stream ? (cudaStream_t)stream : E.stream;
+  if (gdn_fusable(nkh, nvh)) {
+    // one launch: the block's rows and the rollback to row keep - 1 on the
+    // caller's state in place (no scratch, no copy, no replay)
+    GdnLayerArgs g = {};
+    g.proj = proj; g.ps = ps; g.B = B; g.nkh = nkh; g.nvh = nvh;
+    g.a_off = QKV + Z; g.b_off = QKV + Z + nvh;
+    g.convw = convw; g.cstate_in = conv; g.cstate_out = conv;
+    g.A = A; g.dt = dt; g.S_in = S; g.S_out = S; g.out = out; g.z = proj + QKV; g.wn = wn;
+    CW_CHECK(launch_gdn_fused(g, keep, st));
+    return CWEN_OK;
+  }
   const size_t nS = (size_t)nvh * 128 * 128;
   const size_t need = nS + (size_t)QKV * 3 + (size_t)GDN_MAXB * ((size_t)QKV + GS + Z);
   if (g_vs.floats < need) {

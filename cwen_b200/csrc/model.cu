@@ -321,7 +321,7 @@ static int run_layer_block(int l, int B, int pos0, cudaStream_t st) {
     g.S_in = M.S[M.cur][li]; g.S_out = M.S[nxt][li]; g.out = M.gdn_out; g.delta = M.delta[li];
     g.z = M.proj + M.QKV; g.wn = w.ssm_norm;  // gated norm of the head outputs, in the recurrence kernel
     CW_CHECK(launch_gdn_layer(g, st));
-    nl += 2;
+    nl += gdn_fusable(d.ssm_n_kh, d.ssm_n_vh) ? 1 : 2;
   } else {
     const int fi = w.idx;
     CW_CHECK(timed_gemv(w.in_proj, B, M.proj, M.PS, EPI_STORE, st, M.x, H, w.attn_norm));

@@ -127,7 +127,10 @@ CWREF_API int cwref_load_synth(uint64_t seed, int has_mtp, int threads) {
   cw_dims_full(&d);
   d.has_mtp = has_mtp;
   int nt = cw_model_tensor_count(&d);
-  if (nt > (int)(sizeof Tens / sizeof Tens[0])) return -1;
+  if (nt > (int)(sizeof Tens / sizeof Tens[0]) || nt > (int)(sizeof g_model_blobs / sizeof g_model_blobs[0])) return -1;
+  /* a second model in the same process replaces the first */
+  for (int i = 0; i < g_model_nblobs; i++) free(g_model_blobs[i]);
+  g_model_nblobs = 0;
   Ntens = 0;
   for (int i = 0; i < nt; i++) {
     cw_tensor_desc t;
