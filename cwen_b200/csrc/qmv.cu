@@ -1,5 +1,5 @@
-// Batched Q4_0 / Q8_0 GEMV for B <= 16 verify rows: the engine's default
-// kernel ("qmv").  Replaces the reference's gemvb()/gemv() (run.c:1577-1680,
+// Batched Q4_0 / Q8_0 GEMV for B <= 16 verify rows, the alternative to the
+// mma kernel ("qmv", CWEN_GEMV=qmv).  Replaces the reference's gemvb()/gemv() (run.c:1577-1680,
 // 1419-1527) and the row dots under them (dot_q4_0 run.c:1009-1025,
 // dot_nib16 run.c:432, dot_q8_0 run.c:1248-1274); with a norm weight it also
 // takes the rmsnorm that precedes the projection (run.c:346-368).

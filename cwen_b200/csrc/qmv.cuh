@@ -1,6 +1,6 @@
-// The engine's default verify GEMV (qmv.cu): launch arguments and host entry
-// points.  Raw fp32 X in, optional RMSNorm weight folded in; no scratch
-// memory besides the error flag.
+// The qmv verify GEMV (qmv.cu, selected with CWEN_GEMV=qmv): launch arguments
+// and host entry points.  Raw fp32 X in, optional RMSNorm weight folded in;
+// the X operands are converted once per call into a phase buffer.
 #pragma once
 #include <cuda_runtime.h>
 #include <stdint.h>

@@ -80,17 +80,58 @@ static float or_row_dot(int type, const void *W, int K, int i, const float *x) {
   const uint8_t *row = (const uint8_t *)W + (size_t)i * rb;
   return type == CW_T_Q8_0 ? or_dot_q8_0(row, x, K) : or_dot_q4_0(row, x, K);
 }
+/* Operand rounding of the GPU engine, a test-only switch (off by default; not
+   part of the reference).  The engine's tensor-core GEMV scales each X column
+   by a power of two that puts its largest |x| in [2^14, 2^15) and splits it
+   into f16 hi + lo parts: 22 significant bits instead of fp32's 24.  With the
+   switch on, or_gemv and or_gemvb round X that way before the reference's dot
+   products, so a test can measure how far that operand precision alone moves
+   a forward pass from the reference. */
+static int or_xround = 0;
+void or_set_xround(int on) { or_xround = on; }
+static void or_round_x(const float *x, int K, float *out) {
+  float mx = 0.f;
+  for (int k = 0; k < K; k++) mx = fmaxf(mx, fabsf(x[k]));
+  if (!(mx > 0.f) || !isfinite(mx)) {
+    memcpy(out, x, (size_t)K * sizeof(float));
+    return;
+  }
+  int e;
+  frexpf(mx, &e); /* mx in [2^(e-1), 2^e) */
+  const int sh = 15 - e;
+  for (int k = 0; k < K; k++) {
+    const float xs = ldexpf(x[k], sh);
+    const float hi = (float)(_Float16)xs;
+    const float lo = (float)(_Float16)(xs - hi);
+    out[k] = ldexpf(hi + lo, -sh);
+  }
+}
 /* gemv (run.c:1419): y[i] = row i . x */
 void or_gemv(int type, const void *W, int K, int M, const float *x, float *y) {
+  float *xr = NULL;
+  if (or_xround) {
+    xr = (float *)malloc((size_t)K * sizeof(float));
+    or_round_x(x, K, xr);
+    x = xr;
+  }
 #pragma omp parallel for schedule(static)
   for (int i = 0; i < M; i++) y[i] = or_row_dot(type, W, K, i, x);
+  free(xr);
 }
 /* gemvb (run.c:1577) on the GGUF Q4_0/Q8_0 path: B independent column dots
    per row (run.c:1666-1679). */
 void or_gemvb(int type, const void *W, int K, int M, const float *X, int xs, float *Y, int ys, int B) {
+  float *xr = NULL;
+  if (or_xround) {
+    xr = (float *)malloc((size_t)B * K * sizeof(float));
+    for (int b = 0; b < B; b++) or_round_x(X + (size_t)b * xs, K, xr + (size_t)b * K);
+    X = xr;
+    xs = K;
+  }
 #pragma omp parallel for schedule(static)
   for (int i = 0; i < M; i++)
     for (int b = 0; b < B; b++) Y[(size_t)b * ys + i] = or_row_dot(type, W, K, i, X + (size_t)b * xs);
+  free(xr);
 }
 /* embed_token_to, Q4_0 branch (run.c:1873-1881). */
 void or_embed_q4_0(const void *W, int K, int token, float *dst) {

@@ -19,6 +19,9 @@ extern "C" {
 void or_rmsnorm(float *o, const float *x, const float *w, int n);
 void or_gemv(int type, const void *W, int K, int M, const float *x, float *y);
 void or_gemvb(int type, const void *W, int K, int M, const float *X, int xs, float *Y, int ys, int B);
+/* Test-only: round every GEMV's X to the GPU engine's operand precision
+   (f16 hi + lo after a power-of-two column scale) while on != 0. */
+void or_set_xround(int on);
 void or_embed_q4_0(const void *W, int K, int token, float *dst);
 void or_conv1d_update(float *qkv, float *conv_state, const float *conv_w, int qkv_dim);
 void or_gdn_step(const cw_dims *d, float *S, float *qkv, const float *z, const float *decay,

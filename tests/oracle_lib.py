@@ -38,6 +38,7 @@ def load_oracle():
         L.cw_synth_normal.argtypes = [C.c_uint64, C.c_char_p, C.c_float, C.c_float, C.c_void_p, C.c_size_t]
         L.cw_synth_ids.argtypes = [C.c_uint64, C.c_char_p, C.c_int, C.c_void_p, C.c_size_t]
         L.or_gemvb.argtypes = [C.c_int, C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_int]
+        L.or_set_xround.argtypes = [C.c_int]
         L.or_rmsnorm.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int]
         L.or_rope.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int]
         L.or_attention.argtypes = [C.POINTER(CwDims), C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p,

@@ -54,6 +54,9 @@ def test_decode_line(monkeypatch, capsys):
         raise RuntimeError("no engine here")
 
     monkeypatch.setattr(bench, "gdn_ours_line", boom)
+    monkeypatch.setattr(bench, "run_mtp_ours", lambda ws, l: {
+        "tps": 90.0, "clocks": CLK, "prefill": {"tokens": 32495, "seconds": 70.0, "tok_s": 464.2},
+        "identical_to_serial": True, "mtp": {"cycles": 255}})
     monkeypatch.setattr(bench, "peaks", lambda: (6541.1, 1590.0, "measured"))
     import cwen_b200
     monkeypatch.setattr(cwen_b200, "lib", lambda: type("L", (), {"cwen_cuda_shutdown": staticmethod(lambda: None)}))
@@ -68,6 +71,8 @@ def test_decode_line(monkeypatch, capsys):
     assert rec["verify_ceiling"]["8"]["pass"] is True
     assert rec["gemv_config0"]["value"] == 1.0
     assert "no engine here" in rec["gdn_config1"]["error"]
+    assert rec["mtp_config4"]["tok_s"] == 90.0 and rec["mtp_config4"]["identical_to_serial"] is True
+    assert rec["mtp_config4"]["prefill_tok_s"] == 464.2
     assert rec["roofline"]["bound"] == "hbm" and rec["roofline"]["peak"] == 6541.1
     assert abs(rec["roofline"]["achieved"] - 14.4e9 / 3.0e-3 / 1e9) < 0.1  # bytes per token / GEMV time per token
 

@@ -78,3 +78,35 @@ def test_gdn_matches_reference(orc, golden):
         assert rel_l2(o, golden[f"gdn_out_p{p}"]) <= 1e-5, p
     assert rel_l2(S.reshape(-1)[::97], golden["gdn_S_sub"]) <= 1e-5
     assert rel_l2(cs, golden["gdn_conv"]) <= 1e-6
+
+
+def _xround_np(x):
+    """numpy restatement of the oracle's test-only operand rounding: the
+    column scaled by 2^sh (largest |x| in [2^14, 2^15)), split into f16 hi + lo."""
+    mx = float(np.abs(x).max())
+    sh = 15 - int(np.frexp(np.float32(mx))[1])
+    xs = np.ldexp(x.astype(np.float32), sh).astype(np.float32)
+    hi = xs.astype(np.float16).astype(np.float32)
+    lo = (xs - hi).astype(np.float16).astype(np.float32)
+    return np.ldexp(hi + lo, -sh).astype(np.float32)
+
+
+def test_xround_switch(orc):
+    """or_set_xround(1) rounds each X column to 22 significant bits before the
+    dots and changes nothing else; off again, the oracle is the plain fp32 one."""
+    K, M, B = 1024, 96, 3
+    W = gen_q(orc, 5, "xr_w", 2, K, M)
+    X = gen_normal(orc, 6, "xr_x", B * K).reshape(B, K) * np.float32(3.0)
+    X[1] *= np.float32(1e-3)
+    Xr = np.stack([_xround_np(X[b]) for b in range(B)])
+    err = np.abs(Xr - X) / np.maximum(np.abs(X), 1e-30)
+    assert err.max() <= 2.0 ** -22 and (Xr != X).any()
+    plain = oracle_gemvb(orc, 2, W, K, M, X)
+    orc.or_set_xround(1)
+    try:
+        rounded = oracle_gemvb(orc, 2, W, K, M, X)
+    finally:
+        orc.or_set_xround(0)
+    assert np.array_equal(rounded, oracle_gemvb(orc, 2, W, K, M, Xr))
+    assert np.array_equal(plain, oracle_gemvb(orc, 2, W, K, M, X))
+    assert not np.array_equal(rounded, plain)
