@@ -122,11 +122,12 @@ extern "C" int cwen_cuda_gemvb_static(int wid, const float *dX, int xs, float *d
   s.kern = E.gs.kern;
   s.tc = E.gs.tc;  // the engine's kernel (its weights are in that kernel's layout)
   cudaStream_t st = stream ? (cudaStream_t)stream : E.stream;
-  // The arrival counters reset themselves at the end of a complete call;
-  // clear the ones this call uses in case an earlier call stopped part-way.
-  // The wait-timeout flag is left alone: cwen_cuda_gemvb_static_status reads
-  // and clears it.
-  CW_CHECK(cudaMemsetAsync(s.cnt, 0, (size_t)n_tiles * sizeof(int), st));
+  // Clear the split-K sync words this call can use (arrival counters per
+  // tile, or partial flags per CTA slot) in case an earlier call stopped
+  // part-way or an earlier engine left flag values behind.  The wait-timeout
+  // flag is left alone: cwen_cuda_gemvb_static_status reads and clears it.
+  const int nsync = n_tiles > 2 * s.G ? n_tiles : 2 * s.G;
+  CW_CHECK(cudaMemsetAsync(s.cnt, 0, (size_t)nsync * sizeof(int), st));
   // the same path as cwen_cuda_gemvb (local X for the shapes that allow it,
   // else X preparation + GEMV), so both give the same bits
   CW_CHECK(gemv_run_x(m, dX, xs, B, dY, ys, EPI_STORE, s, st, false));

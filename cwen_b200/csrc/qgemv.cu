@@ -861,6 +861,8 @@ static cudaError_t gemv_launch(const QMat &m, int B, float *Y, int ys, int epi, 
   a.epi = epi;
   a.ws = s.ws;
   a.cnt = s.cnt;
+  if (++s.epoch == 0) s.epoch = 1;
+  a.epoch = s.epoch;
   a.err = s.err;
   a.xr = xr;
   a.xrs = xrs;
@@ -879,7 +881,7 @@ static cudaError_t gemv_launch(const QMat &m, int B, float *Y, int ys, int epi, 
   for (int i = 0; i < QG_MAX_PEERS; i++) a.yp[i] = i < s.np ? s.yp[i] : nullptr;
   int n_tiles;
   const long long g = gemv_grid(m, s, n_tiles, a.units);
-  if (n_tiles > s.max_tiles) return cudaErrorInvalidValue;
+  if (n_tiles > s.max_tiles || 2 * g > s.max_tiles) return cudaErrorInvalidValue;  // counters / flags
   a.G = (int)g;
   // 2 to 4 contributors per tile: reduce inside a thread-block cluster
   // (distributed shared memory) instead of through global scratch

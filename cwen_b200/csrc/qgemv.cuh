@@ -76,7 +76,9 @@ struct GemvScratch {
   uint4 *xf = nullptr;   // X operands, >= (Kmax/32) * 128 uint4 (2 KB per 32-block)
   int *xexp = nullptr;   // [16] per-column exponents
   float *ws = nullptr;   // split-K partials [G][2][WS_TILE_FLOATS]
-  int *cnt = nullptr;    // per CTA-tile arrival counters (zero, self-resetting)
+  int *cnt = nullptr;    // split-K sync words (zeroed at allocation): per-tile arrival counters
+                         // of the tcgen05 kernel, per (CTA, slot) partial flags of the mma kernel
+  int epoch = 0;         // the mma kernel's last flag value (never 0)
   int *err = nullptr;    // set when a bounded wait gave up (0 = fine)
   int G = 0;             // persistent grid size (CTAs), at most one per SM
   int kmax = 0;

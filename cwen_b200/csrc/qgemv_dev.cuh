@@ -70,6 +70,8 @@ struct GemvArgs {
   // one per GPU of the shard group (the local one included), all written.
   int row0, np;
   float *yp[QG_MAX_PEERS];
+  // mma kernel, global split-K mode: this launch's value of the partial flags
+  int epoch;
 };
 
 // Offset in Y of local row `row` (row0 + row of the full output), column col.
@@ -114,7 +116,7 @@ CW_DEV float split_unscale(const GemvArgs &a, int col) {
 // calls it (the SwiGLU pairs gate and up rows across the warp's halves).
 template <int NC4>
 CW_DEV void split_epilogue(const GemvArgs &a, int mt0, int mt, int row, bool live, const float4 (&sum)[NC4],
-                           float *wst) {
+                           float *wst, const float *ypre = nullptr) {
 #pragma unroll
   for (int n = 0; n < NC4; n++) {
     const float e4[4] = {sum[n].x, sum[n].y, sum[n].z, sum[n].w};
@@ -126,7 +128,7 @@ CW_DEV void split_epilogue(const GemvArgs &a, int mt0, int mt, int row, bool liv
         float v2 = 0.f;
         const int grow = (mt0 + mt) * 16 + row;
         if (live && grow < a.M) {
-          const float v = a.y[y_off(a, col, grow)] + e4[j] * split_unscale(a, col);
+          const float v = (ypre ? ypre[col] : a.y[y_off(a, col, grow)]) + e4[j] * split_unscale(a, col);
           v2 = v * v;
         }
         v2 = warp_sum(v2);
@@ -141,7 +143,12 @@ CW_DEV void split_epilogue(const GemvArgs &a, int mt0, int mt, int row, bool liv
         }
       } else if (live) {
         const int grow = (mt0 + mt) * 16 + row;
-        if (grow < a.M) y_out(a, col, grow, e4[j] * sc);
+        if (grow < a.M) {
+          if (ypre && a.epi == EPI_ADD)
+            y_put(a, y_off(a, col, grow), ypre[col] + e4[j] * sc);
+          else
+            y_out(a, col, grow, e4[j] * sc);
+        }
       }
     }
   }

@@ -185,8 +185,9 @@ struct QgLayout {
   // local-X variant: the CTA's k-range of X fragments, resident (<= QG_XL_KP k-pairs x 4 n-tiles)
   static constexpr int XL_OFF = BAR_OFF + 256;
   static constexpr int XL_BYTES = XL ? QG_XL_KP * 4 * 1024 : 0;
-  static constexpr int XE_OFF = XL_OFF + XL_BYTES;  // per column: 2^-e [16] floats, scratch [16][16] floats
-  static constexpr int SMEM = XE_OFF + (XL ? 64 + 16 * 16 * 4 : 0);
+  // per column: 2^-e [16] floats, per-warp sums [16][16] floats, prologue maxima [16] ints and scales [16] floats
+  static constexpr int XE_OFF = XL_OFF + XL_BYTES;
+  static constexpr int SMEM = XE_OFF + (XL ? 64 + 16 * 16 * 4 + 128 : 0);
   static_assert(WB % 16 == 0 && XB % 16 == 0 && STAGE % 16 == 0, "bulk copies need 16-byte multiples");
   static_assert(SMEM <= 227 * 1024, "shared memory");
 };
@@ -199,96 +200,127 @@ struct QgLayout {
 // f16 hi/lo fragments in shared memory, scaled by the CTA's own power of two
 // 2^e (max |x| over the range in [2^14, 2^15)); xun[col] = 2^-e unscales the
 // CTA's results.  The fragments hold the same values and layout gemv_prep_x
-// emits, except for the exponent's range.  Warp b owns column b; lane l holds
-// the 32-blocks l and l + 32 of the range in registers (one load round trip),
-// so 2 * nkp <= 64.
+// emits, except for the exponent's range.  The work is spread over all 512
+// threads: an item is (column b, 32-block kb, lane quarter t), the 8 values
+// one B-operand lane holds; every load of the prologue is issued in one
+// round (items, row norm partials), the column maxima meet in shared memory
+// (an integer max of non-negative floats: order-free), and the second pass
+// converts from registers (the first two items of a thread) or reloads.
+// cm: [16] int column maxima, ssc: [16] float row scales (shared memory).
 template <int NT>
-CW_DEV void x_local_prologue(const GemvArgs &a, uint4 *xl, float *xun, int ka0, int nkp) {
-  constexpr int NTH = QG_CONS_WARPS * 32;
-  const int lane = threadIdx.x & 31, b = threadIdx.x >> 5;
-  const int nblk = 2 * nkp;
-  if (b < a.B) {
-    const float4 *x = reinterpret_cast<const float4 *>(a.xr + (size_t)b * a.xrs + (size_t)ka0 * 64);
-    const float4 *wn = reinterpret_cast<const float4 *>(a.xw + (size_t)ka0 * 64);
-    // RMSNorm: the row's sum of squares from the per-CTA partials of the GEMV
-    // that wrote it, in slot order then a fixed xor tree (every CTA, every B)
-    float ss = 0.f;
-    if (a.xw)
+CW_DEV void x_local_prologue(const GemvArgs &a, uint4 *xl, float *xun, int *cm, float *ssc, int ka0, int nkp) {
+  constexpr int NTH = QG_CONS_WARPS * 32, KEEP = 2;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int nblk = 2 * nkp, nitem = a.B * nblk * 4;
+  if (tid < 16) cm[tid] = 0;
+  // RMSNorm: the row's sum of squares from the per-CTA partials of the GEMV
+  // that wrote it, in slot order then a fixed xor tree (warp b, column b)
+  float ss = 0.f;
+  if (a.xw && warp < a.B)
 #pragma unroll
-      for (int i = 0; i < 5; i++)
-        if (lane + 32 * i < a.st_g) ss += __ldcg(a.st_in + (size_t)(lane + 32 * i) * QG_STAT_COLS + b);
-    // pass 1: max |w x| (or |x|) over the range, block j = 0 kept in registers;
-    // pass 2 converts block 0 from registers and reloads block 1 (cache hits)
-    float4 v[8];
-    float m = 0.f;
+    for (int i = 0; i < 5; i++)
+      if (lane + 32 * i < a.st_g) ss += __ldcg(a.st_in + (size_t)(lane + 32 * i) * QG_STAT_COLS + warp);
+  // item it -> column b = it / (nblk * 4), block kb, quarter t: elements
+  // 4t..4t+3 and 16+4t..16+4t+3 of the block
+  auto item_ptr = [&](int it, int &b, int &kb, int &t) {
+    b = it / (nblk * 4);
+    const int r = it - b * nblk * 4;
+    kb = r >> 2;
+    t = r & 3;
+  };
+  float4 kv[KEEP][2];
+  named_bar(1, NTH);  // cm cleared
 #pragma unroll
-    for (int j = 0; j < 2; j++) {
-      const int kb = lane + 32 * j;
-      if (kb < nblk) {
-        float4 u[8];
-#pragma unroll
-        for (int q = 0; q < 8; q++) u[q] = __ldg(x + kb * 8 + q);
-        if (a.xw) {
-#pragma unroll
-          for (int q = 0; q < 8; q++) {
-            const float4 w4 = __ldg(wn + kb * 8 + q);
-            u[q] = make_float4(w4.x * u[q].x, w4.y * u[q].y, w4.z * u[q].z, w4.w * u[q].w);
-          }
-        }
-#pragma unroll
-        for (int q = 0; q < 8; q++) {
-          m = fmaxf(m, fmaxf(fmaxf(fabsf(u[q].x), fabsf(u[q].y)), fmaxf(fabsf(u[q].z), fabsf(u[q].w))));
-          if (j == 0) v[q] = u[q];
-        }
+  for (int j = 0; j < KEEP; j++) {
+    const int it = tid + j * NTH;
+    if (it < nitem) {
+      int b, kb, t;
+      item_ptr(it, b, kb, t);
+      const float *x = a.xr + (size_t)b * a.xrs + (size_t)ka0 * 64 + kb * 32 + 4 * t;
+      float4 u0 = __ldg(reinterpret_cast<const float4 *>(x)), u1 = __ldg(reinterpret_cast<const float4 *>(x + 16));
+      if (a.xw) {
+        const float *w = a.xw + (size_t)ka0 * 64 + kb * 32 + 4 * t;
+        const float4 w0 = __ldg(reinterpret_cast<const float4 *>(w)), w1 = __ldg(reinterpret_cast<const float4 *>(w + 16));
+        u0 = make_float4(w0.x * u0.x, w0.y * u0.y, w0.z * u0.z, w0.w * u0.w);
+        u1 = make_float4(w1.x * u1.x, w1.y * u1.y, w1.z * u1.z, w1.w * u1.w);
       }
+      kv[j][0] = u0;
+      kv[j][1] = u1;
+      const float mi = fmaxf(fmaxf(fmaxf(fabsf(u0.x), fabsf(u0.y)), fmaxf(fabsf(u0.z), fabsf(u0.w))),
+                             fmaxf(fmaxf(fabsf(u1.x), fabsf(u1.y)), fmaxf(fabsf(u1.z), fabsf(u1.w))));
+      atomicMax(cm + b, __float_as_int(mi));
     }
-    m = warp_max(m);
-    float s = 1.f;
+  }
+  for (int it = tid + KEEP * NTH; it < nitem; it += NTH) {
+    int b, kb, t;
+    item_ptr(it, b, kb, t);
+    const float *x = a.xr + (size_t)b * a.xrs + (size_t)ka0 * 64 + kb * 32 + 4 * t;
+    float4 u0 = __ldg(reinterpret_cast<const float4 *>(x)), u1 = __ldg(reinterpret_cast<const float4 *>(x + 16));
     if (a.xw) {
-      s = 1.f / sqrtf(warp_sum(ss) / (float)(a.kp * 64) + 1e-6f);
-      m *= s;  // max |(w x) s| = max |w x| * s: s > 0 and rounding is monotonic
+      const float *w = a.xw + (size_t)ka0 * 64 + kb * 32 + 4 * t;
+      const float4 w0 = __ldg(reinterpret_cast<const float4 *>(w)), w1 = __ldg(reinterpret_cast<const float4 *>(w + 16));
+      u0 = make_float4(w0.x * u0.x, w0.y * u0.y, w0.z * u0.z, w0.w * u0.w);
+      u1 = make_float4(w1.x * u1.x, w1.y * u1.y, w1.z * u1.z, w1.w * u1.w);
     }
-    const int e = xfrag_exponent(m);
-    // ((w x) s) 2^e == (w x) (s 2^e) exactly: 2^e only shifts the exponent
-    const float sc = s * __int_as_float((127 + e) << 23);
-    if (lane == 0) xun[b] = __int_as_float((127 - e) << 23);
-#pragma unroll 1
-    for (int j = 0; j < 2; j++) {
-      const int kb = lane + 32 * j;
-      if (kb < nblk) {
-        if (j == 1) {
-#pragma unroll
-          for (int q = 0; q < 8; q++) v[q] = __ldg(x + kb * 8 + q);
-          if (a.xw) {
-#pragma unroll
-            for (int q = 0; q < 8; q++) {
-              const float4 w4 = __ldg(wn + kb * 8 + q);
-              v[q] = make_float4(w4.x * v[q].x, w4.y * v[q].y, w4.z * v[q].z, w4.w * v[q].w);
-            }
-          }
-        }
-        const float *r = reinterpret_cast<const float *>(v);
-        // B operand lane (col & 3, t): (x[4t], x[4t+2]) (x[4t+1], x[4t+3]) (x[4t+16], x[4t+18]) (x[4t+17], x[4t+19])
-#pragma unroll
-        for (int t = 0; t < 4; t++) {
-          const int js[8] = {4 * t, 4 * t + 2, 4 * t + 1, 4 * t + 3, 4 * t + 16, 4 * t + 18, 4 * t + 17, 4 * t + 19};
-          uint32_t hw[4], lw[4];
-#pragma unroll
-          for (int i = 0; i < 4; i++) {
-            const float v0 = r[js[2 * i]] * sc, v1 = r[js[2 * i + 1]] * sc;
-            const half h0 = __float2half_rn(v0), h1 = __float2half_rn(v1);
-            const half l0 = __float2half_rn(v0 - __half2float(h0)), l1 = __float2half_rn(v1 - __half2float(h1));
-            hw[i] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
-            lw[i] = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
-          }
-          uint4 *o = xl + ((size_t)kb * NT + (b >> 2)) * 32 + (b & 3) * 4 + t;
-          o[0] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-          o[16] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
-        }
+    const float mi = fmaxf(fmaxf(fmaxf(fabsf(u0.x), fabsf(u0.y)), fmaxf(fabsf(u0.z), fabsf(u0.w))),
+                           fmaxf(fmaxf(fabsf(u1.x), fabsf(u1.y)), fmaxf(fabsf(u1.z), fabsf(u1.w))));
+    atomicMax(cm + b, __float_as_int(mi));
+  }
+  if (a.xw && warp < a.B) {
+    ss = warp_sum(ss);
+    if (lane == 0) ssc[warp] = 1.f / sqrtf(ss / (float)(a.kp * 64) + 1e-6f);
+  }
+  named_bar(1, NTH);  // column maxima and row scales complete
+  if (tid < 16) {
+    if (tid < a.B) {
+      float mx = __int_as_float(cm[tid]);
+      const float s = a.xw ? ssc[tid] : 1.f;
+      mx *= s;  // max |(w x) s| = max |w x| * s: s > 0 and rounding is monotonic
+      const int e = xfrag_exponent(mx);
+      xun[tid] = __int_as_float((127 - e) << 23);
+      // ((w x) s) 2^e == (w x) (s 2^e) exactly: 2^e only shifts the exponent
+      ssc[tid] = s * __int_as_float((127 + e) << 23);
+    } else {
+      xun[tid] = 1.f;  // padding column
+    }
+  }
+  named_bar(1, NTH);  // per-column scales ready
+  for (int j = 0, it = tid; it < nitem; j++, it += NTH) {
+    int b, kb, t;
+    item_ptr(it, b, kb, t);
+    float r[8];
+    if (j < KEEP) {
+      const float4 u0 = j == 0 ? kv[0][0] : kv[1][0], u1 = j == 0 ? kv[0][1] : kv[1][1];
+      r[0] = u0.x; r[1] = u0.y; r[2] = u0.z; r[3] = u0.w;
+      r[4] = u1.x; r[5] = u1.y; r[6] = u1.z; r[7] = u1.w;
+    } else {
+      const float *x = a.xr + (size_t)b * a.xrs + (size_t)ka0 * 64 + kb * 32 + 4 * t;
+      float4 u0 = __ldg(reinterpret_cast<const float4 *>(x)), u1 = __ldg(reinterpret_cast<const float4 *>(x + 16));
+      if (a.xw) {
+        const float *w = a.xw + (size_t)ka0 * 64 + kb * 32 + 4 * t;
+        const float4 w0 = __ldg(reinterpret_cast<const float4 *>(w)), w1 = __ldg(reinterpret_cast<const float4 *>(w + 16));
+        u0 = make_float4(w0.x * u0.x, w0.y * u0.y, w0.z * u0.z, w0.w * u0.w);
+        u1 = make_float4(w1.x * u1.x, w1.y * u1.y, w1.z * u1.z, w1.w * u1.w);
       }
+      r[0] = u0.x; r[1] = u0.y; r[2] = u0.z; r[3] = u0.w;
+      r[4] = u1.x; r[5] = u1.y; r[6] = u1.z; r[7] = u1.w;
     }
-  } else if (lane == 0 && b < 16) {
-    xun[b] = 1.f;  // padding column
+    const float sc = ssc[b];
+    // B operand lane (col & 3, t): (x[4t], x[4t+2]) (x[4t+1], x[4t+3]) (x[4t+16], x[4t+18]) (x[4t+17], x[4t+19])
+    // r[] holds x[4t..4t+3] then x[4t+16..4t+19]
+    const int js[8] = {0, 2, 1, 3, 4, 6, 5, 7};
+    uint32_t hw[4], lw[4];
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      const float v0 = r[js[2 * i]] * sc, v1 = r[js[2 * i + 1]] * sc;
+      const half h0 = __float2half_rn(v0), h1 = __float2half_rn(v1);
+      const half l0 = __float2half_rn(v0 - __half2float(h0)), l1 = __float2half_rn(v1 - __half2float(h1));
+      hw[i] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
+      lw[i] = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
+    }
+    uint4 *o = xl + ((size_t)kb * NT + (b >> 2)) * 32 + (b & 3) * 4 + t;
+    o[0] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+    o[16] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
   }
   named_bar(1, NTH);
 }
@@ -395,7 +427,9 @@ __global__ void __launch_bounds__(QGM_THREADS, 1) qgemv_kernel(GemvArgs a) {
   float *wst = XL ? xun + 16 + warp * 16 : nullptr;  // this warp's output sums of squares per column
   if (XL && a.st_out && lane < 16) wst[lane] = 0.f;
   if (XL) {
-    x_local_prologue<NT>(a, reinterpret_cast<uint4 *>(smem + Lay::XL_OFF), xun, ka0, (int)(u_end - u_begin));
+    x_local_prologue<NT>(a, reinterpret_cast<uint4 *>(smem + Lay::XL_OFF), xun,
+                         reinterpret_cast<int *>(xun + 16 + 16 * 16), xun + 16 + 16 * 16 + 16, ka0,
+                         (int)(u_end - u_begin));
     if (threadIdx.x == 0) mbar_arrive(xready);
   }
   const float zero4[4] = {0.f, 0.f, 0.f, 0.f};
@@ -404,7 +438,7 @@ __global__ void __launch_bounds__(QGM_THREADS, 1) qgemv_kernel(GemvArgs a) {
   uint32_t ph = 0;   // its phase parity
   long long u = u_begin;
   bool first_seg = true;
-  int ptile[2];  // split tiles of this CTA (its first and last segments), uniform across the CTA
+  int ptile[2], pslot[2];  // split tiles of this CTA (its first and last segments) and their partial slots
   int np = 0;
   while (u < u_end) {
     const int tile = (int)(u / a.kp);
@@ -512,6 +546,7 @@ __global__ void __launch_bounds__(QGM_THREADS, 1) qgemv_kernel(GemvArgs a) {
               *reinterpret_cast<float2 *>(p) = v;
             }
       }
+      pslot[np] = slot;
       ptile[np++] = tile;
     }
     u += nk;
@@ -575,42 +610,60 @@ __global__ void __launch_bounds__(QGM_THREADS, 1) qgemv_kernel(GemvArgs a) {
   }
   // Global mode.  All contributors of a split tile are resident (one CTA per
   // SM, G <= SMs, and PDL successors start only after every CTA of this grid
-  // started), and each first counts itself in for all its split tiles and
-  // only then waits, so the waits below end; they are bounded all the same.
-  // The counter of a tile goes 0 -> n (partials parked) -> 2n (shares
-  // reduced) -> 0.
-  named_bar(1, QG_CONS_WARPS * 32);
-  if (threadIdx.x == 0) {
-    __threadfence();  // the CTA's partials (ordered before by the barrier), before the arrival
-    for (int j = 0; j < np; j++) atomicAdd(a.cnt + ptile[j], 1);
-  }
+  // started), and each first publishes all its partials and only then waits,
+  // so the waits below end; they are bounded all the same.  A contributor
+  // publishes a partial by storing this launch's epoch into the flag of its
+  // (CTA, slot) with release semantics; flags are never reset (a flag holding
+  // an older epoch is simply not ready), so the CTA leaves right after its
+  // share of the reduction.
+  named_bar(1, QG_CONS_WARPS * 32);  // every partial of this CTA is stored
+  if (threadIdx.x == 0)
+    for (int j = 0; j < np; j++) st_release_gpu(a.cnt + c * 2 + pslot[j], a.epoch);
   for (int j = 0; j < np; j++) {
     const int tile = ptile[j];
     const long long tu0 = (long long)tile * a.kp, tu1 = tu0 + a.kp - 1;
     const int c_first = (int)(((tu0 + 1) * a.G - 1) / a.units);
     const int c_last = (int)(((tu1 + 1) * a.G - 1) / a.units);
     const int ncon = c_last - c_first + 1, r = c - c_first;
-    if (threadIdx.x == 0) {
+    // partial slot of contributor cc: only the first contributor can have
+    // begun before the tile (its slot 1); the tile opens every other's range
+    const int slot_first = (long long)c_first * a.units / a.G >= tu0 ? 0 : 1;
+    const int mt0 = tile * QG_TILE_MT + warp * 2;
+    const bool mine = warp % ncon == r;
+    const bool live = mt0 + mt < a.n_mt;
+    // the rows this lane's share adds onto (EPI_ADD), loaded before the wait
+    float yv[NT * 4];
+    if (mine && a.epi == EPI_ADD)
+#pragma unroll
+      for (int i = 0; i < NT * 4; i++) {
+        const int grow = (mt0 + mt) * 16 + row;
+        yv[i] = live && i < a.B && grow < a.M ? __ldcg(a.y + y_off(a, i, grow)) : 0.f;
+      }
+    if (warp == 0) {  // lane q waits for contributors q, q + 32, ...
       const long long t0 = cycles_now();
-      while (ok && *(volatile int *)(a.cnt + tile) < ncon) {
-        if (spin_expired(t0)) {
-          atomicExch(a.err, 3);
-          ok = false;
+      bool good = ok;
+      for (int q = lane; q < ncon && good; q += 32) {
+        const int cc = c_first + q;
+        const int *f = a.cnt + cc * 2 + (q == 0 ? slot_first : 0);
+        while (ld_acquire_gpu(f) != a.epoch) {
+          if (spin_expired(t0)) {
+            atomicExch(a.err, 3);
+            good = false;
+            break;
+          }
         }
       }
-      __threadfence();  // the other contributors' partials, after their arrivals
-      last_p[0] = ok;
+      good = __all_sync(0xffffffffu, good);
+      if (lane == 0) last_p[0] = good;
     }
-    named_bar(1, QG_CONS_WARPS * 32);
+    named_bar(1, QG_CONS_WARPS * 32);  // warp 0 saw every flag: the partials are visible to the CTA
     const bool go = last_p[0] != 0;
-    const int mt0 = tile * QG_TILE_MT + warp * 2;
-    if (go && warp % ncon == r) {
-      const bool live = mt0 + mt < a.n_mt;
+    if (go && mine) {
       float4 sum[NT];
 #pragma unroll
       for (int n = 0; n < NT; n++) sum[n] = make_float4(0.f, 0.f, 0.f, 0.f);
       const size_t off = (size_t)((warp * 2 + mt) * 16 + row) * 16;
-      constexpr int CH = NT == 1 ? 8 : (NT == 2 ? 4 : 2);  // independent loads in flight per lane
+      constexpr int CH = NT == 1 ? 16 : (NT == 2 ? 4 : 2);  // independent loads in flight per lane
       if (live) {
         for (int c0 = c_first; c0 <= c_last; c0 += CH) {
           float4 v[CH][NT];
@@ -618,8 +671,7 @@ __global__ void __launch_bounds__(QGM_THREADS, 1) qgemv_kernel(GemvArgs a) {
           for (int q = 0; q < CH; q++) {
             const int cc = c0 + q;
             if (cc > c_last) break;
-            const long long cu0 = (long long)cc * a.units / a.G;
-            const float *src = a.ws + ((size_t)cc * 2 + (cu0 >= tu0 ? 0 : 1)) * WS_TILE_FLOATS + off;
+            const float *src = a.ws + ((size_t)cc * 2 + (cc == c_first ? slot_first : 0)) * WS_TILE_FLOATS + off;
 #pragma unroll
             for (int n = 0; n < NT; n++) v[q][n] = __ldcg(reinterpret_cast<const float4 *>(src + 4 * n));
           }
@@ -636,13 +688,11 @@ __global__ void __launch_bounds__(QGM_THREADS, 1) qgemv_kernel(GemvArgs a) {
           }
         }
       }
-      split_epilogue<NT>(a, mt0, mt, row, live, sum, wst);
+      split_epilogue<NT>(a, mt0, mt, row, live, sum, wst, a.epi == EPI_ADD ? yv : nullptr);
     }
-    named_bar(1, QG_CONS_WARPS * 32);  // every read of the partials of this tile is done
-    if (threadIdx.x == 0 && go) {
-      if (atomicAdd(a.cnt + tile, 1) == 2 * ncon - 1) a.cnt[tile] = 0;
-    }
+    if (j + 1 < np) named_bar(1, QG_CONS_WARPS * 32);  // last_p is reused by the next tile
   }
+  if (XL && a.st_out) named_bar(1, QG_CONS_WARPS * 32);  // every warp's sums of squares are in
   if (XL && a.st_out && threadIdx.x < QG_STAT_COLS) {  // this CTA's slot: the warps' sums in warp order
     const float *w0 = xun + 16;
     float ss = 0.f;

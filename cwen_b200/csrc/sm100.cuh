@@ -38,6 +38,15 @@ CW_DEV bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
 constexpr long long SPIN_TIMEOUT_CYCLES = 4000000000ll;
 CW_DEV long long cycles_now() { return clock64(); }
 CW_DEV bool spin_expired(long long t0) { return clock64() - t0 > SPIN_TIMEOUT_CYCLES; }
+// GPU-scope release store / acquire load of a flag in global memory.
+CW_DEV void st_release_gpu(int *p, int v) {
+  asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+CW_DEV int ld_acquire_gpu(const int *p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
 // Bounded wait for the phase of `parity` to complete.  Gives up (returns
 // false) after SPIN_TIMEOUT_CYCLES or as soon as another thread of the CTA
 // raised *abort.
