@@ -333,21 +333,18 @@ static int run_layer_block(int l, int B, int pos0, cudaStream_t st) {
     nl += 3;
   }
   // ssm_out reads the gated-norm rows raw, wo the attention combine's rows
-  if (w.linear) CW_CHECK(timed_gemv(w.out_proj, B, M.x, H, EPI_ADD, st, M.gdn_out, M.Z));
-  else CW_CHECK(timed_gemv(w.out_proj, B, M.x, H, EPI_ADD, st, M.attn_o, d.n_head * 256));
-  const bool raw = gemv_raw_x(E.gs);  // post_attention_norm inside the gate/up GEMV
-  if (!raw) {
-    CW_CHECK(launch_norm_prep(M.x, w.post_norm, H, B, E.gs, nullptr, st));
-    nl++;
-  }
+  // (with the new residual rows' sums of squares for the gate/up GEMV's norm)
+  if (w.linear) CW_CHECK(timed_gemv(w.out_proj, B, M.x, H, EPI_ADD, st, M.gdn_out, M.Z, nullptr, true));
+  else CW_CHECK(timed_gemv(w.out_proj, B, M.x, H, EPI_ADD, st, M.attn_o, d.n_head * 256, nullptr, true));
   const bool sh = shard().on();
   int r0, r1;
   if (sh) {
     shard_rows(I, 16, r0, r1);
     shard_target(E.gs, M.h, r0);
   }
-  cudaError_t ge = raw ? timed_gemv(w.gate_up, B, M.h, I, EPI_SWIGLU, st, M.x, H, w.post_norm)
-                       : timed_gemv(w.gate_up, B, M.h, I, EPI_SWIGLU, st);
+  // post_attention_norm inside the gate/up GEMV when its shape allows local
+  // X, else a row kernel first (gemv_run_xn decides; the launch count follows)
+  cudaError_t ge = timed_gemv(w.gate_up, B, M.h, I, EPI_SWIGLU, st, M.x, H, w.post_norm);
   if (sh) {
     shard_untarget(E.gs);
     if (ge == cudaSuccess) ge = shard_barrier(st);

@@ -822,7 +822,7 @@ static long long gemv_grid(const QMat &m, const GemvScratch &s, int &n_tiles, lo
 }
 
 // The local-X variant applies when the grid is tile-aligned and every CTA's
-// k-range holds at most QG_XL_KP k-pairs -- decided on the shape alone, so
+// k-range holds at most QG_XL_KP (tcgen05) / QG_XL_KP_MMA k-pairs -- decided on the shape alone, so
 // that every B takes the same path (batch invariance).
 static bool gemv_local_x(const QMat &m, const GemvScratch &s) {
   int n_tiles;
@@ -830,7 +830,7 @@ static bool gemv_local_x(const QMat &m, const GemvScratch &s) {
   const long long g = gemv_grid(m, s, n_tiles, units);
   if (m.type != 2 || n_tiles > g) return false;
   const long long ncon = g / n_tiles, kp = m.K / 64;
-  return (kp + ncon - 1) / ncon <= QG_XL_KP;
+  return (kp + ncon - 1) / ncon <= (s.tc ? QG_XL_KP : QG_XL_KP_MMA);
 }
 
 // Every tile split between >= 2 CTAs (each CTA one segment): the epilogue's

@@ -52,7 +52,8 @@ struct QgStage {
   static constexpr int WB = 2 * QB + 2 * QG_TILE_ROWS * 2;     // both blocks + their f16 scales
 };
 constexpr int WS_TILE_FLOATS = QG_TILE_MT * 16 * 16;   // split-K partials of one tile (16 columns)
-constexpr int QG_XL_KP = 20;  // local-X variant: at most this many k-pairs per CTA
+constexpr int QG_XL_KP = 20;  // local-X variant: at most this many k-pairs per CTA (tcgen05 kernel)
+constexpr int QG_XL_KP_MMA = 40;  // the same for the mma.sync kernel (its ring shrinks to make room)
 constexpr int QG_STAT_COLS = 16;  // per-CTA statistics slot: one float per column
 constexpr int QG_MAX_PEERS = 8;   // GPUs of a row-shard group
 

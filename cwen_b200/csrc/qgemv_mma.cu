@@ -180,14 +180,19 @@ struct QgLayout {
   static constexpr int WB = QG_TILE_MT * CHUNK;              // weights of one (tile, k-pair)
   static constexpr int XB = XL ? 0 : NT * 1024;              // X fragments of one k-pair (streamed)
   static constexpr int STAGE = WB + XB;
-  static constexpr int STAGES = TYPE == 8 ? 5 : 8;
-  static constexpr int BAR_OFF = STAGES * STAGE;
-  // local-X variant: the CTA's k-range of X fragments, resident (<= QG_XL_KP k-pairs x 4 n-tiles)
-  static constexpr int XL_OFF = BAR_OFF + 256;
-  static constexpr int XL_BYTES = XL ? QG_XL_KP * 4 * 1024 : 0;
+  // local-X variant: the CTA's k-range of X fragments, resident (<= QG_XL_KP_MMA k-pairs x NT n-tiles)
+  static constexpr int XL_BYTES = XL ? QG_XL_KP_MMA * NT * 1024 : 0;
   // per column: 2^-e [16] floats, per-warp sums [16][16] floats, prologue maxima [16] ints and scales [16] floats
+  static constexpr int XE_BYTES = XL ? 64 + 16 * 16 * 4 + 128 : 0;
+  // ring depth: 8 stages, fewer when the resident X needs the room (the
+  // depth changes only the overlap, never the arithmetic)
+  static constexpr int FIT = (227 * 1024 - 256 - XL_BYTES - XE_BYTES) / STAGE;
+  static constexpr int STAGES = TYPE == 8 ? 5 : (FIT < 8 ? FIT : 8);
+  static constexpr int BAR_OFF = STAGES * STAGE;
+  static constexpr int XL_OFF = BAR_OFF + 256;
   static constexpr int XE_OFF = XL_OFF + XL_BYTES;
-  static constexpr int SMEM = XE_OFF + (XL ? 64 + 16 * 16 * 4 + 128 : 0);
+  static constexpr int SMEM = XE_OFF + XE_BYTES;
+  static_assert(STAGES >= 3, "ring depth");
   static_assert(WB % 16 == 0 && XB % 16 == 0 && STAGE % 16 == 0, "bulk copies need 16-byte multiples");
   static_assert(SMEM <= 227 * 1024, "shared memory");
 };
@@ -337,7 +342,10 @@ __global__ void __launch_bounds__(QGM_THREADS, 1) qgemv_kernel(GemvArgs a) {
   int *last_p = const_cast<int *>(abort_p) + 1;  // [2]
 
   const int c = blockIdx.x;
-  const long long u_begin = (long long)c * a.units / a.G, u_end = (long long)(c + 1) * a.units / a.G;
+  // unit arithmetic in 32 bits (the launcher checks units * (G + 1) < 2^31):
+  // a 64-bit division is a long software sequence on the critical path
+  const int units = (int)a.units;
+  const int u_begin = c * units / a.G, u_end = (c + 1) * units / a.G;
   if (u_begin >= u_end) return;  // whole CTA, before any barrier
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   pdl_trigger();
@@ -361,14 +369,14 @@ __global__ void __launch_bounds__(QGM_THREADS, 1) qgemv_kernel(GemvArgs a) {
     // weights, so the weight source just advances; no divisions in the loops.
     if (lane == 0 && (!XL || warp == QG_CONS_WARPS)) {  // local X: no X copies
       const bool wprod = warp == QG_CONS_WARPS;
-      const int n = (int)(u_end - u_begin);
+      const int n = u_end - u_begin;
       const uint8_t *wsrc = a.w + (size_t)u_begin * Lay::WB;
       const uint8_t *xbase = reinterpret_cast<const uint8_t *>(a.xf);
       // Weights are not written by any kernel of the decode step: the weight
       // producer never waits for the previous kernel (PDL), so the ring fills
       // while that kernel finishes.  X is that kernel's output.
       if (!wprod) pdl_wait();
-      int k = (int)(u_begin % a.kp);
+      int k = u_begin % a.kp;
       int st = 0;
       uint32_t ph = 0;
       int issued = 0;
@@ -422,29 +430,29 @@ __global__ void __launch_bounds__(QGM_THREADS, 1) qgemv_kernel(GemvArgs a) {
   // ---------------- consumers ----------------
   pdl_wait();  // before touching Y, the split-K partials or the tile counters
   const int g = lane >> 2, t = lane & 3;
-  const int ka0 = (int)(u_begin % a.kp);  // local X: the CTA's one segment starts here
+  const int ka0 = u_begin % a.kp;  // local X: the CTA's one segment starts here
   float *xun = XL ? reinterpret_cast<float *>(smem + Lay::XE_OFF) : nullptr;
   float *wst = XL ? xun + 16 + warp * 16 : nullptr;  // this warp's output sums of squares per column
   if (XL && a.st_out && lane < 16) wst[lane] = 0.f;
   if (XL) {
     x_local_prologue<NT>(a, reinterpret_cast<uint4 *>(smem + Lay::XL_OFF), xun,
                          reinterpret_cast<int *>(xun + 16 + 16 * 16), xun + 16 + 16 * 16 + 16, ka0,
-                         (int)(u_end - u_begin));
+                         u_end - u_begin);
     if (threadIdx.x == 0) mbar_arrive(xready);
   }
   const float zero4[4] = {0.f, 0.f, 0.f, 0.f};
   bool ok = true;
   int st = 0;        // ring position, advanced identically by every consumer warp and the producer
   uint32_t ph = 0;   // its phase parity
-  long long u = u_begin;
+  int u = u_begin;
   bool first_seg = true;
   int ptile[2], pslot[2];  // split tiles of this CTA (its first and last segments) and their partial slots
   int np = 0;
   while (u < u_end) {
-    const int tile = (int)(u / a.kp);
-    const int ka = (int)(u % a.kp);
-    const long long remain = u_end - u;
-    const int kb_end = (int)((long long)(a.kp - ka) < remain ? a.kp : ka + remain);
+    const int tile = u / a.kp;
+    const int ka = u - tile * a.kp;
+    const int remain = u_end - u;
+    const int kb_end = a.kp - ka < remain ? a.kp : ka + remain;
     const int nk = kb_end - ka;
     const int mt0 = tile * QG_TILE_MT + warp * 2;
     const bool has0 = mt0 < a.n_mt, has1 = mt0 + 1 < a.n_mt;
@@ -621,13 +629,13 @@ __global__ void __launch_bounds__(QGM_THREADS, 1) qgemv_kernel(GemvArgs a) {
     for (int j = 0; j < np; j++) st_release_gpu(a.cnt + c * 2 + pslot[j], a.epoch);
   for (int j = 0; j < np; j++) {
     const int tile = ptile[j];
-    const long long tu0 = (long long)tile * a.kp, tu1 = tu0 + a.kp - 1;
-    const int c_first = (int)(((tu0 + 1) * a.G - 1) / a.units);
-    const int c_last = (int)(((tu1 + 1) * a.G - 1) / a.units);
+    const int tu0 = tile * a.kp, tu1 = tu0 + a.kp - 1;
+    const int c_first = ((tu0 + 1) * a.G - 1) / units;
+    const int c_last = ((tu1 + 1) * a.G - 1) / units;
     const int ncon = c_last - c_first + 1, r = c - c_first;
     // partial slot of contributor cc: only the first contributor can have
     // begun before the tile (its slot 1); the tile opens every other's range
-    const int slot_first = (long long)c_first * a.units / a.G >= tu0 ? 0 : 1;
+    const int slot_first = c_first * units / a.G >= tu0 ? 0 : 1;
     const int mt0 = tile * QG_TILE_MT + warp * 2;
     const bool mine = warp % ncon == r;
     const bool live = mt0 + mt < a.n_mt;
@@ -753,6 +761,7 @@ static cudaError_t launch_t(GemvArgs a, cudaStream_t st) {
 
 
 cudaError_t launch(const GemvArgs &a, int type, bool xl, cudaStream_t st) {
+  if (a.units * (a.G + 1) >= (1ll << 31)) return cudaErrorInvalidValue;  // the kernel's 32-bit unit arithmetic
   const int nt = (a.B + 3) / 4;  // n-tiles of 4 columns (hi | lo)
   if (xl) switch (nt) {
       case 1: return launch_t<2, 1, true>(a, st);
