@@ -4,7 +4,7 @@
 // write (run.c:2714-2737) and attention_heads_kv (run.c:2362-2409).
 //
 // Split-K decode: the KV range [t0, pos] of a query row is cut into splits of
-// S(pos) slots, the smallest power of two >= 64 with pos < 64 * S -- at most
+// S(pos) slots, the smallest power of two >= 32 with pos < 64 * S -- at most
 // 64 splits per row, so short contexts spread over many CTAs and long ones
 // leave few partials to merge.  One CTA per (kv head, slot range, row group)
 // runs an online softmax over its range in 32-slot chunks staged in shared
@@ -22,7 +22,8 @@ namespace cw {
 
 constexpr int HD = 256;
 constexpr int ACH = 32;     // slots per staged chunk
-constexpr int SPS = 64;     // smallest split
+static_assert(ACH <= 32, "one slot per lane");
+constexpr int SPS = 32;     // smallest split (>= ACH: a staged chunk never crosses a split)
 constexpr int NSPLIT = 64;  // splits per row at most
 CW_HOST_DEV int split_of(int p) {
   int S = SPS;

@@ -193,6 +193,7 @@ struct QgLayout {
   static constexpr int XE_OFF = XL_OFF + XL_BYTES;
   static constexpr int SMEM = XE_OFF + XE_BYTES;
   static_assert(STAGES >= 3, "ring depth");
+  static constexpr int XL_AHEAD = STAGES > 5 ? 4 : 2;  // weight stages issued before the local-X prologue ends
   static_assert(WB % 16 == 0 && XB % 16 == 0 && STAGE % 16 == 0, "bulk copies need 16-byte multiples");
   static_assert(SMEM <= 227 * 1024, "shared memory");
 };
@@ -334,6 +335,7 @@ template <int TYPE, int NT, bool XL>
 __global__ void __launch_bounds__(QGM_THREADS, 1) qgemv_kernel(GemvArgs a) {
   using Lay = QgLayout<TYPE, NT, XL>;
   constexpr int S = Lay::STAGES;
+  constexpr int XL_AHEAD = Lay::XL_AHEAD;
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t *full = reinterpret_cast<uint64_t *>(smem + Lay::BAR_OFF);
   uint64_t *empty = full + S;
@@ -387,9 +389,10 @@ __global__ void __launch_bounds__(QGM_THREADS, 1) qgemv_kernel(GemvArgs a) {
           break;
         }
         if (*abort_p) break;  // consumers gave up: issue nothing more
-        // Local X: two weight stages go ahead, the rest after the prologue has
-        // read X -- its loads would otherwise queue behind a full ring of weights.
-        if (XL && wprod && issued == 2 && !mbar_wait(xready, 0, abort_p)) {
+        // Local X: XL_AHEAD weight stages go ahead, the rest after the
+        // prologue has read X -- its loads would otherwise queue behind a
+        // full ring of weights.
+        if (XL && wprod && issued == XL_AHEAD && !mbar_wait(xready, 0, abort_p)) {
           ok = false;
           break;
         }
