@@ -80,6 +80,7 @@ _SIGS = {
     "cwen_cuda_stream": (C.c_void_p, []),
     "cwen_load_gguf": (C.c_int, [C.c_char_p]),
     "cwen_gguf_dims": (C.c_int, [C.c_char_p, C.POINTER(Dims)]),
+    "cwen_gguf_tensor_bytes": (C.c_int, [C.c_char_p, C.c_char_p, C.c_void_p, C.c_size_t, C.POINTER(C.c_int)]),
     "cwen_write_synth_gguf": (C.c_int, [C.c_char_p, C.POINTER(Dims), C.c_uint64, C.c_int]),
     "cw_model_tensor_count": (C.c_int, [C.POINTER(Dims)]),
     "cwen_load_synth": (C.c_int, [C.c_uint64, C.POINTER(Dims), C.c_int]),

@@ -7,7 +7,7 @@
  * Generated ids go to stdout, logs to stderr.  Knobs: CWEN_SPEC, CWEN_MTP,
  * CWEN_CTX (64..32768), CWEN_SPEC_NGRAM_N/MAX_DRAFT/MIN_DRAFT/COOLDOWN/DEBUG,
  * CWEN_NGRAM_CACHE, CWEN_SERVER (binary-frame server on stdin/stdout,
- * host/server.c), CWEN_DEVICE (GPU index).
+ * host/server.c), CWEN_DEVICE (GPU index), CWEN_REPACK (CWENR sidecar).
  */
 #define _GNU_SOURCE
 #include <errno.h>
@@ -30,6 +30,7 @@ static void usage(FILE *o) {
           "Environment:\n"
           "  CWEN_CTX=N             context window, 64..32768 (default 4096)\n"
           "  CWEN_DEVICE=N          GPU index (default 0)\n"
+          "  CWEN_REPACK=FILE       CWENR sidecar (auto: MODEL with .cwenr)\n"
           "  CWEN_SERVER=1          binary-frame server on stdin/stdout\n"
           "  CWEN_SPEC=1            block speculation (greedy-lossless); drafter: the\n"
           "                         model's MTP nextn head when present, else the n-gram map\n"

@@ -271,6 +271,249 @@ static int gg_open(const char *path, gg_file *g) {
   return CWEN_OK;
 }
 
+/* ---- CWENR sidecar (load_cwenr, run.c:3305-3643) ----
+ *
+ * The reference can take its Q4_0 weights from an offline sidecar written by
+ * its repack tool (format: tools/repack_q4.py:1-30).  Header, 32 bytes:
+ * "CWENR001", u32 version (2, 3 or 4), u32 entry count, u64 data base, and a
+ * stamp {u32 "CWEN", u32 size of the source GGUF in 4 KiB pages} (zeros: an
+ * unstamped sidecar).  Then one 128-byte entry per tensor: name[96], i32 ne0,
+ * i32 rows, u64 off_a, u64 off_b, u32 flags.  v2 entries point at packed
+ * 20-byte blocks {qs[16], f32 d} (off_a, off_b = byte count); v3 entries at a
+ * qs stream (16 B per block) and an f16 scale stream; v4 adds interleaved
+ * pairs (ffn_gate + ffn_up, attn_k + attn_v) that share one qs stream
+ * (qsA|qsB per block) and one scale stream (dA|dB), flags 1 and 2 naming the
+ * side (any other flag value is a solo v3 entry).
+ *
+ * The engine lays Q4_0 weights out for its own kernels when they are
+ * uploaded, so a sidecar only decides the bytes: a bound tensor's blocks are
+ * put back into GGUF block form (f16 d, qs[16]; a v2 f32 scale rounded to
+ * f16, nearest-even) on the host and uploaded like GGUF bytes.  What binds,
+ * and what makes the whole sidecar ignored, follows the reference:
+ *  - path: CWEN_REPACK when set and non-empty, else the GGUF path with
+ *    ".gguf" replaced by ".cwenr", else the GGUF path + ".cwenr"; no file
+ *    there means no sidecar;
+ *  - ignored: shorter than 32 bytes, bad magic, a stamp whose page count
+ *    is not the GGUF's (stale), version outside 2..4, more than 1024
+ *    entries, a data base outside the file or a directory past its end, or
+ *    no entry that binds;
+ *  - an entry is skipped when its name is not a Q4_0 tensor of the GGUF, its
+ *    shape differs, its streams reach past the end of the file (checked as
+ *    remainders, so offsets cannot wrap), or (v2) its byte count is not
+ *    20 B per block. */
+#define CR_ENT 128
+#define CR_MAX_ENT 1024
+#define CR_STAMP_TAG 0x4e455743u /* "CWEN" */
+
+typedef struct {
+  int ver;           /* 0: not bound; 2, 3 or 4 */
+  int side;          /* interleaved pair: 0 (flags 1) or 1 (flags 2); -1 solo */
+  const uint8_t *qs; /* v2: packed blocks; v3/v4: qs stream */
+  const uint8_t *sc; /* v3/v4: f16 scale stream */
+} cr_bind;
+
+typedef struct {
+  uint8_t *map;
+  size_t len;
+  cr_bind *b; /* one per GGUF tensor */
+  int bound, n_il;
+} cr_file;
+
+static void cr_close(cr_file *r) {
+  free(r->b);
+  if (r->map) munmap(r->map, r->len);
+  memset(r, 0, sizeof *r);
+}
+
+/* The sidecar path for a GGUF path (cwenr_path_for, run.c:3310-3325): 0, or
+ * -1 when it does not fit in cap. */
+static int cr_path(const char *gguf, char *out, size_t cap) {
+  const char *env = getenv("CWEN_REPACK");
+  if (env && env[0]) {
+    int k = snprintf(out, cap, "%s", env);
+    return k < 0 || (size_t)k >= cap ? -1 : 0;
+  }
+  const size_t n = strlen(gguf);
+  if (n > 5 && !strcmp(gguf + n - 5, ".gguf")) {
+    if (n + 1 >= cap) return -1; /* ".cwenr" is one byte longer than ".gguf" */
+    memcpy(out, gguf, n - 5);
+    memcpy(out + n - 5, ".cwenr", 7);
+    return 0;
+  }
+  int k = snprintf(out, cap, "%s.cwenr", gguf);
+  return k < 0 || (size_t)k >= cap ? -1 : 0;
+}
+
+/* Map the sidecar of the GGUF at gguf_path and bind its entries to g's
+ * tensors.  Never an error: an absent or unusable sidecar leaves r empty (the
+ * GGUF bytes are used), with the reason on stderr like the reference. */
+static void cr_open(const char *gguf_path, const gg_file *g, cr_file *r) {
+  memset(r, 0, sizeof *r);
+  char path[4096];
+  if (cr_path(gguf_path, path, sizeof path)) {
+    fprintf(stderr, "cwenr: sidecar path for %s does not fit; skipping sidecar\n", gguf_path);
+    return;
+  }
+  int fd = open(path, O_RDONLY);
+  if (fd < 0) return; /* optional */
+  struct stat st;
+  if (fstat(fd, &st) || !S_ISREG(st.st_mode) || st.st_size < 32) {
+    fprintf(stderr, "cwenr: %s: unusable, ignoring sidecar\n", path);
+    close(fd);
+    return;
+  }
+  r->len = (size_t)st.st_size;
+  void *m = mmap(NULL, r->len, PROT_READ, MAP_PRIVATE, fd, 0);
+  close(fd);
+  if (m == MAP_FAILED) {
+    fprintf(stderr, "cwenr: %s: mmap: %s\n", path, strerror(errno));
+    r->len = 0;
+    return;
+  }
+  r->map = (uint8_t *)m;
+  const uint8_t *p = r->map;
+  const char *why = NULL;
+  uint32_t ver = 0, n = 0, tag = 0, pages = 0;
+  uint64_t base = 0;
+  memcpy(&ver, p + 8, 4);
+  memcpy(&n, p + 12, 4);
+  memcpy(&base, p + 16, 8);
+  memcpy(&tag, p + 24, 4);
+  memcpy(&pages, p + 28, 4);
+  struct stat gs;
+  if (memcmp(p, "CWENR001", 8))
+    why = "bad magic";
+  else if (tag == CR_STAMP_TAG &&
+           (uint64_t)pages != (stat(gguf_path, &gs) == 0 ? ((uint64_t)gs.st_size + 4095) / 4096 : 0))
+    why = "stale sidecar (the GGUF changed since the repack)";
+  else if ((ver != 2 && ver != 3 && ver != 4) || n > CR_MAX_ENT || base >= r->len ||
+           32u + (size_t)n * CR_ENT > r->len)
+    why = "bad header";
+  if (!why) {
+    r->b = (cr_bind *)calloc(g->nt ? (size_t)g->nt : 1, sizeof *r->b);
+    if (!r->b) why = "out of host memory";
+  }
+  const size_t rem = r->len - (size_t)base; /* bytes from the data base on */
+  for (uint32_t i = 0; !why && i < n; i++) {
+    const uint8_t *e = p + 32 + (size_t)i * CR_ENT;
+    char name[96];
+    memcpy(name, e, 96);
+    name[95] = 0;
+    int32_t ne0, ne1;
+    uint64_t oa, ob;
+    uint32_t flags = 0;
+    memcpy(&ne0, e + 96, 4);
+    memcpy(&ne1, e + 100, 4);
+    memcpy(&oa, e + 104, 8);
+    memcpy(&ob, e + 112, 8);
+    if (ver >= 3) memcpy(&flags, e + 120, 4);
+    int ti = -1;
+    for (int k = 0; k < g->nt; k++)
+      if (!strcmp(g->t[k].name, name)) { ti = k; break; }
+    if (ti < 0) { fprintf(stderr, "cwenr: unknown %s\n", name); continue; }
+    const gg_tensor *x = &g->t[ti];
+    if (x->type != CWEN_T_Q4_0) { fprintf(stderr, "cwenr: skip non-Q4_0 %s\n", name); continue; }
+    const uint64_t rows = x->ne[1] * x->ne[2] * x->ne[3];
+    if ((uint64_t)(int64_t)ne0 != x->ne[0] || (uint64_t)(int64_t)ne1 != rows) {
+      fprintf(stderr, "cwenr: shape %s\n", name);
+      continue;
+    }
+    const uint64_t nblk = x->ne[0] / 32 * rows;
+    cr_bind b = {(int)ver, -1, NULL, NULL};
+    if (ver == 2) {
+      if (oa > rem || ob > rem - oa) { fprintf(stderr, "cwenr: OOB %s\n", name); continue; }
+      if (ob != nblk * 20) { fprintf(stderr, "cwenr: size %s\n", name); continue; }
+      b.qs = p + base + oa;
+    } else {
+      const int il = flags == 1 || flags == 2;
+      const uint64_t qsb = nblk * (il ? 32u : 16u), scb = nblk * (il ? 4u : 2u);
+      if (oa > rem || ob > rem || qsb > rem - oa || scb > rem - ob) {
+        fprintf(stderr, "cwenr: OOB %s\n", name);
+        continue;
+      }
+      b.side = il ? (int)flags - 1 : -1;
+      b.qs = p + base + oa;
+      b.sc = p + base + ob;
+      r->n_il += il;
+    }
+    r->b[ti] = b;
+    r->bound++;
+  }
+  if (!why && !r->bound) why = "no usable entries";
+  if (why) {
+    fprintf(stderr, "cwenr: %s: %s; ignoring sidecar\n", path, why);
+    cr_close(r);
+    return;
+  }
+  fprintf(stderr, "cwenr: v%u bound %d Q4 tensors (il=%d) from %s\n", ver, r->bound, r->n_il, path);
+}
+
+/* f32 -> f16 bits, round to nearest even (the conversion the reference
+ * applies to v2 scales, run.c:3623). */
+static uint16_t cr_f16(float f) {
+  _Float16 h = (_Float16)f;
+  uint16_t u;
+  memcpy(&u, &h, 2);
+  return u;
+}
+
+/* nblk blocks of a bound tensor in GGUF Q4_0 form {f16 d, qs[16]}. */
+static void cr_blocks(const cr_bind *b, uint64_t nblk, uint8_t *dst) {
+  for (uint64_t k = 0; k < nblk; k++, dst += 18) {
+    if (b->ver == 2) {
+      const uint8_t *s = b->qs + k * 20;
+      float d;
+      memcpy(&d, s + 16, 4);
+      const uint16_t h = cr_f16(d);
+      memcpy(dst, &h, 2);
+      memcpy(dst + 2, s, 16);
+    } else if (b->side >= 0) {
+      memcpy(dst, b->sc + k * 4 + (size_t)b->side * 2, 2);
+      memcpy(dst + 2, b->qs + k * 32 + (size_t)b->side * 16, 16);
+    } else {
+      memcpy(dst, b->sc + k * 2, 2);
+      memcpy(dst + 2, b->qs + k * 16, 16);
+    }
+  }
+}
+
+int cwen_gguf_tensor_bytes(const char *path, const char *name, void *out, size_t cap, int *from_sidecar) {
+  if (!path || !name) return host_fail(CWEN_EINVAL, "cwen_gguf_tensor_bytes: null argument");
+  gg_file g;
+  int rc = gg_open(path, &g);
+  if (rc) return rc;
+  int ti = -1;
+  for (int k = 0; k < g.nt; k++)
+    if (!strcmp(g.t[k].name, name)) { ti = k; break; }
+  if (ti < 0) {
+    gg_close(&g);
+    return host_fail(CWEN_EINVAL, "gguf: %s: no tensor %s", path, name);
+  }
+  const gg_tensor *x = &g.t[ti];
+  const uint64_t rows = x->ne[1] * x->ne[2] * x->ne[3];
+  const size_t nb = gg_nbytes(x->type, x->ne[0], rows);
+  if (!nb || nb > 0x7fffffffull) {
+    gg_close(&g);
+    return host_fail(CWEN_EINVAL, "gguf: %s: %s: type %d not readable here", path, name, x->type);
+  }
+  cr_file r;
+  cr_open(path, &g, &r);
+  const int side = r.b && r.b[ti].ver;
+  if (from_sidecar) *from_sidecar = side;
+  if (out) {
+    if (cap < nb) {
+      rc = host_fail(CWEN_EINVAL, "cwen_gguf_tensor_bytes: %s needs %zu bytes", name, nb);
+    } else if (side) {
+      cr_blocks(&r.b[ti], x->ne[0] / 32 * rows, (uint8_t *)out);
+    } else {
+      memcpy(out, x->data, nb);
+    }
+  }
+  cr_close(&r);
+  gg_close(&g);
+  return rc ? rc : (int)nb;
+}
+
 int cwen_gguf_dims(const char *path, cwen_dims *out) {
   if (!path || !out) return host_fail(CWEN_EINVAL, "cwen_gguf_dims: null argument");
   gg_file g;
@@ -294,11 +537,33 @@ int cwen_load_gguf(const char *path) {
     goto out;
   }
   rc = cwen_cuda_model_config(&d);
+  cr_file r;
+  cr_open(path, &g, &r);
+  uint8_t *buf = NULL; /* GGUF-form blocks of one sidecar-bound tensor */
+  size_t buf_len = 0;
   for (int i = 0; i < g.nt && !rc; i++) {
     const gg_tensor *x = &g.t[i];
     if (x->type != CWEN_T_F32 && x->type != CWEN_T_Q4_0 && x->type != CWEN_T_Q8_0) continue;
-    rc = cwen_cuda_upload(x->name, x->type, x->data, (int)x->ne[0], (int)(x->ne[1] * x->ne[2] * x->ne[3]));
+    const uint64_t rows = x->ne[1] * x->ne[2] * x->ne[3];
+    const void *src = x->data;
+    if (r.b && r.b[i].ver) {
+      const size_t nb = gg_nbytes(x->type, x->ne[0], rows);
+      if (nb > buf_len) {
+        free(buf);
+        buf = (uint8_t *)malloc(nb);
+        buf_len = buf ? nb : 0;
+        if (!buf) {
+          rc = host_fail(CWEN_ENOMEM, "cwenr: out of host memory for %s", x->name);
+          break;
+        }
+      }
+      cr_blocks(&r.b[i], x->ne[0] / 32 * rows, buf);
+      src = buf;
+    }
+    rc = cwen_cuda_upload(x->name, x->type, src, (int)x->ne[0], (int)rows);
   }
+  free(buf);
+  cr_close(&r);
   if (!rc) rc = cwen_cuda_model_finalize();
 out:
   gg_close(&g);

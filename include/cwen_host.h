@@ -15,8 +15,20 @@ extern "C" {
 /* ---- loading ---- */
 /* Parse a GGUF v2/v3 file (bounds-checked like load_gguf, run.c:3230-3303),
  * derive the geometry from the tensor shapes, upload every tensor and
- * finalize.  The engine must be initialised (cwen_cuda_init). */
+ * finalize.  The engine must be initialised (cwen_cuda_init).  Q4_0 tensors
+ * that the file's CWENR sidecar binds (load_cwenr, run.c:3305-3643: v2
+ * packed, v3 split, v4 split + interleaved pairs; path from CWEN_REPACK, else
+ * MODEL.gguf -> MODEL.cwenr) are uploaded from the sidecar's bytes; a
+ * missing, stale or malformed sidecar is ignored with a note on stderr, as
+ * the reference does. */
 int cwen_load_gguf(const char *path);
+/* The bytes cwen_load_gguf uploads for tensor `name` of the GGUF at `path`
+ * (GGUF block layout: f32 rows, or 18-byte Q4_0 / 34-byte Q8_0 blocks): from
+ * its CWENR sidecar when one binds the tensor, else from the GGUF.  Writes
+ * them to out (when out is non-NULL and cap is large enough), sets
+ * *from_sidecar (when non-NULL), and returns the byte count, or a negative
+ * CWEN_E* code.  No GPU needed. */
+int cwen_gguf_tensor_bytes(const char *path, const char *name, void *out, size_t cap, int *from_sidecar);
 /* The geometry cwen_load_gguf would derive from the file's tensor shapes,
  * with the same parse and bounds checks, without touching the engine (no
  * GPU needed).  CWEN_EINVAL with the reason in cwen_cuda_last_error() for a

@@ -48,3 +48,41 @@ def test_gguf_load_equals_synth(tmp_path):
     assert np.array_equal(a[1], b[1]) and np.array_equal(a[1], a[0])
     assert a[2] == b[2]
     assert np.array_equal(a[3], b[3])
+
+
+def test_cwenr_sidecar_supplies_the_q4_weights(tmp_path, monkeypatch):
+    """A CWENR sidecar beside the GGUF (load_cwenr, run.c:3486-3643) supplies
+    the Q4_0 weights the engine runs: GGUF A with a v4 sidecar that holds the
+    Q4_0 tensors of another seed's model gives, bit for bit, the logits and
+    serial stream of GGUF A with those tensors written into the file itself
+    (and not A's own).  A v3 sidecar of A's own tensors changes nothing."""
+    import cwen_b200
+    from cwen_b200 import build
+    from cwenr_util import GGUF_Q4_0, read_gguf_table, write_cwenr
+    build.build()
+    monkeypatch.delenv("CWEN_REPACK", raising=False)
+    L = cwen_b200.lib()
+    d = cwen_b200.dims("small")
+    d.has_mtp = 1
+    a_path, b_path = tmp_path / "a.gguf", tmp_path / "b.gguf"
+    cwen_b200.check(L.cwen_write_synth_gguf(str(a_path).encode(), C.byref(d), SEED, 0), "write a")
+    cwen_b200.check(L.cwen_write_synth_gguf(str(b_path).encode(), C.byref(d), SEED + 1, 0), "write b")
+    a, b = a_path.read_bytes(), b_path.read_bytes()
+    ta, tb = read_gguf_table(a), {n: (o, nb) for n, t, _, _, o, nb in read_gguf_table(b)}
+    blobs = {n: b[tb[n][0]:tb[n][0] + tb[n][1]] for n, t, _, _, _, _ in ta if t == GGUF_Q4_0}
+    assert blobs
+    c = bytearray(a)  # A with B's Q4_0 tensors in the file
+    for n, t, _, _, o, nb in ta:
+        if t == GGUF_Q4_0:
+            c[o:o + nb] = blobs[n]
+    c_path = tmp_path / "c.gguf"
+    c_path.write_bytes(bytes(c))
+    ref_c = _run(L, lambda d: L.cwen_load_gguf(str(c_path).encode()))
+    ref_a = _run(L, lambda d: L.cwen_load_gguf(str(a_path).encode()))
+    (tmp_path / "a.cwenr").write_bytes(write_cwenr(a, 4, blobs=blobs))
+    got = _run(L, lambda d: L.cwen_load_gguf(str(a_path).encode()))
+    assert np.array_equal(got[3], ref_c[3]) and np.array_equal(got[0], ref_c[0])
+    assert not np.array_equal(got[3], ref_a[3])
+    (tmp_path / "a.cwenr").write_bytes(write_cwenr(a, 3))
+    same = _run(L, lambda d: L.cwen_load_gguf(str(a_path).encode()))
+    assert np.array_equal(same[3], ref_a[3]) and np.array_equal(same[0], ref_a[0])
