@@ -211,11 +211,12 @@ struct QgLayout {
 // one B-operand lane holds; every load of the prologue is issued in one
 // round (items, row norm partials), the column maxima meet in shared memory
 // (an integer max of non-negative floats: order-free), and the second pass
-// converts from registers (the first two items of a thread) or reloads.
+// converts from registers (the first KEEP items of a thread: every item of
+// up to 8 columns x 40 k-pairs) or reloads.
 // cm: [16] int column maxima, ssc: [16] float row scales (shared memory).
 template <int NT>
 CW_DEV void x_local_prologue(const GemvArgs &a, uint4 *xl, float *xun, int *cm, float *ssc, int ka0, int nkp) {
-  constexpr int NTH = QG_CONS_WARPS * 32, KEEP = 2;
+  constexpr int NTH = QG_CONS_WARPS * 32, KEEP = NT == 1 ? 2 : 3;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int nblk = 2 * nkp, nitem = a.B * nblk * 4;
   if (tid < 16) cm[tid] = 0;
@@ -291,26 +292,13 @@ CW_DEV void x_local_prologue(const GemvArgs &a, uint4 *xl, float *xun, int *cm, 
     }
   }
   named_bar(1, NTH);  // per-column scales ready
-  for (int j = 0, it = tid; it < nitem; j++, it += NTH) {
+  // item it -> its 8 values as hi / lo fragments (u0: x[4t..4t+3], u1: x[4t+16..4t+19])
+  auto emit = [&](int it, const float4 &u0, const float4 &u1) {
     int b, kb, t;
     item_ptr(it, b, kb, t);
     float r[8];
-    if (j < KEEP) {
-      const float4 u0 = j == 0 ? kv[0][0] : kv[1][0], u1 = j == 0 ? kv[0][1] : kv[1][1];
-      r[0] = u0.x; r[1] = u0.y; r[2] = u0.z; r[3] = u0.w;
-      r[4] = u1.x; r[5] = u1.y; r[6] = u1.z; r[7] = u1.w;
-    } else {
-      const float *x = a.xr + (size_t)b * a.xrs + (size_t)ka0 * 64 + kb * 32 + 4 * t;
-      float4 u0 = __ldg(reinterpret_cast<const float4 *>(x)), u1 = __ldg(reinterpret_cast<const float4 *>(x + 16));
-      if (a.xw) {
-        const float *w = a.xw + (size_t)ka0 * 64 + kb * 32 + 4 * t;
-        const float4 w0 = __ldg(reinterpret_cast<const float4 *>(w)), w1 = __ldg(reinterpret_cast<const float4 *>(w + 16));
-        u0 = make_float4(w0.x * u0.x, w0.y * u0.y, w0.z * u0.z, w0.w * u0.w);
-        u1 = make_float4(w1.x * u1.x, w1.y * u1.y, w1.z * u1.z, w1.w * u1.w);
-      }
-      r[0] = u0.x; r[1] = u0.y; r[2] = u0.z; r[3] = u0.w;
-      r[4] = u1.x; r[5] = u1.y; r[6] = u1.z; r[7] = u1.w;
-    }
+    r[0] = u0.x; r[1] = u0.y; r[2] = u0.z; r[3] = u0.w;
+    r[4] = u1.x; r[5] = u1.y; r[6] = u1.z; r[7] = u1.w;
     const float sc = ssc[b];
     // B operand lane (col & 3, t): (x[4t], x[4t+2]) (x[4t+1], x[4t+3]) (x[4t+16], x[4t+18]) (x[4t+17], x[4t+19])
     // r[] holds x[4t..4t+3] then x[4t+16..4t+19]
@@ -327,6 +315,22 @@ CW_DEV void x_local_prologue(const GemvArgs &a, uint4 *xl, float *xun, int *cm, 
     uint4 *o = xl + ((size_t)kb * NT + (b >> 2)) * 32 + (b & 3) * 4 + t;
     o[0] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
     o[16] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+  };
+#pragma unroll
+  for (int j = 0; j < KEEP; j++)
+    if (tid + j * NTH < nitem) emit(tid + j * NTH, kv[j][0], kv[j][1]);
+  for (int it = tid + KEEP * NTH; it < nitem; it += NTH) {
+    int b, kb, t;
+    item_ptr(it, b, kb, t);
+    const float *x = a.xr + (size_t)b * a.xrs + (size_t)ka0 * 64 + kb * 32 + 4 * t;
+    float4 u0 = __ldg(reinterpret_cast<const float4 *>(x)), u1 = __ldg(reinterpret_cast<const float4 *>(x + 16));
+    if (a.xw) {
+      const float *w = a.xw + (size_t)ka0 * 64 + kb * 32 + 4 * t;
+      const float4 w0 = __ldg(reinterpret_cast<const float4 *>(w)), w1 = __ldg(reinterpret_cast<const float4 *>(w + 16));
+      u0 = make_float4(w0.x * u0.x, w0.y * u0.y, w0.z * u0.z, w0.w * u0.w);
+      u1 = make_float4(w1.x * u1.x, w1.y * u1.y, w1.z * u1.z, w1.w * u1.w);
+    }
+    emit(it, u0, u1);
   }
   named_bar(1, NTH);
 }
@@ -478,11 +482,16 @@ __global__ void __launch_bounds__(QGM_THREADS, 1) qgemv_kernel(GemvArgs a) {
         const uint8_t *stg = smem + st * Lay::STAGE;
         const uint4 *xs = XL ? reinterpret_cast<const uint4 *>(smem + Lay::XL_OFF) + (size_t)(ka + i - ka0) * (2 * NT * 32)
                              : reinterpret_cast<const uint4 *>(stg + Lay::WB);
-        // one n-tile: both m-tiles share the X loads; more: reload (registers)
-        uint4 xv1[2];
-        if (NT == 1) {
-          xv1[0] = xs[lane];
-          xv1[1] = xs[32 + lane];
+        // up to two n-tiles: both m-tiles share the stage's X loads; more:
+        // reload per m-tile (registers)
+        constexpr bool XH = NT <= 2;
+        constexpr int NH = XH ? NT : 1;
+        uint4 xh[2][NH];
+        if (XH) {
+#pragma unroll
+          for (int kbi = 0; kbi < 2; kbi++)
+#pragma unroll
+            for (int n = 0; n < NH; n++) xh[kbi][n] = xs[(kbi * NT + n) * 32 + lane];
         }
 #pragma unroll
         for (int mt = 0; mt < 2; mt++) {
@@ -509,7 +518,7 @@ __global__ void __launch_bounds__(QGM_THREADS, 1) qgemv_kernel(GemvArgs a) {
             const float dg8 = __half2float(__ushort_as_half((unsigned short)(dw >> 16)));
 #pragma unroll
             for (int n = 0; n < NT; n++) {
-              const uint4 xv = NT == 1 ? xv1[kbi] : xs[(kbi * NT + n) * 32 + lane];
+              const uint4 xv = XH ? xh[kbi][XH ? n : 0] : xs[(kbi * NT + n) * 32 + lane];
               float cc[4];
               mma_16816(cc, a0s0, a1s0, a2s0, a3s0, xv.x, xv.y, zero4);
               mma_16816(cc, a0s1, a1s1, a2s1, a3s1, xv.z, xv.w, cc);
