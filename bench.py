@@ -326,7 +326,7 @@ def gemv_ours_line(args, ws, rank, local, config):
     line["roofline"] = {"bound": "hbm", "achieved": round(ach, 1), "peak": hbm, "unit": "GB/s",
                         "frac": round(ach / hbm, 4), "peak_kind": peak_kind, "traffic": GEMV_NCU_TRAFFIC,
                         "traffic_source": GEMV_NCU_SOURCE,
-                        "kernel": "qgemv_kernel<Q4_0, one n-tile of 8 columns, local X>",
+                        "kernel": "qgemv_kernel<Q4_0, two n-tiles of 4 columns (f16 hi | lo), local X>",
                         "kernel_ms": round(ms, 5), "serialised_kernel_ms": round(kern["ms"], 5)}
     e2e_gbs = GEMV_BYTES / e2e_s / 1e9
     line["e2e"] = {"value": round(e2e_gbs * ws, 2), "unit": "GB/s", "h2d_bytes_per_step": GEMV_B * GEMV_K * 4,
