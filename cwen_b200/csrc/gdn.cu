@@ -96,7 +96,55 @@ __global__ void __launch_bounds__(128) gdn_conv_kernel(const float *__restrict__
 // one exchange of the halves' per-row sums of squares through distributed
 // shared memory after the last row. ----
 constexpr int GDN_T = 256;
-constexpr int KQ_PAD = 33;  // a quarter's 32 keys + 1: the 4 quarters read 4 different banks
+// a quarter's 32 keys + 4: the 4 quarters' float4 reads start on banks 0, 4, 8
+// and 12 (conflict-free) and stay 16-byte aligned
+constexpr int KQ_PAD = 36;
+
+// One row of the delta rule on this thread's quarter (32 keys) of value
+// column j, the state slice s in registers:
+//   s *= g;  sk = S^T k (this quarter, then the four quarters);
+//   d = beta (v - sk);  s += k d;  o = S^T q (likewise).
+// The quarter's dot products run as four interleaved partial sums (keys i,
+// i+4, ... in each) added pairwise, so the dependent FMA chains are 8 long;
+// the state update is the plain fma(k, d, s * g) the rollback replay
+// repeats from the stored (g, k, d).
+CW_DEV void gdn_row(float (&s)[32], const float *kk, const float *qq, float g, float beta, float v, float &d,
+                    float &o) {
+  const float4 *k4 = reinterpret_cast<const float4 *>(kk), *q4v = reinterpret_cast<const float4 *>(qq);
+  float p0 = 0.f, p1 = 0.f, p2 = 0.f, p3 = 0.f;
+#pragma unroll
+  for (int m = 0; m < 8; m++) {
+    const float4 k = k4[m];
+    s[4 * m + 0] *= g;
+    s[4 * m + 1] *= g;
+    s[4 * m + 2] *= g;
+    s[4 * m + 3] *= g;
+    p0 = fmaf(s[4 * m + 0], k.x, p0);
+    p1 = fmaf(s[4 * m + 1], k.y, p1);
+    p2 = fmaf(s[4 * m + 2], k.z, p2);
+    p3 = fmaf(s[4 * m + 3], k.w, p3);
+  }
+  float sk = (p0 + p1) + (p2 + p3);
+  sk += __shfl_xor_sync(0xffffffffu, sk, 8);
+  sk += __shfl_xor_sync(0xffffffffu, sk, 16);
+  d = beta * (v - sk);
+  p0 = p1 = p2 = p3 = 0.f;
+#pragma unroll
+  for (int m = 0; m < 8; m++) {
+    const float4 k = k4[m], q = q4v[m];
+    s[4 * m + 0] = fmaf(k.x, d, s[4 * m + 0]);
+    s[4 * m + 1] = fmaf(k.y, d, s[4 * m + 1]);
+    s[4 * m + 2] = fmaf(k.z, d, s[4 * m + 2]);
+    s[4 * m + 3] = fmaf(k.w, d, s[4 * m + 3]);
+    p0 = fmaf(s[4 * m + 0], q.x, p0);
+    p1 = fmaf(s[4 * m + 1], q.y, p1);
+    p2 = fmaf(s[4 * m + 2], q.z, p2);
+    p3 = fmaf(s[4 * m + 3], q.w, p3);
+  }
+  o = (p0 + p1) + (p2 + p3);
+  o += __shfl_xor_sync(0xffffffffu, o, 8);
+  o += __shfl_xor_sync(0xffffffffu, o, 16);
+}
 
 __global__ void __launch_bounds__(GDN_T) gdn_recur_kernel(const float *__restrict__ Sin, float *__restrict__ Sout,
                                                           const float *__restrict__ gin, int B, int nkh, int nvh,
@@ -112,7 +160,7 @@ __global__ void __launch_bounds__(GDN_T) gdn_recur_kernel(const float *__restric
   const int j = half * 64 + col;
   const int QKV = (2 * nkh + nvh) * 128;
   const int GS = QKV + 2 * nvh;
-  __shared__ float kq[GDN_MAXB][2][4 * KQ_PAD];  // per row: k, q of key head hk
+  __shared__ __align__(16) float kq[GDN_MAXB][2][4 * KQ_PAD];  // per row: k, q of key head hk
   __shared__ float vsh[GDN_MAXB][64];             // v of this half's columns
   __shared__ float gb[GDN_MAXB][2];               // gate, beta
   __shared__ float ob[GDN_MAXB][64];              // raw outputs of this half, per row
@@ -138,26 +186,9 @@ __global__ void __launch_bounds__(GDN_T) gdn_recur_kernel(const float *__restric
   const float scale = 1.f / sqrtf(128.f);
   for (int b = 0; b < B; b++) {
     const float *kk = &kq[b][0][q4 * KQ_PAD], *qq = &kq[b][1][q4 * KQ_PAD];
-    const float g = gb[b][0], beta = gb[b][1];
-    // S *= g; S^T k over this quarter, then over the four quarters
-    float sk = 0.f;
-#pragma unroll
-    for (int i = 0; i < 32; i++) {
-      s[i] = s[i] * g;
-      sk = fmaf(s[i], kk[i], sk);
-    }
-    sk += __shfl_xor_sync(0xffffffffu, sk, 8);
-    sk += __shfl_xor_sync(0xffffffffu, sk, 16);
-    const float d = beta * (vsh[b][col] - sk);
+    float d, o;
+    gdn_row(s, kk, qq, gb[b][0], gb[b][1], vsh[b][col], d, o);
     if (q4 == 0) delta[(size_t)b * nvh * 128 + hv * 128 + j] = d;
-    float o = 0.f;
-#pragma unroll
-    for (int i = 0; i < 32; i++) {
-      s[i] = fmaf(kk[i], d, s[i]);
-      o = fmaf(s[i], qq[i], o);
-    }
-    o += __shfl_xor_sync(0xffffffffu, o, 8);
-    o += __shfl_xor_sync(0xffffffffu, o, 16);
     if (q4 == 0) ob[b][col] = o * scale;
   }
   float *S1 = Sout + (size_t)hv * 128 * 128;
@@ -216,7 +247,7 @@ __global__ void __launch_bounds__(GDN_T) gdn_fused_kernel(const GdnLayerArgs a, 
   const int j = half * 64 + col;
   const int QKV = (2 * nkh + nvh) * 128;
   const int GS = QKV + 2 * nvh;
-  __shared__ float kq[GDN_MAXB][2][4 * KQ_PAD];
+  __shared__ __align__(16) float kq[GDN_MAXB][2][4 * KQ_PAD];
   __shared__ float vsh[GDN_MAXB][64];
   __shared__ float gb[GDN_MAXB][2];
   __shared__ float ob[GDN_MAXB][64];
@@ -345,25 +376,9 @@ __global__ void __launch_bounds__(GDN_T) gdn_fused_kernel(const GdnLayerArgs a, 
   const float scale = 1.f / sqrtf(128.f);
   for (int b = 0; b < B; b++) {
     const float *kk = &kq[b][0][q4 * KQ_PAD], *qq = &kq[b][1][q4 * KQ_PAD];
-    const float g = gb[b][0], beta = gb[b][1];
-    float sk = 0.f;
-#pragma unroll
-    for (int i = 0; i < 32; i++) {
-      s[i] = s[i] * g;
-      sk = fmaf(s[i], kk[i], sk);
-    }
-    sk += __shfl_xor_sync(0xffffffffu, sk, 8);
-    sk += __shfl_xor_sync(0xffffffffu, sk, 16);
-    const float d = beta * (vsh[b][col] - sk);
+    float d, o;
+    gdn_row(s, kk, qq, gb[b][0], gb[b][1], vsh[b][col], d, o);
     if (keep < 0 && q4 == 0) a.delta[(size_t)b * nvh * 128 + hv * 128 + j] = d;
-    float o = 0.f;
-#pragma unroll
-    for (int i = 0; i < 32; i++) {
-      s[i] = fmaf(kk[i], d, s[i]);
-      o = fmaf(s[i], qq[i], o);
-    }
-    o += __shfl_xor_sync(0xffffffffu, o, 8);
-    o += __shfl_xor_sync(0xffffffffu, o, 16);
     if (q4 == 0) ob[b][col] = o * scale;
     if (b == nsnap - 1) {
 #pragma unroll
