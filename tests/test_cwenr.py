@@ -237,3 +237,30 @@ def test_stamp_follows_the_gguf_size(L, tmp_path):
     with open(g, "ab") as f:  # one page more: stale
         f.write(bytes(2))
     assert _read(L, g, "blk.0.ssm_out.weight")[1] == 0
+
+
+def test_v2_scale_rounds_to_nearest_even(L, tmp_path):
+    """A v2 sidecar stores f32 scales; the loader rounds them to f16 the way
+    the reference's runtime split does (f32_to_f16, run.c:3623: IEEE
+    round-to-nearest-even, as F16C's vcvtps2ph), including ties, the
+    subnormal range and overflow to infinity."""
+    import numpy as np
+    sc = bytearray((GOLD / "cwenr_tiny.v2.cwenr").read_bytes())
+    _, base, ents = _entries(sc)
+    _, ne0, ne1, a, b, _ = ents["blk.0.ssm_out.weight"]
+    nblk = ne0 // 32 * ne1
+    one = np.float32(1.0)
+    tie = np.float32(1.0 + 2.0 ** -11)       # halfway between two f16 values: rounds to even (1.0)
+    tie_up = np.float32(1.0 + 3 * 2.0 ** -11)  # halfway, rounds up to the even neighbour
+    vals = [np.float32(0.0123456), tie, tie_up, np.float32(3e-6), np.float32(-7.5e-8), np.float32(7e4),
+            np.float32(-0.0), one]
+    vals = (vals * ((nblk + len(vals) - 1) // len(vals)))[:nblk]
+    for k, v in enumerate(vals):
+        struct.pack_into("<f", sc, base + a + 20 * k + 16, float(v))
+    g = _setup(tmp_path, bytes(sc))
+    data, side = _read(L, g, "blk.0.ssm_out.weight")
+    assert side == 1
+    got = np.frombuffer(data, np.uint8).reshape(nblk, 18)[:, :2].copy().view("<u2").ravel()
+    with np.errstate(over="ignore"):  # 7e4 is past the f16 range: +inf, as in the reference
+        want = np.array(vals, np.float32).astype(np.float16).view("<u2")
+    assert np.array_equal(got, want), (got[:8], want[:8])
